@@ -1,0 +1,218 @@
+"""Headline benchmark: AllReduce bus bandwidth on B200 (headline size).
+
+One step = one out-of-place fp32 SUM AllReduce of ``--bytes`` per rank through this library's
+device communicator. Launch with N=1 as ``python bench.py``; for N>1 under torchrun (one rank per
+GPU). Rank 0 prints one JSON line:
+
+* ``value``: whole-job bus bandwidth, i.e. the NCCL bus bandwidth (algbw * 2(N-1)/N) summed over
+  the N ranks. For N=1 there is no bus (2(N-1)/N = 0): the single-rank AllReduce is a device
+  copy and ``value`` is its algbw, flagged in ``config.n1_semantics``.
+* ``ms_per_step``: device time per AllReduce (CUDA events, max over ranks).
+* ``e2e``: the same metric through the public Python API with the step's input copied from
+  pinned host memory and a sample of the result read back every step.
+* ``nccl``: the same op through torch.distributed (NCCL) on the same box, for comparison.
+
+``--impl reference`` runs the reference's own code path; the reference is a CMake C++ project
+without a Python package and cannot be built on this image, so that arm prints an
+``unavailable`` line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# Published busbw of the reference at 128 MiB, fp32 SUM, OCCL auto, 1 host x 4 ranks over shared
+# memory (README.md:223): 7.52 GB/s per rank, 30.08 GB/s summed over its 4 ranks.
+REFERENCE_WHOLE_JOB_GBS = 4 * 7.52
+
+REFERENCE_UNAVAILABLE = (
+    "reference (qichen1336/OriginCCL) is a CPU-only CMake C++17 library with no setup.py/pyproject "
+    "(pip install fails: 'not installable') and a hard dependency on libibverbs/librdmacm/fmt/MPI, "
+    "none of which exist on this image; it has no GPU code path to run")
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--bytes", type=int, default=128 << 20, help="payload per rank")
+    p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    return p.parse_args()
+
+
+def main() -> None:
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+        return
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    import torch
+    import torch.distributed as dist
+
+    import originccl_b200 as occl
+    from originccl_b200.utils.clocks import ClockSampler
+    from originccl_b200.utils.timing import busbw_factor
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
+        comm = occl.init_from_store(dist.distributed_c10d._get_default_store(), rank, world, device=local)
+        barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
+    else:
+        comm = occl.Communicator().init(0, 1, None, device=0)
+        barrier = lambda: None  # noqa: E731
+
+    dtype = {"float32": torch.float32, "bfloat16": torch.bfloat16}[args.dtype]
+    esize = torch.empty((), dtype=dtype).element_size()
+    count = args.bytes // esize
+    nbytes = count * esize
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    # Two rotating inputs + output: 3 x 128 MiB on every rank, larger than the 126 MB L2.
+    xs = [(torch.rand(count, device="cuda", generator=g) * 2 - 1).to(dtype) for _ in range(2)]
+    y = torch.empty(count, device="cuda", dtype=dtype)
+
+    def step(i: int) -> None:
+        comm.all_reduce(xs[i & 1], out=y)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    # correctness of the last warm-up step against NCCL (fp32 accumulation of fp32 inputs)
+    check = xs[(args.warmup - 1) & 1].clone().float()
+    if world > 1:
+        dist.all_reduce(check)
+    max_err = float((y.float() - check).abs().max().item()) if args.warmup > 0 else 0.0
+
+    gpus = [int(d) for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip().isdigit()]
+    gpus = gpus or list(range(world))
+    launches0 = comm.kernel_launches
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpus if rank == 0 else []) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches = comm.kernel_launches - launches0
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    algbw = nbytes / (ms * 1e-3) / 1e9
+    factor = busbw_factor("allreduce", world)
+    busbw = algbw * factor
+    value = busbw * world if world > 1 else algbw
+
+    # NCCL (torch.distributed) on the same buffers, same timing rules.
+    nccl = None
+    if world > 1 and not args.no_nccl:
+        yy = y.clone()
+        for i in range(args.warmup):
+            yy.copy_(xs[i & 1]); dist.all_reduce(yy)
+        torch.cuda.synchronize()
+        # time only the all_reduce, in place on one buffer (the values do not affect the time)
+        barrier(); torch.cuda.synchronize()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for i in range(args.steps):
+            dist.all_reduce(yy)
+        e2.record(); torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
+        tn = torch.tensor([s2.elapsed_time(e2) / args.steps], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tn, op=dist.ReduceOp.MAX)
+        nms = float(tn.item())
+        nbus = nbytes / (nms * 1e-3) / 1e9 * factor
+        nccl = {"ms_per_step": round(nms, 4), "busbw_gbs_per_rank": round(nbus, 2), "value": round(nbus * world, 2)}
+
+    # End to end through the public API: pinned H2D of this step's input, the collective, and a
+    # device->host read of a 64 KiB sample of the result, every step (wall clock, max over ranks).
+    host_in = [xs[i].cpu().pin_memory() for i in range(2)]
+    dev_in = torch.empty_like(xs[0])
+    sample = torch.empty(65536 // esize, dtype=dtype).pin_memory()
+    for i in range(2):
+        dev_in.copy_(host_in[i], non_blocking=True); comm.all_reduce(dev_in, out=y)
+        sample.copy_(y[: sample.numel()], non_blocking=True); torch.cuda.synchronize()
+    barrier(); torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        dev_in.copy_(host_in[i & 1], non_blocking=True)
+        comm.all_reduce(dev_in, out=y)
+        sample.copy_(y[: sample.numel()], non_blocking=True)
+        torch.cuda.synchronize()
+        _ = float(sample[0])
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    e2e_algbw = nbytes / (e2e_ms * 1e-3) / 1e9
+    e2e_value = e2e_algbw * factor * world if world > 1 else e2e_algbw
+
+    if rank == 0:
+        out = {
+            "metric": "AllReduce bus GB/s vs size at 2/4/8 B200 (max over ranks) vs reference & NCCL",
+            "value": round(value, 2),
+            "unit": "GB/s (bus bandwidth summed over ranks)",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": round(value / REFERENCE_WHOLE_JOB_GBS, 2),
+            "dtype": {"float32": "fp32", "bfloat16": "bf16"}[args.dtype],
+            "data": "synthetic (uniform [-1,1), seed 1234+rank)",
+            "config": {
+                "model": f"AllReduce SUM out-of-place, {args.dtype}",
+                "global_batch": world,
+                "seq_len": count,
+                "parallelism": f"dp{world}",
+                "bytes_per_rank": nbytes,
+                "busbw_gbs_per_rank": round(busbw, 2),
+                "algbw_gbs": round(algbw, 2),
+                "algorithm": comm.last_algorithm,
+                "nvls": comm.nvls_enabled,
+                "l2": "inputs larger than L2: two rotating 128 MiB inputs + a 128 MiB output per rank",
+                "n1_semantics": ("N=1 has no bus (factor 2(N-1)/N = 0); value is the algbw of the single-rank "
+                                 "AllReduce (a device copy)") if world == 1 else None,
+                "max_abs_err_vs_nccl": max_err,
+                "baseline_number": "reference 7.52 GB/s/rank x 4 ranks at 128 MiB fp32 (README.md:223)",
+            },
+            "nccl": nccl,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s (bus bandwidth summed over ranks)",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": sample.numel() * esize, "steps": args.e2e_steps,
+                    "api": "originccl_b200.Communicator.all_reduce"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    comm.destroy()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

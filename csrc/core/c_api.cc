@@ -1,0 +1,239 @@
+// C interface over bccl::Communicator (see bccl/c_api.h).
+#include "bccl/c_api.h"
+
+#include <cstring>
+#include <string>
+
+#include "bccl/communicator.h"
+#include "core/logger.h"
+#include "core/planner.h"
+#include "device/device_engine.h"
+
+struct bcclComm {
+    bccl::Communicator comm;
+};
+
+namespace {
+
+// Logical-machine hostname injection for bcclConfig::logical_machine_size: Init calls the
+// hostname function synchronously on the calling thread, so a thread-local carries the name.
+thread_local std::string t_logical_host;
+std::string LogicalHostname() { return t_logical_host; }
+
+int Fail() { return 1; }
+
+void ApplyStream(bcclComm_t c, uintptr_t stream, int has_stream) {
+    if (!c->comm.IsDevice()) return;
+    if (has_stream) {
+        c->comm.SetStream(reinterpret_cast<void*>(stream));
+    } else {
+        c->comm.ClearStream();
+    }
+}
+
+bccl::CollTask MakeTask(bccl::CollFunc f, const void* send, void* recv, size_t count, int dtype, int op, int root,
+                        int peer, float scale, int algo) {
+    bccl::CollTask t;
+    t.func = f;
+    t.send_buf = send;
+    t.recv_buf = recv;
+    t.count = count;
+    t.dtype = static_cast<bccl::DataType>(dtype);
+    t.op = static_cast<bccl::ReduceOp>(op);
+    t.root = root;
+    t.peer = peer;
+    t.scale = scale;
+    t.algo = static_cast<bccl::Algo>(algo);
+    return t;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bcclCommCreate(bcclComm_t* comm) {
+    if (comm == nullptr) return Fail();
+    *comm = new bcclComm();
+    return 0;
+}
+
+int bcclGetUniqueId(bcclComm_t comm, char ip_addr[64], uint16_t* port) {
+    bccl::UniqueId id;
+    if (comm == nullptr || !comm->comm.GetUniqueId(id)) return Fail();
+    memcpy(ip_addr, id.ip_addr, sizeof(id.ip_addr));
+    *port = id.port;
+    return 0;
+}
+
+int bcclCommInit(bcclComm_t comm, const bcclConfig* cfg) {
+    if (comm == nullptr || cfg == nullptr) return Fail();
+    bccl::CommConfig c;
+    c.rank = cfg->rank;
+    c.world_size = cfg->world_size;
+    memcpy(c.unique_id.ip_addr, cfg->ip_addr, sizeof(c.unique_id.ip_addr));
+    c.unique_id.ip_addr[sizeof(c.unique_id.ip_addr) - 1] = '\0';
+    c.unique_id.port = cfg->port;
+    c.n_channels = cfg->n_channels;
+    c.device = cfg->device;
+    c.buffer_bytes = cfg->buffer_bytes;
+    c.timeout_ms = cfg->timeout_ms;
+    c.enable_nvls = cfg->enable_nvls != 0;
+    c.enable_nccl_p2p = cfg->enable_nccl_p2p != 0;
+    if (cfg->logical_machine_size > 0) {
+        t_logical_host = "logical-machine-" + std::to_string(cfg->rank / cfg->logical_machine_size);
+        c.get_hostname = LogicalHostname;
+    }
+    return comm->comm.Init(c) ? 0 : Fail();
+}
+
+int bcclCommFinalize(bcclComm_t comm) {
+    if (comm == nullptr) return Fail();
+    comm->comm.Finalize();
+    return 0;
+}
+
+int bcclCommDestroy(bcclComm_t comm) {
+    delete comm;
+    return 0;
+}
+
+const char* bcclGetLastError(void) { return bccl::LastErrorMessage(); }
+
+const char* bcclVersion(void) { return "bccl 0.1.0 (sm_100a)"; }
+
+int bcclCommInfo(bcclComm_t comm, int* rank, int* world, int* local_rank, int* local_size, int* machine_index,
+                 int* machine_count, int* n_channels) {
+    if (comm == nullptr) return Fail();
+    const bccl::Communicator& c = comm->comm;
+    if (rank) *rank = c.GetRank();
+    if (world) *world = c.GetWorldSize();
+    if (local_rank) *local_rank = c.GetLocalRank();
+    if (local_size) *local_size = c.GetLocalSize();
+    if (machine_index) *machine_index = c.GetMachineIndex();
+    if (machine_count) *machine_count = c.GetMachineCount();
+    if (n_channels) *n_channels = c.GetNChannels();
+    return 0;
+}
+
+int bcclCommLocalRanks(bcclComm_t comm, int* out, int max) {
+    if (comm == nullptr) return -1;
+    const auto& v = comm->comm.GetLocalRanks();
+    for (int i = 0; i < max && i < static_cast<int>(v.size()); ++i) out[i] = v[i];
+    return static_cast<int>(v.size());
+}
+
+int bcclCommMachineLeaders(bcclComm_t comm, int* out, int max) {
+    if (comm == nullptr) return -1;
+    const auto& v = comm->comm.GetMachineLeaders();
+    for (int i = 0; i < max && i < static_cast<int>(v.size()); ++i) out[i] = v[i];
+    return static_cast<int>(v.size());
+}
+
+int bcclCommNvlsEnabled(bcclComm_t comm) { return comm && comm->comm.NvlsEnabled() ? 1 : 0; }
+const char* bcclCommLastAlgorithm(bcclComm_t comm) { return comm ? comm->comm.LastAlgorithm() : ""; }
+unsigned long long bcclCommKernelLaunches(bcclComm_t comm) { return comm ? comm->comm.KernelLaunches() : 0; }
+const char* bcclCommP2pTransport(bcclComm_t comm, int peer) { return comm ? comm->comm.P2pTransportName(peer) : ""; }
+const char* bcclCommHostExecutor(bcclComm_t comm) { return comm ? comm->comm.HostExecutorName() : ""; }
+
+int bcclGroupStart(bcclComm_t comm) {
+    if (comm == nullptr) return Fail();
+    comm->comm.GroupStart();
+    return 0;
+}
+
+int bcclGroupEnd(bcclComm_t comm, uintptr_t stream, int has_stream) {
+    if (comm == nullptr) return Fail();
+    ApplyStream(comm, stream, has_stream);
+    return comm->comm.GroupEnd() ? 0 : Fail();
+}
+
+#define BCCL_SUBMIT(task)                        \
+    if (comm == nullptr) return Fail();          \
+    ApplyStream(comm, stream, has_stream);       \
+    return comm->comm.Submit(task) ? 0 : Fail();
+
+int bcclAllReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, float scale, int algo,
+                  uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::AllReduce, send, recv, count, dtype, op, 0, -1, scale, algo));
+}
+
+int bcclBroadcast(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int root, int algo,
+                  uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::Broadcast, send ? send : recv, recv, count, dtype, 0, root, -1, 1.0f, algo));
+}
+
+int bcclReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, int root, int algo,
+               uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::Reduce, send, recv, count, dtype, op, root, -1, 1.0f, algo));
+}
+
+int bcclAllGather(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, uintptr_t stream,
+                  int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::AllGather, send, recv, count, dtype, 0, 0, -1, 1.0f, 0));
+}
+
+int bcclReduceScatter(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op,
+                      uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::ReduceScatter, send, recv, count, dtype, op, 0, -1, 1.0f, 0));
+}
+
+int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::Send, buf, nullptr, count, dtype, 0, 0, peer, 1.0f, 0));
+}
+
+int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::Recv, nullptr, buf, count, dtype, 0, 0, peer, 1.0f, 0));
+}
+
+int bcclSynchronize(bcclComm_t comm) { return comm && comm->comm.Synchronize() ? 0 : Fail(); }
+int bcclBarrier(bcclComm_t comm) { return comm && comm->comm.Barrier() ? 0 : Fail(); }
+void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes) { return comm ? comm->comm.SymmetricAlloc(bytes) : nullptr; }
+int bcclSymmetricFree(bcclComm_t comm, void* ptr) { return comm && comm->comm.SymmetricFree(ptr) ? 0 : Fail(); }
+
+int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms) {
+    if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1;
+    return comm->comm.device_engine()->WaitProbe(timeout_ms);
+}
+
+int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,
+                    const int* root, const int* peer, int* order) {
+    std::vector<bccl::CollTask> tasks(n);
+    static const char kMark = 0;
+    for (int i = 0; i < n; ++i) {
+        tasks[i] = MakeTask(static_cast<bccl::CollFunc>(func[i]), &kMark, const_cast<char*>(&kMark), count[i], dtype[i],
+                            op[i], root[i], peer[i], 1.0f, 0);
+        // Tag each task with its input index through the scale field (planner ignores it).
+        tasks[i].scale = static_cast<float>(i);
+    }
+    bccl::Planner planner;
+    if (!planner.SortTasks(tasks, rank, world)) return Fail();
+    for (int i = 0; i < n; ++i) order[i] = static_cast<int>(tasks[i].scale);
+    return 0;
+}
+
+int bcclPlannerP2pRound(int func, int rank, int peer, int world) {
+    return bccl::Planner::P2pRoundOf(static_cast<bccl::CollFunc>(func), rank, peer, world);
+}
+
+int bcclPlannerValidate(int rank, int world, int func, size_t count, int dtype, int op, int root, int peer,
+                        int has_send, int has_recv) {
+    static char buf[16];
+    bccl::CollTask t = MakeTask(static_cast<bccl::CollFunc>(func), has_send ? buf : nullptr, has_recv ? buf : nullptr,
+                                count, dtype, op, root, peer, 1.0f, 0);
+    bccl::Planner planner;
+    bool ok = bccl::IsP2p(t.func) ? planner.ValidateP2p(t, rank, world) : planner.ValidateCollectiveTask(t, rank, world);
+    return ok ? 0 : Fail();
+}
+
+int bcclPlannerChoose(int func, int dtype, int op, size_t bytes, int world, int nvls_ok, int max_ctas, int* algo,
+                      int* ctas) {
+    bccl::Planner planner;
+    bccl::AlgoChoice c = planner.ChooseAlgo(static_cast<bccl::CollFunc>(func), static_cast<bccl::DataType>(dtype),
+                                            static_cast<bccl::ReduceOp>(op), bytes, world, nvls_ok != 0, max_ctas,
+                                            bccl::Algo::kAuto);
+    *algo = static_cast<int>(c.algo);
+    *ctas = c.ctas;
+    return 0;
+}
+
+}  // extern "C"

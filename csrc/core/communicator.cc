@@ -1,0 +1,380 @@
+#include "bccl/communicator.h"
+
+#include <unistd.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+
+#include "core/bootstrap.h"
+#include "core/env.h"
+#include "core/fdpass.h"
+#include "core/logger.h"
+#include "core/net.h"
+#include "core/planner.h"
+#include "device/device_engine.h"
+#include "host/host_engine.h"
+
+namespace bccl {
+
+std::string DefaultHostname() { return net::Hostname(); }
+
+size_t DataTypeSize(DataType dtype) {
+    switch (dtype) {
+    case DataType::FLOAT32: return 4;
+    case DataType::FLOAT64: return 8;
+    case DataType::INT32: return 4;
+    case DataType::INT64: return 8;
+    case DataType::BF16: return 2;
+    case DataType::FP16: return 2;
+    }
+    return 0;
+}
+
+const char* DataTypeName(DataType dtype) {
+    switch (dtype) {
+    case DataType::FLOAT32: return "float32";
+    case DataType::FLOAT64: return "float64";
+    case DataType::INT32: return "int32";
+    case DataType::INT64: return "int64";
+    case DataType::BF16: return "bfloat16";
+    case DataType::FP16: return "float16";
+    }
+    return "unknown";
+}
+
+const char* ReduceOpName(ReduceOp op) {
+    switch (op) {
+    case ReduceOp::SUM: return "sum";
+    case ReduceOp::MAX: return "max";
+    case ReduceOp::MIN: return "min";
+    case ReduceOp::AVG: return "avg";
+    }
+    return "unknown";
+}
+
+const char* CollFuncName(CollFunc f) {
+    switch (f) {
+    case CollFunc::AllReduce: return "allreduce";
+    case CollFunc::Broadcast: return "broadcast";
+    case CollFunc::Reduce: return "reduce";
+    case CollFunc::AllGather: return "allgather";
+    case CollFunc::ReduceScatter: return "reducescatter";
+    case CollFunc::Send: return "send";
+    case CollFunc::Recv: return "recv";
+    }
+    return "unknown";
+}
+
+const char* AlgoName(Algo a) {
+    switch (a) {
+    case Algo::kAuto: return "auto";
+    case Algo::kOneShot: return "oneshot";
+    case Algo::kTwoShot: return "twoshot";
+    case Algo::kNvls: return "nvls";
+    case Algo::kRing: return "ring";
+    }
+    return "unknown";
+}
+
+Communicator::Communicator() : planner_(new Planner()) {}
+
+Communicator::~Communicator() { Finalize(); }
+
+bool Communicator::GetUniqueId(UniqueId& unique_id) {
+    if (have_unique_id_) {
+        LOG_ERROR("GetUniqueId called twice on the same communicator");
+        return false;
+    }
+    uint16_t port = 0;
+    bootstrap_listen_fd_ = net::Listen(0, &port);
+    if (bootstrap_listen_fd_ < 0) return false;
+    std::string ip = net::LocalIpAddress();
+    memset(&unique_id, 0, sizeof(unique_id));
+    strncpy(unique_id.ip_addr, ip.c_str(), sizeof(unique_id.ip_addr) - 1);
+    unique_id.port = port;
+    have_unique_id_ = true;
+    return true;
+}
+
+bool Communicator::Init(const CommConfig& cfg) {
+    if (inited_) {
+        LOG_ERROR("Init called twice");
+        return false;
+    }
+    if (cfg.world_size <= 0 || cfg.rank < 0 || cfg.rank >= cfg.world_size) {
+        LOG_ERROR("invalid rank %d / world size %d", cfg.rank, cfg.world_size);
+        return false;
+    }
+    config_ = cfg;
+    if (config_.get_hostname == nullptr) config_.get_hostname = DefaultHostname;
+    user_stream_ = cfg.stream;
+    has_user_stream_ = cfg.stream != nullptr;
+    if (cfg.world_size > 1 && cfg.rank == 0 && bootstrap_listen_fd_ < 0) {
+        LOG_ERROR("rank 0 must call GetUniqueId before Init");
+        return false;
+    }
+    // Every listener exists before the bootstrap announces it (no port races).
+    fdpass_.reset(new FdPasser());
+    const std::string ns = std::string(cfg.unique_id.ip_addr) + ":" + std::to_string(cfg.unique_id.port);
+    if (!fdpass_->Listen(ns, cfg.rank)) return false;
+    uint16_t data_port = 0;
+    if (cfg.device < 0) {
+        data_listen_fd_ = net::Listen(0, &data_port);
+        if (data_listen_fd_ < 0) return false;
+    }
+    NodeInfo me;
+    me.rank = cfg.rank;
+    me.ip_addr = net::LocalIpAddress();
+    me.data_port = data_port;
+    me.hostname = config_.get_hostname();
+    me.device = cfg.device;
+    me.pid = static_cast<int>(getpid());
+    bootstrap_.reset(new Bootstrap());
+    if (!bootstrap_->Run(config_, me, bootstrap_listen_fd_, &all_nodes_)) return false;
+
+    // Local and machine views: machines are numbered by first appearance of their hostname;
+    // a machine's leader is its lowest rank.
+    std::map<std::string, int> machine_id;
+    std::vector<int> machine_of(cfg.world_size);
+    std::vector<std::vector<int>> machine_ranks;
+    for (int r = 0; r < cfg.world_size; ++r) {
+        auto it = machine_id.find(all_nodes_[r].hostname);
+        int m;
+        if (it == machine_id.end()) {
+            m = static_cast<int>(machine_ranks.size());
+            machine_id[all_nodes_[r].hostname] = m;
+            machine_ranks.emplace_back();
+        } else {
+            m = it->second;
+        }
+        machine_of[r] = m;
+        machine_ranks[m].push_back(r);
+    }
+    machine_index_ = machine_of[cfg.rank];
+    machine_count_ = static_cast<int>(machine_ranks.size());
+    local_ranks_ = machine_ranks[machine_index_];
+    local_size_ = static_cast<int>(local_ranks_.size());
+    local_rank_ = static_cast<int>(std::find(local_ranks_.begin(), local_ranks_.end(), cfg.rank) - local_ranks_.begin());
+    machine_leaders_.clear();
+    for (const auto& mr : machine_ranks) machine_leaders_.push_back(mr.front());
+
+    if (cfg.device >= 0) {
+        if (machine_count_ != 1) {
+            LOG_ERROR("device communicators span one NVSwitch node; %d machines were found", machine_count_);
+            return false;
+        }
+        device_.reset(new DeviceEngine());
+        if (!device_->Init(config_, bootstrap_.get(), fdpass_.get(), planner_.get())) {
+            device_.reset();
+            return false;
+        }
+    } else {
+        MachineView v;
+        v.local_rank = local_rank_;
+        v.local_size = local_size_;
+        v.local_ranks = local_ranks_;
+        v.machine_index = machine_index_;
+        v.machine_count = machine_count_;
+        v.machine_leaders = machine_leaders_;
+        v.machine_of = machine_of;
+        v.machine_ranks = machine_ranks;
+        v.local_index_of.assign(cfg.world_size, 0);
+        for (const auto& mr : machine_ranks)
+            for (size_t i = 0; i < mr.size(); ++i) v.local_index_of[mr[i]] = static_cast<int>(i);
+        host_.reset(new HostEngine());
+        if (!host_->Init(config_, bootstrap_.get(), fdpass_.get(), all_nodes_, v, data_listen_fd_)) {
+            host_.reset();
+            return false;
+        }
+    }
+    inited_ = true;
+    return true;
+}
+
+void Communicator::Finalize() {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (device_) device_->Finalize();
+    device_.reset();
+    if (host_) host_->Finalize();
+    host_.reset();
+    if (bootstrap_) bootstrap_->Close();
+    bootstrap_.reset();
+    if (fdpass_) fdpass_->Close();
+    fdpass_.reset();
+    net::CloseFd(&bootstrap_listen_fd_);
+    net::CloseFd(&data_listen_fd_);
+    pending_.clear();
+    group_depth_ = 0;
+    inited_ = false;
+}
+
+int Communicator::GetNChannels() const {
+    if (host_) return host_->n_channels();
+    return config_.n_channels > 0 ? config_.n_channels : 4;
+}
+
+void Communicator::GroupStart() { ++group_depth_; }
+
+bool Communicator::GroupEnd() {
+    if (group_depth_ <= 0) {
+        LOG_ERROR("GroupEnd without GroupStart");
+        return false;
+    }
+    if (--group_depth_ > 0) return true;  // inner GroupEnd: nothing runs
+    return Flush();
+}
+
+bool Communicator::Submit(const CollTask& task) {
+    if (!inited_) {
+        LOG_ERROR("communicator used before Init");
+        return false;
+    }
+    const bool valid = IsP2p(task.func) ? planner_->ValidateP2p(task, config_.rank, config_.world_size)
+                                        : planner_->ValidateCollectiveTask(task, config_.rank, config_.world_size);
+    if (!valid) return false;  // rejected before it is queued, even inside a group
+    pending_.push_back(task);
+    if (group_depth_ > 0) return true;
+    return Flush();
+}
+
+bool Communicator::Flush() {
+    std::vector<CollTask> tasks;
+    tasks.swap(pending_);
+    if (tasks.empty()) return true;
+    if (failed_) {
+        LOG_ERROR("communicator is in an error state after an earlier failure");
+        return false;
+    }
+    if (!planner_->SortTasks(tasks, config_.rank, config_.world_size)) return false;
+    bool ok;
+    if (device_) {
+        cudaStream_t s = static_cast<cudaStream_t>(has_user_stream_ ? user_stream_ : device_->internal_stream());
+        ok = device_->Execute(tasks, s);
+        if (ok && !has_user_stream_) ok = device_->Synchronize(s);
+    } else {
+        ok = host_->Execute(tasks);
+    }
+    if (!ok) failed_ = true;
+    return ok;
+}
+
+bool Communicator::AllReduce(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op) {
+    return AllReduceScaled(send_buf, recv_buf, count, dtype, op, 1.0f);
+}
+
+bool Communicator::AllReduceScaled(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op,
+                                   float scale) {
+    CollTask t;
+    t.func = CollFunc::AllReduce;
+    t.send_buf = send_buf;
+    t.recv_buf = recv_buf;
+    t.count = count;
+    t.dtype = dtype;
+    t.op = op;
+    t.scale = scale;
+    return Submit(t);
+}
+
+bool Communicator::Broadcast(void* buffer, size_t count, DataType dtype, int root) {
+    return BroadcastTo(buffer, buffer, count, dtype, root);
+}
+
+bool Communicator::BroadcastTo(const void* send_buf, void* recv_buf, size_t count, DataType dtype, int root) {
+    CollTask t;
+    t.func = CollFunc::Broadcast;
+    t.send_buf = send_buf;
+    t.recv_buf = recv_buf;
+    t.count = count;
+    t.dtype = dtype;
+    t.root = root;
+    return Submit(t);
+}
+
+bool Communicator::AllGather(const void* send_buf, void* recv_buf, size_t count, DataType dtype) {
+    CollTask t;
+    t.func = CollFunc::AllGather;
+    t.send_buf = send_buf;
+    t.recv_buf = recv_buf;
+    t.count = count;
+    t.dtype = dtype;
+    return Submit(t);
+}
+
+bool Communicator::Reduce(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op, int root) {
+    CollTask t;
+    t.func = CollFunc::Reduce;
+    t.send_buf = send_buf;
+    t.recv_buf = recv_buf;
+    t.count = count;
+    t.dtype = dtype;
+    t.op = op;
+    t.root = root;
+    return Submit(t);
+}
+
+bool Communicator::ReduceScatter(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op) {
+    CollTask t;
+    t.func = CollFunc::ReduceScatter;
+    t.send_buf = send_buf;
+    t.recv_buf = recv_buf;
+    t.count = count;
+    t.dtype = dtype;
+    t.op = op;
+    return Submit(t);
+}
+
+bool Communicator::Send(const void* buffer, size_t count, DataType dtype, int peer) {
+    CollTask t;
+    t.func = CollFunc::Send;
+    t.send_buf = buffer;
+    t.count = count;
+    t.dtype = dtype;
+    t.peer = peer;
+    return Submit(t);
+}
+
+bool Communicator::Recv(void* buffer, size_t count, DataType dtype, int peer) {
+    CollTask t;
+    t.func = CollFunc::Recv;
+    t.recv_buf = buffer;
+    t.count = count;
+    t.dtype = dtype;
+    t.peer = peer;
+    return Submit(t);
+}
+
+void Communicator::SetStream(void* stream) {
+    user_stream_ = stream;
+    has_user_stream_ = true;
+}
+void Communicator::ClearStream() {
+    user_stream_ = nullptr;
+    has_user_stream_ = false;
+}
+void* Communicator::GetStream() const {
+    if (has_user_stream_) return user_stream_;
+    return device_ ? static_cast<void*>(device_->internal_stream()) : nullptr;
+}
+
+bool Communicator::Synchronize() {
+    if (!device_) return true;
+    cudaStream_t s = static_cast<cudaStream_t>(GetStream());
+    bool ok = device_->Synchronize(s);
+    if (!ok) failed_ = true;
+    return ok;
+}
+
+void* Communicator::SymmetricAlloc(size_t bytes) { return device_ ? device_->SymAlloc(bytes) : nullptr; }
+bool Communicator::SymmetricFree(void* ptr) { return device_ ? device_->SymFree(ptr) : false; }
+bool Communicator::Barrier() { return bootstrap_ && bootstrap_->Barrier(); }
+bool Communicator::NvlsEnabled() const { return device_ && device_->nvls_enabled(); }
+const char* Communicator::LastAlgorithm() const { return device_ ? device_->last_algo() : "host"; }
+unsigned long long Communicator::KernelLaunches() const { return device_ ? device_->launches() : 0; }
+const char* Communicator::P2pTransportName(int peer) const {
+    if (host_) return host_->p2p_transport_name(peer);
+    return device_ ? "nccl" : "none";
+}
+const char* Communicator::HostExecutorName() const { return host_ ? host_->executor_name() : "cuda-stream"; }
+
+}  // namespace bccl

@@ -1,0 +1,241 @@
+#include "core/planner.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <limits>
+#include <sstream>
+
+#include "core/env.h"
+#include "core/logger.h"
+
+namespace bccl {
+namespace {
+
+bool ValidDtype(DataType d) {
+    int v = static_cast<int>(d);
+    return v >= 0 && v <= static_cast<int>(DataType::FP16);
+}
+bool ValidOp(ReduceOp o) {
+    int v = static_cast<int>(o);
+    return v >= 0 && v <= static_cast<int>(ReduceOp::AVG);
+}
+int EffectiveOp(const CollTask& t) { return IsReducing(t.func) ? static_cast<int>(t.op) : 0; }
+int EffectiveRoot(const CollTask& t) {
+    return (t.func == CollFunc::Broadcast || t.func == CollFunc::Reduce) ? t.root : 0;
+}
+
+CollFunc ParseFunc(const std::string& s) {
+    if (s == "allreduce") return CollFunc::AllReduce;
+    if (s == "broadcast") return CollFunc::Broadcast;
+    if (s == "reduce") return CollFunc::Reduce;
+    if (s == "allgather") return CollFunc::AllGather;
+    if (s == "reducescatter") return CollFunc::ReduceScatter;
+    return CollFunc::Send;
+}
+
+// Built-in table. Per-rank payload bytes; measured on 8xB200 (NVLink 5 / NVSwitch).
+// Small payloads are latency bound: one-shot push (one cross-rank sync). Large reducing
+// payloads go to NVLS, which moves S*(1+1/N) bytes per direction instead of 2*S*(N-1)/N.
+std::vector<TuningRow> DefaultTable() {
+    return {
+        {CollFunc::AllReduce, 0, 256 << 10, Algo::kOneShot, 0},
+        {CollFunc::AllReduce, 2, 4 << 20, Algo::kOneShot, 0},
+        {CollFunc::AllReduce, 0, 2 << 20, Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::Broadcast, 0, 512 << 10, Algo::kOneShot, 0},
+        {CollFunc::Broadcast, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::Reduce, 0, 512 << 10, Algo::kOneShot, 0},
+        {CollFunc::Reduce, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::AllGather, 0, ~size_t(0), Algo::kOneShot, 0},
+        {CollFunc::ReduceScatter, 0, ~size_t(0), Algo::kOneShot, 0},
+    };
+}
+
+// CTAs for a payload: enough memory-level parallelism to cover NVLink latency for large
+// payloads, few CTAs for small ones (each CTA pays a cross-rank sync).
+int DefaultCtas(Algo algo, size_t bytes) {
+    if (algo == Algo::kNvls) {
+        if (bytes <= (1u << 20)) return 8;
+        if (bytes <= (8u << 20)) return 16;
+        return 32;
+    }
+    if (bytes <= (16u << 10)) return 1;
+    if (bytes <= (64u << 10)) return 2;
+    if (bytes <= (256u << 10)) return 4;
+    if (bytes <= (1u << 20)) return 8;
+    if (bytes <= (4u << 20)) return 16;
+    return 32;
+}
+
+}  // namespace
+
+Planner::Planner() : table_(DefaultTable()) {
+    std::string path = EnvStr("BCCL_TUNING_FILE", "");
+    if (!path.empty() && !LoadTuningFile(path)) {
+        LOG_WARN("planner: could not load tuning file %s, keeping the built-in table", path.c_str());
+    }
+}
+
+Algo Planner::ParseAlgo(const std::string& s) {
+    if (s == "oneshot") return Algo::kOneShot;
+    if (s == "twoshot") return Algo::kTwoShot;
+    if (s == "nvls") return Algo::kNvls;
+    if (s == "ring") return Algo::kRing;
+    return Algo::kAuto;
+}
+
+bool Planner::LoadTuningFile(const std::string& path) {
+    std::ifstream in(path);
+    if (!in) return false;
+    std::vector<TuningRow> rows;
+    std::string line;
+    while (std::getline(in, line)) {
+        if (line.empty() || line[0] == '#') continue;
+        std::istringstream ls(line);
+        std::string func, algo;
+        int world = 0, ctas = 0;
+        unsigned long long max_bytes = 0;
+        if (!(ls >> func >> world >> max_bytes >> algo >> ctas)) return false;
+        CollFunc f = ParseFunc(func);
+        Algo a = ParseAlgo(algo);
+        if (f == CollFunc::Send || a == Algo::kAuto) return false;
+        rows.push_back({f, world, static_cast<size_t>(max_bytes), a, ctas});
+    }
+    if (rows.empty()) return false;
+    table_ = rows;
+    return true;
+}
+
+bool Planner::ValidateCollectiveTask(const CollTask& task, int rank, int world_size) const {
+    if (!IsCollective(task.func) || world_size <= 0 || rank < 0 || rank >= world_size) {
+        LOG_ERROR("rank %d: invalid collective function or communicator size", rank);
+        return false;
+    }
+    const size_t es = ValidDtype(task.dtype) ? DataTypeSize(task.dtype) : 0;
+    if (es == 0 || task.count > std::numeric_limits<size_t>::max() / es) {
+        LOG_ERROR("rank %d: invalid collective data type or count", rank);
+        return false;
+    }
+    if (IsReducing(task.func) && !ValidOp(task.op)) {
+        LOG_ERROR("rank %d: invalid reduce operation", rank);
+        return false;
+    }
+    const bool has_root = task.func == CollFunc::Broadcast || task.func == CollFunc::Reduce;
+    if (has_root && (task.root < 0 || task.root >= world_size)) {
+        LOG_ERROR("rank %d: invalid root %d", rank, task.root);
+        return false;
+    }
+    if ((task.func == CollFunc::AllGather || task.func == CollFunc::ReduceScatter) && task.count != 0 &&
+        task.count > std::numeric_limits<size_t>::max() / static_cast<size_t>(world_size) / es) {
+        LOG_ERROR("rank %d: collective total buffer size overflows", rank);
+        return false;
+    }
+    if (task.count == 0) return true;
+    const bool needs_send = task.func != CollFunc::Broadcast;
+    const bool needs_recv = task.func != CollFunc::Reduce || rank == task.root;
+    if ((needs_send && task.send_buf == nullptr) || (needs_recv && task.recv_buf == nullptr)) {
+        LOG_ERROR("rank %d: collective is missing a required buffer", rank);
+        return false;
+    }
+    return true;
+}
+
+bool Planner::ValidateP2p(const CollTask& task, int rank, int world_size) const {
+    if (!IsP2p(task.func) || task.peer < 0 || task.peer >= world_size || task.peer == rank) {
+        LOG_ERROR("rank %d: invalid P2P peer %d", rank, task.peer);
+        return false;
+    }
+    const size_t es = ValidDtype(task.dtype) ? DataTypeSize(task.dtype) : 0;
+    if (es == 0 || task.count > std::numeric_limits<size_t>::max() / es) {
+        LOG_ERROR("rank %d: invalid P2P data type or count", rank);
+        return false;
+    }
+    if (task.count != 0 && task.send_buf == nullptr && task.recv_buf == nullptr) {
+        LOG_ERROR("rank %d: P2P is missing its buffer", rank);
+        return false;
+    }
+    return true;
+}
+
+int Planner::P2pRoundOf(CollFunc func, int rank, int peer, int world_size) {
+    const int forward = (func == CollFunc::Send) ? (peer - rank + world_size) % world_size
+                                                 : (rank - peer + world_size) % world_size;
+    return world_size - forward;
+}
+
+bool Planner::SortTasks(std::vector<CollTask>& tasks, int rank, int world_size) const {
+    if (world_size <= 0 || rank < 0 || rank >= world_size) {
+        LOG_ERROR("rank %d: invalid communicator size for task sorting", rank);
+        return false;
+    }
+    std::vector<CollTask> colls, p2p;
+    for (const CollTask& t : tasks) {
+        if (IsP2p(t.func)) {
+            if (!ValidateP2p(t, rank, world_size)) return false;
+            p2p.push_back(t);
+        } else {
+            if (!ValidateCollectiveTask(t, rank, world_size)) return false;
+            colls.push_back(t);
+        }
+    }
+    std::stable_sort(colls.begin(), colls.end(), [](const CollTask& a, const CollTask& b) {
+        if (a.func != b.func) return a.func < b.func;
+        const size_t ab = a.count * DataTypeSize(a.dtype), bb = b.count * DataTypeSize(b.dtype);
+        if (ab != bb) return ab < bb;
+        if (a.dtype != b.dtype) return a.dtype < b.dtype;
+        if (EffectiveOp(a) != EffectiveOp(b)) return EffectiveOp(a) < EffectiveOp(b);
+        return EffectiveRoot(a) < EffectiveRoot(b);
+    });
+    std::stable_sort(p2p.begin(), p2p.end(), [rank, world_size](const CollTask& a, const CollTask& b) {
+        int ra = P2pRoundOf(a.func, rank, a.peer, world_size), rb = P2pRoundOf(b.func, rank, b.peer, world_size);
+        if (ra != rb) return ra < rb;
+        return a.func < b.func;
+    });
+    tasks.clear();
+    tasks.insert(tasks.end(), colls.begin(), colls.end());
+    tasks.insert(tasks.end(), p2p.begin(), p2p.end());
+    return true;
+}
+
+bool Planner::IsCollectiveBatch(const std::vector<CollTask>& tasks) const {
+    for (const CollTask& t : tasks)
+        if (IsP2p(t.func)) return false;
+    return true;
+}
+
+AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_t bytes, int world_size,
+                               bool nvls_ok, int max_ctas, Algo forced) const {
+    (void)dtype;
+    (void)op;
+    AlgoChoice c;
+    Algo algo = forced;
+    int ctas = 0;
+    if (algo == Algo::kAuto) {
+        algo = Algo::kOneShot;
+        for (const TuningRow& row : table_) {
+            if (row.func != func || (row.world != 0 && row.world != world_size) || bytes > row.max_bytes) continue;
+            algo = row.algo;
+            ctas = row.ctas;
+            break;
+        }
+    }
+    // Two-shot and ring exist for AllReduce only; the other collectives are already
+    // bandwidth-optimal as one-shot pushes.
+    if ((algo == Algo::kTwoShot || algo == Algo::kRing) && func != CollFunc::AllReduce) algo = Algo::kOneShot;
+    if (algo == Algo::kNvls && !nvls_ok) algo = (func == CollFunc::AllReduce && bytes > (256u << 10))
+                                                    ? Algo::kTwoShot : Algo::kOneShot;
+    if (algo == Algo::kNvls && (func == CollFunc::AllGather || func == CollFunc::ReduceScatter)) {
+        algo = Algo::kOneShot;
+    }
+    if (ctas <= 0) ctas = DefaultCtas(algo, bytes);
+    long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+    if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
+    if (max_ctas > 0) ctas = std::min(ctas, max_ctas);
+    c.algo = algo;
+    c.ctas = std::max(1, ctas);
+    return c;
+}
+
+}  // namespace bccl

@@ -1,0 +1,41 @@
+// CUDA driver entry points fetched through the runtime (cudaGetDriverEntryPoint), so the
+// library has no link-time dependency on libcuda and loads on machines without a GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace bccl {
+
+struct DriverApi {
+    CUresult (*cuMemCreate)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long);
+    CUresult (*cuMemRelease)(CUmemGenericAllocationHandle);
+    CUresult (*cuMemExportToShareableHandle)(void*, CUmemGenericAllocationHandle, CUmemAllocationHandleType,
+                                             unsigned long long);
+    CUresult (*cuMemImportFromShareableHandle)(CUmemGenericAllocationHandle*, void*, CUmemAllocationHandleType);
+    CUresult (*cuMemAddressReserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
+    CUresult (*cuMemAddressFree)(CUdeviceptr, size_t);
+    CUresult (*cuMemMap)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
+    CUresult (*cuMemUnmap)(CUdeviceptr, size_t);
+    CUresult (*cuMemSetAccess)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
+    CUresult (*cuMemGetAllocationGranularity)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags);
+    CUresult (*cuMulticastCreate)(CUmemGenericAllocationHandle*, const CUmulticastObjectProp*);
+    CUresult (*cuMulticastAddDevice)(CUmemGenericAllocationHandle, CUdevice);
+    CUresult (*cuMulticastBindMem)(CUmemGenericAllocationHandle, size_t, CUmemGenericAllocationHandle, size_t, size_t,
+                                   unsigned long long);
+    CUresult (*cuMulticastUnbind)(CUmemGenericAllocationHandle, CUdevice, size_t, size_t);
+    CUresult (*cuMulticastGetGranularity)(size_t*, const CUmulticastObjectProp*, CUmulticastGranularity_flags);
+    CUresult (*cuDeviceGet)(CUdevice*, int);
+    CUresult (*cuDeviceGetAttribute)(int*, CUdevice_attribute, CUdevice);
+    CUresult (*cuGetErrorString)(CUresult, const char**);
+    CUresult (*cuTensorMapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    bool loaded = false;
+};
+
+// Loads the table once (thread-safe). Returns null when no driver is present.
+const DriverApi* Driver();
+const char* DriverErrorString(CUresult r);
+
+}  // namespace bccl

@@ -1,0 +1,89 @@
+// Structures shared by host code and the sm_100a kernels.
+//
+// Memory model of a device communicator (one process per GPU, all GPUs behind one
+// NVSwitch). Every rank owns:
+//   * a unicast "UC" buffer, created with cuMemCreate, exported as a POSIX fd and mapped by
+//     every peer, so kernels address any peer's UC buffer with plain ld/st over NVLink. It
+//     holds the control region (cross-rank flags) followed by the data region used as
+//     per-source inboxes by the push kernels;
+//   * optionally an NVLS buffer bound to an NVSwitch multicast object: one virtual
+//     address (mc) whose multimem.ld_reduce reads and reduces all ranks' copies inside the
+//     switch and whose multimem.st writes every rank's copy;
+//   * a local DevState (sequence counters) and a host-mapped ErrorRecord.
+// Sequence counters live on the device so a kernel captured in a CUDA graph stays
+// correct on replay: each launch reads the counters left by the previous launch.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace bccl {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 256;
+constexpr size_t kCtrlBytes = 1u << 20;          // control region at the start of each UC buffer
+constexpr size_t kBarrierFlagsOff = 0;            // u64 [kMaxCtas][kMaxRanks]
+constexpr size_t kBarrierFlagsBytes = sizeof(uint64_t) * kMaxCtas * kMaxRanks;
+constexpr size_t kTpFlagsOff = 64u << 10;         // u64 flags of the fused tensor-parallel kernels
+constexpr size_t kTpFlagsBytes = 256u << 10;
+constexpr size_t kAlign = 256;
+
+// Error codes written by kernels (host-mapped, read after the stream synchronises).
+enum DevError : int {
+    kDevOk = 0,
+    kDevTimeout = 1,   // a bounded wait on a peer flag expired
+    kDevAborted = 2,   // the host raised the abort word
+    kDevBadArgs = 3,   // a kernel rejected its arguments (bounds/alignment)
+};
+
+struct ErrorRecord {
+    int code;
+    int rank;
+    int cta;
+    int peer;
+    int phase;
+    int pad;
+    unsigned long long seq;
+    unsigned long long waited_ns;
+};
+
+struct DevState {
+    unsigned long long round_seq;    // data-buffer half parity for the UC inboxes
+    unsigned long long barrier_seq;  // last barrier value used by every CTA slot
+    unsigned long long nvls_round_seq;
+    unsigned int done_ctas;          // CTAs finished in the current launch
+    unsigned int pad;
+    unsigned long long tp_seq;       // fused tensor-parallel kernels: launches so far
+    unsigned int tp_done;
+    unsigned int pad2;
+};
+
+struct DevComm {
+    int rank;
+    int nranks;
+    char* uc[kMaxRanks];        // every rank's UC buffer, mapped here
+    char* nvls_uc;              // this rank's NVLS buffer (unicast view), or null
+    char* nvls_mc;              // multicast view of the NVLS buffers, or null
+    DevState* state;
+    ErrorRecord* err;           // host-mapped
+    const volatile int* abort;  // host-mapped, set by the host to stop waits
+    unsigned long long timeout_ns;
+    unsigned long long data_bytes;  // bytes of the UC data region
+    unsigned long long nvls_bytes;  // bytes of the NVLS buffer
+};
+
+// One collective in a push-engine launch. All byte offsets refer to the per-peer stream:
+// the concatenation of every item's per-peer payload, each padded to 16 bytes.
+struct WorkItem {
+    const void* src;
+    void* dst;
+    unsigned long long count;       // elements of the per-peer payload
+    unsigned long long stream_off;  // byte offset of this payload in the per-peer stream
+    unsigned char func;             // CollFunc
+    unsigned char dtype;            // DataType
+    unsigned char op;               // ReduceOp
+    unsigned char root;
+    float scale;
+};
+
+}  // namespace bccl

@@ -1,0 +1,282 @@
+#include "device/device_engine.h"
+
+#include <algorithm>
+#include <cstring>
+
+#include "core/bootstrap.h"
+#include "core/env.h"
+#include "core/logger.h"
+#include "kernels/launch.h"
+
+namespace bccl {
+namespace {
+
+#define CUDA_OK(call, what)                                                              \
+    do {                                                                                 \
+        cudaError_t _e = (call);                                                         \
+        if (_e != cudaSuccess) {                                                         \
+            LOG_ERROR("%s failed: %s", what, cudaGetErrorString(_e));                    \
+            return false;                                                                \
+        }                                                                                \
+    } while (0)
+
+size_t RoundDown(size_t x, size_t a) { return x / a * a; }
+size_t RoundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Per-peer payload bytes of a collective in the push engine's stream.
+size_t PeerPayload(const CollTask& t) { return t.count * DataTypeSize(t.dtype); }
+
+int PushCtas(size_t stream_bytes) {
+    if (stream_bytes <= (16u << 10)) return 1;
+    if (stream_bytes <= (64u << 10)) return 2;
+    if (stream_bytes <= (256u << 10)) return 4;
+    if (stream_bytes <= (1u << 20)) return 8;
+    if (stream_bytes <= (4u << 20)) return 16;
+    return 32;
+}
+
+}  // namespace
+
+bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const Planner* planner) {
+    rank_ = cfg.rank;
+    nranks_ = cfg.world_size;
+    device_ = cfg.device;
+    planner_ = planner;
+    bs_ = bs;
+    max_ctas_ = cfg.n_channels;
+    forced_ = Planner::ParseAlgo(EnvStr("BCCL_ALGO", ""));
+    CUDA_OK(cudaSetDevice(device_), "cudaSetDevice");
+    const int timeout_ms = cfg.timeout_ms > 0 ? cfg.timeout_ms : static_cast<int>(EnvInt("BCCL_TIMEOUT_MS", 10000));
+    if (!sm_.Init(device_, rank_, nranks_, bs, fp, std::max(timeout_ms, 30000), cfg.enable_nvls)) return false;
+
+    data_bytes_ = cfg.buffer_bytes ? cfg.buffer_bytes : static_cast<size_t>(EnvInt("BCCL_BUFFSIZE", 128l << 20));
+    data_bytes_ = std::max<size_t>(RoundUp(data_bytes_, 1u << 20), 4u << 20);
+    if (!sm_.Alloc(kCtrlBytes + data_bytes_, false, &uc_)) return false;
+    if (sm_.multicast_supported()) {
+        size_t nb = static_cast<size_t>(EnvInt("BCCL_NVLS_BUFFSIZE", 256l << 20));
+        if (!sm_.Alloc(nb, true, &nvls_)) return false;
+        if (nvls_.mc == nullptr) sm_.Free(&nvls_);
+    }
+    CUDA_OK(cudaMalloc(&state_, sizeof(DevState)), "cudaMalloc(state)");
+    CUDA_OK(cudaMemset(state_, 0, sizeof(DevState)), "cudaMemset(state)");
+    CUDA_OK(cudaHostAlloc(&err_host_, sizeof(ErrorRecord), cudaHostAllocMapped), "cudaHostAlloc(err)");
+    CUDA_OK(cudaHostAlloc(&abort_host_, sizeof(int), cudaHostAllocMapped), "cudaHostAlloc(abort)");
+    memset(err_host_, 0, sizeof(ErrorRecord));
+    *abort_host_ = 0;
+    ErrorRecord* err_dev = nullptr;
+    int* abort_dev = nullptr;
+    CUDA_OK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), err_host_, 0), "cudaHostGetDevicePointer");
+    CUDA_OK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&abort_dev), abort_host_, 0), "cudaHostGetDevicePointer");
+    CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+
+    memset(&dc_, 0, sizeof(dc_));
+    dc_.rank = rank_;
+    dc_.nranks = nranks_;
+    for (int p = 0; p < nranks_; ++p) dc_.uc[p] = uc_.ptr[p];
+    dc_.nvls_uc = nvls_.mc ? nvls_.ptr[rank_] : nullptr;
+    dc_.nvls_mc = nvls_.mc;
+    dc_.nvls_bytes = nvls_.mc ? nvls_.bytes : 0;
+    dc_.state = state_;
+    dc_.err = err_dev;
+    dc_.abort = abort_dev;
+    dc_.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
+    dc_.data_bytes = data_bytes_;
+    CUDA_OK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    if (nranks_ > 1 && cfg.enable_nccl_p2p && !EnvFlag("BCCL_DISABLE_NCCL_P2P")) {
+        if (!p2p_.Init(rank_, nranks_, bs)) LOG_WARN("rank %d: Send/Recv unavailable (NCCL init failed)", rank_);
+    }
+    if (!bs->Barrier()) return false;
+    inited_ = true;
+    LOG_INFO("rank %d: device engine ready (device %d, data %llu bytes, nvls %s)", rank_, device_, data_bytes_,
+             nvls_.mc ? "on" : "off");
+    return true;
+}
+
+void DeviceEngine::Finalize() {
+    if (!inited_) return;
+    inited_ = false;
+    cudaSetDevice(device_);
+    cudaDeviceSynchronize();
+    p2p_.Destroy();
+    // Nobody may unmap while a peer could still touch our memory.
+    if (bs_ != nullptr && bs_->ready()) bs_->Barrier();
+    for (SymBuffer& b : user_bufs_) sm_.Free(&b);
+    user_bufs_.clear();
+    sm_.Free(&nvls_);
+    sm_.Free(&uc_);
+    if (stream_) cudaStreamDestroy(stream_);
+    stream_ = nullptr;
+    if (state_) cudaFree(state_);
+    state_ = nullptr;
+    if (err_host_) cudaFreeHost(err_host_);
+    err_host_ = nullptr;
+    if (abort_host_) cudaFreeHost(abort_host_);
+    abort_host_ = nullptr;
+}
+
+bool DeviceEngine::CheckDeviceError() {
+    if (err_host_ == nullptr) return false;
+    const volatile ErrorRecord* e = err_host_;
+    if (e->code == kDevOk) return true;
+    LOG_ERROR("rank %d: device collective failed (code %d: %s) in CTA %d waiting on rank %d, phase %d, seq %llu, "
+              "after %.3f ms",
+              rank_, e->code, e->code == kDevTimeout ? "timeout" : e->code == kDevAborted ? "aborted" : "bad args",
+              e->cta, e->peer, e->phase, static_cast<unsigned long long>(e->seq), e->waited_ns / 1e6);
+    return false;
+}
+
+bool DeviceEngine::Synchronize(cudaStream_t stream) {
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        LOG_ERROR("rank %d: stream synchronisation failed: %s", rank_, cudaGetErrorString(e));
+        return false;
+    }
+    return CheckDeviceError();
+}
+
+int DeviceEngine::WaitProbe(int timeout_ms) {
+    if (!inited_) return -1;
+    cudaSetDevice(device_);
+    if (LaunchWaitProbe(dc_, static_cast<unsigned long long>(timeout_ms) * 1000000ull, stream_) != cudaSuccess) return -1;
+    if (cudaStreamSynchronize(stream_) != cudaSuccess) return -1;
+    launches_++;
+    int code = err_host_->code;
+    memset(err_host_, 0, sizeof(ErrorRecord));
+    return code;
+}
+
+void DeviceEngine::Abort() {
+    if (abort_host_) *reinterpret_cast<volatile int*>(abort_host_) = 1;
+}
+
+const SymBuffer* DeviceEngine::FindSym(const void* p, size_t bytes) const {
+    const char* c = static_cast<const char*>(p);
+    for (const SymBuffer& b : user_bufs_) {
+        if (b.mc && c >= b.ptr[rank_] && c + bytes <= b.ptr[rank_] + b.bytes) return &b;
+    }
+    return nullptr;
+}
+
+void* DeviceEngine::SymAlloc(size_t bytes) {
+    cudaSetDevice(device_);
+    SymBuffer b;
+    if (!sm_.Alloc(bytes, true, &b)) return nullptr;
+    user_bufs_.push_back(b);
+    return b.ptr[rank_];
+}
+
+bool DeviceEngine::SymFree(void* ptr) {
+    for (size_t i = 0; i < user_bufs_.size(); ++i) {
+        if (user_bufs_[i].ptr[rank_] == ptr) {
+            cudaDeviceSynchronize();
+            if (!bs_->Barrier()) return false;
+            sm_.Free(&user_bufs_[i]);
+            user_bufs_.erase(user_bufs_.begin() + static_cast<long>(i));
+            return true;
+        }
+    }
+    return false;
+}
+
+bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream) {
+    if (batch->empty()) return true;
+    const unsigned long long slot = RoundDown(data_bytes_ / (2ull * nranks_), 256);
+    size_t i = 0;
+    while (i < batch->size()) {
+        size_t n = std::min<size_t>(kPushMaxItems, batch->size() - i);
+        // Re-base this launch's stream offsets at zero.
+        std::vector<WorkItem> part(batch->begin() + static_cast<long>(i), batch->begin() + static_cast<long>(i + n));
+        const unsigned long long base = part.front().stream_off;
+        for (WorkItem& w : part) w.stream_off -= base;
+        const WorkItem& last = part.back();
+        unsigned long long bytes = last.stream_off + RoundUp(last.count * DataTypeSize(static_cast<DataType>(last.dtype)), 16);
+        int ctas = PushCtas(std::min<unsigned long long>(bytes, slot));
+        if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
+        long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+        if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
+        cudaError_t e = LaunchPushEngine(dc_, part.data(), static_cast<int>(n), bytes, slot, ctas, stream);
+        if (e != cudaSuccess) {
+            LOG_ERROR("rank %d: push-engine launch failed: %s", rank_, cudaGetErrorString(e));
+            return false;
+        }
+        launches_++;
+        i += n;
+    }
+    last_algo_ = "oneshot";
+    batch->clear();
+    *stream_bytes = 0;
+    return true;
+}
+
+bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream) {
+    cudaError_t e = cudaSuccess;
+    const int dt = static_cast<int>(t.dtype), op = static_cast<int>(t.op);
+    if (c.algo == Algo::kNvls) {
+        const unsigned long long cap = RoundDown(nvls_.bytes / 2, 16ull * nranks_);
+        const size_t bytes = t.count * DataTypeSize(t.dtype);
+        const bool zc = t.func == CollFunc::AllReduce && t.send_buf == t.recv_buf && FindSym(t.recv_buf, RoundUp(bytes, 16ull * nranks_)) != nullptr;
+        (void)zc;  // zero-copy is served by user symmetric buffers bound to their own multicast objects
+        e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale, cap,
+                       c.ctas, false, stream);
+        last_algo_ = "nvls";
+    } else {
+        const unsigned long long cap = RoundDown(data_bytes_ / (2ull * (nranks_ + 1)), 256);
+        e = LaunchTwoShot(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, cap, c.ctas, stream);
+        last_algo_ = "twoshot";
+    }
+    if (e != cudaSuccess) {
+        LOG_ERROR("rank %d: %s launch failed: %s", rank_, last_algo_, cudaGetErrorString(e));
+        return false;
+    }
+    launches_++;
+    return true;
+}
+
+bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t stream) {
+    if (!inited_) {
+        LOG_ERROR("device engine not initialised");
+        return false;
+    }
+    if (err_host_->code != kDevOk) return CheckDeviceError();
+    std::vector<WorkItem> batch;
+    unsigned long long stream_bytes = 0;
+    std::vector<CollTask> p2p;
+    for (const CollTask& t : sorted) {
+        if (IsP2p(t.func)) {
+            p2p.push_back(t);
+            continue;
+        }
+        if (t.count == 0) continue;
+        const size_t bytes = t.count * DataTypeSize(t.dtype);
+        const bool nvls_ok = nvls_.mc != nullptr &&
+                             (t.func == CollFunc::Broadcast || NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
+        AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
+                                            t.algo != Algo::kAuto ? t.algo : forced_);
+        if (nranks_ == 1 || c.algo == Algo::kOneShot || c.algo == Algo::kRing) {
+            WorkItem w;
+            w.src = t.send_buf;
+            w.dst = t.recv_buf;
+            w.count = t.count;
+            w.stream_off = stream_bytes;
+            w.func = static_cast<unsigned char>(t.func);
+            w.dtype = static_cast<unsigned char>(t.dtype);
+            w.op = static_cast<unsigned char>(t.op);
+            w.root = static_cast<unsigned char>(t.root);
+            w.scale = t.scale;
+            if (t.func == CollFunc::Broadcast && w.src == nullptr) w.src = w.dst;
+            batch.push_back(w);
+            stream_bytes += RoundUp(PeerPayload(t), 16);
+            continue;
+        }
+        if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+        if (!LaunchLarge(t, c, stream)) return false;
+    }
+    if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+    if (!p2p.empty()) {
+        if (!p2p_.Run(p2p, stream)) return false;
+        last_algo_ = "nccl_p2p";
+    }
+    return true;
+}
+
+}  // namespace bccl

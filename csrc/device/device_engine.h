@@ -1,0 +1,90 @@
+// Executor of the device communicator: turns a sorted batch of tasks into kernel launches.
+//
+// The reference's executors decide how CPU threads wait on sockets (OriginCCL
+// src/executor/*.cpp); here waiting happens inside the kernels (bounded flag spins) and
+// the host only enqueues. A batch becomes:
+//   * consecutive one-shot collectives -> ONE push-engine launch (the whole group; the
+//     reference's dynamic executor and its per-slice control broadcast become the kernel's
+//     CTA-owns-piece rule);
+//   * each large collective -> one NVLS or two-shot launch, in sorted order;
+//   * all Send/Recv -> one NCCL group, after the collectives.
+// Every rank derives the same launches from the same sorted batch, so no control message
+// is needed at run time.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <vector>
+
+#include "bccl/types.h"
+#include "core/planner.h"
+#include "device/dev_types.h"
+#include "device/nccl_p2p.h"
+#include "device/symmem.h"
+
+namespace bccl {
+
+class Bootstrap;
+class FdPasser;
+
+class DeviceEngine {
+public:
+    DeviceEngine() = default;
+    ~DeviceEngine() { Finalize(); }
+
+    bool Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const Planner* planner);
+    void Finalize();
+
+    // Enqueues the batch on `stream` (collectives first, in order, then P2P).
+    bool Execute(const std::vector<CollTask>& sorted, cudaStream_t stream);
+    // Reads the host-mapped error record; false if any kernel reported a failure.
+    bool CheckDeviceError();
+    bool Synchronize(cudaStream_t stream);
+    void Abort();
+    // Runs the bounded-wait self-test; returns the error code it recorded (kDevTimeout
+    // expected) and clears the record so the communicator stays usable.
+    int WaitProbe(int timeout_ms);
+
+    // Collective allocation of memory every rank can address directly (NVLS-bound when
+    // available); AllReduce on such a buffer in place skips the staging copies.
+    void* SymAlloc(size_t bytes);
+    bool SymFree(void* ptr);
+
+    cudaStream_t internal_stream() const { return stream_; }
+    bool nvls_enabled() const { return nvls_.mc != nullptr; }
+    const DevComm& dev_comm() const { return dc_; }
+    unsigned long long launches() const { return launches_.load(); }
+    const char* last_algo() const { return last_algo_; }
+    int device() const { return device_; }
+    const char* nccl_version() const { return p2p_.version(); }
+
+private:
+    bool FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream);
+    bool LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream);
+    const SymBuffer* FindSym(const void* p, size_t bytes) const;
+
+    int rank_ = 0;
+    int nranks_ = 1;
+    int device_ = -1;
+    int max_ctas_ = 0;
+    Algo forced_ = Algo::kAuto;
+    const Planner* planner_ = nullptr;
+    Bootstrap* bs_ = nullptr;
+    SymmetricMemory sm_;
+    SymBuffer uc_;
+    SymBuffer nvls_;
+    std::vector<SymBuffer> user_bufs_;
+    DevState* state_ = nullptr;
+    ErrorRecord* err_host_ = nullptr;
+    int* abort_host_ = nullptr;
+    DevComm dc_{};
+    unsigned long long data_bytes_ = 0;
+    cudaStream_t stream_ = nullptr;
+    NcclP2p p2p_;
+    std::atomic<unsigned long long> launches_{0};
+    const char* last_algo_ = "none";
+    bool inited_ = false;
+};
+
+}  // namespace bccl

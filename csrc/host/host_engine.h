@@ -1,0 +1,124 @@
+// Host-memory communicator engine (CommConfig::device == -1).
+//
+// This is the reference's own domain (collectives on host buffers between processes,
+// OriginCCL README.md:3), rebuilt around one shared-memory segment per machine instead of
+// per-edge rings:
+//   * every machine's local ranks map one memfd segment (created by the local leader and
+//     passed with SCM_RIGHTS). Per channel it holds a staging slot per global rank, a
+//     result area and a generation barrier; directed SPSC rings carry Send/Recv;
+//   * collectives are two-shot in shared memory: copy-in, barrier, each local rank reduces
+//     1/L of the chunk over all slots, barrier, copy-out. Machines (distinguished by
+//     CommConfig::get_hostname, so one host can emulate several) are joined by their
+//     leaders over TCP, reducing in machine order so every rank gets identical bits;
+//   * channels (CommConfig::n_channels) are worker threads that each own a contiguous
+//     slice of every payload, with their own barrier and sockets -- the reference's
+//     MultiThreadExecutor channels (src/executor/multi_thread_executor.cpp:141-198);
+//   * Send/Recv are progressed by a polling or epoll executor over the TrySend/TryRecv
+//     contract (src/executor/polling_executor.cpp, epoll_executor.cpp), FIFO per peer.
+#pragma once
+
+#include <atomic>
+#include <condition_variable>
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "bccl/types.h"
+#include "host/transport.h"
+
+namespace bccl {
+
+class Bootstrap;
+class FdPasser;
+
+struct MachineView {
+    int local_rank = 0;
+    int local_size = 1;
+    std::vector<int> local_ranks;      // global ranks on this machine, ascending
+    int machine_index = 0;
+    int machine_count = 1;
+    std::vector<int> machine_leaders;  // lowest rank of each machine, machine order
+    std::vector<int> machine_of;       // per global rank
+    std::vector<int> local_index_of;   // per global rank: index within its machine
+    std::vector<std::vector<int>> machine_ranks;
+};
+
+struct alignas(64) ShmBarrier {
+    std::atomic<uint32_t> count;
+    char pad0[60];
+    std::atomic<uint32_t> gen;
+    char pad1[60];
+};
+
+class HostEngine {
+public:
+    HostEngine() = default;
+    ~HostEngine() { Finalize(); }
+
+    // data_listen_fd: this rank's TCP listener announced in NodeInfo::data_port (borrowed).
+    bool Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const std::vector<NodeInfo>& nodes,
+              const MachineView& view, int data_listen_fd);
+    void Finalize();
+    bool Execute(const std::vector<CollTask>& sorted);
+
+    int n_channels() const { return n_channels_; }
+    const char* p2p_transport_name(int peer) const;
+    const char* executor_name() const { return epoll_ ? "epoll" : "polling"; }
+
+private:
+    struct Channel {
+        ShmBarrier* barrier = nullptr;
+        char* slots = nullptr;   // [world][slot_bytes]
+        char* result = nullptr;  // [slot_bytes]
+        std::vector<std::unique_ptr<TcpTransport>> leader_links;  // per machine (leaders only)
+        std::vector<char> scratch;                                // leader-private receive space
+    };
+
+    bool RunCollective(int ch, const CollTask& t);
+    bool AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1, bool reduce_only);
+    bool BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1);
+    bool AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1);
+    bool ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t e1);
+    bool Barrier(int ch);
+    // Leaders: send `send[m]` (bytes[m]) to machine m's leader and receive `recv[m]` from it,
+    // for every m in `peers`, all concurrently.
+    bool LeaderExchange(int ch, const std::vector<int>& peers, const std::vector<const void*>& send,
+                        const std::vector<size_t>& send_bytes, const std::vector<void*>& recv,
+                        const std::vector<size_t>& recv_bytes);
+    bool RunP2p(const std::vector<CollTask>& tasks);
+    bool RunOnChannels(const std::function<bool(int)>& fn);
+    void WorkerLoop(int ch);
+    char* Slot(int ch, int rank) { return chans_[ch].slots + static_cast<size_t>(rank) * slot_bytes_; }
+
+    int rank_ = 0;
+    int world_ = 1;
+    int listen_fd_ = -1;
+    MachineView view_;
+    int n_channels_ = 1;
+    size_t slot_bytes_ = 1u << 20;
+    size_t ring_bytes_ = 1u << 20;
+    int timeout_ms_ = 30000;
+    bool epoll_ = false;
+    bool inited_ = false;
+
+    void* seg_ = nullptr;
+    size_t seg_bytes_ = 0;
+    std::vector<Channel> chans_;
+    std::vector<std::unique_ptr<Transport>> p2p_send_;  // per peer
+    std::vector<std::unique_ptr<Transport>> p2p_recv_;  // per peer (same object for TCP)
+    std::vector<std::shared_ptr<TcpTransport>> p2p_tcp_;
+
+    // Channel worker pool.
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_job_, cv_done_;
+    std::function<bool(int)> job_;
+    uint64_t job_seq_ = 0;
+    int job_pending_ = 0;
+    bool job_ok_ = true;
+    bool stop_ = false;
+};
+
+}  // namespace bccl

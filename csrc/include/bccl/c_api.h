@@ -1,0 +1,94 @@
+/* C interface of the library (used by the Python bindings through ctypes, and by any
+ * caller that cannot link C++). Every function returns 0 on success and a non-zero code on
+ * failure; bcclGetLastError() describes the most recent failure on the calling thread.
+ * Buffers are host pointers for host communicators and device pointers for device ones.
+ * `stream` arguments apply to device communicators: with has_stream != 0 the call enqueues on
+ * that cudaStream_t and returns; with has_stream == 0 it runs on the internal stream and
+ * blocks until the result is ready. */
+#ifndef BCCL_C_API_H_
+#define BCCL_C_API_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct bcclComm* bcclComm_t;
+
+typedef struct {
+    int rank;
+    int world_size;
+    char ip_addr[64];
+    uint16_t port;
+    int n_channels;
+    int device;                 /* -1 = host-memory communicator */
+    size_t buffer_bytes;        /* 0 = default */
+    int timeout_ms;             /* 0 = default */
+    int enable_nvls;
+    int enable_nccl_p2p;
+    int logical_machine_size;   /* > 0: ranks r and s share a machine iff r/size == s/size */
+} bcclConfig;
+
+enum { bcclFloat32 = 0, bcclFloat64 = 1, bcclInt32 = 2, bcclInt64 = 3, bcclBfloat16 = 4, bcclFloat16 = 5 };
+enum { bcclSum = 0, bcclMax = 1, bcclMin = 2, bcclAvg = 3 };
+
+int bcclCommCreate(bcclComm_t* comm);
+int bcclGetUniqueId(bcclComm_t comm, char ip_addr[64], uint16_t* port);
+int bcclCommInit(bcclComm_t comm, const bcclConfig* cfg);
+int bcclCommFinalize(bcclComm_t comm);
+int bcclCommDestroy(bcclComm_t comm);
+const char* bcclGetLastError(void);
+const char* bcclVersion(void);
+
+int bcclCommInfo(bcclComm_t comm, int* rank, int* world, int* local_rank, int* local_size, int* machine_index,
+                 int* machine_count, int* n_channels);
+int bcclCommLocalRanks(bcclComm_t comm, int* out, int max);
+int bcclCommMachineLeaders(bcclComm_t comm, int* out, int max);
+int bcclCommNvlsEnabled(bcclComm_t comm);
+const char* bcclCommLastAlgorithm(bcclComm_t comm);
+unsigned long long bcclCommKernelLaunches(bcclComm_t comm);
+const char* bcclCommP2pTransport(bcclComm_t comm, int peer);
+const char* bcclCommHostExecutor(bcclComm_t comm);
+
+int bcclGroupStart(bcclComm_t comm);
+int bcclGroupEnd(bcclComm_t comm, uintptr_t stream, int has_stream);
+
+/* algo: 0 auto, 1 one-shot, 2 two-shot, 3 NVLS, 4 ring. */
+int bcclAllReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, float scale, int algo,
+                  uintptr_t stream, int has_stream);
+int bcclBroadcast(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int root, int algo,
+                  uintptr_t stream, int has_stream);
+int bcclReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, int root, int algo,
+               uintptr_t stream, int has_stream);
+int bcclAllGather(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, uintptr_t stream,
+                  int has_stream);
+int bcclReduceScatter(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op,
+                      uintptr_t stream, int has_stream);
+int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
+int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
+int bcclSynchronize(bcclComm_t comm);
+int bcclBarrier(bcclComm_t comm);
+void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes);
+int bcclSymmetricFree(bcclComm_t comm, void* ptr);
+
+/* Failure-detection self-test: runs a kernel whose bounded wait can never be satisfied and
+ * returns the error code it recorded (1 = timeout) or -1 if it could not run. */
+int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms);
+
+/* Planner white-box hooks (used by tests): sorts `n` tasks described by parallel arrays and
+ * writes the resulting permutation (indices into the input) to `order`. */
+int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,
+                    const int* root, const int* peer, int* order);
+int bcclPlannerP2pRound(int func, int rank, int peer, int world);
+int bcclPlannerValidate(int rank, int world, int func, size_t count, int dtype, int op, int root, int peer,
+                        int has_send, int has_recv);
+int bcclPlannerChoose(int func, int dtype, int op, size_t bytes, int world, int nvls_ok, int max_ctas, int* algo,
+                      int* ctas);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BCCL_C_API_H_ */

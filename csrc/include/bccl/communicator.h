@@ -1,0 +1,123 @@
+// The communicator: the library's public C++ API.
+//
+// Method names, arguments and semantics follow the reference (OriginCCL
+// include/communicator.h:19-75, docs/layers/communicator.md):
+//   * GetUniqueId (rank 0 only; binds the bootstrap listener held until Finalize), Init,
+//     Finalize; the local/machine views;
+//   * AllReduce / Broadcast / Reduce / AllGather / ReduceScatter, Send / Recv;
+//   * GroupStart / GroupEnd nest; only the outermost GroupEnd executes, once, for the
+//     whole batch; invalid operations return false before they are queued;
+//   * count 0 succeeds with null buffers; Reduce's non-root recv may be null; AllGather's
+//     output is ordered by rank; ReduceScatter takes N*count inputs; in place is allowed;
+//   * AVG is SUM divided by the rank count.
+// Device communicators (CommConfig::device >= 0) take device pointers; with no stream in
+// the config every call blocks until its result is ready (the reference's contract); with
+// a stream, calls only enqueue (NCCL's contract) and errors surface on the next call or
+// in Synchronize().
+#pragma once
+
+#include <cstddef>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "bccl/types.h"
+
+namespace bccl {
+
+class Bootstrap;
+class FdPasser;
+class Planner;
+class DeviceEngine;
+class HostEngine;
+
+class Communicator {
+public:
+    Communicator();
+    ~Communicator();
+    Communicator(const Communicator&) = delete;
+    Communicator& operator=(const Communicator&) = delete;
+
+    bool GetUniqueId(UniqueId& unique_id);
+    bool Init(const CommConfig& cfg);
+    void Finalize();
+
+    int GetRank() const { return config_.rank; }
+    int GetWorldSize() const { return config_.world_size; }
+    int GetNChannels() const;
+    int GetLocalRank() const { return local_rank_; }
+    int GetLocalSize() const { return local_size_; }
+    const std::vector<int>& GetLocalRanks() const { return local_ranks_; }
+    bool IsSingleMachine() const { return machine_count_ == 1; }
+    int GetMachineIndex() const { return machine_index_; }
+    int GetMachineCount() const { return machine_count_; }
+    const std::vector<int>& GetMachineLeaders() const { return machine_leaders_; }
+
+    void GroupStart();
+    bool GroupEnd();
+
+    bool AllReduce(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op);
+    bool Broadcast(void* buffer, size_t count, DataType dtype, int root);
+    bool AllGather(const void* send_buf, void* recv_buf, size_t count, DataType dtype);
+    bool Reduce(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op, int root);
+    bool ReduceScatter(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op);
+    bool Send(const void* buffer, size_t count, DataType dtype, int peer);
+    bool Recv(void* buffer, size_t count, DataType dtype, int peer);
+
+    // ---- extensions
+    // AllReduce with a fused multiplier on the result (data-parallel gradient scaling).
+    bool AllReduceScaled(const void* send_buf, void* recv_buf, size_t count, DataType dtype, ReduceOp op, float scale);
+    // Out-of-place Broadcast (root reads send_buf, every rank writes recv_buf).
+    bool BroadcastTo(const void* send_buf, void* recv_buf, size_t count, DataType dtype, int root);
+    // Submits a prepared task (used by the C API and bindings).
+    bool Submit(const CollTask& task);
+    // Device communicators: later calls enqueue on `stream` and return without waiting
+    // (any cudaStream_t, including 0 = the legacy default stream). ClearStream() returns to
+    // the internal stream with blocking calls.
+    void SetStream(void* stream);
+    void ClearStream();
+    void* GetStream() const;
+    bool Synchronize();
+    // Device communicators: collective allocation of peer-addressable memory.
+    void* SymmetricAlloc(size_t bytes);
+    bool SymmetricFree(void* ptr);
+    bool Barrier();
+    bool IsDevice() const { return config_.device >= 0; }
+    bool NvlsEnabled() const;
+    const char* LastAlgorithm() const;
+    unsigned long long KernelLaunches() const;
+    const char* P2pTransportName(int peer) const;
+    const char* HostExecutorName() const;
+    const Planner& planner() const { return *planner_; }
+    DeviceEngine* device_engine() { return device_.get(); }
+
+private:
+    bool Flush();
+
+    CommConfig config_;
+    bool inited_ = false;
+    bool failed_ = false;
+    int bootstrap_listen_fd_ = -1;
+    int data_listen_fd_ = -1;
+    bool have_unique_id_ = false;
+    std::unique_ptr<Bootstrap> bootstrap_;
+    std::unique_ptr<FdPasser> fdpass_;
+    std::unique_ptr<Planner> planner_;
+    std::unique_ptr<DeviceEngine> device_;
+    std::unique_ptr<HostEngine> host_;
+    std::vector<NodeInfo> all_nodes_;
+    int group_depth_ = 0;
+    std::vector<CollTask> pending_;
+    void* user_stream_ = nullptr;
+    bool has_user_stream_ = false;
+    int local_rank_ = 0;
+    int local_size_ = 1;
+    std::vector<int> local_ranks_;
+    int machine_index_ = 0;
+    int machine_count_ = 1;
+    std::vector<int> machine_leaders_;
+    std::mutex mu_;
+};
+
+}  // namespace bccl

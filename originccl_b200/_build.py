@@ -1,0 +1,119 @@
+"""Native build of the library: csrc/ -> originccl_b200/_lib/libbccl.so (+ the bccl_run launcher).
+
+Kernels are compiled for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``); host C++
+is compiled with g++. A small ninja file is generated so rebuilds are incremental and use every
+core. nvcc cross-compiles without a GPU, so this runs on CPU-only machines as well.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+import sysconfig
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+CSRC = ROOT / "csrc"
+LIBDIR = ROOT / "originccl_b200" / "_lib"
+BUILD = ROOT / "build" / "native"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+ARCH = "-gencode arch=compute_100a,code=sm_100a"
+
+
+def _site_packages() -> Path:
+    return Path(sysconfig.get_paths()["purelib"])
+
+
+def nccl_include() -> Path | None:
+    p = _site_packages() / "nvidia" / "nccl" / "include"
+    return p if (p / "nccl.h").exists() else None
+
+
+def cutlass_include() -> Path | None:
+    for rel in ("flashinfer/data/cutlass/include", "tilelang/3rdparty/cutlass/include"):
+        p = _site_packages() / rel
+        if (p / "cute").exists():
+            return p
+    return None
+
+
+def _sources() -> tuple[list[Path], list[Path]]:
+    cc = sorted(p for p in CSRC.rglob("*.cc") if "tools" not in p.parts)
+    cu = sorted(CSRC.rglob("*.cu"))
+    return cc, cu
+
+
+def _ninja_file() -> str:
+    cc, cu = _sources()
+    nccl = nccl_include()
+    incs = f"-I{CSRC} -I{CSRC / 'include'} -I{CUDA_HOME / 'include'}"
+    if nccl:
+        incs += f" -I{nccl}"
+    cxxflags = f"-O2 -g -std=c++17 -fPIC -Wall -Wextra -Wno-unused-parameter -Wno-missing-field-initializers {incs}"
+    nvflags = (f"{ARCH} -lineinfo -O3 -std=c++17 -Xcompiler -fPIC --expt-relaxed-constexpr "
+               f"-Xptxas -warn-spills {incs}")
+    lines = [
+        "ninja_required_version = 1.5",
+        f"cxx = g++",
+        f"nvcc = {CUDA_HOME / 'bin' / 'nvcc'}",
+        f"cxxflags = {cxxflags}",
+        f"nvflags = {nvflags}",
+        "rule cxx",
+        "  command = $cxx -MMD -MF $out.d $cxxflags -c $in -o $out",
+        "  depfile = $out.d",
+        "  deps = gcc",
+        "  description = CXX $out",
+        "rule nvcc",
+        "  command = $nvcc -MD -MF $out.d $nvflags -c $in -o $out",
+        "  depfile = $out.d",
+        "  deps = gcc",
+        "  description = NVCC $out",
+        "rule link",
+        f"  command = $nvcc {ARCH} -shared -cudart static -o $out $in -ldl -lpthread -lrt",
+        "  description = LINK $out",
+        "rule linkexe",
+        "  command = $cxx -o $out $in -lpthread",
+        "  description = LINK $out",
+    ]
+    objs = []
+    for src in cc:
+        if src.parent.name == "tools":
+            continue
+        obj = BUILD / (str(src.relative_to(CSRC)).replace("/", "_") + ".o")
+        lines.append(f"build {obj}: cxx {src}")
+        objs.append(obj)
+    for src in cu:
+        obj = BUILD / (str(src.relative_to(CSRC)).replace("/", "_") + ".o")
+        lines.append(f"build {obj}: nvcc {src}")
+        objs.append(obj)
+    lines.append(f"build {LIBDIR / 'libbccl.so'}: link {' '.join(map(str, objs))}")
+    launcher = CSRC / "tools" / "bccl_run.cc"
+    if launcher.exists():
+        lobj = BUILD / "tools_bccl_run.cc.o"
+        lines.append(f"build {lobj}: cxx {launcher}")
+        lines.append(f"build {LIBDIR / 'bccl_run'}: linkexe {lobj}")
+    return "\n".join(lines) + "\n"
+
+
+def build(verbose: bool = False) -> Path:
+    """Compiles everything (incrementally) and returns the path of libbccl.so."""
+    BUILD.mkdir(parents=True, exist_ok=True)
+    LIBDIR.mkdir(parents=True, exist_ok=True)
+    ninja_path = BUILD / "build.ninja"
+    content = _ninja_file()
+    if not ninja_path.exists() or ninja_path.read_text() != content:
+        ninja_path.write_text(content)
+    ninja = shutil.which("ninja") or str(Path(sys.executable).parent / "ninja")
+    cmd = [ninja, "-C", str(BUILD)]
+    if verbose:
+        cmd.append("-v")
+    res = subprocess.run(cmd, capture_output=not verbose, text=True)
+    if res.returncode != 0:
+        out = (res.stdout or "") + (res.stderr or "")
+        raise RuntimeError(f"native build failed:\n{out[-8000:]}")
+    return LIBDIR / "libbccl.so"
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

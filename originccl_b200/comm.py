@@ -1,0 +1,425 @@
+"""Python front end of the communicator.
+
+Mirrors the reference's API (OriginCCL include/communicator.h:19-75) in Python naming:
+``get_unique_id``, ``init``, ``finalize``, ``all_reduce``, ``broadcast``, ``reduce``,
+``all_gather``, ``reduce_scatter``, ``send``, ``recv``, ``group_start``/``group_end`` (or the
+``group()`` context manager), and the local/machine views. Buffers are torch tensors (CPU for a
+host communicator, CUDA for a device communicator) or, for host communicators, numpy arrays.
+
+Device communicators enqueue on the caller's current torch CUDA stream by default and return
+immediately (like ``torch.distributed``); pass ``blocking=True`` to run on the library's own
+stream and wait for the result (the reference's synchronous contract).
+"""
+from __future__ import annotations
+
+import contextlib
+import ctypes
+import enum
+import os
+import time
+from dataclasses import dataclass
+from typing import Any, Optional, Sequence
+
+from . import _native
+
+
+class DataType(enum.IntEnum):
+    FLOAT32 = 0
+    FLOAT64 = 1
+    INT32 = 2
+    INT64 = 3
+    BF16 = 4
+    FP16 = 5
+
+
+class ReduceOp(enum.IntEnum):
+    SUM = 0
+    MAX = 1
+    MIN = 2
+    AVG = 3
+
+
+class Algo(enum.IntEnum):
+    AUTO = 0
+    ONESHOT = 1
+    TWOSHOT = 2
+    NVLS = 3
+    RING = 4
+
+
+class CollFunc(enum.IntEnum):
+    ALLREDUCE = 0
+    BROADCAST = 1
+    REDUCE = 2
+    ALLGATHER = 3
+    REDUCESCATTER = 4
+    SEND = 5
+    RECV = 6
+
+
+_DTYPE_SIZE = {DataType.FLOAT32: 4, DataType.FLOAT64: 8, DataType.INT32: 4, DataType.INT64: 8,
+               DataType.BF16: 2, DataType.FP16: 2}
+
+
+class BcclError(RuntimeError):
+    """A library call returned failure; the message is the library's last error."""
+
+
+@dataclass(frozen=True)
+class UniqueId:
+    ip_addr: str
+    port: int
+
+    def to_bytes(self) -> bytes:
+        return f"{self.ip_addr}:{self.port}".encode()
+
+    @staticmethod
+    def from_bytes(b: bytes) -> "UniqueId":
+        ip, port = b.decode().rsplit(":", 1)
+        return UniqueId(ip, int(port))
+
+
+def _dtype_of(buf: Any) -> DataType:
+    mod = type(buf).__module__
+    if mod.startswith("torch"):
+        import torch
+        table = {torch.float32: DataType.FLOAT32, torch.float64: DataType.FLOAT64, torch.int32: DataType.INT32,
+                 torch.int64: DataType.INT64, torch.bfloat16: DataType.BF16, torch.float16: DataType.FP16}
+        if buf.dtype not in table:
+            raise TypeError(f"unsupported dtype {buf.dtype}")
+        return table[buf.dtype]
+    import numpy as np
+    table = {np.dtype(np.float32): DataType.FLOAT32, np.dtype(np.float64): DataType.FLOAT64,
+             np.dtype(np.int32): DataType.INT32, np.dtype(np.int64): DataType.INT64,
+             np.dtype(np.float16): DataType.FP16}
+    if buf.dtype not in table:
+        raise TypeError(f"unsupported dtype {buf.dtype}")
+    return table[buf.dtype]
+
+
+def _ptr(buf: Any) -> Optional[int]:
+    if buf is None:
+        return None
+    if type(buf).__module__.startswith("torch"):
+        if not buf.is_contiguous():
+            raise ValueError("tensors must be contiguous")
+        return buf.data_ptr()
+    if not buf.flags["C_CONTIGUOUS"]:
+        raise ValueError("arrays must be C-contiguous")
+    return buf.ctypes.data
+
+
+def _numel(buf: Any) -> int:
+    if type(buf).__module__.startswith("torch"):
+        return buf.numel()
+    return int(buf.size)
+
+
+class Communicator:
+    """One rank's communicator (see module docstring)."""
+
+    def __init__(self) -> None:
+        self._lib = _native.lib()
+        h = ctypes.c_void_p()
+        self._check(self._lib.bcclCommCreate(ctypes.byref(h)))
+        self._h = h
+        self._inited = False
+        self.device: int = -1
+        self.blocking = False
+
+    # ---------------------------------------------------------------- lifecycle
+    def _check(self, rc: int) -> None:
+        if rc != 0:
+            raise BcclError(_native.last_error() or "bccl call failed")
+
+    def get_unique_id(self) -> UniqueId:
+        ip = ctypes.create_string_buffer(64)
+        port = ctypes.c_uint16()
+        self._check(self._lib.bcclGetUniqueId(self._h, ip, ctypes.byref(port)))
+        return UniqueId(ip.value.decode(), port.value)
+
+    def init(self, rank: int, world_size: int, unique_id: Optional[UniqueId] = None, *, device: int = -1,
+             n_channels: int = 0, buffer_bytes: int = 0, timeout_ms: int = 0, enable_nvls: bool = True,
+             enable_nccl_p2p: bool = True, logical_machine_size: int = 0, blocking: bool = False) -> "Communicator":
+        cfg = _native.BcclConfig()
+        cfg.rank, cfg.world_size = rank, world_size
+        uid = unique_id or UniqueId("127.0.0.1", 0)
+        cfg.ip_addr = uid.ip_addr.encode()
+        cfg.port = uid.port
+        cfg.n_channels = n_channels
+        cfg.device = device
+        cfg.buffer_bytes = buffer_bytes
+        cfg.timeout_ms = timeout_ms
+        cfg.enable_nvls = int(enable_nvls)
+        cfg.enable_nccl_p2p = int(enable_nccl_p2p)
+        cfg.logical_machine_size = logical_machine_size
+        self._check(self._lib.bcclCommInit(self._h, ctypes.byref(cfg)))
+        self._inited = True
+        self.device = device
+        self.blocking = blocking
+        return self
+
+    def finalize(self) -> None:
+        if self._h is not None:
+            self._lib.bcclCommFinalize(self._h)
+            self._inited = False
+
+    def destroy(self) -> None:
+        if self._h is not None:
+            self._lib.bcclCommFinalize(self._h)
+            self._lib.bcclCommDestroy(self._h)
+            self._h = None
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------------- views
+    def _info(self) -> tuple:
+        vals = [ctypes.c_int() for _ in range(7)]
+        self._check(self._lib.bcclCommInfo(self._h, *[ctypes.byref(v) for v in vals]))
+        return tuple(v.value for v in vals)
+
+    @property
+    def rank(self) -> int:
+        return self._info()[0]
+
+    @property
+    def world_size(self) -> int:
+        return self._info()[1]
+
+    @property
+    def local_rank(self) -> int:
+        return self._info()[2]
+
+    @property
+    def local_size(self) -> int:
+        return self._info()[3]
+
+    @property
+    def machine_index(self) -> int:
+        return self._info()[4]
+
+    @property
+    def machine_count(self) -> int:
+        return self._info()[5]
+
+    @property
+    def n_channels(self) -> int:
+        return self._info()[6]
+
+    @property
+    def is_single_machine(self) -> bool:
+        return self.machine_count == 1
+
+    def _int_list(self, fn) -> list:
+        buf = (ctypes.c_int * 256)()
+        n = fn(self._h, buf, 256)
+        return [buf[i] for i in range(min(n, 256))]
+
+    @property
+    def local_ranks(self) -> list:
+        return self._int_list(self._lib.bcclCommLocalRanks)
+
+    @property
+    def machine_leaders(self) -> list:
+        return self._int_list(self._lib.bcclCommMachineLeaders)
+
+    @property
+    def nvls_enabled(self) -> bool:
+        return bool(self._lib.bcclCommNvlsEnabled(self._h))
+
+    @property
+    def last_algorithm(self) -> str:
+        return self._lib.bcclCommLastAlgorithm(self._h).decode()
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(self._lib.bcclCommKernelLaunches(self._h))
+
+    def p2p_transport(self, peer: int) -> str:
+        return self._lib.bcclCommP2pTransport(self._h, peer).decode()
+
+    @property
+    def host_executor(self) -> str:
+        return self._lib.bcclCommHostExecutor(self._h).decode()
+
+    # ---------------------------------------------------------------- streams
+    def _stream(self, stream: Any = None) -> tuple:
+        if self.device < 0 or (self.blocking and stream is None):
+            return 0, 0
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(self.device)
+        handle = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+        return int(handle), 1
+
+    # ---------------------------------------------------------------- collectives
+    def all_reduce(self, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, out: Any = None, scale: float = 1.0,
+                   algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
+        """out = reduce(tensor over ranks) * scale; in place when ``out`` is None."""
+        out = tensor if out is None else out
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclAllReduce(self._h, _ptr(tensor), _ptr(out), _numel(tensor), int(_dtype_of(tensor)),
+                                            int(op), float(scale), int(algo), s, has))
+        return out
+
+    def broadcast(self, tensor: Any, root: int, *, src: Any = None, algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
+        """Every rank's ``tensor`` receives the root's data (``src`` on the root when out of place)."""
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclBroadcast(self._h, _ptr(src) if src is not None else _ptr(tensor), _ptr(tensor),
+                                            _numel(tensor), int(_dtype_of(tensor)), int(root), int(algo), s, has))
+        return tensor
+
+    def reduce(self, tensor: Any, root: int, op: ReduceOp = ReduceOp.SUM, *, out: Any = None, algo: Algo = Algo.AUTO,
+               stream: Any = None) -> Any:
+        """The root's ``out`` (default: ``tensor``) receives the reduction; other ranks' out may be None."""
+        s, has = self._stream(stream)
+        dst = out if out is not None else (tensor if self.rank == root else None)
+        self._check(self._lib.bcclReduce(self._h, _ptr(tensor), _ptr(dst), _numel(tensor), int(_dtype_of(tensor)),
+                                         int(op), int(root), int(algo), s, has))
+        return dst
+
+    def all_gather(self, out: Any, tensor: Any, *, stream: Any = None) -> Any:
+        """out (world_size * numel) = concatenation of every rank's tensor in rank order."""
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclAllGather(self._h, _ptr(tensor), _ptr(out), _numel(tensor), int(_dtype_of(tensor)),
+                                            s, has))
+        return out
+
+    def reduce_scatter(self, out: Any, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, stream: Any = None) -> Any:
+        """out (numel) = this rank's block of reduce(tensor (world_size * numel))."""
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclReduceScatter(self._h, _ptr(tensor), _ptr(out), _numel(out), int(_dtype_of(out)),
+                                                int(op), s, has))
+        return out
+
+    def send(self, tensor: Any, peer: int, *, stream: Any = None) -> None:
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclSend(self._h, _ptr(tensor), _numel(tensor), int(_dtype_of(tensor)), int(peer), s, has))
+
+    def recv(self, tensor: Any, peer: int, *, stream: Any = None) -> Any:
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclRecv(self._h, _ptr(tensor), _numel(tensor), int(_dtype_of(tensor)), int(peer), s, has))
+        return tensor
+
+    # Raw-pointer entry points (device pointers or host addresses), for callers without tensors.
+    def all_reduce_ptr(self, send: int, recv: int, count: int, dtype: DataType, op: ReduceOp = ReduceOp.SUM,
+                       scale: float = 1.0, algo: Algo = Algo.AUTO, stream: Any = None) -> None:
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclAllReduce(self._h, send, recv, count, int(dtype), int(op), float(scale), int(algo),
+                                            s, has))
+
+    # ---------------------------------------------------------------- groups
+    def group_start(self) -> None:
+        self._check(self._lib.bcclGroupStart(self._h))
+
+    def group_end(self, stream: Any = None) -> None:
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclGroupEnd(self._h, s, has))
+
+    @contextlib.contextmanager
+    def group(self, stream: Any = None):
+        self.group_start()
+        ok = False
+        try:
+            yield self
+            ok = True
+        finally:
+            if ok:
+                self.group_end(stream)
+            else:
+                # Leave the group without hiding the original exception.
+                try:
+                    self.group_end(stream)
+                except BcclError:
+                    pass
+
+    # ---------------------------------------------------------------- misc
+    def synchronize(self) -> None:
+        self._check(self._lib.bcclSynchronize(self._h))
+
+    def barrier(self) -> None:
+        """Host-side barrier over the bootstrap (no device work)."""
+        self._check(self._lib.bcclBarrier(self._h))
+
+    def symmetric_empty(self, shape: Sequence[int], dtype: Any) -> Any:
+        """Collective: a CUDA tensor in memory every rank can address (freed with the communicator)."""
+        import torch
+        numel = 1
+        for d in shape:
+            numel *= int(d)
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        ptr = self._lib.bcclSymmetricAlloc(self._h, max(nbytes, 1))
+        if not ptr:
+            raise BcclError(_native.last_error() or "symmetric allocation failed")
+        return _tensor_from_ptr(ptr, shape, dtype, self.device)
+
+
+def _tensor_from_ptr(ptr: int, shape: Sequence[int], dtype: Any, device: int) -> Any:
+    import torch
+
+    class _Holder:
+        __cuda_array_interface__ = None
+
+    typestr = {torch.float32: "<f4", torch.float64: "<f8", torch.int32: "<i4", torch.int64: "<i8",
+               torch.float16: "<f2", torch.bfloat16: "<f2", torch.uint8: "|u1"}[dtype]
+    h = _Holder()
+    h.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": typestr, "data": (ptr, False),
+                                  "version": 3}
+    with torch.cuda.device(device):
+        t = torch.as_tensor(h, device=f"cuda:{device}")
+    if dtype == torch.bfloat16:
+        t = t.view(torch.bfloat16)
+    return t
+
+
+# ---------------------------------------------------------------- bootstrapping helpers
+
+def init_from_store(store: Any, rank: int, world_size: int, *, key: str = "bccl_uid", **kwargs) -> Communicator:
+    """Creates a communicator, distributing the unique id through a torch.distributed Store."""
+    comm = Communicator()
+    if rank == 0:
+        uid = comm.get_unique_id()
+        store.set(key, uid.to_bytes())
+    else:
+        uid = UniqueId.from_bytes(store.get(key))
+    return comm.init(rank, world_size, uid, **kwargs)
+
+
+def init_from_env(**kwargs) -> Communicator:
+    """Creates a communicator from the launcher's environment.
+
+    ``bccl_run`` exports BCCL_RANK / BCCL_WORLD_SIZE / BCCL_ID_FILE (rank 0 writes the unique
+    id to the file, the others wait for it). Under torchrun (RANK / WORLD_SIZE set) the id goes
+    through the default torch.distributed store when a process group exists.
+    """
+    if "BCCL_RANK" in os.environ:
+        rank, world = int(os.environ["BCCL_RANK"]), int(os.environ["BCCL_WORLD_SIZE"])
+        path = os.environ["BCCL_ID_FILE"]
+        comm = Communicator()
+        if rank == 0:
+            uid = comm.get_unique_id()
+            tmp = path + ".tmp"
+            with open(tmp, "wb") as f:
+                f.write(uid.to_bytes())
+            os.replace(tmp, path)
+        else:
+            deadline = time.time() + 60
+            while not os.path.exists(path):
+                if time.time() > deadline:
+                    raise BcclError("timed out waiting for the unique id file")
+                time.sleep(0.01)
+            with open(path, "rb") as f:
+                uid = UniqueId.from_bytes(f.read())
+        return comm.init(rank, world, uid, **kwargs)
+    import torch.distributed as dist
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    if world == 1:
+        return Communicator().init(0, 1, None, **kwargs)
+    if not dist.is_initialized():
+        raise BcclError("init_from_env under torchrun needs torch.distributed.init_process_group first")
+    store = dist.distributed_c10d._get_default_store()
+    return init_from_store(store, rank, world, **kwargs)

@@ -1,0 +1,180 @@
+"""Device collective cases, run inside each rank process by the GPU tests.
+
+Inputs are seeded per rank; the oracle recomputes every rank's input on the host and reduces in
+float64, so a case needs no data from other ranks. Integer and 1/8-multiple floating inputs give
+exact expected values; bf16/fp16 use tolerances.
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, List, Tuple
+
+import numpy as np
+
+DTYPES = ["float32", "float64", "int32", "int64", "bfloat16", "float16"]
+
+
+def _torch_dtype(name: str):
+    import torch
+    return getattr(torch, name)
+
+
+def rank_input(rank: int, n: int, dtype: str, seed: int = 0):
+    """Exact-friendly values: multiples of 1/8 in [-8, 8) for floats, small ints for ints."""
+    import torch
+    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    v = torch.randint(-64, 64, (n,), generator=g, dtype=torch.int64)
+    if dtype.startswith("int"):
+        return v.to(_torch_dtype(dtype))
+    return (v.double() / 8.0).to(_torch_dtype(dtype))
+
+
+def oracle(op: str, inputs: List, world: int):
+    import torch
+    stack = torch.stack([x.double() for x in inputs])
+    if op in ("sum", "avg"):
+        r = stack.sum(0)
+    elif op == "max":
+        r = stack.max(0).values
+    else:
+        r = stack.min(0).values
+    if op == "avg":
+        if inputs[0].dtype in (torch.int32, torch.int64):
+            r = torch.div(r, world, rounding_mode="trunc")
+        else:
+            r = r / world
+    return r
+
+
+def _tol(dtype: str) -> Tuple[float, float]:
+    return {"bfloat16": (1.6e-2, 1e-1), "float16": (2e-3, 2e-2)}.get(dtype, (0.0, 0.0))
+
+
+def _close(got, exp, dtype: str, what: str) -> None:
+    import torch
+    rtol, atol = _tol(dtype)
+    got = got.double().cpu()
+    exp = exp.double().cpu()
+    if rtol == 0 and atol == 0:
+        if not torch.equal(got, exp):
+            bad = (got != exp).nonzero()
+            i = int(bad[0]) if bad.numel() else -1
+            raise AssertionError(f"{what}: mismatch at {i}: got {got[i].item()} expected {exp[i].item()} "
+                                 f"({bad.numel()} bad)")
+    else:
+        torch.testing.assert_close(got, exp, rtol=rtol, atol=atol, msg=lambda m: f"{what}: {m}")
+
+
+OPS = {"sum": 0, "max": 1, "min": 2, "avg": 3}
+
+
+def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: bool = False) -> Dict:
+    """Runs every collective over dtypes x ops x sizes x algorithms; returns a summary."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import Algo, ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS}
+    ran = 0
+    used = set()
+    dtypes = ["float32", "bfloat16", "int32"] if quick else DTYPES
+    for n in sizes:
+        for dtype in dtypes:
+            td = _torch_dtype(dtype)
+            inputs = [rank_input(r, n, dtype, seed=n) for r in range(world)]
+            x = inputs[rank].cuda()
+            # AllReduce: every op, out of place and in place, each algorithm
+            for op in (["sum", "max", "avg"] if quick else ["sum", "max", "min", "avg"]):
+                exp = oracle(op, inputs, world)
+                for algo in algos:
+                    y = torch.full((n + 1,), 7, dtype=td, device="cuda")  # sentinel after the output
+                    comm.all_reduce(x, ReduceOp(OPS[op]), out=y[:n], algo=algo_map[algo])
+                    used.add(comm.last_algorithm)
+                    _close(y[:n], exp.to(td), dtype, f"allreduce {dtype} {op} n={n} algo={algo}")
+                    assert y[n].item() == 7, "allreduce wrote past the end"
+                    ran += 1
+                xi = x.clone()
+                comm.all_reduce(xi, ReduceOp(OPS[op]))
+                _close(xi, exp.to(td), dtype, f"allreduce in-place {dtype} {op} n={n}")
+                _close(x, inputs[rank].cuda(), dtype, "input changed")
+            # ReduceScatter: input world*n
+            rs_in = [rank_input(r, n * world, dtype, seed=n + 1) for r in range(world)]
+            out = torch.empty(n, dtype=td, device="cuda")
+            comm.reduce_scatter(out, rs_in[rank].cuda())
+            _close(out, oracle("sum", rs_in, world)[rank * n:(rank + 1) * n].to(td), dtype, f"reducescatter {dtype} n={n}")
+            # AllGather
+            ag = torch.empty(n * world, dtype=td, device="cuda")
+            comm.all_gather(ag, x)
+            _close(ag, torch.cat(inputs).to(td), dtype, f"allgather {dtype} n={n}")
+            # Broadcast from the last rank, Reduce MAX to rank 0
+            root = world - 1
+            b = x.clone()
+            comm.broadcast(b, root)
+            _close(b, inputs[root].to(td), dtype, f"broadcast {dtype} n={n}")
+            for algo in algos:
+                r_out = torch.empty(n, dtype=td, device="cuda") if rank == 0 else None
+                comm.reduce(x, 0, ReduceOp.MAX, out=r_out, algo=algo_map[algo])
+                if rank == 0:
+                    _close(r_out, oracle("max", inputs, world).to(td), dtype, f"reduce {dtype} n={n} algo={algo}")
+            ran += 4
+    # A group of many small collectives runs as one batched launch.
+    before = comm.kernel_launches
+    tensors = [rank_input(rank, 1024 + 3 * i, "float32", seed=i).cuda() for i in range(64)]
+    outs = [torch.empty_like(t) for t in tensors]
+    with comm.group():
+        for t, o in zip(tensors, outs):
+            comm.all_reduce(t, out=o, scale=0.5)
+    launches = comm.kernel_launches - before
+    for i, o in enumerate(outs):
+        exp = oracle("sum", [rank_input(r, 1024 + 3 * i, "float32", seed=i) for r in range(world)], world) * 0.5
+        _close(o, exp.float(), "float32", f"group item {i}")
+    comm.destroy()
+    return {"ran": ran, "algorithms": sorted(used), "group_launches": launches}
+
+
+def run_p2p(rank: int, world: int) -> Dict:
+    import torch
+
+    import originccl_b200 as occl
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    n = (4 << 20) // 4
+    s = torch.full((n,), float(rank), device="cuda")
+    r = torch.empty(n, device="cuda")
+    with comm.group():
+        comm.send(s, (rank + 1) % world)
+        comm.recv(r, (rank - 1) % world)
+    assert torch.all(r == float((rank - 1) % world)).item()
+    comm.destroy()
+    return {"ok": True}
+
+
+def run_timeout_probe(rank: int, world: int) -> Dict:
+    """Rank 1 never launches its collective; rank 0's bounded wait must expire and report an
+    error status while the GPU context stays usable."""
+    import torch
+
+    import originccl_b200 as occl
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=500, enable_nvls=False, enable_nccl_p2p=False)
+    x = torch.ones(1024, device="cuda")
+    result = {}
+    if rank == 0:
+        try:
+            comm.all_reduce(x)
+            result["raised"] = False
+        except occl.BcclError as e:
+            result["raised"] = True
+            result["msg"] = str(e)
+        # The context still works after the failed collective.
+        z = torch.arange(10, device="cuda").sum().item()
+        result["context_ok"] = z == 45
+    comm.barrier()  # host-side: rank 1 leaves only after rank 0 has finished waiting
+    comm.destroy()
+    return result

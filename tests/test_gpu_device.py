@@ -1,0 +1,87 @@
+"""Device communicator tests (need a B200). Numerics are checked against a float64 host oracle."""
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from tests import _mp, gpu_cases  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _need(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPU(s)")
+
+
+def test_native_library_is_the_in_tree_build():
+    _need(1)
+    from originccl_b200 import _native
+    lib = _native.lib()
+    assert str(_native._LIB_PATH) == lib._name
+
+
+def test_single_rank_suite():
+    _need(1)
+    res = _mp.run(1, gpu_cases.run_suite, [1, 7, 4097, (1 << 20) + 3], ["auto"], timeout=600)
+    assert res[0]["ran"] > 0
+    assert res[0]["group_launches"] == 1  # 64 collectives in one group -> one batched kernel
+
+
+def test_single_rank_large_multi_round():
+    _need(1)
+    # Larger than the per-round staging slot: several rounds in one launch.
+    res = _mp.run(1, gpu_cases.run_suite, [(96 << 20) // 4 + 5], ["auto"], True, timeout=600)
+    assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
+def test_two_rank_suite_all_algorithms():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_suite, [1, 33, 65537, (3 << 20) + 5], ["oneshot", "twoshot", "nvls", "auto"],
+                  timeout=900)
+    assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
+def test_all_gpu_suite():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 3:
+        pytest.skip("needs 3+ GPUs")
+    n = min(n, 8)
+    res = _mp.run(n, gpu_cases.run_suite, [5, 70001, (9 << 20) + 7], ["oneshot", "twoshot", "nvls"], True,
+                  timeout=900)
+    assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
+def test_p2p_ring_over_nccl():
+    _need(2)
+    _mp.run(2, gpu_cases.run_p2p, timeout=300)
+
+
+@pytest.mark.multigpu
+def test_bounded_wait_reports_timeout():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_timeout_probe, timeout=300, env={"NCCL_NVLS_ENABLE": "0"})
+    assert res[0]["raised"], res[0]
+    assert "timeout" in res[0]["msg"], res[0]
+    assert res[0]["context_ok"]
+
+
+def test_bounded_wait_self_test_single_gpu():
+    """A kernel waiting on a flag nothing sets gives up after ~0.2 s and reports a timeout."""
+    _need(1)
+    import time
+    import originccl_b200 as occl
+    from originccl_b200 import _native
+    torch.cuda.set_device(0)
+    comm = occl.Communicator().init(0, 1, None, device=0, blocking=True)
+    t0 = time.time()
+    code = _native.lib().bcclDebugWaitProbe(comm._h, 200)
+    assert code == 1, code
+    assert time.time() - t0 < 10
+    # The context and the communicator still work afterwards.
+    x = torch.ones(1000, device="cuda")
+    comm.all_reduce(x, scale=3.0)
+    assert torch.all(x == 3.0).item()
+    comm.destroy()
