@@ -195,6 +195,16 @@ int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms) {
     return comm->comm.device_engine()->WaitProbe(timeout_ms);
 }
 
+double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int ctas, int iters) {
+    if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1.0;
+    return comm->comm.device_engine()->BandwidthProbe(mode, peer, bytes, ctas, iters);
+}
+
+long bcclTraceDump(bcclComm_t comm, const char* path) {
+    if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1;
+    return comm->comm.device_engine()->DumpTrace(path);
+}
+
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,
                     const int* root, const int* peer, int* order) {
     std::vector<bccl::CollTask> tasks(n);

@@ -41,8 +41,11 @@ CollFunc ParseFunc(const std::string& s) {
 std::vector<TuningRow> DefaultTable() {
     return {
         {CollFunc::AllReduce, 0, 256 << 10, Algo::kOneShot, 0},
-        {CollFunc::AllReduce, 2, 4 << 20, Algo::kOneShot, 0},
-        {CollFunc::AllReduce, 0, 2 << 20, Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 2, 1 << 20, Algo::kOneShot, 0},
+        // Two ranks: the switch reads the issuing GPU's own copy too, so NVLS moves 1.5*S per
+        // direction against S for two-shot.
+        {CollFunc::AllReduce, 2, ~size_t(0), Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 0, 1 << 20, Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 0, ~size_t(0), Algo::kNvls, 0},
         {CollFunc::Broadcast, 0, 512 << 10, Algo::kOneShot, 0},
         {CollFunc::Broadcast, 0, ~size_t(0), Algo::kNvls, 0},

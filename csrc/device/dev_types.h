@@ -24,6 +24,9 @@ constexpr int kMaxCtas = 256;
 constexpr size_t kCtrlBytes = 1u << 20;          // control region at the start of each UC buffer
 constexpr size_t kBarrierFlagsOff = 0;            // u64 [kMaxCtas][kMaxRanks]
 constexpr size_t kBarrierFlagsBytes = sizeof(uint64_t) * kMaxCtas * kMaxRanks;
+constexpr size_t kPipeReadyOff = 16u << 10;      // u64 [kMaxCtas][kMaxRanks], pipelined AllReduce
+constexpr size_t kPipeDoneOff = 32u << 10;       // u64 [kMaxCtas][kMaxRanks]
+constexpr size_t kPipeLocalOff = 48u << 10;      // u64 [kMaxCtas], same-GPU progress (finish -> stage)
 constexpr size_t kTpFlagsOff = 64u << 10;         // u64 flags of the fused tensor-parallel kernels
 constexpr size_t kTpFlagsBytes = 256u << 10;
 constexpr size_t kAlign = 256;
@@ -58,6 +61,28 @@ struct DevState {
     unsigned int pad2;
 };
 
+// One device trace record (written when tracing is on): who did what, when.
+struct TraceRecord {
+    unsigned long long t_ns;  // %globaltimer
+    unsigned int cta;
+    unsigned short group;     // warp group (0 = whole CTA)
+    unsigned short event;     // TraceEvent
+    unsigned int round;
+    unsigned int kernel;      // launch serial
+};
+
+enum TraceEvent : unsigned short {
+    kTrBegin = 1,     // kernel start
+    kTrStaged = 2,    // G1: round staged (copy-in / push done, flag sent)
+    kTrReadyWait = 3, // G2: ready flags observed
+    kTrReduced = 4,   // G2: reduce done, flag sent
+    kTrDoneWait = 5,  // G3: reduced flags observed
+    kTrFinished = 6,  // G3: round copied out
+    kTrBarrier = 7,   // push engine: barrier passed
+    kTrEnd = 8,       // kernel end
+    kTrSlotWait = 9,  // G1: slot became free
+};
+
 struct DevComm {
     int rank;
     int nranks;
@@ -70,6 +95,10 @@ struct DevComm {
     unsigned long long timeout_ns;
     unsigned long long data_bytes;  // bytes of the UC data region
     unsigned long long nvls_bytes;  // bytes of the NVLS buffer
+    TraceRecord* trace;             // null unless tracing is on
+    unsigned int* trace_count;
+    unsigned int trace_cap;
+    unsigned int kernel_serial;     // host launch counter (trace labels only)
 };
 
 // One collective in a push-engine launch. All byte offsets refer to the per-peer stream:

@@ -20,19 +20,23 @@ namespace {
         }                                                                                \
     } while (0)
 
+// Staging ring depth of the pipelined kernels (BCCL_PIPE_SLOTS); every rank must agree.
+int PipeSlots() { return static_cast<int>(std::max<long>(3, std::min<long>(16, EnvInt("BCCL_PIPE_SLOTS", 3)))); }
+
 size_t RoundDown(size_t x, size_t a) { return x / a * a; }
 size_t RoundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Per-peer payload bytes of a collective in the push engine's stream.
 size_t PeerPayload(const CollTask& t) { return t.count * DataTypeSize(t.dtype); }
 
-int PushCtas(size_t stream_bytes) {
+// CTAs for a push-engine launch: few for latency-bound payloads (each CTA pays one
+// cross-rank barrier per round), up to one per SM for bandwidth-bound ones.
+int PushCtas(size_t stream_bytes, int num_sms) {
     if (stream_bytes <= (16u << 10)) return 1;
     if (stream_bytes <= (64u << 10)) return 2;
     if (stream_bytes <= (256u << 10)) return 4;
     if (stream_bytes <= (1u << 20)) return 8;
-    if (stream_bytes <= (4u << 20)) return 16;
-    return 32;
+    return static_cast<int>(std::min<size_t>(std::max<size_t>(16, stream_bytes / (128u << 10)), static_cast<size_t>(num_sms)));
 }
 
 }  // namespace
@@ -46,10 +50,11 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     max_ctas_ = cfg.n_channels;
     forced_ = Planner::ParseAlgo(EnvStr("BCCL_ALGO", ""));
     CUDA_OK(cudaSetDevice(device_), "cudaSetDevice");
+    CUDA_OK(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_), "cudaDeviceGetAttribute");
     const int timeout_ms = cfg.timeout_ms > 0 ? cfg.timeout_ms : static_cast<int>(EnvInt("BCCL_TIMEOUT_MS", 10000));
     if (!sm_.Init(device_, rank_, nranks_, bs, fp, std::max(timeout_ms, 30000), cfg.enable_nvls)) return false;
 
-    data_bytes_ = cfg.buffer_bytes ? cfg.buffer_bytes : static_cast<size_t>(EnvInt("BCCL_BUFFSIZE", 128l << 20));
+    data_bytes_ = cfg.buffer_bytes ? cfg.buffer_bytes : static_cast<size_t>(EnvInt("BCCL_BUFFSIZE", 512l << 20));
     data_bytes_ = std::max<size_t>(RoundUp(data_bytes_, 1u << 20), 4u << 20);
     if (!sm_.Alloc(kCtrlBytes + data_bytes_, false, &uc_)) return false;
     if (sm_.multicast_supported()) {
@@ -81,6 +86,15 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     dc_.abort = abort_dev;
     dc_.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
     dc_.data_bytes = data_bytes_;
+    const long trace_cap = EnvInt("BCCL_TRACE", 0);
+    if (trace_cap > 0) {
+        CUDA_OK(cudaMalloc(&trace_, sizeof(TraceRecord) * static_cast<size_t>(trace_cap)), "cudaMalloc(trace)");
+        CUDA_OK(cudaMalloc(&trace_count_, sizeof(unsigned int)), "cudaMalloc(trace count)");
+        CUDA_OK(cudaMemset(trace_count_, 0, sizeof(unsigned int)), "cudaMemset(trace count)");
+        dc_.trace = trace_;
+        dc_.trace_count = trace_count_;
+        dc_.trace_cap = static_cast<unsigned int>(trace_cap);
+    }
     CUDA_OK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
     if (nranks_ > 1 && cfg.enable_nccl_p2p && !EnvFlag("BCCL_DISABLE_NCCL_P2P")) {
         if (!p2p_.Init(rank_, nranks_, bs)) LOG_WARN("rank %d: Send/Recv unavailable (NCCL init failed)", rank_);
@@ -110,6 +124,10 @@ void DeviceEngine::Finalize() {
     state_ = nullptr;
     if (err_host_) cudaFreeHost(err_host_);
     err_host_ = nullptr;
+    if (trace_) cudaFree(trace_);
+    if (trace_count_) cudaFree(trace_count_);
+    trace_ = nullptr;
+    trace_count_ = nullptr;
     if (abort_host_) cudaFreeHost(abort_host_);
     abort_host_ = nullptr;
 }
@@ -143,6 +161,82 @@ int DeviceEngine::WaitProbe(int timeout_ms) {
     int code = err_host_->code;
     memset(err_host_, 0, sizeof(ErrorRecord));
     return code;
+}
+
+double DeviceEngine::BandwidthProbe(int mode, int peer, size_t bytes, int ctas, int iters) {
+    if (!inited_ || peer < 0 || peer >= nranks_ || ctas <= 0 || ctas > 1024 || iters <= 0) return -1.0;
+    cudaSetDevice(device_);
+    // Both halves of the own data region serve as source/destination; the peer's data region
+    // is the remote end. Probes must not overlap a collective on the peer.
+    bytes = std::min(RoundDown(bytes, 16), static_cast<size_t>(data_bytes_ / 2));
+    char* mine = uc_.ptr[rank_] + kCtrlBytes;
+    char* theirs = uc_.ptr[peer] + kCtrlBytes;
+    char *dst = mine + data_bytes_ / 2, *src = mine;
+    bool mc = false;
+    if (mode == 1) dst = theirs;
+    if (mode == 2) src = theirs;
+    if (mode == 3) {
+        if (nvls_.mc == nullptr) return -1.0;
+        bytes = std::min(bytes, static_cast<size_t>(nvls_.bytes));
+        dst = nvls_.mc;
+        mc = true;
+    }
+    // Modes 4..9: fence-cost probe over a peer write (4-6) or a local copy (7-9) with a fence
+    // every `seg` bytes per CTA; seg is taken from BCCL_PROBE_SEG (default 256 KiB).
+    const bool fence_probe = mode >= 4;
+    const int fmode = fence_probe ? (mode - 4) % 3 : 0;
+    const size_t seg = static_cast<size_t>(EnvInt("BCCL_PROBE_SEG", 256 << 10));
+    if (fence_probe) {
+        src = mine;
+        dst = mode <= 6 ? theirs : mine + data_bytes_ / 2;
+        bytes = RoundDown(bytes, seg);
+    }
+    auto launch = [&]() {
+        if (fence_probe) LaunchFenceProbe(dst, src, bytes, seg, fmode, ctas, stream_);
+        else LaunchBandwidthProbe(dst, src, bytes, mc, ctas, stream_);
+    };
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    launch();  // warm-up
+    cudaEventRecord(e0, stream_);
+    for (int i = 0; i < iters; ++i) launch();
+    cudaEventRecord(e1, stream_);
+    cudaError_t err = cudaStreamSynchronize(stream_);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    launches_ += static_cast<unsigned long long>(iters) + 1;
+    if (err != cudaSuccess || ms <= 0) return -1.0;
+    return static_cast<double>(bytes) * iters / (ms * 1e-3) / 1e9;
+}
+
+long DeviceEngine::DumpTrace(const char* path) {
+    if (trace_ == nullptr) return -1;
+    cudaSetDevice(device_);
+    cudaDeviceSynchronize();
+    unsigned int n = 0;
+    cudaMemcpy(&n, trace_count_, sizeof(n), cudaMemcpyDeviceToHost);
+    n = std::min(n, dc_.trace_cap);
+    std::vector<TraceRecord> recs(n);
+    if (n) cudaMemcpy(recs.data(), trace_, sizeof(TraceRecord) * n, cudaMemcpyDeviceToHost);
+    cudaMemset(trace_count_, 0, sizeof(unsigned int));
+    FILE* f = fopen(path, "w");
+    if (f == nullptr) return -1;
+    static const char* kNames[] = {"?", "begin", "staged", "ready_seen", "reduced", "reduced_seen", "finished",
+                                   "barrier", "end", "slot_free"};
+    fprintf(f, "{\"traceEvents\":[\n");
+    for (unsigned int i = 0; i < n; ++i) {
+        const TraceRecord& r = recs[i];
+        fprintf(f, "%s{\"name\":\"%s r%u\",\"ph\":\"i\",\"s\":\"t\",\"ts\":%.3f,\"pid\":%d,\"tid\":%u,"
+                   "\"args\":{\"kernel\":%u,\"group\":%u,\"round\":%u}}\n",
+                i ? "," : "", kNames[r.event < 10 ? r.event : 0], r.round, r.t_ns / 1000.0, rank_, r.cta * 4 + r.group,
+                r.kernel, r.group, r.round);
+    }
+    fprintf(f, "]}\n");
+    fclose(f);
+    return static_cast<long>(n);
 }
 
 void DeviceEngine::Abort() {
@@ -180,7 +274,8 @@ bool DeviceEngine::SymFree(void* ptr) {
 
 bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream) {
     if (batch->empty()) return true;
-    const unsigned long long slot = RoundDown(data_bytes_ / (2ull * nranks_), 256);
+    // The push engine owns the first half of the UC data region (two halves x N sources).
+    const unsigned long long slot = RoundDown(data_bytes_ / 2 / (2ull * nranks_), 256);
     size_t i = 0;
     while (i < batch->size()) {
         size_t n = std::min<size_t>(kPushMaxItems, batch->size() - i);
@@ -190,10 +285,11 @@ bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* 
         for (WorkItem& w : part) w.stream_off -= base;
         const WorkItem& last = part.back();
         unsigned long long bytes = last.stream_off + RoundUp(last.count * DataTypeSize(static_cast<DataType>(last.dtype)), 16);
-        int ctas = PushCtas(std::min<unsigned long long>(bytes, slot));
+        int ctas = PushCtas(std::min<unsigned long long>(bytes, slot), num_sms_);
         if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
         long env_max = EnvInt("BCCL_MAX_CTAS", 0);
         if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
+        dc_.kernel_serial = ++kernel_serial_;
         cudaError_t e = LaunchPushEngine(dc_, part.data(), static_cast<int>(n), bytes, slot, ctas, stream);
         if (e != cudaSuccess) {
             LOG_ERROR("rank %d: push-engine launch failed: %s", rank_, cudaGetErrorString(e));
@@ -211,18 +307,49 @@ bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* 
 bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream) {
     cudaError_t e = cudaSuccess;
     const int dt = static_cast<int>(t.dtype), op = static_cast<int>(t.op);
+    const size_t bytes = t.count * DataTypeSize(t.dtype);
+    const unsigned long long q = 16ull * nranks_;
+    const int slots = PipeSlots();
+    // Rounds of at least `min_chunk` bytes (each CTA then moves >= ~100 KB between fences),
+    // about `rounds` of them so the software pipeline has something to overlap.
+    const unsigned long long rounds = static_cast<unsigned long long>(std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", 4)));
+    const unsigned long long min_chunk = static_cast<unsigned long long>(EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20));
+    auto pick_chunk = [&](unsigned long long cap) {
+        unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, q);
+        want = std::max<unsigned long long>(want, RoundUp(min_chunk, q));
+        return std::max<unsigned long long>(q, std::min<unsigned long long>(want, RoundDown(cap, q)));
+    };
+    const int debug = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
+    int ctas = c.ctas;
+    dc_.kernel_serial = ++kernel_serial_;
     if (c.algo == Algo::kNvls) {
-        const unsigned long long cap = RoundDown(nvls_.bytes / 2, 16ull * nranks_);
-        const size_t bytes = t.count * DataTypeSize(t.dtype);
-        const bool zc = t.func == CollFunc::AllReduce && t.send_buf == t.recv_buf && FindSym(t.recv_buf, RoundUp(bytes, 16ull * nranks_)) != nullptr;
-        (void)zc;  // zero-copy is served by user symmetric buffers bound to their own multicast objects
-        e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale, cap,
-                       c.ctas, false, stream);
+        const unsigned long long slot = RoundDown(nvls_.bytes / slots, 256);
+        const unsigned long long chunk = pick_chunk(slot);
+        if (t.func == CollFunc::AllReduce) {
+            e = LaunchAllReducePipe(dc_, kPipeNvls, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots,
+                                    ctas, stream, debug);
+        } else {
+            e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale,
+                           chunk, slot, slots, ctas, stream);
+        }
         last_algo_ = "nvls";
     } else {
-        const unsigned long long cap = RoundDown(data_bytes_ / (2ull * (nranks_ + 1)), 256);
-        e = LaunchTwoShot(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, cap, c.ctas, stream);
-        last_algo_ = "twoshot";
+        // Two ranks: a one-shot push moves the same NVLink bytes as two-shot with one
+        // reduction step per round instead of two.
+        int kind = nranks_ == 2 ? kPipeOneShot : kPipeTwoShot;
+        const long forced_kind = EnvInt("BCCL_PIPE_KIND", -1);
+        if (forced_kind == kPipeOneShot || forced_kind == kPipeTwoShot) kind = static_cast<int>(forced_kind);
+        unsigned long long slot, chunk;
+        if (kind == kPipeOneShot) {
+            slot = RoundDown(data_bytes_ / 2 / (static_cast<unsigned long long>(slots) * nranks_), 256);
+            chunk = pick_chunk(slot);
+        } else {
+            slot = RoundDown(data_bytes_ / 2 / (static_cast<unsigned long long>(slots) * 2ull * nranks_), 256);
+            chunk = pick_chunk(slot * nranks_);
+        }
+        e = LaunchAllReducePipe(dc_, kind, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots, ctas,
+                                stream, debug);
+        last_algo_ = kind == kPipeOneShot ? "oneshot_pipe" : "twoshot";
     }
     if (e != cudaSuccess) {
         LOG_ERROR("rank %d: %s launch failed: %s", rank_, last_algo_, cudaGetErrorString(e));
@@ -252,6 +379,16 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                              (t.func == CollFunc::Broadcast || NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
         AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
                                             t.algo != Algo::kAuto ? t.algo : forced_);
+        if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls) {
+            // Large-payload kernels: per-CTA barriers with the same CTA index on every rank, so
+            // every CTA must be resident: at most one per SM.
+            int want = static_cast<int>(std::min<size_t>(std::max<size_t>(bytes / (128u << 10), 4),
+                                                         static_cast<size_t>(num_sms_)));
+            c.ctas = std::min(want, kMaxCtas);
+            if (max_ctas_ > 0) c.ctas = std::min(c.ctas, max_ctas_);
+            long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+            if (env_max > 0) c.ctas = std::min<int>(c.ctas, static_cast<int>(env_max));
+        }
         if (nranks_ == 1 || c.algo == Algo::kOneShot || c.algo == Algo::kRing) {
             WorkItem w;
             w.src = t.send_buf;

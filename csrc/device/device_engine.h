@@ -45,6 +45,13 @@ public:
     // Runs the bounded-wait self-test; returns the error code it recorded (kDevTimeout
     // expected) and clears the record so the communicator stays usable.
     int WaitProbe(int timeout_ms);
+    // Transport probe (no peer participation needed; run it while peers are idle):
+    // mode 0 local copy, 1 write to `peer`, 2 read from `peer`, 3 multimem.st. Returns GB/s
+    // of the copied bytes, or a negative value on error.
+    double BandwidthProbe(int mode, int peer, size_t bytes, int ctas, int iters);
+    // Device trace (BCCL_TRACE=<records>): writes the records gathered so far as a Chrome
+    // trace (chrome://tracing, Perfetto) and resets the buffer. Returns records written.
+    long DumpTrace(const char* path);
 
     // Collective allocation of memory every rank can address directly (NVLS-bound when
     // available); AllReduce on such a buffer in place skips the staging copies.
@@ -68,6 +75,7 @@ private:
     int nranks_ = 1;
     int device_ = -1;
     int max_ctas_ = 0;
+    int num_sms_ = 148;
     Algo forced_ = Algo::kAuto;
     const Planner* planner_ = nullptr;
     Bootstrap* bs_ = nullptr;
@@ -84,6 +92,9 @@ private:
     NcclP2p p2p_;
     std::atomic<unsigned long long> launches_{0};
     const char* last_algo_ = "none";
+    TraceRecord* trace_ = nullptr;
+    unsigned int* trace_count_ = nullptr;
+    unsigned int kernel_serial_ = 0;
     bool inited_ = false;
 };
 

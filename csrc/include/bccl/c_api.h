@@ -77,6 +77,14 @@ int bcclSymmetricFree(bcclComm_t comm, void* ptr);
  * returns the error code it recorded (1 = timeout) or -1 if it could not run. */
 int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms);
 
+/* Transport probe: copy bandwidth in GB/s for mode 0 local, 1 write to peer, 2 read from peer,
+ * 3 multimem.st (peers must be idle). */
+double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int ctas, int iters);
+
+/* Device trace (enabled with BCCL_TRACE=<records>): writes a Chrome trace JSON and resets the
+ * buffer; returns the number of records or -1 when tracing is off. */
+long bcclTraceDump(bcclComm_t comm, const char* path);
+
 /* Planner white-box hooks (used by tests): sorts `n` tasks described by parallel arrays and
  * writes the resulting permutation (indices into the input) to `order`. */
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,

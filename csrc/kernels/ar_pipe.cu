@@ -1,0 +1,536 @@
+// Software-pipelined AllReduce for large payloads.
+//
+// All CTAs run the same phase; CTA b owns piece b of every round on every rank, and one
+// per-CTA barrier (flags in peer memory) closes each iteration. Iteration t does
+//   ONESHOT: A = push round t's piece to every peer's inbox slot
+//            B = reduce round t-1: own input + N-1 inbox slots -> output
+//   TWOSHOT: A = push shard q of round t to peer q's inbox slot
+//            B = reduce own shard of round t-1 -> own output, and push it into every peer's
+//                gather slot
+//            C = copy round t-2's peer shards out of the local gather slot
+//   NVLS:    A = copy round t's piece into the local NVLS slot
+//            B = multimem.ld_reduce + multimem.st of the own shard of round t-1
+//            C = copy round t-2 out of the local NVLS slot
+// then fence + signal + wait (barrier t). B(t-1) only needs A(t-1) from every rank and C(t-2)
+// only needs B(t-2) from every rank, both proven by barrier t-1. NVLink writes are issued
+// first in an iteration, so by the time the CTA fences (after its local work) they have
+// mostly drained: a system-scope fence costs little when it is not waiting on fresh
+// traffic, and a lot when it is (measured: a pipeline that fenced right behind its own
+// NVLink stream ran 5-10x slower).
+// Slots form a ring of S >= 3 per kind, indexed by a device-side round counter; a slot is
+// rewritten at least two barriers after its last reader finished, and a completed launch
+// implies every rank finished all its work (the last iteration's work precedes the last
+// barrier), so launches of any kind can follow each other.
+#include "kernels/common.cuh"
+#include "kernels/launch.h"
+
+namespace bccl {
+namespace dev {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kUnroll = 4;
+
+struct PipeParams {
+    DevComm comm;
+    const void* src;
+    void* dst;
+    unsigned long long bytes;
+    unsigned long long chunk;       // bytes per round (multiple of 16 * nranks)
+    unsigned long long slot_bytes;  // NVLS: bytes per slot (>= chunk); TWOSHOT: per-source inbox slot (>= shard)
+    int nrounds;
+    int nslots;
+    int dtype;
+    int op;
+    float scale;
+    int nvls;   // PipeKind
+    int debug;  // BCCL_PIPE_DEBUG bits (experiments): 1 no sys fences, 2 no alias fences, 4 serialise groups
+};
+
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// bar_id 0 = the whole CTA.
+__device__ __forceinline__ void sync_group(int bar_id, int nthreads) {
+    if (bar_id == 0) __syncthreads();
+    else named_bar(bar_id, nthreads);
+}
+__device__ __forceinline__ uint64_t ld_relaxed_gpu(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ __forceinline__ void st_relaxed_sys_flag(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t* pipe_flag(char* uc_base, size_t off, int cta, int src) {
+    return reinterpret_cast<uint64_t*>(uc_base + off) + (size_t)cta * kMaxRanks + src;
+}
+
+// Group copy, `kUnroll` 16-byte vectors in flight per thread.
+__device__ __forceinline__ void grp_copy(char* d, const char* s, size_t bytes, int tid, int nt, bool cg) {
+    if (((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(s)) & 15) == 0) {
+        const size_t nv = bytes >> 4;
+        size_t i = tid;
+        for (; i + (kUnroll - 1) * (size_t)nt < nv; i += kUnroll * (size_t)nt) {
+            uint4 v[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const char* p = s + ((i + u * (size_t)nt) << 4);
+                v[u] = cg ? ld_cg(p) : *reinterpret_cast<const uint4*>(p);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) st_cg(d + ((i + u * (size_t)nt) << 4), v[u]);
+        }
+        for (; i < nv; i += nt) {
+            const char* p = s + (i << 4);
+            st_cg(d + (i << 4), cg ? ld_cg(p) : *reinterpret_cast<const uint4*>(p));
+        }
+        for (size_t j = (nv << 4) + tid; j < bytes; j += nt) d[j] = s[j];
+    } else {
+        for (size_t j = tid; j < bytes; j += nt) d[j] = cg ? (char)__ldcg(reinterpret_cast<const signed char*>(s + j)) : s[j];
+    }
+}
+
+// Loads each 16-byte vector once and stores it to every destination in outs[0..no).
+__device__ __forceinline__ void grp_push_multi(char* const* outs, int no, const char* src, size_t bytes, int tid,
+                                               int nt) {
+    char* op[kMaxRanks];
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) op[q] = outs[q < no ? q : 0];
+    uintptr_t mis = reinterpret_cast<uintptr_t>(src);
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) mis |= reinterpret_cast<uintptr_t>(op[q]);
+    const size_t nv = (mis & 15) ? 0 : (bytes >> 4);
+    size_t i = tid;
+    for (; i + (kUnroll - 1) * (size_t)nt < nv; i += kUnroll * (size_t)nt) {
+        uint4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) v[u] = *reinterpret_cast<const uint4*>(src + ((i + u * (size_t)nt) << 4));
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q) {
+            if (q < no) {
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) st_cg(op[q] + ((i + u * (size_t)nt) << 4), v[u]);
+            }
+        }
+    }
+    for (; i < nv; i += nt) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + (i << 4));
+        for (int q = 0; q < no; ++q) st_cg(op[q] + (i << 4), v);
+    }
+    for (size_t j = (nv << 4) + tid; j < bytes; j += nt) {
+        const char b = src[j];
+        for (int q = 0; q < no; ++q) op[q][j] = b;
+    }
+}
+
+// ---- multimem (16-byte) -------------------------------------------------------------------
+// (dtype, op) pairs with a multimem.ld_reduce form on sm_100a (checked against ptxas):
+// f32 and f64 add only; bf16/f16 add (fp32 accumulation), max, min; integers add/max/min.
+template <int D, int O>
+struct NvlsOk {
+    static constexpr bool value = (O == kSum) || (O == kAvg) ? true : (D != kF32 && D != kF64);
+};
+template <int D, int O> __device__ __forceinline__ uint4 mm_ld_reduce(const void* p);
+#define PIPE_MM_V4(D, O, SPEC)                                                                  \
+    template <> __device__ __forceinline__ uint4 mm_ld_reduce<D, O>(const void* p) {            \
+        uint4 r;                                                                              \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " {%0,%1,%2,%3}, [%4];"    \
+                     : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p) : "memory");       \
+        return r;                                                                             \
+    }
+#define PIPE_MM_S32(D, O, SPEC)                                                                 \
+    template <> __device__ __forceinline__ uint4 mm_ld_reduce<D, O>(const void* p) {            \
+        uint4 r;                                                                              \
+        const char* c = static_cast<const char*>(p);                                          \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=r"(r.x) : "l"(c) : "memory");      \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=r"(r.y) : "l"(c + 4) : "memory");  \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=r"(r.z) : "l"(c + 8) : "memory");  \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=r"(r.w) : "l"(c + 12) : "memory"); \
+        return r;                                                                             \
+    }
+#define PIPE_MM_S64(D, O, SPEC)                                                                 \
+    template <> __device__ __forceinline__ uint4 mm_ld_reduce<D, O>(const void* p) {            \
+        unsigned long long a, b;                                                              \
+        const char* c = static_cast<const char*>(p);                                          \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=l"(a) : "l"(c) : "memory");     \
+        asm volatile("multimem.ld_reduce.relaxed.sys.global." SPEC " %0, [%1];" : "=l"(b) : "l"(c + 8) : "memory"); \
+        return make_uint4((unsigned)a, (unsigned)(a >> 32), (unsigned)b, (unsigned)(b >> 32));                      \
+    }
+PIPE_MM_V4(kF32, kSum, "add.v4.f32")
+PIPE_MM_V4(kBF16, kSum, "add.acc::f32.v4.bf16x2")
+PIPE_MM_V4(kBF16, kMax, "max.v4.bf16x2")
+PIPE_MM_V4(kBF16, kMin, "min.v4.bf16x2")
+PIPE_MM_V4(kF16, kSum, "add.acc::f32.v4.f16x2")
+PIPE_MM_V4(kF16, kMax, "max.v4.f16x2")
+PIPE_MM_V4(kF16, kMin, "min.v4.f16x2")
+PIPE_MM_S32(kI32, kSum, "add.u32")
+PIPE_MM_S32(kI32, kMax, "max.s32")
+PIPE_MM_S32(kI32, kMin, "min.s32")
+PIPE_MM_S64(kI64, kSum, "add.u64")
+PIPE_MM_S64(kI64, kMax, "max.s64")
+PIPE_MM_S64(kI64, kMin, "min.s64")
+PIPE_MM_S64(kF64, kSum, "add.f64")
+
+__device__ __forceinline__ void mm_st(void* p, const uint4& v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+template <int D>
+__device__ __forceinline__ uint4 post16(uint4 u, int op, int nranks, float scale) {
+    if (op != kAvg && scale == 1.0f) return u;
+    using V = Vec<D>;
+    typename Ty<D>::Acc a[V::E];
+    V::unpack(u, a);
+#pragma unroll
+    for (int e = 0; e < V::E; ++e) a[e] = epilogue<typename Ty<D>::Acc>(op, a[e], nranks, scale);
+    return V::pack(a);
+}
+
+// G2 body (NVLS): reduce+broadcast [lo, hi) of the slot through the multicast address.
+template <int D, int O>
+__device__ __forceinline__ void nvls_reduce_bcast(char* mc, size_t lo, size_t hi, int tid, int nt, int op, int nranks,
+                                                  float scale) {
+    constexpr int U = 8;  // the switch round trip is long: keep 8 reductions in flight per thread
+    const size_t nv = (hi - lo) >> 4;  // [lo, hi) is 16-byte aligned and padded
+    size_t i = tid;
+    for (; i + (U - 1) * (size_t)nt < nv; i += U * (size_t)nt) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = mm_ld_reduce<D, O>(mc + lo + ((i + u * (size_t)nt) << 4));
+#pragma unroll
+        for (int u = 0; u < U; ++u) mm_st(mc + lo + ((i + u * (size_t)nt) << 4), post16<D>(v[u], op, nranks, scale));
+    }
+    for (; i < nv; i += nt) {
+        char* p = mc + lo + (i << 4);
+        mm_st(p, post16<D>(mm_ld_reduce<D, O>(p), op, nranks, scale));
+    }
+}
+
+// G2 body (TWOSHOT): dst = reduce(srcs[0..n)) over `bytes`, srcs[p] for p != own read with ld.cg.
+template <int D, int O>
+__device__ __forceinline__ void grp_reduce(char* dst, const char* const* srcs, int n, int own, size_t bytes, int tid,
+                                           int nt, int nranks, float scale) {
+    using V = Vec<D>;
+    using Acc = typename Ty<D>::Acc;
+    using Bits = typename Ty<D>::Bits;
+    const char* sp[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) sp[p] = srcs[p < n ? p : 0];
+    uintptr_t mis = reinterpret_cast<uintptr_t>(dst);
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) mis |= reinterpret_cast<uintptr_t>(sp[p]);
+    const size_t nv = (mis & 15) ? 0 : (bytes >> 4);
+    const bool post = O == kAvg || scale != 1.0f;
+    for (size_t i = tid; i < nv; i += nt) {
+        const size_t off = i << 4;
+        uint4 w[kMaxRanks];
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+            if (p < n) w[p] = (p == own) ? *reinterpret_cast<const uint4*>(sp[p] + off) : ld_cg(sp[p] + off);
+        Acc acc[V::E], x[V::E];
+        V::unpack(w[0], acc);
+#pragma unroll
+        for (int p = 1; p < kMaxRanks; ++p) {
+            if (p < n) {
+                V::unpack(w[p], x);
+#pragma unroll
+                for (int e = 0; e < V::E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
+            }
+        }
+        if (post) {
+#pragma unroll
+            for (int e = 0; e < V::E; ++e) acc[e] = epilogue<Acc>(O, acc[e], nranks, scale);
+        }
+        st_cg(dst + off, V::pack(acc));
+    }
+    const size_t done = nv << 4;
+    for (size_t j = done + (size_t)tid * sizeof(Bits); j < bytes; j += (size_t)nt * sizeof(Bits)) {
+        Acc acc = Acc(0);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p) {
+            if (p < n) {
+                const Bits* e = reinterpret_cast<const Bits*>(sp[p] + j);
+                const Bits b = (p == own) ? *e : __ldcg(e);
+                acc = (p == 0) ? Ty<D>::load(b) : combine<Acc>(O, acc, Ty<D>::load(b));
+            }
+        }
+        *reinterpret_cast<Bits*>(dst + j) = Ty<D>::store(epilogue<Acc>(O, acc, nranks, scale));
+    }
+}
+
+// dst_p = reduce(srcs) for every output pointer (one local, the rest in peers' memory).
+template <int D, int O>
+__device__ __forceinline__ void grp_reduce_multi(char* const* outs, int no, const char* const* srcs, int n, int own,
+                                                 size_t bytes, int tid, int nt, int nranks, float scale) {
+    using V = Vec<D>;
+    using Acc = typename Ty<D>::Acc;
+    using Bits = typename Ty<D>::Bits;
+    const char* sp[kMaxRanks];
+    char* op[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) {
+        sp[p] = srcs[p < n ? p : 0];
+        op[p] = outs[p < no ? p : 0];
+    }
+    uintptr_t mis = 0;
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) mis |= reinterpret_cast<uintptr_t>(sp[p]) | reinterpret_cast<uintptr_t>(op[p]);
+    const size_t nv = (mis & 15) ? 0 : (bytes >> 4);
+    const bool post = O == kAvg || scale != 1.0f;
+    for (size_t i = tid; i < nv; i += nt) {
+        const size_t off = i << 4;
+        uint4 w[kMaxRanks];
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+            if (p < n) w[p] = (p == own) ? *reinterpret_cast<const uint4*>(sp[p] + off) : ld_cg(sp[p] + off);
+        Acc acc[V::E], x[V::E];
+        V::unpack(w[0], acc);
+#pragma unroll
+        for (int p = 1; p < kMaxRanks; ++p) {
+            if (p < n) {
+                V::unpack(w[p], x);
+#pragma unroll
+                for (int e = 0; e < V::E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
+            }
+        }
+        if (post) {
+#pragma unroll
+            for (int e = 0; e < V::E; ++e) acc[e] = epilogue<Acc>(O, acc[e], nranks, scale);
+        }
+        const uint4 res = V::pack(acc);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+            if (p < no) st_cg(op[p] + off, res);
+    }
+    const size_t done = nv << 4;
+    for (size_t j = done + (size_t)tid * sizeof(Bits); j < bytes; j += (size_t)nt * sizeof(Bits)) {
+        Acc acc = Acc(0);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p) {
+            if (p < n) {
+                const Bits* e = reinterpret_cast<const Bits*>(sp[p] + j);
+                const Bits b = (p == own) ? *e : __ldcg(e);
+                acc = (p == 0) ? Ty<D>::load(b) : combine<Acc>(O, acc, Ty<D>::load(b));
+            }
+        }
+        const Bits out = Ty<D>::store(epilogue<Acc>(O, acc, nranks, scale));
+        for (int p = 0; p < no; ++p) *reinterpret_cast<Bits*>(op[p] + j) = out;
+    }
+}
+
+// TWOSHOT data region (second half of the UC data region, disjoint from the push engine):
+//   inbox  [nslots][nranks][slot_bytes]   pieces pushed by the peers' stage CTAs
+//   gather [nslots][nranks][slot_bytes]   reduced shards pushed by the peers' reduce CTAs
+__device__ __forceinline__ char* ts_region(const DevComm& c, int owner) {
+    return c.uc[owner] + kCtrlBytes + (size_t)(c.data_bytes / 2);
+}
+
+template <int D, int O>
+__global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_constant__ PipeParams p) {
+    const DevComm& c = p.comm;
+    const int r = c.rank, n = c.nranks;
+    const int kind = p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const bool sysf = (p.debug & 1) == 0;
+    const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
+    const uint64_t round0 = kind == kPipeNvls ? load_state_u64(&c.state->nvls_round_seq)
+                                              : load_state_u64(&c.state->round_seq);
+    const int S = p.nslots;
+    const size_t sb = p.slot_bytes;
+    const char* src = static_cast<const char*>(p.src);
+    char* dst = static_cast<char*>(p.dst);
+    const int depth = (kind == kPipeOneShot) ? 1 : 2;
+    const int iters = p.nrounds + depth;
+    if (tid == 0) trace(c, 0, kTrBegin, 0);
+
+    // Geometry of round j for this CTA: shard size and this CTA's [s0, s1) inside a shard
+    // (ONESHOT: inside the whole chunk).
+    auto geom = [&](int j, size_t* cbeg, size_t* clen, size_t* shard, size_t* s0, size_t* s1) {
+        *cbeg = (size_t)j * p.chunk;
+        *clen = min((size_t)p.bytes - *cbeg, (size_t)p.chunk);
+        *shard = (kind == kPipeOneShot) ? *clen : round_up((*clen + n - 1) / n, 16);
+        const size_t piece = round_up((*shard + gridDim.x - 1) / gridDim.x, 16);
+        *s0 = min(*shard, (size_t)blockIdx.x * piece);
+        *s1 = min(*shard, *s0 + piece);
+    };
+    bool ok = true;
+    for (int t = 0; t < iters && ok; ++t) {
+        size_t cbeg, clen, shard, s0, s1;
+        // ---- A: round t
+        if (t < p.nrounds) {
+            const int j = t;
+            geom(j, &cbeg, &clen, &shard, &s0, &s1);
+            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+            if (kind == kPipeOneShot) {
+                if (s0 < s1) {
+                    char* outs[kMaxRanks];
+                    int no = 0;
+                    for (int q = 0; q < n; ++q)
+                        if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
+                    if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
+                }
+            } else if (kind == kPipeTwoShot) {
+                for (int q = 0; q < n; ++q) {
+                    if (q == r) continue;
+                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                    char* inb = ts_region(c, q) + ((size_t)slot * n + r) * sb;
+                    if (lo < hi) grp_copy(inb + s0, src + cbeg + lo, hi - lo, tid, nt, false);
+                }
+            } else {
+                char* slotp = c.nvls_uc + (size_t)slot * sb;
+                for (int q = 0; q < n; ++q) {
+                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                    if (lo < hi) grp_copy(slotp + lo, src + cbeg + lo, hi - lo, tid, nt, false);
+                }
+            }
+        }
+        // ---- B: round t-1
+        if (t >= 1 && t - 1 < p.nrounds) {
+            const int j = t - 1;
+            geom(j, &cbeg, &clen, &shard, &s0, &s1);
+            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+            if (kind == kPipeOneShot) {
+                if (s0 < s1) {
+                    const char* srcs[kMaxRanks];
+                    char* mine = ts_region(c, r);
+                    for (int q = 0; q < n; ++q)
+                        srcs[q] = (q == r) ? src + cbeg + s0 : mine + ((size_t)slot * n + q) * sb + s0;
+                    char* outs[1] = {dst + cbeg + s0};
+                    grp_reduce_multi<D, O>(outs, 1, srcs, n, r, s1 - s0, tid, nt, n, p.scale);
+                }
+            } else if (kind == kPipeTwoShot) {
+                const size_t lo = min(clen, r * shard + s0), hi = min(clen, r * shard + s1);
+                if (lo < hi) {
+                    const char* srcs[kMaxRanks];
+                    char* mine = ts_region(c, r);
+                    for (int q = 0; q < n; ++q)
+                        srcs[q] = (q == r) ? src + cbeg + lo : mine + ((size_t)slot * n + q) * sb + s0;
+                    char* outs[kMaxRanks];
+                    int no = 0;
+                    outs[no++] = dst + cbeg + lo;
+                    for (int q = 0; q < n; ++q)
+                        if (q != r) outs[no++] = ts_region(c, q) + (size_t)S * n * sb + ((size_t)slot * n + r) * sb + s0;
+                    grp_reduce_multi<D, O>(outs, no, srcs, n, r, hi - lo, tid, nt, n, p.scale);
+                }
+            } else {
+                if constexpr (NvlsOk<D, O>::value) {
+                    const size_t padded = round_up(clen, 16);
+                    const size_t lo = min(padded, r * shard + s0), hi = min(padded, r * shard + s1);
+                    if (lo < hi) {
+                        nvls_reduce_bcast<D, (O == kAvg ? kSum : O)>(c.nvls_mc + (size_t)slot * sb, lo, hi, tid, nt,
+                                                                     p.op, n, p.scale);
+                    }
+                }
+            }
+        }
+        // ---- C: round t-2
+        if (depth == 2 && t >= 2 && t - 2 < p.nrounds) {
+            const int j = t - 2;
+            geom(j, &cbeg, &clen, &shard, &s0, &s1);
+            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+            if (kind == kPipeTwoShot) {
+                const char* gather = ts_region(c, r) + (size_t)S * n * sb + (size_t)slot * n * sb;
+                for (int q = 0; q < n; ++q) {
+                    if (q == r) continue;
+                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                    if (lo < hi) grp_copy(dst + cbeg + lo, gather + (size_t)q * sb + s0, hi - lo, tid, nt, true);
+                }
+            } else {
+                const char* slotp = c.nvls_uc + (size_t)slot * sb;
+                for (int q = 0; q < n; ++q) {
+                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                    if (lo < hi) grp_copy(dst + cbeg + lo, slotp + lo, hi - lo, tid, nt, true);
+                }
+            }
+        }
+        // ---- barrier t (fence + signal every peer + wait for every peer)
+        __syncthreads();
+        if (tid < n && tid != r) {
+            if (sysf) fence_acq_rel_sys();
+            st_relaxed_sys_flag(barrier_flag(c.uc[tid], blockIdx.x, r), bar0 + (uint64_t)t + 1);
+            ok = wait_flag_geq(c, barrier_flag(c.uc[r], blockIdx.x, tid), bar0 + (uint64_t)t + 1, tid, t);
+        }
+        ok = __syncthreads_and(ok) != 0;
+        if (tid == 0) trace(c, 0, kTrBarrier, t);
+    }
+    if (tid == 0) trace(c, 0, kTrEnd, iters);
+    if (kind == kPipeNvls) finish_launch(c, 0, (uint64_t)iters, (uint64_t)p.nrounds);
+    else finish_launch(c, (uint64_t)p.nrounds, (uint64_t)iters, 0);
+}
+
+template <int D, int O>
+cudaError_t launch_t(const PipeParams& p, int nctas, cudaStream_t s) {
+    ar_sched_kernel<D, O><<<nctas, kThreads, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch_op(const PipeParams& p, int nctas, cudaStream_t s) {
+    switch (p.op) {
+    case kSum: return launch_t<D, kSum>(p, nctas, s);
+    case kAvg: return launch_t<D, kAvg>(p, nctas, s);  // AVG = SUM, then divide in the epilogue
+    case kMax: return launch_t<D, kMax>(p, nctas, s);
+    case kMin: return launch_t<D, kMin>(p, nctas, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+}  // namespace dev
+
+cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
+                                int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
+                                int nslots, int nctas, cudaStream_t stream, int debug) {
+    using namespace dev;
+    const bool nvls = kind == kPipeNvls;
+    if (nctas < 1 || nctas > kMaxCtas || nslots < 3 || chunk == 0 || (chunk % (16ull * c.nranks)) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    if (kind == kPipeOneShot && ((size_t)nslots * c.nranks * slot_bytes > c.data_bytes / 2 || slot_bytes < chunk)) {
+        return cudaErrorInvalidValue;
+    }
+    if (nvls && (c.nvls_mc == nullptr || !NvlsSupports(dtype, op) || (size_t)nslots * slot_bytes > c.nvls_bytes ||
+                 slot_bytes < chunk)) {
+        return cudaErrorInvalidValue;
+    }
+    if (kind == kPipeTwoShot && ((size_t)nslots * 2 * c.nranks * slot_bytes > c.data_bytes / 2 || slot_bytes * c.nranks < chunk)) {
+        return cudaErrorInvalidValue;
+    }
+    PipeParams p;
+    p.comm = c;
+    p.src = src;
+    p.dst = dst;
+    p.bytes = count * (unsigned long long)dtype_size(dtype);
+    p.chunk = chunk;
+    p.slot_bytes = slot_bytes;
+    p.nrounds = (int)((p.bytes + chunk - 1) / chunk);
+    if (p.nrounds == 0) p.nrounds = 1;
+    p.nslots = nslots;
+    p.dtype = dtype;
+    p.op = op;
+    p.scale = scale;
+    p.nvls = kind == kPipeNvls ? 1 : (kind == kPipeOneShot ? 2 : 0);
+    p.debug = debug;
+    // f32 MAX/MIN and f64 MAX/MIN have no multimem form; they only reach here for TWOSHOT.
+    switch (dtype) {
+    case kF32: return launch_op<kF32>(p, nctas, stream);
+    case kF64: return launch_op<kF64>(p, nctas, stream);
+    case kI32: return launch_op<kI32>(p, nctas, stream);
+    case kI64: return launch_op<kI64>(p, nctas, stream);
+    case kBF16: return launch_op<kBF16>(p, nctas, stream);
+    case kF16: return launch_op<kF16>(p, nctas, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace bccl

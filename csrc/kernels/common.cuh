@@ -47,6 +47,9 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
     return v;
 }
 
+// Acquire fence at system scope (turns a preceding relaxed read into an acquire pattern).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // Orders accesses made through different virtual aliases of the same memory (the
 // multicast and the unicast view of an NVLS buffer).
 __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
@@ -54,6 +57,23 @@ __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.
 __device__ __forceinline__ uint4 ld_cg(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ uint4 ld_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ void st_cg(void* p, const uint4& v) { __stcg(reinterpret_cast<uint4*>(p), v); }
+
+// ---------------------------------------------------------------- tracing
+
+// Appends one record when tracing is on (one thread per call site).
+__device__ __forceinline__ void trace(const DevComm& c, int group, int event, int round) {
+    if (c.trace == nullptr) return;
+    unsigned int i = atomicAdd(c.trace_count, 1u);
+    if (i >= c.trace_cap) return;
+    TraceRecord r;
+    r.t_ns = globaltimer();
+    r.cta = blockIdx.x;
+    r.group = (unsigned short)group;
+    r.event = (unsigned short)event;
+    r.round = (unsigned int)round;
+    r.kernel = c.kernel_serial;
+    c.trace[i] = r;
+}
 
 // ---------------------------------------------------------------- flags, waits, barriers
 
@@ -75,14 +95,24 @@ __device__ __forceinline__ void record_error(const DevComm& c, int code, int pee
 }
 
 // Spin until *flag >= target. Returns false (and records the error) on timeout or abort.
+// Polling uses relaxed loads with a short sleep between them (an acquire load per poll
+// invalidates the SM's L1 and stalls its memory pipeline, which slows every other warp of
+// the CTA); a single acquire fence follows the successful read.
 __device__ __forceinline__ bool wait_flag_geq(const DevComm& c, const uint64_t* flag, uint64_t target, int peer,
                                               int phase) {
-    if (ld_acquire_sys(flag) >= target) return true;
+    if (ld_relaxed_sys(flag) >= target) {
+        fence_acq_rel_sys();
+        return true;
+    }
     const uint64_t t0 = globaltimer();
     uint32_t iter = 0;
     for (;;) {
-        if (ld_acquire_sys(flag) >= target) return true;
-        if ((++iter & 255u) == 0) {
+        __nanosleep(iter < 64 ? 32 : 256);
+        if (ld_relaxed_sys(flag) >= target) {
+            fence_acq_rel_sys();
+            return true;
+        }
+        if ((++iter & 63u) == 0) {
             const uint64_t waited = globaltimer() - t0;
             if (*c.abort != 0) {
                 record_error(c, kDevAborted, peer, phase, target, waited);
@@ -92,7 +122,6 @@ __device__ __forceinline__ bool wait_flag_geq(const DevComm& c, const uint64_t* 
                 record_error(c, kDevTimeout, peer, phase, target, waited);
                 return false;
             }
-            if (iter > 4096u) __nanosleep(64);
         }
     }
 }
@@ -106,7 +135,6 @@ __device__ __forceinline__ bool cta_barrier(const DevComm& c, uint64_t seq, int 
     const int t = threadIdx.x;
     bool ok = true;
     if (t < c.nranks && t != c.rank) {
-        __threadfence_system();
         st_release_sys(barrier_flag(c.uc[t], blockIdx.x, c.rank), seq);
         ok = wait_flag_geq(c, barrier_flag(c.uc[c.rank], blockIdx.x, t), seq, t, phase);
     }

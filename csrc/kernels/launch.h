@@ -14,16 +14,30 @@ constexpr int kPushMaxItems = 256;  // WorkItems carried in one push-engine laun
 cudaError_t LaunchPushEngine(const DevComm& c, const WorkItem* items, int nitems, unsigned long long stream_bytes,
                              unsigned long long slot_bytes, int nctas, cudaStream_t stream);
 
-// AllReduce by reduce-scatter (push) + all-gather (pull) through the UC data region.
-cudaError_t LaunchTwoShot(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype, int op,
-                          float scale, unsigned long long shard_cap, int nctas, cudaStream_t stream);
+// Pipelined AllReduce (kernels/ar_pipe.cu): NVSwitch multicast, two-shot (push reduce-scatter
+// + push all-gather) or one-shot (push everything, reduce locally) through the second half of
+// the UC data region.
+enum PipeKind : int { kPipeTwoShot = 0, kPipeNvls = 1, kPipeOneShot = 2 };
+cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
+                                int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
+                                int nslots, int nctas, cudaStream_t stream, int debug = 0);
 
-// NVSwitch multicast collectives: func is AllReduce, Broadcast or Reduce.
+// NVSwitch multicast Broadcast (func 1) and Reduce (func 2) over the NVLS slot ring.
 cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, unsigned long long count, int dtype,
-                       int op, int root, float scale, unsigned long long chunk_cap, int nctas, bool zero_copy,
-                       cudaStream_t stream);
+                       int op, int root, float scale, unsigned long long chunk, unsigned long long slot_bytes,
+                       int nslots, int nctas, cudaStream_t stream);
+
 // Bounded-wait self-test: waits on a flag nothing sets; must time out and report.
 cudaError_t LaunchWaitProbe(const DevComm& c, unsigned long long timeout_ns, cudaStream_t stream);
+
+// Copy-bandwidth probe over local, peer or multicast addresses.
+cudaError_t LaunchBandwidthProbe(void* dst, const void* src, unsigned long long bytes, bool multicast, int nctas,
+                                 cudaStream_t stream);
+
+// Fence-cost probe: copy in `seg`-byte segments per CTA with a fence after each (mode 0 none,
+// 1 fence.acq_rel.sys, 2 fence.acq_rel.gpu).
+cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long bytes, unsigned long long seg, int mode,
+                             int nctas, cudaStream_t stream);
 
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.
 bool NvlsSupports(int dtype, int op);

@@ -51,14 +51,15 @@ __device__ __forceinline__ void cta_push_multi(char* const* dsts, int n, const c
         if (p < n) mis |= reinterpret_cast<uintptr_t>(dsts[p]);
     const size_t nv = ((mis & 15) == 0) ? (bytes >> 4) : 0;
     size_t i = t;
-    for (; i + nt < nv; i += 2 * nt) {
-        uint4 v0 = *reinterpret_cast<const uint4*>(src + (i << 4));
-        uint4 v1 = *reinterpret_cast<const uint4*>(src + ((i + nt) << 4));
+    for (; i + 3 * nt < nv; i += 4 * nt) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(src + ((i + u * nt) << 4));
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p) {
             if (p < n) {
-                st_cg(dsts[p] + (i << 4), v0);
-                st_cg(dsts[p] + ((i + nt) << 4), v1);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) st_cg(dsts[p] + ((i + u * nt) << 4), v[u]);
             }
         }
     }
@@ -177,6 +178,7 @@ __global__ void __launch_bounds__(512, 1) push_engine_kernel(const __grid_consta
     const uint64_t round0 = load_state_u64(&c.state->round_seq);
     const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
     const size_t slot = p.slot_bytes;
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, 0);
     bool ok = true;
     int first = 0;  // first item that can still overlap this CTA's pieces (items are sorted)
     for (int j = 0; j < p.nrounds && ok; ++j) {
@@ -196,6 +198,7 @@ __global__ void __launch_bounds__(512, 1) push_engine_kernel(const __grid_consta
         }
         ok = cta_barrier(c, bar0 + (uint64_t)j + 1, j);
         if (!ok) break;
+        if (threadIdx.x == 0) trace(c, 0, kTrBarrier, j);
         for (int i = first; i < p.nitems && a < b; ++i) {
             const WorkItem& it = p.items[i];
             const size_t s0 = it.stream_off, s1 = s0 + payload_bytes(it);
@@ -204,6 +207,7 @@ __global__ void __launch_bounds__(512, 1) push_engine_kernel(const __grid_consta
             if (lo < hi) consume(c, it, lo - s0, hi - s0, lo - rbeg, half, slot);
         }
     }
+    if (threadIdx.x == 0) trace(c, 0, kTrEnd, p.nrounds);
     finish_launch(c, (uint64_t)p.nrounds, (uint64_t)p.nrounds, 0);
 }
 

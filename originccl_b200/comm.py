@@ -341,6 +341,10 @@ class Communicator:
     def synchronize(self) -> None:
         self._check(self._lib.bcclSynchronize(self._h))
 
+    def dump_trace(self, path: str) -> int:
+        """Writes the device trace (BCCL_TRACE=<records> at init) as Chrome-trace JSON."""
+        return int(self._lib.bcclTraceDump(self._h, path.encode()))
+
     def barrier(self) -> None:
         """Host-side barrier over the bootstrap (no device work)."""
         self._check(self._lib.bcclBarrier(self._h))

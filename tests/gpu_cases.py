@@ -178,3 +178,55 @@ def run_timeout_probe(rank: int, world: int) -> Dict:
     comm.barrier()  # host-side: rank 1 leaves only after rank 0 has finished waiting
     comm.destroy()
     return result
+
+
+def run_mixed_sequence(rank: int, world: int, steps: int = 60) -> Dict:
+    """Random interleaving of every kernel kind and size (same sequence on every rank): checks
+    that consecutive launches of different algorithms never corrupt each other's staging."""
+    import random
+
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import Algo, ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, timeout_ms=20000)  # async: enqueue back to back
+    rng = random.Random(99)
+    pending = []
+    algos = [Algo.AUTO, Algo.ONESHOT, Algo.TWOSHOT, Algo.NVLS]
+    for i in range(steps):
+        n = rng.choice([3, 1000, 65536 + 7, 1 << 20, (5 << 20) + 11])
+        kind = rng.choice(["ar", "ar", "ag", "rs", "bc", "red"])
+        inputs = [rank_input(r, n, "float32", seed=i) for r in range(world)]
+        x = inputs[rank].cuda()
+        if kind == "ar":
+            y = torch.empty_like(x)
+            comm.all_reduce(x, out=y, algo=rng.choice(algos))
+            pending.append((y, oracle("sum", inputs, world).float(), f"ar step {i}"))
+        elif kind == "ag":
+            y = torch.empty(n * world, device="cuda")
+            comm.all_gather(y, x)
+            pending.append((y, torch.cat(inputs).float(), f"ag step {i}"))
+        elif kind == "rs":
+            big = [rank_input(r, n * world, "float32", seed=i) for r in range(world)]
+            y = torch.empty(n, device="cuda")
+            comm.reduce_scatter(y, big[rank].cuda())
+            pending.append((y, oracle("sum", big, world)[rank * n:(rank + 1) * n].float(), f"rs step {i}"))
+        elif kind == "bc":
+            root = i % world
+            y = x.clone()
+            comm.broadcast(y, root, algo=rng.choice([Algo.AUTO, Algo.NVLS, Algo.ONESHOT]))
+            pending.append((y, inputs[root].float(), f"bc step {i}"))
+        else:
+            root = (i + 1) % world
+            y = torch.empty_like(x) if rank == root else None
+            comm.reduce(x, root, ReduceOp.SUM, out=y, algo=rng.choice([Algo.AUTO, Algo.NVLS, Algo.ONESHOT]))
+            if rank == root:
+                pending.append((y, oracle("sum", inputs, world).float(), f"reduce step {i}"))
+    comm.synchronize()
+    for got, exp, what in pending:
+        _close(got, exp, "float32", what)
+    comm.destroy()
+    return {"checked": len(pending)}

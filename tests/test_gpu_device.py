@@ -85,3 +85,12 @@ def test_bounded_wait_self_test_single_gpu():
     comm.all_reduce(x, scale=3.0)
     assert torch.all(x == 3.0).item()
     comm.destroy()
+
+
+@pytest.mark.multigpu
+def test_mixed_algorithm_sequence():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 2:
+        pytest.skip("needs 2+ GPUs")
+    res = _mp.run(min(n, 8), gpu_cases.run_mixed_sequence, timeout=900)
+    assert res[0]["checked"] > 0
