@@ -11,7 +11,9 @@
 //   NVLS:    A = copy round t's piece into the local NVLS slot
 //            B = multimem.ld_reduce + multimem.st of the own shard of round t-1
 //            C = copy round t-2 out of the local NVLS slot
-// then fence + signal + wait (barrier t). B(t-1) only needs A(t-1) from every rank and C(t-2)
+// then fence + signal + wait (barrier t). The phase that crosses NVLink runs on one warp
+// group while the local phases run on the other, so copies overlap link traffic; both
+// groups finish before the single fence of the iteration. B(t-1) only needs A(t-1) from every rank and C(t-2)
 // only needs B(t-2) from every rank, both proven by barrier t-1. NVLink writes are issued
 // first in an iteration, so by the time the CTA fences (after its local work) they have
 // mostly drained: a system-scope fence costs little when it is not waiting on fresh
@@ -340,8 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
     const int kind = p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
-    const int tid = threadIdx.x, nt = blockDim.x;
     const bool sysf = (p.debug & 1) == 0;
+    // Warp groups run their phases concurrently for NVLS (two local copies against one switch
+    // phase); for the push kinds a single group measured faster (BCCL_PIPE_DEBUG bit 2 flips it).
+    const bool split = (kind == kPipeNvls) != ((p.debug & 4) != 0);
     const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
     const uint64_t round0 = kind == kPipeNvls ? load_state_u64(&c.state->nvls_round_seq)
                                               : load_state_u64(&c.state->round_seq);
@@ -351,10 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     char* dst = static_cast<char*>(p.dst);
     const int depth = (kind == kPipeOneShot) ? 1 : 2;
     const int iters = p.nrounds + depth;
-    if (tid == 0) trace(c, 0, kTrBegin, 0);
+    // Two warp groups: "net" (warps 0-7) runs the phase that crosses NVLink, "local" (warps
+    // 8-15) the phases that stay in this GPU's memory; without the split both do everything.
+    const int half = blockDim.x / 2;
+    const bool is_net = threadIdx.x < half;
+    const int gtid = split ? (is_net ? threadIdx.x : threadIdx.x - half) : threadIdx.x;
+    const int gnt = split ? half : blockDim.x;
+    const bool do_net = !split || is_net, do_local = !split || !is_net;
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, 0);
 
-    // Geometry of round j for this CTA: shard size and this CTA's [s0, s1) inside a shard
-    // (ONESHOT: inside the whole chunk).
     auto geom = [&](int j, size_t* cbeg, size_t* clen, size_t* shard, size_t* s0, size_t* s1) {
         *cbeg = (size_t)j * p.chunk;
         *clen = min((size_t)p.bytes - *cbeg, (size_t)p.chunk);
@@ -363,98 +372,109 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         *s0 = min(*shard, (size_t)blockIdx.x * piece);
         *s1 = min(*shard, *s0 + piece);
     };
+    // ---- phase bodies (tid/nt are group-relative)
+    auto phase_a = [&](int j, int tid, int nt) {  // stage round j
+        size_t cbeg, clen, shard, s0, s1;
+        geom(j, &cbeg, &clen, &shard, &s0, &s1);
+        const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+        if (kind == kPipeOneShot) {
+            if (s0 < s1) {
+                char* outs[kMaxRanks];
+                int no = 0;
+                for (int q = 0; q < n; ++q)
+                    if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
+                if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
+            }
+        } else if (kind == kPipeTwoShot) {
+            for (int q = 0; q < n; ++q) {
+                if (q == r) continue;
+                const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                char* inb = ts_region(c, q) + ((size_t)slot * n + r) * sb;
+                if (lo < hi) grp_copy(inb + s0, src + cbeg + lo, hi - lo, tid, nt, false);
+            }
+        } else {
+            char* slotp = c.nvls_uc + (size_t)slot * sb;
+            for (int q = 0; q < n; ++q) {
+                const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                if (lo < hi) grp_copy(slotp + lo, src + cbeg + lo, hi - lo, tid, nt, false);
+            }
+        }
+    };
+    auto phase_b = [&](int j, int tid, int nt) {  // reduce round j
+        size_t cbeg, clen, shard, s0, s1;
+        geom(j, &cbeg, &clen, &shard, &s0, &s1);
+        const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+        if (kind == kPipeOneShot) {
+            if (s0 < s1) {
+                const char* srcs[kMaxRanks];
+                char* mine = ts_region(c, r);
+                for (int q = 0; q < n; ++q)
+                    srcs[q] = (q == r) ? src + cbeg + s0 : mine + ((size_t)slot * n + q) * sb + s0;
+                char* outs[1] = {dst + cbeg + s0};
+                grp_reduce_multi<D, O>(outs, 1, srcs, n, r, s1 - s0, tid, nt, n, p.scale);
+            }
+        } else if (kind == kPipeTwoShot) {
+            const size_t lo = min(clen, r * shard + s0), hi = min(clen, r * shard + s1);
+            if (lo < hi) {
+                const char* srcs[kMaxRanks];
+                char* mine = ts_region(c, r);
+                for (int q = 0; q < n; ++q)
+                    srcs[q] = (q == r) ? src + cbeg + lo : mine + ((size_t)slot * n + q) * sb + s0;
+                char* outs[kMaxRanks];
+                int no = 0;
+                outs[no++] = dst + cbeg + lo;
+                for (int q = 0; q < n; ++q)
+                    if (q != r) outs[no++] = ts_region(c, q) + (size_t)S * n * sb + ((size_t)slot * n + r) * sb + s0;
+                grp_reduce_multi<D, O>(outs, no, srcs, n, r, hi - lo, tid, nt, n, p.scale);
+            }
+        } else {
+            if constexpr (NvlsOk<D, O>::value) {
+                const size_t padded = round_up(clen, 16);
+                const size_t lo = min(padded, r * shard + s0), hi = min(padded, r * shard + s1);
+                if (lo < hi) {
+                    nvls_reduce_bcast<D, (O == kAvg ? kSum : O)>(c.nvls_mc + (size_t)slot * sb, lo, hi, tid, nt, p.op,
+                                                                 n, p.scale);
+                }
+            }
+        }
+    };
+    auto phase_c = [&](int j, int tid, int nt) {  // finish round j
+        size_t cbeg, clen, shard, s0, s1;
+        geom(j, &cbeg, &clen, &shard, &s0, &s1);
+        const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
+        if (kind == kPipeTwoShot) {
+            const char* gather = ts_region(c, r) + (size_t)S * n * sb + (size_t)slot * n * sb;
+            for (int q = 0; q < n; ++q) {
+                if (q == r) continue;
+                const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                if (lo < hi) grp_copy(dst + cbeg + lo, gather + (size_t)q * sb + s0, hi - lo, tid, nt, true);
+            }
+        } else {
+            const char* slotp = c.nvls_uc + (size_t)slot * sb;
+            for (int q = 0; q < n; ++q) {
+                const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
+                if (lo < hi) grp_copy(dst + cbeg + lo, slotp + lo, hi - lo, tid, nt, true);
+            }
+        }
+    };
     bool ok = true;
     for (int t = 0; t < iters && ok; ++t) {
-        size_t cbeg, clen, shard, s0, s1;
-        // ---- A: round t
-        if (t < p.nrounds) {
-            const int j = t;
-            geom(j, &cbeg, &clen, &shard, &s0, &s1);
-            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
-            if (kind == kPipeOneShot) {
-                if (s0 < s1) {
-                    char* outs[kMaxRanks];
-                    int no = 0;
-                    for (int q = 0; q < n; ++q)
-                        if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
-                    if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
-                }
-            } else if (kind == kPipeTwoShot) {
-                for (int q = 0; q < n; ++q) {
-                    if (q == r) continue;
-                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
-                    char* inb = ts_region(c, q) + ((size_t)slot * n + r) * sb;
-                    if (lo < hi) grp_copy(inb + s0, src + cbeg + lo, hi - lo, tid, nt, false);
-                }
-            } else {
-                char* slotp = c.nvls_uc + (size_t)slot * sb;
-                for (int q = 0; q < n; ++q) {
-                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
-                    if (lo < hi) grp_copy(slotp + lo, src + cbeg + lo, hi - lo, tid, nt, false);
-                }
-            }
+        const bool has_a = t < p.nrounds, has_b = t >= 1 && t - 1 < p.nrounds;
+        const bool has_c = depth == 2 && t >= 2 && t - 2 < p.nrounds;
+        // Which group runs what: NVLS crosses NVLink in B (multimem); two-shot and one-shot
+        // cross it in A (pushes). The other phases run on the local group.
+        if (kind == kPipeNvls) {
+            if (do_net && has_b) phase_b(t - 1, gtid, gnt);
+            if (do_local && has_a) phase_a(t, gtid, gnt);
+            if (do_local && has_c) phase_c(t - 2, gtid, gnt);
+        } else {
+            if (do_net && has_a) phase_a(t, gtid, gnt);
+            if (do_local && has_b) phase_b(t - 1, gtid, gnt);
+            if (do_local && has_c) phase_c(t - 2, gtid, gnt);
         }
-        // ---- B: round t-1
-        if (t >= 1 && t - 1 < p.nrounds) {
-            const int j = t - 1;
-            geom(j, &cbeg, &clen, &shard, &s0, &s1);
-            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
-            if (kind == kPipeOneShot) {
-                if (s0 < s1) {
-                    const char* srcs[kMaxRanks];
-                    char* mine = ts_region(c, r);
-                    for (int q = 0; q < n; ++q)
-                        srcs[q] = (q == r) ? src + cbeg + s0 : mine + ((size_t)slot * n + q) * sb + s0;
-                    char* outs[1] = {dst + cbeg + s0};
-                    grp_reduce_multi<D, O>(outs, 1, srcs, n, r, s1 - s0, tid, nt, n, p.scale);
-                }
-            } else if (kind == kPipeTwoShot) {
-                const size_t lo = min(clen, r * shard + s0), hi = min(clen, r * shard + s1);
-                if (lo < hi) {
-                    const char* srcs[kMaxRanks];
-                    char* mine = ts_region(c, r);
-                    for (int q = 0; q < n; ++q)
-                        srcs[q] = (q == r) ? src + cbeg + lo : mine + ((size_t)slot * n + q) * sb + s0;
-                    char* outs[kMaxRanks];
-                    int no = 0;
-                    outs[no++] = dst + cbeg + lo;
-                    for (int q = 0; q < n; ++q)
-                        if (q != r) outs[no++] = ts_region(c, q) + (size_t)S * n * sb + ((size_t)slot * n + r) * sb + s0;
-                    grp_reduce_multi<D, O>(outs, no, srcs, n, r, hi - lo, tid, nt, n, p.scale);
-                }
-            } else {
-                if constexpr (NvlsOk<D, O>::value) {
-                    const size_t padded = round_up(clen, 16);
-                    const size_t lo = min(padded, r * shard + s0), hi = min(padded, r * shard + s1);
-                    if (lo < hi) {
-                        nvls_reduce_bcast<D, (O == kAvg ? kSum : O)>(c.nvls_mc + (size_t)slot * sb, lo, hi, tid, nt,
-                                                                     p.op, n, p.scale);
-                    }
-                }
-            }
-        }
-        // ---- C: round t-2
-        if (depth == 2 && t >= 2 && t - 2 < p.nrounds) {
-            const int j = t - 2;
-            geom(j, &cbeg, &clen, &shard, &s0, &s1);
-            const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
-            if (kind == kPipeTwoShot) {
-                const char* gather = ts_region(c, r) + (size_t)S * n * sb + (size_t)slot * n * sb;
-                for (int q = 0; q < n; ++q) {
-                    if (q == r) continue;
-                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
-                    if (lo < hi) grp_copy(dst + cbeg + lo, gather + (size_t)q * sb + s0, hi - lo, tid, nt, true);
-                }
-            } else {
-                const char* slotp = c.nvls_uc + (size_t)slot * sb;
-                for (int q = 0; q < n; ++q) {
-                    const size_t lo = min(clen, q * shard + s0), hi = min(clen, q * shard + s1);
-                    if (lo < hi) grp_copy(dst + cbeg + lo, slotp + lo, hi - lo, tid, nt, true);
-                }
-            }
-        }
-        // ---- barrier t (fence + signal every peer + wait for every peer)
+        // ---- barrier t: both groups' writes are issued; fence + signal + wait.
         __syncthreads();
+        const int tid = threadIdx.x;
         if (tid < n && tid != r) {
             if (sysf) fence_acq_rel_sys();
             st_relaxed_sys_flag(barrier_flag(c.uc[tid], blockIdx.x, r), bar0 + (uint64_t)t + 1);
@@ -463,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         ok = __syncthreads_and(ok) != 0;
         if (tid == 0) trace(c, 0, kTrBarrier, t);
     }
-    if (tid == 0) trace(c, 0, kTrEnd, iters);
+    if (threadIdx.x == 0) trace(c, 0, kTrEnd, iters);
     if (kind == kPipeNvls) finish_launch(c, 0, (uint64_t)iters, (uint64_t)p.nrounds);
     else finish_launch(c, (uint64_t)p.nrounds, (uint64_t)iters, 0);
 }
