@@ -13,6 +13,7 @@
 //   BCCL_FAULT=bootstrap_delay:1:500       rank 1 joins 500 ms late
 //   BCCL_FAULT=bootstrap_corrupt:3         rank 3 sends a malformed hello
 //   BCCL_FAULT=handle_drop:1               rank 1 never sends its memory handle fds
+//   BCCL_FAULT=segment_drop:0              local leader 0 never shares the host segment
 #pragma once
 
 #include <cstdint>

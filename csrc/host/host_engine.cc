@@ -93,7 +93,7 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     if (view_.local_rank == 0) {
         seg_fd = static_cast<int>(memfd_create("bccl-host", MFD_CLOEXEC));
         ok = seg_fd >= 0 && ftruncate(seg_fd, static_cast<off_t>(seg_bytes_)) == 0;
-        if (ok) {
+        if (ok && !FaultActive("segment_drop", rank_)) {
             for (int i = 1; ok && i < L; ++i) ok = fp->SendFd(view_.local_ranks[i], kSegFdTag, seg_fd, timeout_ms_);
         }
         if (!ok) LOG_ERROR("rank %d: creating the shared segment failed", rank_);

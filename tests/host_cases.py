@@ -1,0 +1,226 @@
+"""Host-memory (CPU) collective cases, run inside each rank process.
+
+Modeled on the reference's black-box suite (OriginCCL tests/test_common.cpp:28-399): values are
+multiples of 1/8 so float and integer results compare exactly regardless of reduction order,
+every output carries a sentinel element after its end, out-of-place inputs must come back
+unchanged, and contract cases (count 0, missing buffer, bad root) are checked on every rank.
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import numpy as np
+
+NP_DTYPES = {"float32": np.float32, "float64": np.float64, "int32": np.int32, "int64": np.int64,
+             "float16": np.float16}
+SENTINEL = 77
+
+
+def value(rank: int, n: int, dtype: str, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed * 131 + rank)
+    v = rng.integers(-64, 64, size=n)
+    if dtype.startswith("int"):
+        return v.astype(NP_DTYPES[dtype])
+    return (v / 8.0).astype(NP_DTYPES[dtype])
+
+
+def reduce_ref(op: str, arrays: List[np.ndarray], world: int) -> np.ndarray:
+    st = np.stack([a.astype(np.float64) for a in arrays])
+    if op == "sum":
+        r = st.sum(0)
+    elif op == "max":
+        r = st.max(0)
+    elif op == "min":
+        r = st.min(0)
+    else:
+        r = st.sum(0)
+        if np.issubdtype(arrays[0].dtype, np.integer):
+            r = np.trunc(r / world)
+        else:
+            r = r / world
+    return r.astype(arrays[0].dtype)
+
+
+OPS = {"sum": 0, "max": 1, "min": 2, "avg": 3}
+
+
+def _out(n: int, dtype: str) -> np.ndarray:
+    return np.full(n + 1, SENTINEL, dtype=NP_DTYPES[dtype])
+
+
+def _check(got: np.ndarray, exp: np.ndarray, n: int, what: str) -> None:
+    assert got[n] == SENTINEL, f"{what}: wrote past the end"
+    assert np.array_equal(got[:n], exp), f"{what}: mismatch (first bad {np.nonzero(got[:n] != exp)[0][:5]})"
+
+
+def run_matrix(rank: int, world: int, counts: List[int], dtypes: List[str], n_channels: int = 2,
+               logical_machine_size: int = 0) -> Dict:
+    from originccl_b200 import ReduceOp, init_from_env
+    comm = init_from_env(n_channels=n_channels, logical_machine_size=logical_machine_size, timeout_ms=30000)
+    done = 0
+    for n in counts:
+        for dtype in dtypes:
+            ins = [value(r, n, dtype, n) for r in range(world)]
+            x = ins[rank].copy()
+            for op in OPS:
+                if dtype == "float16" and op == "avg":
+                    continue
+                y = _out(n, dtype)
+                comm.all_reduce(x, ReduceOp(OPS[op]), out=y[:n])
+                _check(y, reduce_ref(op, ins, world), n, f"allreduce {dtype} {op} n={n}")
+                assert np.array_equal(x, ins[rank]), "allreduce changed its input"
+                done += 1
+            # in place
+            xi = ins[rank].copy()
+            comm.all_reduce(xi)
+            assert np.array_equal(xi, reduce_ref("sum", ins, world)), f"in-place allreduce {dtype} n={n}"
+            # reduce to every root with MAX
+            for root in range(world):
+                y = _out(n, dtype) if rank == root else None
+                comm.reduce(x, root, ReduceOp.MAX, out=None if y is None else y[:n])
+                if rank == root:
+                    _check(y, reduce_ref("max", ins, world), n, f"reduce {dtype} root={root} n={n}")
+            # broadcast from every root
+            for root in range(world):
+                b = ins[rank].copy()
+                comm.broadcast(b, root)
+                assert np.array_equal(b, ins[root]), f"broadcast {dtype} root={root} n={n}"
+            # allgather (rank order) and reducescatter (N*count input)
+            g = _out(n * world, dtype)
+            comm.all_gather(g[:n * world], x)
+            _check(g, np.concatenate(ins), n * world, f"allgather {dtype} n={n}")
+            rs_in = [value(r, n * world, dtype, n + 7) for r in range(world)]
+            rs = _out(n, dtype)
+            comm.reduce_scatter(rs[:n], rs_in[rank].copy())
+            _check(rs, reduce_ref("sum", rs_in, world)[rank * n:(rank + 1) * n], n, f"reducescatter {dtype} n={n}")
+            done += 4
+    info = {"ran": done, "machine_count": comm.machine_count, "local_ranks": comm.local_ranks,
+            "leaders": comm.machine_leaders, "local_rank": comm.local_rank, "local_size": comm.local_size,
+            "single": comm.is_single_machine, "machine_index": comm.machine_index}
+    comm.destroy()
+    return info
+
+
+def run_contract(rank: int, world: int) -> Dict:
+    """count 0 with null buffers succeeds; missing buffers, bad roots, bad peers, self peers and
+    bad dtypes/ops fail on every rank before anything is queued, also inside a group."""
+    import ctypes
+
+    from originccl_b200 import BcclError, ReduceOp, init_from_env
+    from originccl_b200 import _native
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    lib = _native.lib()
+    h = comm._h
+    null = None
+    rej = 0
+    # zero count, null buffers: success
+    assert lib.bcclAllReduce(h, null, null, 0, 0, 0, 1.0, 0, 0, 0) == 0
+    assert lib.bcclAllGather(h, null, null, 0, 0, 0, 0) == 0
+    assert lib.bcclSend(h, null, 0, 0, (rank + 1) % world, 0, 0) == 0
+    buf = np.zeros(8, np.float32)
+    p = buf.ctypes.data
+    bad = [
+        lambda: lib.bcclAllReduce(h, null, p, 8, 0, 0, 1.0, 0, 0, 0),      # missing send buffer
+        lambda: lib.bcclAllReduce(h, p, null, 8, 0, 0, 1.0, 0, 0, 0),      # missing recv buffer
+        lambda: lib.bcclAllReduce(h, p, p, 8, 9, 0, 1.0, 0, 0, 0),         # bad dtype
+        lambda: lib.bcclAllReduce(h, p, p, 8, 0, 9, 1.0, 0, 0, 0),         # bad op
+        lambda: lib.bcclBroadcast(h, p, p, 8, 0, world, 0, 0, 0),          # bad root
+        lambda: lib.bcclReduce(h, p, p, 8, 0, 0, -1, 0, 0, 0),             # bad root
+        lambda: lib.bcclSend(h, p, 8, 0, rank, 0, 0),                      # self peer
+        lambda: lib.bcclRecv(h, p, 8, 0, world, 0, 0),                     # out-of-range peer
+        lambda: lib.bcclAllGather(h, p, p, (1 << 62), 0, 0, 0),            # size overflow
+    ]
+    for f in bad:
+        assert f() != 0
+        rej += 1
+    # rejections inside a group are not queued: the group then runs only the valid op
+    comm.group_start()
+    assert bad[0]() != 0
+    y = np.zeros(8, np.float32)
+    x = np.full(8, rank + 1, np.float32)
+    comm.all_reduce(x, out=y)
+    comm.group_end()
+    assert np.all(y == world * (world + 1) / 2)
+    # Reduce: a non-root may pass a null recv buffer
+    assert lib.bcclReduce(h, p, null if rank != 0 else p, 8, 0, 0, 0, 0, 0, 0) == 0
+    comm.destroy()
+    return {"rejected": rej}
+
+
+def run_groups(rank: int, world: int) -> Dict:
+    """Nested groups: the inner GroupEnd runs nothing; the outermost runs the whole batch."""
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    xs = [np.full(1000 + i, rank + i, np.float64) for i in range(6)]
+    ys = [np.zeros_like(x) for x in xs]
+    comm.group_start()
+    comm.all_reduce(xs[0], out=ys[0])
+    comm.group_start()
+    comm.all_reduce(xs[1], out=ys[1])
+    comm.group_end()                     # inner: nothing runs yet
+    inner_untouched = bool(np.all(ys[1] == 0))
+    for i in range(2, 6):
+        comm.all_reduce(xs[i], out=ys[i])
+    comm.group_end()                     # outermost: everything runs
+    for i in range(6):
+        assert np.all(ys[i] == sum(r + i for r in range(world))), f"group item {i}"
+    comm.destroy()
+    return {"inner_untouched": inner_untouched}
+
+
+def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str = "") -> Dict:
+    """Ring exchange in a group, FIFO for a repeated peer, a mixed 10-op group, typed messages
+    around the ring-buffer capacity, and the transport each pair uses."""
+    import os
+    if executor:
+        os.environ["BCCL_HOST_EXECUTOR"] = executor
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=2, logical_machine_size=logical_machine_size, timeout_ms=30000)
+    nxt, prv = (rank + 1) % world, (rank - 1) % world
+    for n in [1, 63, 64, 65, (64 << 10) - 1, (1 << 20) + 1, 5 << 20]:
+        s = (np.arange(n, dtype=np.int64) % 251 + rank).astype(np.uint8).view(np.uint8)
+        s = s.astype(np.float32)
+        r = np.zeros(n, np.float32)
+        with comm.group():
+            comm.send(s, nxt)
+            comm.recv(r, prv)
+        assert np.array_equal(r, (np.arange(n, dtype=np.int64) % 251 + prv).astype(np.uint8).astype(np.float32)), n
+    # FIFO: three messages to the same peer arrive in order
+    outs = [np.zeros(5000, np.int32) for _ in range(3)]
+    ins = [np.full(5000, 10 * rank + k, np.int32) for k in range(3)]  # buffers live until group_end
+    with comm.group():
+        for k in range(3):
+            comm.send(ins[k], nxt)
+        for k in range(3):
+            comm.recv(outs[k], prv)
+    for k in range(3):
+        assert np.all(outs[k] == 10 * prv + k), "FIFO order"
+    # mixed group: collectives and P2P together (10 ops)
+    a = np.full(777, rank, np.float64)
+    b = np.zeros(777, np.float64)
+    mesh_out = [np.zeros(64, np.int64) for _ in range(world)]
+    mesh_in = [np.full(64, 100 * rank + q, np.int64) for q in range(world)]
+    with comm.group():
+        comm.all_reduce(a, out=b)
+        for q in range(world):
+            if q == rank:
+                continue
+            comm.send(mesh_in[q], q)
+            comm.recv(mesh_out[q], q)
+    assert np.all(b == sum(range(world)))
+    for q in range(world):
+        if q != rank:
+            assert np.all(mesh_out[q] == 100 * q + rank), "mesh exchange"
+    kinds = {q: comm.p2p_transport(q) for q in range(world) if q != rank}
+    ex = comm.host_executor
+    comm.destroy()
+    return {"transports": kinds, "executor": ex}
+
+
+def run_init_only(rank: int, world: int) -> Dict:
+    """Init and report (used by the bootstrap fault tests; errors propagate as exceptions)."""
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=1, timeout_ms=3000)
+    r = comm.rank
+    comm.destroy()
+    return {"rank": r}

@@ -1,0 +1,55 @@
+"""Host-memory communicator (CPU ranks over shared memory and TCP) -- no GPU needed."""
+import pytest
+
+from tests import _mp, host_cases
+
+
+def test_level0_matrix_four_ranks_one_machine():
+    res = _mp.run(4, host_cases.run_matrix, [1, 128, 32768, 131072 + 3], ["float32", "int32"], timeout=300)
+    assert all(r["ran"] > 0 for r in res)
+    assert res[0]["single"] and res[0]["local_size"] == 4 and res[0]["local_ranks"] == [0, 1, 2, 3]
+
+
+def test_all_dtypes_odd_sizes():
+    res = _mp.run(3, host_cases.run_matrix, [7, 4099], ["float32", "float64", "int32", "int64", "float16"], 3,
+                  timeout=300)
+    assert res[0]["ran"] > 0
+
+
+def test_logical_two_machines():
+    # Ranks r and s share a logical machine iff r // 2 == s // 2 (hostname injection).
+    res = _mp.run(4, host_cases.run_matrix, [1000, 70001], ["float32", "int64"], 2, 2, timeout=300)
+    assert res[0]["machine_count"] == 2 and res[0]["leaders"] == [0, 2]
+    assert res[3]["local_ranks"] == [2, 3] and res[3]["machine_index"] == 1 and res[3]["local_rank"] == 1
+    assert not res[0]["single"]
+
+
+def test_logical_uneven_machines():
+    res = _mp.run(5, host_cases.run_matrix, [513], ["float64"], 1, 2, timeout=300)
+    assert res[0]["machine_count"] == 3 and res[4]["local_ranks"] == [4] and res[0]["leaders"] == [0, 2, 4]
+
+
+def test_contract_cases():
+    res = _mp.run(3, host_cases.run_contract, timeout=120)
+    assert res[0]["rejected"] == 9
+
+
+def test_nested_groups():
+    res = _mp.run(3, host_cases.run_groups, timeout=120)
+    assert all(r["inner_untouched"] for r in res)
+
+
+def test_single_rank():
+    res = _mp.run(1, host_cases.run_matrix, [5, 1000], ["float32", "int32"], timeout=120)
+    assert res[0]["ran"] > 0
+
+
+def test_p2p_shared_memory():
+    res = _mp.run(4, host_cases.run_p2p, timeout=300)
+    assert set(res[0]["transports"].values()) == {"shm"}
+
+
+def test_p2p_across_logical_machines_tcp_epoll():
+    res = _mp.run(4, host_cases.run_p2p, 2, "epoll", timeout=300)
+    assert res[0]["transports"] == {1: "shm", 2: "tcp", 3: "tcp"}
+    assert res[0]["executor"] == "epoll"
