@@ -8,6 +8,9 @@
 #include "core/logger.h"
 #include "core/planner.h"
 #include "device/device_engine.h"
+#include "kernels/gemm.h"
+
+#include <mutex>
 
 struct bcclComm {
     bccl::Communicator comm;
@@ -203,6 +206,45 @@ double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int
 long bcclTraceDump(bcclComm_t comm, const char* path) {
     if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1;
     return comm->comm.device_engine()->DumpTrace(path);
+}
+
+namespace {
+std::mutex g_gemm_mu;
+int* g_gemm_err[64] = {};
+int* GemmErrWord() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    if (g_gemm_err[dev] == nullptr) {
+        if (cudaMalloc(&g_gemm_err[dev], sizeof(int)) != cudaSuccess) return nullptr;
+        cudaMemset(g_gemm_err[dev], 0, sizeof(int));
+    }
+    return g_gemm_err[dev];
+}
+}  // namespace
+
+int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, void* stream) {
+    int* err = GemmErrWord();
+    if (err == nullptr) {
+        LOG_ERROR("gemm: no device error word");
+        return 1;
+    }
+    cudaError_t e = bccl::LaunchGemmBf16(A, B, C, M, N, K, ldc, act, err, 0, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        LOG_ERROR("gemm launch failed: %s (M=%d N=%d K=%d)", cudaGetErrorString(e), M, N, K);
+        return 1;
+    }
+    return 0;
+}
+
+int bcclGemmCheckError(void) {
+    int* err = GemmErrWord();
+    if (err == nullptr) return -1;
+    int v = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaMemset(err, 0, sizeof(int));
+    return v;
 }
 
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,

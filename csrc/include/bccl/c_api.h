@@ -85,6 +85,12 @@ double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int
  * buffer; returns the number of records or -1 when tracing is off. */
 long bcclTraceDump(bcclComm_t comm, const char* path);
 
+/* Tensor-core GEMM (sm_100a tcgen05): C[M,N] = act(A[M,K] * B[N,K]^T), bf16 in/out, f32
+ * accumulation; act 0 = none, 1 = SiLU. Asynchronous on `stream`. bcclGemmCheckError()
+ * synchronises the current device and returns (and clears) the kernels' error word. */
+int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, void* stream);
+int bcclGemmCheckError(void);
+
 /* Planner white-box hooks (used by tests): sorts `n` tasks described by parallel arrays and
  * writes the resulting permutation (indices into the input) to `order`. */
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,

@@ -1,0 +1,253 @@
+// bf16 GEMM on the 5th-generation tensor cores: C[M,N] = act(A[M,K] * B[N,K]^T), f32 accumulate.
+//
+// Persistent, warp-specialised, one CTA per SM (192 threads):
+//   warp 0     TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
+//   warp 1     allocates 512 TMEM columns; one thread issues tcgen05.mma (M=128, N=256, K=16)
+//              into one of two TMEM accumulators and tcgen05.commit's stage/accumulator barriers
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quarter, optional
+//              SiLU, bf16 rounding, store to global
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Every mbarrier
+// wait is bounded; a role that gives up raises a shared abort word that stops the others, the
+// MMA thread drains its in-flight MMAs and the producer its in-flight TMA loads before the
+// TMEM columns are freed, and the failure is recorded in the caller's error word.
+// The tile schedule walks N fastest so consecutive CTAs share an A row block in L2.
+#include <cuda_bf16.h>
+
+#include "kernels/gemm.h"
+#include "kernels/sm100.cuh"
+
+namespace bccl {
+namespace gemm {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int kABytes = BM * BK * 2;
+constexpr int kBBytes = BN * BK * 2;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kTmemCols = 2 * BN;
+constexpr int kThreads = 192;
+constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*alignment*/ + 256 /*barriers*/;
+
+struct Args {
+    __nv_bfloat16* C;
+    int M, N, K, ldc;
+    int act;      // 0 none, 1 SiLU
+    int* err;     // device word: non-zero after a failed wait
+};
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                const __grid_constant__ CUtensorMap tmB,
+                                                                const __grid_constant__ Args g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+    // full[0..S) empty[S..2S) acc_full[2S..2S+2) acc_empty[2S+2..2S+4) drain[2S+4]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    auto smemA = [&](int s) { return smem_u32(smem + s * kStageBytes); };
+    auto smemB = [&](int s) { return smem_u32(smem + s * kStageBytes + kABytes); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(bar(s), 1);
+            mbar_init(bar(STAGES + s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar(2 * STAGES + a), 1);
+            mbar_init(bar(2 * STAGES + 2 + a), 4);
+        }
+        mbar_init(bar(2 * STAGES + 4), 1);
+        *s_abort = 0;
+        fence_proxy_async_shared();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int num_m = (g.M + BM - 1) / BM, num_n = (g.N + BN - 1) / BN;
+    const int tiles = num_m * num_n;
+    const int kblocks = (g.K + BK - 1) / BK;
+    auto fail = [&]() {
+        *s_abort = 1;
+        atomicExch(g.err, 1);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t kb = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*s_abort; tile += gridDim.x) {
+                const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+                for (int k = 0; k < kblocks; ++k, ++kb) {
+                    const int s = kb % STAGES;
+                    const uint32_t ph = (kb / STAGES) & 1;
+                    if (!mbar_wait(bar(STAGES + s), ph ^ 1, s_abort)) {
+                        fail();
+                        break;
+                    }
+                    mbar_arrive_expect_tx(bar(s), kStageBytes);
+                    tma_load_2d(smemA(s), &tmA, bar(s), k * BK, m0);
+                    tma_load_2d(smemB(s), &tmB, bar(s), k * BK, n0);
+                }
+            }
+            // Drain: every load this thread issued lands before the CTA can exit.
+            for (uint32_t i = (kb > STAGES ? kb - STAGES : 0); i < kb; ++i) {
+                mbar_wait(bar(i % STAGES), (i / STAGES) & 1, s_abort, 1u << 22);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16_f32(BM, BN);
+            uint32_t kb = 0, local = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*s_abort; tile += gridDim.x, ++local) {
+                const int a = local & 1;
+                const uint32_t use = local >> 1;
+                if (!mbar_wait(bar(2 * STAGES + 2 + a), (use & 1) ^ 1, s_abort)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(a * BN);
+                bool ok = true;
+                for (int k = 0; k < kblocks; ++k, ++kb) {
+                    const int s = kb % STAGES;
+                    if (!mbar_wait(bar(s), (kb / STAGES) & 1, s_abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc_sw128(smemA(s)), bd = smem_desc_sw128(smemB(s));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        // +32 bytes per K=16 step inside the 128-byte swizzle atom (encoded >> 4).
+                        umma_f16(d, ad + static_cast<uint64_t>(kk * 2), bd + static_cast<uint64_t>(kk * 2), idesc,
+                                 (k > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(bar(STAGES + s));
+                }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                umma_commit(bar(2 * STAGES + a));
+            }
+            // Drain every MMA this thread issued before TMEM is freed.
+            umma_commit(bar(2 * STAGES + 4));
+            mbar_wait(bar(2 * STAGES + 4), 0, s_abort, 1u << 22);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        uint32_t local = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*s_abort; tile += gridDim.x, ++local) {
+            const int a = local & 1;
+            const uint32_t use = local >> 1;
+            if (!mbar_wait(bar(2 * STAGES + a), use & 1, s_abort)) {
+                if (lane == 0) fail();
+                break;
+            }
+            tc_fence_after();
+            const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+            const int row = m0 + row_in_tile;
+            __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * BN + c),
+                                   v);
+                tmem_ld_wait();
+                const int col = n0 + c;
+                if (row >= g.M || col >= g.N) continue;
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    f[j] = __uint_as_float(v[j]);
+                    if (g.act == 1) f[j] = silu(f[j]);
+                }
+                if (col + 32 <= g.N && (reinterpret_cast<uintptr_t>(crow + col) & 15) == 0) {
+                    uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        dst[j] = make_uint4(pack_bf16x2(f[8 * j], f[8 * j + 1]), pack_bf16x2(f[8 * j + 2], f[8 * j + 3]),
+                                            pack_bf16x2(f[8 * j + 4], f[8 * j + 5]),
+                                            pack_bf16x2(f[8 * j + 6], f[8 * j + 7]));
+                    }
+                } else {
+                    for (int j = 0; j < 32 && col + j < g.N; ++j) crow[col + j] = __float2bfloat16_rn(f[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(2 * STAGES + 2 + a));
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+bool MakeMap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+    const DriverApi* d = Driver();
+    if (d == nullptr || d->cuTensorMapEncodeTiled == nullptr) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = d->cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+}  // namespace gemm
+
+cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, int* err,
+                           int max_ctas, cudaStream_t stream) {
+    using namespace gemm;
+    if (M <= 0 || N <= 0 || K <= 0 || (K % 8) != 0 || (reinterpret_cast<uintptr_t>(A) & 15) ||
+        (reinterpret_cast<uintptr_t>(B) & 15) || err == nullptr) {
+        return cudaErrorInvalidValue;
+    }
+    CUtensorMap ta, tb;
+    if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, BN)) return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    int grid = tiles < sms ? tiles : sms;
+    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+    Args g{static_cast<__nv_bfloat16*>(C), M, N, K, ldc, act, err};
+    gemm_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, g);
+    return cudaGetLastError();
+}
+
+}  // namespace bccl
