@@ -237,6 +237,34 @@ int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int
     return 0;
 }
 
+int bcclTpAllGatherGemm(bcclComm_t comm, const void* x, const void* w, void* y, int ms, int k, int n, int act,
+                        uintptr_t stream, int has_stream) {
+    if (comm == nullptr || comm->comm.device_engine() == nullptr) {
+        LOG_ERROR("bcclTpAllGatherGemm needs a device communicator");
+        return 1;
+    }
+    ApplyStream(comm, stream, has_stream);
+    bccl::DeviceEngine* d = comm->comm.device_engine();
+    cudaStream_t s = static_cast<cudaStream_t>(comm->comm.GetStream());
+    if (!d->TpAllGatherGemm(x, w, y, ms, k, n, act, s)) return 1;
+    if (!has_stream && !d->Synchronize(s)) return 1;
+    return 0;
+}
+
+int bcclTpGemmReduceScatter(bcclComm_t comm, const void* h, const void* w, void* out, int ms, int k, int n,
+                            uintptr_t stream, int has_stream) {
+    if (comm == nullptr || comm->comm.device_engine() == nullptr) {
+        LOG_ERROR("bcclTpGemmReduceScatter needs a device communicator");
+        return 1;
+    }
+    ApplyStream(comm, stream, has_stream);
+    bccl::DeviceEngine* d = comm->comm.device_engine();
+    cudaStream_t s = static_cast<cudaStream_t>(comm->comm.GetStream());
+    if (!d->TpGemmReduceScatter(h, w, out, ms, k, n, s)) return 1;
+    if (!has_stream && !d->Synchronize(s)) return 1;
+    return 0;
+}
+
 int bcclGemmCheckError(void) {
     int* err = GemmErrWord();
     if (err == nullptr) return -1;

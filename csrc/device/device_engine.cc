@@ -6,6 +6,9 @@
 #include "core/bootstrap.h"
 #include "core/env.h"
 #include "core/logger.h"
+#include <cuda_bf16.h>
+
+#include "kernels/gemm.h"
 #include "kernels/launch.h"
 
 namespace bccl {
@@ -116,6 +119,11 @@ void DeviceEngine::Finalize() {
     if (bs_ != nullptr && bs_->ready()) bs_->Barrier();
     for (SymBuffer& b : user_bufs_) sm_.Free(&b);
     user_bufs_.clear();
+    for (SymBuffer& b : tp_xg_) sm_.Free(&b);
+    for (SymBuffer& b : tp_rs_) sm_.Free(&b);
+    tp_xg_bytes_ = tp_rs_bytes_ = 0;
+    if (tp_err_) cudaFree(tp_err_);
+    tp_err_ = nullptr;
     sm_.Free(&nvls_);
     sm_.Free(&uc_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -134,6 +142,14 @@ void DeviceEngine::Finalize() {
 
 bool DeviceEngine::CheckDeviceError() {
     if (err_host_ == nullptr) return false;
+    if (tp_err_ != nullptr) {
+        int v = 0;
+        if (cudaMemcpy(&v, tp_err_, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && v != 0) {
+            cudaMemset(tp_err_, 0, sizeof(int));
+            LOG_ERROR("rank %d: a fused tensor-parallel GEMM gave up waiting for a peer", rank_);
+            return false;
+        }
+    }
     const volatile ErrorRecord* e = err_host_;
     if (e->code == kDevOk) return true;
     LOG_ERROR("rank %d: device collective failed (code %d: %s) in CTA %d waiting on rank %d, phase %d, seq %llu, "
@@ -150,6 +166,111 @@ bool DeviceEngine::Synchronize(cudaStream_t stream) {
         return false;
     }
     return CheckDeviceError();
+}
+
+bool DeviceEngine::EnsureTpBuffer(SymBuffer (&bufs)[2], size_t* have, size_t need) {
+    if (*have >= need) return true;
+    cudaDeviceSynchronize();
+    if (!bs_->Barrier()) return false;  // no peer may still use the old buffers
+    for (SymBuffer& b : bufs) sm_.Free(&b);
+    *have = 0;
+    for (SymBuffer& b : bufs) {
+        if (!sm_.Alloc(need, false, &b)) return false;
+    }
+    *have = need;
+    return true;
+}
+
+namespace {
+bool FillTpCommon(TpArgs* t, const DevComm& dc, int ms, unsigned long long seq) {
+    memset(t, 0, sizeof(*t));
+    t->rank = dc.rank;
+    t->nranks = dc.nranks;
+    t->ms = ms;
+    t->seq = seq;
+    return true;
+}
+unsigned long long* TpFlags(char* uc_base, size_t off) {
+    return reinterpret_cast<unsigned long long*>(uc_base + kTpFlagsOff + off);
+}
+constexpr size_t kAgCountersOff = 0;         // [kMaxRanks][kTpMaxChunks]
+constexpr size_t kRsStartedOff = 8u << 10;   // [kMaxRanks]
+constexpr size_t kRsCountersOff = 16u << 10; // [own tiles] (<= 16K tiles)
+}  // namespace
+
+bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, int ms, int k, int n, int act,
+                                   cudaStream_t stream) {
+    if (!inited_) return false;
+    cudaSetDevice(device_);
+    if (tp_err_ == nullptr) {
+        CUDA_OK(cudaMalloc(&tp_err_, sizeof(int)), "cudaMalloc(tp err)");
+        CUDA_OK(cudaMemset(tp_err_, 0, sizeof(int)), "cudaMemset(tp err)");
+    }
+    const int m = ms * nranks_;
+    cudaError_t e;
+    if (nranks_ == 1) {
+        e = LaunchGemmBf16(x_local, w, y, m, n, k, n, act, tp_err_, 0, stream);
+    } else {
+        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2)) return false;
+        const unsigned long long seq = ++tp_ag_calls_;
+        const int par = static_cast<int>(seq & 1ull);
+        TpArgs t;
+        FillTpCommon(&t, dc_, ms, seq);
+        t.x_local = x_local;
+        for (int p = 0; p < nranks_; ++p) {
+            t.xg[p] = tp_xg_[par].ptr[p];
+            t.ag_counters_peer[p] = TpFlags(uc_.ptr[p], kAgCountersOff);
+        }
+        t.ag_counters = TpFlags(uc_.ptr[rank_], kAgCountersOff);
+        e = LaunchTpGemm(kModeAllGather, x_local, tp_xg_[par].ptr[rank_], w, y, m, n, k, act, tp_err_, t, stream);
+    }
+    if (e != cudaSuccess) {
+        LOG_ERROR("rank %d: AllGather-GEMM launch failed: %s", rank_, cudaGetErrorString(e));
+        return false;
+    }
+    launches_++;
+    last_algo_ = "tp_ag_gemm";
+    return true;
+}
+
+bool DeviceEngine::TpGemmReduceScatter(const void* h, const void* w, void* out, int ms, int k, int n,
+                                       cudaStream_t stream) {
+    if (!inited_) return false;
+    cudaSetDevice(device_);
+    if (tp_err_ == nullptr) {
+        CUDA_OK(cudaMalloc(&tp_err_, sizeof(int)), "cudaMalloc(tp err)");
+        CUDA_OK(cudaMemset(tp_err_, 0, sizeof(int)), "cudaMemset(tp err)");
+    }
+    const int m = ms * nranks_;
+    cudaError_t e;
+    if (nranks_ == 1) {
+        e = LaunchGemmBf16(h, w, out, m, n, k, n, 0, tp_err_, 0, stream);
+    } else {
+        if ((static_cast<size_t>(ms) / 128) * ((static_cast<size_t>(n) + 255) / 256) > (16u << 10) / 8) {
+            LOG_ERROR("GEMM-ReduceScatter: too many output tiles per rank");
+            return false;
+        }
+        if (!EnsureTpBuffer(tp_rs_, &tp_rs_bytes_, static_cast<size_t>(m) * n * 2)) return false;
+        const unsigned long long seq = ++tp_rs_calls_;
+        const int par = static_cast<int>(seq & 1ull);
+        TpArgs t;
+        FillTpCommon(&t, dc_, ms, seq);
+        for (int p = 0; p < nranks_; ++p) {
+            t.rs_stage[p] = reinterpret_cast<__nv_bfloat16*>(tp_rs_[par].ptr[p]);
+            t.rs_counters[p] = TpFlags(uc_.ptr[p], kRsCountersOff);
+            t.rs_started_peer[p] = TpFlags(uc_.ptr[p], kRsStartedOff);
+        }
+        t.rs_started = TpFlags(uc_.ptr[rank_], kRsStartedOff);
+        t.out = static_cast<__nv_bfloat16*>(out);
+        e = LaunchTpGemm(kModeReduceScatter, h, nullptr, w, tp_rs_[par].ptr[rank_], m, n, k, 0, tp_err_, t, stream);
+    }
+    if (e != cudaSuccess) {
+        LOG_ERROR("rank %d: GEMM-ReduceScatter launch failed: %s", rank_, cudaGetErrorString(e));
+        return false;
+    }
+    launches_++;
+    last_algo_ = "tp_gemm_rs";
+    return true;
 }
 
 int DeviceEngine::WaitProbe(int timeout_ms) {

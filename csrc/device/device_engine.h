@@ -58,6 +58,12 @@ public:
     void* SymAlloc(size_t bytes);
     bool SymFree(void* ptr);
 
+    // Fused tensor-parallel GEMMs (bf16). x_local [ms,K] -> y [nranks*ms, n] = act(AllGather(x) * w^T)
+    // with w [n,K]; h [nranks*ms, K] -> out [ms, n] = this rank's rows of sum_ranks(h * w^T).
+    bool TpAllGatherGemm(const void* x_local, const void* w, void* y, int ms, int k, int n, int act,
+                         cudaStream_t stream);
+    bool TpGemmReduceScatter(const void* h, const void* w, void* out, int ms, int k, int n, cudaStream_t stream);
+
     cudaStream_t internal_stream() const { return stream_; }
     bool nvls_enabled() const { return nvls_.mc != nullptr; }
     const DevComm& dev_comm() const { return dc_; }
@@ -92,6 +98,14 @@ private:
     NcclP2p p2p_;
     std::atomic<unsigned long long> launches_{0};
     const char* last_algo_ = "none";
+    // Tensor-parallel workspaces (symmetric, double-buffered by call parity) and call counters.
+    SymBuffer tp_xg_[2];
+    size_t tp_xg_bytes_ = 0;
+    SymBuffer tp_rs_[2];
+    size_t tp_rs_bytes_ = 0;
+    unsigned long long tp_ag_calls_ = 0, tp_rs_calls_ = 0;
+    int* tp_err_ = nullptr;
+    bool EnsureTpBuffer(SymBuffer (&bufs)[2], size_t* have, size_t need);
     TraceRecord* trace_ = nullptr;
     unsigned int* trace_count_ = nullptr;
     unsigned int kernel_serial_ = 0;

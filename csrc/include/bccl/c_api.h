@@ -91,6 +91,15 @@ long bcclTraceDump(bcclComm_t comm, const char* path);
 int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, void* stream);
 int bcclGemmCheckError(void);
 
+/* Fused tensor-parallel GEMMs on a device communicator (bf16, one kernel each):
+ *   bcclTpAllGatherGemm: y[nranks*ms, n] = act(AllGather(x[ms, k]) * w[n, k]^T)
+ *   bcclTpGemmReduceScatter: out[ms, n] = this rank's rows of sum over ranks of h[nranks*ms, k] * w[n, k]^T
+ * ms must be a multiple of 128 (at most 64*128), k and n multiples of 8. Every rank calls them together. */
+int bcclTpAllGatherGemm(bcclComm_t comm, const void* x, const void* w, void* y, int ms, int k, int n, int act,
+                        uintptr_t stream, int has_stream);
+int bcclTpGemmReduceScatter(bcclComm_t comm, const void* h, const void* w, void* out, int ms, int k, int n,
+                            uintptr_t stream, int has_stream);
+
 /* Planner white-box hooks (used by tests): sorts `n` tasks described by parallel arrays and
  * writes the resulting permutation (indices into the input) to `order`. */
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,

@@ -13,6 +13,8 @@
 // The tile schedule walks N fastest so consecutive CTAs share an A row block in L2.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "kernels/gemm.h"
 #include "kernels/sm100.cuh"
 
@@ -27,7 +29,7 @@ constexpr int kABytes = BM * BK * 2;
 constexpr int kBBytes = BN * BK * 2;
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kTmemCols = 2 * BN;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // 6 GEMM warps + 4 communication warps (fused modes)
 constexpr int kSmemBytes = STAGES * kStageBytes + 1024 /*alignment*/ + 256 /*barriers*/;
 
 struct Args {
@@ -35,6 +37,7 @@ struct Args {
     int M, N, K, ldc;
     int act;      // 0 none, 1 SiLU
     int* err;     // device word: non-zero after a failed wait
+    TpArgs tp;    // fused tensor-parallel modes only
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -44,8 +47,50 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void red_add_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded spin until *p >= target (relaxed polls, then one acquire fence).
+__device__ __forceinline__ bool wait_geq_sys(const unsigned long long* p, unsigned long long target,
+                                             const volatile int* abort) {
+    for (uint32_t i = 0;; ++i) {
+        if (ld_relaxed_sys_u64(p) >= target) {
+            fence_sys();
+            return true;
+        }
+        if ((i & 255u) == 255u && *abort) return false;
+        if (i > (1u << 24)) return false;
+        __nanosleep(i < 256 ? 32 : 256);
+    }
+}
+
+// Row block `rb` of the A operand in AG mode: ranks' shards are ms/BM row blocks each;
+// the schedule takes this rank's row blocks first, then chunk 0 of every peer, chunk 1 of
+// every peer, ... (the order in which every rank pushes its shard).
+__device__ __forceinline__ int ag_row_block(int i, const TpArgs& tp, int num_m) {
+    const int per = tp.ms / BM;
+    const int r = tp.rank, n = tp.nranks;
+    if (i < per) return r * per + i;
+    i -= per;
+    const int c = i / (n - 1), k = i % (n - 1);
+    const int src = (r + 1 + k) % n;
+    (void)num_m;
+    return src * per + c;
+}
+
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                 const __grid_constant__ CUtensorMap tmB,
+                                                                const __grid_constant__ CUtensorMap tmG,
                                                                 const __grid_constant__ Args g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -53,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     // full[0..S) empty[S..2S) acc_full[2S..2S+2) acc_empty[2S+2..2S+4) drain[2S+4]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* s_comm_stop = s_abort + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     auto bar = [&](int i) { return smem_u32(bars + i); };
     auto smemA = [&](int s) { return smem_u32(smem + s * kStageBytes); };
@@ -69,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
         }
         mbar_init(bar(2 * STAGES + 4), 1);
         *s_abort = 0;
+        *s_comm_stop = 0;
         fence_proxy_async_shared();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
@@ -85,6 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     const int num_m = (g.M + BM - 1) / BM, num_n = (g.N + BN - 1) / BN;
     const int tiles = num_m * num_n;
     const int kblocks = (g.K + BK - 1) / BK;
+    // Tile t -> (row block, column block); N walks fastest.
+    auto tile_rb = [&](int t) { return MODE == kModeAllGather ? ag_row_block(t / num_n, g.tp, num_m) : t / num_n; };
     auto fail = [&]() {
         *s_abort = 1;
         atomicExch(g.err, 1);
@@ -94,7 +143,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
         if (lane == 0) {
             uint32_t kb = 0;
             for (int tile = blockIdx.x; tile < tiles && !*s_abort; tile += gridDim.x) {
-                const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+                const int rb = tile_rb(tile);
+                const int n0 = (tile % num_n) * BN;
+                const CUtensorMap* amap = &tmA;
+                int arow = rb * BM;
+                if (MODE == kModeAllGather) {
+                    const int per = g.tp.ms / BM, src = rb / per, chunk = rb % per;
+                    if (src == g.tp.rank) {
+                        arow = chunk * BM;  // own shard, straight from the caller's tensor
+                    } else {
+                        // Peer rows: wait until every CTA of rank `src` pushed this chunk here.
+                        const unsigned long long* cnt = g.tp.ag_counters + (size_t)src * kTpMaxChunks + chunk;
+                        if (!wait_geq_sys(cnt, g.tp.seq * (uint64_t)g.tp.contributors, s_abort)) {
+                            fail();
+                            break;
+                        }
+                        fence_proxy_async_global();  // generic-proxy writes -> TMA reads
+                        amap = &tmG;
+                    }
+                }
                 for (int k = 0; k < kblocks; ++k, ++kb) {
                     const int s = kb % STAGES;
                     const uint32_t ph = (kb / STAGES) & 1;
@@ -103,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
                         break;
                     }
                     mbar_arrive_expect_tx(bar(s), kStageBytes);
-                    tma_load_2d(smemA(s), &tmA, bar(s), k * BK, m0);
+                    tma_load_2d(smemA(s), amap, bar(s), k * BK, arow);
                     tma_load_2d(smemB(s), &tmB, bar(s), k * BK, n0);
                 }
             }
@@ -152,10 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
             umma_commit(bar(2 * STAGES + 4));
             mbar_wait(bar(2 * STAGES + 4), 0, s_abort, 1u << 22);
         }
-    } else {
+    } else if (warp < 6) {
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = q * 32 + lane;
         uint32_t local = 0;
+        unsigned char rs_ready_checked[kMaxRanks] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int tile = blockIdx.x; tile < tiles && !*s_abort; tile += gridDim.x, ++local) {
             const int a = local & 1;
             const uint32_t use = local >> 1;
@@ -164,9 +232,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
                 break;
             }
             tc_fence_after();
-            const int m0 = (tile / num_n) * BM, n0 = (tile % num_n) * BN;
+            const int rb = tile_rb(tile);
+            const int m0 = rb * BM, n0 = (tile % num_n) * BN;
             const int row = m0 + row_in_tile;
             __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
+            int owner = 0;
+            if (MODE == kModeReduceScatter) {
+                // Partial tile goes to its owner's staging slot for this rank.
+                const int per = g.tp.ms / BM;
+                owner = rb / per;
+                if (owner != g.tp.rank && !rs_ready_checked[owner]) {
+                    // The owner must have started the previous call (so it finished reading
+                    // this parity's staging two calls ago) before the first push to it.
+                    if (lane == 0 && !wait_geq_sys(g.tp.rs_started + owner, g.tp.seq - 1, s_abort)) fail();
+                    __syncwarp();
+                    rs_ready_checked[owner] = 1;
+                }
+                const int local_row = (rb % per) * BM + row_in_tile;
+                crow = g.tp.rs_stage[owner] + ((size_t)g.tp.rank * g.tp.ms + local_row) * g.N;
+            }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
@@ -197,6 +281,83 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(2 * STAGES + 2 + a));
+            if (MODE == kModeReduceScatter && lane == 0) {
+                // This warp's 32 rows of the tile are stored: release them to the owner (the
+                // owner waits for 4 warps x nranks bumps per call).
+                const int per = g.tp.ms / BM;
+                const int owner_tile = (rb % per) * num_n + (tile % num_n);
+                fence_sys();
+                red_add_sys(g.tp.rs_counters[owner] + owner_tile, 1ull);
+            }
+        }
+    } else {
+        // Communication warps (fused modes).
+        const int ctid = threadIdx.x - 6 * 32, cnt_threads = kThreads - 6 * 32;
+        if (MODE == kModeAllGather) {
+            // Push this rank's shard, chunk by chunk, into every peer's gathered-X buffer;
+            // CTA b owns slice b of every chunk. One counter bump per (peer, chunk) per CTA.
+            const int per = g.tp.ms / BM;
+            const size_t chunk_bytes = (size_t)BM * g.K * 2;
+            const size_t slice = ((chunk_bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+            const size_t lo = min(chunk_bytes, (size_t)blockIdx.x * slice), hi = min(chunk_bytes, lo + slice);
+            // No waits here: the loop always runs to the end (uniform named barriers).
+            for (int c = 0; c < per; ++c) {
+                const char* srcp = reinterpret_cast<const char*>(g.tp.x_local) + (size_t)c * chunk_bytes;
+                const size_t dst_off = ((size_t)g.tp.rank * per + c) * chunk_bytes;
+                for (size_t o = lo + (size_t)ctid * 16; o < hi; o += (size_t)cnt_threads * 16) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
+                    for (int q = 0; q < g.tp.nranks; ++q) {
+                        if (q == g.tp.rank) continue;
+                        __stcg(reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.tp.xg[q]) + dst_off + o), v);
+                    }
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
+                if (ctid < g.tp.nranks && ctid != g.tp.rank) {
+                    fence_sys();
+                    red_add_sys(g.tp.ag_counters_peer[ctid] + (size_t)g.tp.rank * kTpMaxChunks + c, 1ull);
+                }
+            }
+        } else if (MODE == kModeReduceScatter) {
+            // Announce this call, then sum the tiles this rank owns as their N partials land.
+            if (blockIdx.x == 0 && ctid < g.tp.nranks && ctid != g.tp.rank) {
+                st_relaxed_sys_u64(g.tp.rs_started_peer[ctid] + g.tp.rank, g.tp.seq);
+            }
+            const int per = g.tp.ms / BM;
+            const int own_tiles = per * num_n;
+            for (int t = blockIdx.x; t < own_tiles; t += gridDim.x) {
+                // Only ctid 0 writes s_comm_stop, before the barrier: every thread reads the same value.
+                if (ctid == 0 && !wait_geq_sys(g.tp.rs_counters[g.tp.rank] + t,
+                                               g.tp.seq * 4ull * (unsigned long long)g.tp.nranks, s_abort)) {
+                    fail();
+                    *s_comm_stop = 1;
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
+                if (*s_comm_stop) break;
+                const int lrb = t / num_n, nb = t % num_n;
+                const int ncols = min(BN, g.N - nb * BN);
+                // 8 bf16 per thread-iteration; rows x ncols of the tile.
+                const int vec_per_row = ncols / 8;
+                for (int e = ctid; e < BM * vec_per_row; e += cnt_threads) {
+                    const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
+                    const int lrow = lrb * BM + rr;
+                    if (lrow >= g.tp.ms) continue;
+                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    for (int srcr = 0; srcr < g.tp.nranks; ++srcr) {
+                        const __nv_bfloat16* part =
+                            g.tp.rs_stage[g.tp.rank] + ((size_t)srcr * g.tp.ms + lrow) * g.N + nb * BN + cc;
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part));
+                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            acc[2 * j] += __uint_as_float(w[j] << 16);
+                            acc[2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
+                        }
+                    }
+                    uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+                    *reinterpret_cast<uint4*>(g.tp.out + (size_t)lrow * g.N + nb * BN + cc) = o;
+                }
+            }
         }
     }
     __syncthreads();
@@ -220,6 +381,29 @@ bool MakeMap(CUtensorMap* map, const void* base, int rows, int cols, int box_row
     return r == CUDA_SUCCESS;
 }
 
+template <int MODE>
+cudaError_t LaunchMode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tg, const Args& g, int grid,
+                       cudaStream_t stream) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(gemm_bf16_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    gemm_bf16_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tg, g);
+    return cudaGetLastError();
+}
+
+int NumSms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
 }  // namespace
 }  // namespace gemm
 
@@ -232,22 +416,36 @@ cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, 
     }
     CUtensorMap ta, tb;
     if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, BN)) return cudaErrorInvalidValue;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    int grid = tiles < sms ? tiles : sms;
+    int grid = std::min(tiles, NumSms());
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-    Args g{static_cast<__nv_bfloat16*>(C), M, N, K, ldc, act, err};
-    gemm_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, g);
-    return cudaGetLastError();
+    Args g{static_cast<__nv_bfloat16*>(C), M, N, K, ldc, act, err, TpArgs{}};
+    return LaunchMode<kModePlain>(ta, tb, tb, g, grid, stream);
+}
+
+cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, const void* B, void* C, int M, int N,
+                         int K, int act, int* err, const TpArgs& tp, cudaStream_t stream) {
+    using namespace gemm;
+    if (M <= 0 || N <= 0 || K <= 0 || (K % 8) != 0 || (N % 8) != 0 || tp.ms % BM != 0 || tp.ms / BM > kTpMaxChunks ||
+        tp.nranks < 1 || tp.nranks > kMaxRanks || err == nullptr || M != tp.ms * tp.nranks) {
+        return cudaErrorInvalidValue;
+    }
+    CUtensorMap ta, tb, tg;
+    const int grid = NumSms();
+    TpArgs t = tp;
+    t.contributors = grid;
+    Args g{static_cast<__nv_bfloat16*>(C), M, N, K, N, act, err, t};
+    if (mode == kModeAllGather) {
+        if (!MakeMap(&ta, A_local, tp.ms, K, BM) || !MakeMap(&tb, B, N, K, BN) || !MakeMap(&tg, A_gathered, M, K, BM)) {
+            return cudaErrorInvalidValue;
+        }
+        return LaunchMode<kModeAllGather>(ta, tb, tg, g, grid, stream);
+    }
+    if (mode == kModeReduceScatter) {
+        if (!MakeMap(&ta, A_local, M, K, BM) || !MakeMap(&tb, B, N, K, BN)) return cudaErrorInvalidValue;
+        return LaunchMode<kModeReduceScatter>(ta, tb, ta, g, grid, stream);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace bccl

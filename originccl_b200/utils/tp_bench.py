@@ -1,0 +1,88 @@
+"""Tensor-parallel MLP benchmark: fused kernels vs NCCL + cuBLAS.
+
+``torchrun --nproc-per-node 8 -m originccl_b200.utils.tp_bench`` runs X [tokens, hidden] sequence-
+sharded over the ranks through AllGather->GEMM(SiLU) and GEMM->ReduceScatter, random-init
+normal(0, 0.02) weights, bf16. Timing: CUDA events, warm-up, max over ranks. Reports ms per MLP
+forward, TFLOP/s per GPU, and the fraction of the roofline max(FLOPs / measured GEMM peak,
+NVLink bytes / 770 GB/s).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+
+
+def main(argv=None) -> None:
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--tokens", type=int, default=8192)
+    p.add_argument("--hidden", type=int, default=8192)
+    p.add_argument("--ffn", type=int, default=28672)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--gemm-peak-tflops", type=float, default=1383.8, help="measured sustained cuBLAS bf16 peak")
+    p.add_argument("--nvlink-gbs", type=float, default=770.0)
+    args = p.parse_args(argv)
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    import originccl_b200 as occl
+    from originccl_b200.parallel.tensor_parallel import TensorParallelMLP
+
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=300))
+        comm = occl.init_from_store(dist.distributed_c10d._get_default_store(), rank, world, device=local)
+    else:
+        comm = occl.Communicator().init(0, 1, None, device=0)
+    mlp = TensorParallelMLP(comm, args.hidden, args.ffn, seed=3)
+    ms = args.tokens // world
+    g = torch.Generator(device="cuda").manual_seed(42 + rank)
+    x = (torch.randn(ms, args.hidden, device="cuda", generator=g)).bfloat16()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / args.iters], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ours = timed(lambda: mlp(x))
+    ref = timed(lambda: mlp.forward_reference(x))
+    y = mlp(x)
+    yr = mlp.forward_reference(x)
+    torch.cuda.synchronize()
+    rel = ((y.float() - yr.float()).abs().max() / yr.float().abs().max()).item()
+    flops = 2 * 2.0 * args.tokens * args.hidden * (args.ffn // world)  # per rank, both GEMMs
+    nvlink_bytes = 2 * (world - 1) * ms * args.hidden * 2  # AG in + RS out per rank, bf16
+    roof_ms = max(flops / (args.gemm_peak_tflops * 1e12), nvlink_bytes / (args.nvlink_gbs * 1e9)) * 1e3
+    if rank == 0:
+        print(json.dumps({"bench": "tp_mlp", "world": world, "tokens": args.tokens, "hidden": args.hidden,
+                          "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
+                          "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
+                          "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
+                          "max_rel_diff_vs_reference": rel}), flush=True)
+    comm.destroy()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -230,3 +230,52 @@ def run_mixed_sequence(rank: int, world: int, steps: int = 60) -> Dict:
         _close(got, exp, "float32", what)
     comm.destroy()
     return {"checked": len(pending)}
+
+
+def run_tp(rank: int, world: int, ms: int = 256, k: int = 512, nf: int = 384, hd: int = 512, calls: int = 3) -> Dict:
+    """Fused AllGather->GEMM(SiLU) and GEMM->ReduceScatter against an fp32 oracle rebuilt from seeds."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200.ops import tp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+
+    def shard(r, c):
+        g = torch.Generator(device="cuda").manual_seed(1000 * c + r)
+        return (torch.randn(ms, k, device="cuda", generator=g) * 0.5).bfloat16()
+
+    def w_up(r):
+        g = torch.Generator(device="cuda").manual_seed(50000 + r)
+        return (torch.randn(nf, k, device="cuda", generator=g) * 0.05).bfloat16()
+
+    def w_down(r):
+        g = torch.Generator(device="cuda").manual_seed(60000 + r)
+        return (torch.randn(hd, nf, device="cuda", generator=g) * 0.05).bfloat16()
+
+    worst_ag = worst_rs = 0.0
+    for c in range(calls):
+        x = shard(rank, c)
+        y = tp.all_gather_gemm(comm, x, w_up(rank), "silu")
+        comm.synchronize()
+        full = torch.cat([shard(q, c) for q in range(world)]).float()
+        ref = torch.nn.functional.silu(full @ w_up(rank).float().t())
+        err = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+        worst_ag = max(worst_ag, err)
+        assert err < 2e-2, f"all_gather_gemm call {c}: rel err {err}"
+        # GEMM->ReduceScatter with h = this call's y (same on... each rank has its own h)
+        out = tp.gemm_reduce_scatter(comm, y, w_down(rank))
+        comm.synchronize()
+        acc = torch.zeros(ms * world, hd, device="cuda")
+        for q in range(world):
+            fq = torch.cat([shard(p, c) for p in range(world)]).float()
+            hq = torch.nn.functional.silu(fq @ w_up(q).float().t()).bfloat16().float()
+            acc += hq @ w_down(q).float().t()
+        ref2 = acc[rank * ms:(rank + 1) * ms]
+        err2 = ((out.float() - ref2).abs().max() / ref2.abs().max()).item()
+        worst_rs = max(worst_rs, err2)
+        assert err2 < 3e-2, f"gemm_reduce_scatter call {c}: rel err {err2}"
+    comm.destroy()
+    return {"ag_err": worst_ag, "rs_err": worst_rs}

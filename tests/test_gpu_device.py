@@ -94,3 +94,16 @@ def test_mixed_algorithm_sequence():
         pytest.skip("needs 2+ GPUs")
     res = _mp.run(min(n, 8), gpu_cases.run_mixed_sequence, timeout=900)
     assert res[0]["checked"] > 0
+
+
+def test_tp_fused_single_rank():
+    _need(1)
+    res = _mp.run(1, gpu_cases.run_tp, timeout=300)
+    assert res[0]["ag_err"] < 2e-2
+
+
+@pytest.mark.multigpu
+def test_tp_fused_two_ranks():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_tp, timeout=600)
+    assert res[0]["rs_err"] < 3e-2
