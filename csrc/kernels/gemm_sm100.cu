@@ -14,6 +14,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "kernels/gemm.h"
 #include "kernels/sm100.cuh"
@@ -76,8 +77,8 @@ __device__ __forceinline__ bool wait_geq_sys(const unsigned long long* p, unsign
 // Row block `rb` of the A operand in AG mode: ranks' shards are ms/BM row blocks each;
 // the schedule takes this rank's row blocks first, then chunk 0 of every peer, chunk 1 of
 // every peer, ... (the order in which every rank pushes its shard).
-__device__ __forceinline__ int ag_row_block(int i, const TpArgs& tp, int num_m) {
-    const int per = tp.ms / BM;
+__device__ __forceinline__ int ag_row_block(int i, const TpArgs& tp, int num_m, int block_rows = BM) {
+    const int per = tp.ms / block_rows;
     const int r = tp.rank, n = tp.nranks;
     if (i < per) return r * per + i;
     i -= per;
@@ -86,6 +87,82 @@ __device__ __forceinline__ int ag_row_block(int i, const TpArgs& tp, int num_m) 
     (void)num_m;
     return src * per + c;
 }
+
+// Communication warps of the fused modes (warps 6-9): AllGather pushes / ReduceScatter sums.
+template <int MODE>
+__device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile int* s_abort, volatile int* s_comm_stop) {
+    auto fail = [&]() {
+        *s_abort = 1;
+        atomicExch(g.err, 1);
+    };
+        const int ctid = threadIdx.x - 6 * 32, cnt_threads = kThreads - 6 * 32;
+        if (MODE == kModeAllGather) {
+            // Push this rank's shard, chunk by chunk, into every peer's gathered-X buffer;
+            // CTA b owns slice b of every chunk. One counter bump per (peer, chunk) per CTA.
+            const int per = g.tp.ms / BM;
+            const size_t chunk_bytes = (size_t)BM * g.K * 2;
+            const size_t slice = ((chunk_bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+            const size_t lo = min(chunk_bytes, (size_t)blockIdx.x * slice), hi = min(chunk_bytes, lo + slice);
+            // No waits here: the loop always runs to the end (uniform named barriers).
+            for (int c = 0; c < per; ++c) {
+                const char* srcp = reinterpret_cast<const char*>(g.tp.x_local) + (size_t)c * chunk_bytes;
+                const size_t dst_off = ((size_t)g.tp.rank * per + c) * chunk_bytes;
+                for (size_t o = lo + (size_t)ctid * 16; o < hi; o += (size_t)cnt_threads * 16) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
+                    for (int q = 0; q < g.tp.nranks; ++q) {
+                        if (q == g.tp.rank) continue;
+                        __stcg(reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.tp.xg[q]) + dst_off + o), v);
+                    }
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
+                if (ctid < g.tp.nranks && ctid != g.tp.rank) {
+                    fence_sys();
+                    red_add_sys(g.tp.ag_counters_peer[ctid] + (size_t)g.tp.rank * kTpMaxChunks + c, 1ull);
+                }
+            }
+        } else if (MODE == kModeReduceScatter) {
+            // Announce this call, then sum the tiles this rank owns as their N partials land.
+            if (blockIdx.x == 0 && ctid < g.tp.nranks && ctid != g.tp.rank) {
+                st_relaxed_sys_u64(g.tp.rs_started_peer[ctid] + g.tp.rank, g.tp.seq);
+            }
+            const int per = g.tp.ms / BM;
+            const int own_tiles = per * num_n;
+            for (int t = blockIdx.x; t < own_tiles; t += gridDim.x) {
+                // Only ctid 0 writes s_comm_stop, before the barrier: every thread reads the same value.
+                if (ctid == 0 && !wait_geq_sys(g.tp.rs_counters[g.tp.rank] + t,
+                                               g.tp.seq * 4ull * (unsigned long long)g.tp.nranks, s_abort)) {
+                    fail();
+                    *s_comm_stop = 1;
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
+                if (*s_comm_stop) break;
+                const int lrb = t / num_n, nb = t % num_n;
+                const int ncols = min(BN, g.N - nb * BN);
+                // 8 bf16 per thread-iteration; rows x ncols of the tile.
+                const int vec_per_row = ncols / 8;
+                for (int e = ctid; e < BM * vec_per_row; e += cnt_threads) {
+                    const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
+                    const int lrow = lrb * BM + rr;
+                    if (lrow >= g.tp.ms) continue;
+                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                    for (int srcr = 0; srcr < g.tp.nranks; ++srcr) {
+                        const __nv_bfloat16* part =
+                            g.tp.rs_stage[g.tp.rank] + ((size_t)srcr * g.tp.ms + lrow) * g.N + nb * BN + cc;
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part));
+                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            acc[2 * j] += __uint_as_float(w[j] << 16);
+                            acc[2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
+                        }
+                    }
+                    uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+                    *reinterpret_cast<uint4*>(g.tp.out + (size_t)lrow * g.N + nb * BN + cc) = o;
+                }
+            }
+        }
+    }
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -291,79 +368,239 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
             }
         }
     } else {
-        // Communication warps (fused modes).
-        const int ctid = threadIdx.x - 6 * 32, cnt_threads = kThreads - 6 * 32;
-        if (MODE == kModeAllGather) {
-            // Push this rank's shard, chunk by chunk, into every peer's gathered-X buffer;
-            // CTA b owns slice b of every chunk. One counter bump per (peer, chunk) per CTA.
-            const int per = g.tp.ms / BM;
-            const size_t chunk_bytes = (size_t)BM * g.K * 2;
-            const size_t slice = ((chunk_bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
-            const size_t lo = min(chunk_bytes, (size_t)blockIdx.x * slice), hi = min(chunk_bytes, lo + slice);
-            // No waits here: the loop always runs to the end (uniform named barriers).
-            for (int c = 0; c < per; ++c) {
-                const char* srcp = reinterpret_cast<const char*>(g.tp.x_local) + (size_t)c * chunk_bytes;
-                const size_t dst_off = ((size_t)g.tp.rank * per + c) * chunk_bytes;
-                for (size_t o = lo + (size_t)ctid * 16; o < hi; o += (size_t)cnt_threads * 16) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
-                    for (int q = 0; q < g.tp.nranks; ++q) {
-                        if (q == g.tp.rank) continue;
-                        __stcg(reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.tp.xg[q]) + dst_off + o), v);
-                    }
-                }
-                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
-                if (ctid < g.tp.nranks && ctid != g.tp.rank) {
-                    fence_sys();
-                    red_add_sys(g.tp.ag_counters_peer[ctid] + (size_t)g.tp.rank * kTpMaxChunks + c, 1ull);
-                }
-            }
-        } else if (MODE == kModeReduceScatter) {
-            // Announce this call, then sum the tiles this rank owns as their N partials land.
-            if (blockIdx.x == 0 && ctid < g.tp.nranks && ctid != g.tp.rank) {
-                st_relaxed_sys_u64(g.tp.rs_started_peer[ctid] + g.tp.rank, g.tp.seq);
-            }
-            const int per = g.tp.ms / BM;
-            const int own_tiles = per * num_n;
-            for (int t = blockIdx.x; t < own_tiles; t += gridDim.x) {
-                // Only ctid 0 writes s_comm_stop, before the barrier: every thread reads the same value.
-                if (ctid == 0 && !wait_geq_sys(g.tp.rs_counters[g.tp.rank] + t,
-                                               g.tp.seq * 4ull * (unsigned long long)g.tp.nranks, s_abort)) {
-                    fail();
-                    *s_comm_stop = 1;
-                }
-                asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
-                if (*s_comm_stop) break;
-                const int lrb = t / num_n, nb = t % num_n;
-                const int ncols = min(BN, g.N - nb * BN);
-                // 8 bf16 per thread-iteration; rows x ncols of the tile.
-                const int vec_per_row = ncols / 8;
-                for (int e = ctid; e < BM * vec_per_row; e += cnt_threads) {
-                    const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
-                    const int lrow = lrb * BM + rr;
-                    if (lrow >= g.tp.ms) continue;
-                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    for (int srcr = 0; srcr < g.tp.nranks; ++srcr) {
-                        const __nv_bfloat16* part =
-                            g.tp.rs_stage[g.tp.rank] + ((size_t)srcr * g.tp.ms + lrow) * g.N + nb * BN + cc;
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part));
-                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            acc[2 * j] += __uint_as_float(w[j] << 16);
-                            acc[2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
-                        }
-                    }
-                    uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
-                    *reinterpret_cast<uint4*>(g.tp.out + (size_t)lrow * g.N + nb * BN + cc) = o;
-                }
-            }
-        }
+        comm_warps<MODE>(g, num_n, s_abort, s_comm_stop);
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// 2-SM variant: a CTA pair (cluster of 2) computes a 256x256 tile with tcgen05.mma.cta_group::2.
+// Each CTA TMA-loads its own 128 rows of A and its own 128 rows of B (N/2) into a 6-stage ring
+// and counts the bytes on the leader's full barrier; the leader's single MMA thread reads both
+// CTAs' shared memory, and its commits arrive on both CTAs' barriers. Each CTA's TMEM holds its
+// 128 rows x 256 columns of the accumulator, so the epilogue is the same as the 1-SM kernel.
+// Per FLOP this moves a third less data from L2 into shared memory than 128x256 tiles. No load
+// uses cluster multicast.
+constexpr int PSTAGES = 6;
+constexpr int kPStageBytes = 2 * (BM * BK * 2);  // 16 KiB of A + 16 KiB of B per CTA
+constexpr int kPSmemBytes = PSTAGES * kPStageBytes + 1024 + 256;
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmG, const __grid_constant__ Args g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PSTAGES * kPStageBytes);
+    // full[0..S) (leader's count both CTAs) empty[S..2S) acc_full[2S..2S+2) acc_empty[2S+2..2S+4) drain[2S+4]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PSTAGES + 5);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* s_comm_stop = s_abort + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t cta = cluster_ctarank();
+    const bool leader = cta == 0;
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    auto smemA = [&](int s) { return smem_u32(smem + s * kPStageBytes); };
+    auto smemB = [&](int s) { return smem_u32(smem + s * kPStageBytes + BM * BK * 2); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PSTAGES; ++s) {
+            mbar_init(bar(s), 2);
+            mbar_init(bar(PSTAGES + s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar(2 * PSTAGES + a), 1);
+            mbar_init(bar(2 * PSTAGES + 2 + a), 8);
+        }
+        mbar_init(bar(2 * PSTAGES + 4), 1);
+        *s_abort = 0;
+        *s_comm_stop = 0;
+        fence_proxy_async_shared();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    cluster_sync();  // both CTAs' barriers exist before any remote arrive
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int PM = 2 * BM;  // rows per pair tile
+    const int num_m = (g.M + PM - 1) / PM, num_n = (g.N + BN - 1) / BN;
+    const int tiles = num_m * num_n;
+    const int kblocks = (g.K + BK - 1) / BK;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    auto tile_rb = [&](int t) { return MODE == kModeAllGather ? ag_row_block(t / num_n, g.tp, num_m, PM) : t / num_n; };
+    auto fail = [&]() {
+        *s_abort = 1;
+        atomicExch(g.err, 1);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t kb = 0;
+            for (int tile = pair; tile < tiles && !*s_abort; tile += npairs) {
+                const int rb = tile_rb(tile);
+                const int n0 = (tile % num_n) * BN + static_cast<int>(cta) * BM;  // this CTA's half of N
+                const CUtensorMap* amap = &tmA;
+                int arow = rb * PM + static_cast<int>(cta) * BM;
+                if (MODE == kModeAllGather) {
+                    const int per = g.tp.ms / BM, rb128 = rb * 2 + static_cast<int>(cta);
+                    const int src = rb128 / per, chunk = rb128 % per;
+                    if (src == g.tp.rank) {
+                        arow = chunk * BM;
+                    } else {
+                        const unsigned long long* cnt = g.tp.ag_counters + (size_t)src * kTpMaxChunks + chunk;
+                        if (!wait_geq_sys(cnt, g.tp.seq * (uint64_t)g.tp.contributors, s_abort)) {
+                            fail();
+                            break;
+                        }
+                        fence_proxy_async_global();
+                        amap = &tmG;
+                    }
+                }
+                bool ok = true;
+                for (int k = 0; k < kblocks; ++k, ++kb) {
+                    const int s = kb % PSTAGES;
+                    if (!mbar_wait(bar(PSTAGES + s), ((kb / PSTAGES) & 1) ^ 1, s_abort)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t lfull = mapa_shared(bar(s), 0);
+                    mbar_arrive_expect_tx_cluster(lfull, kPStageBytes);
+                    tma_load_2d_pair(smemA(s), amap, lfull, k * BK, arow);
+                    tma_load_2d_pair(smemB(s), &tmB, lfull, k * BK, n0);
+                }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            const uint32_t idesc = idesc_bf16_f32(2 * BM, BN);
+            uint32_t kb = 0, local = 0;
+            for (int tile = pair; tile < tiles && !*s_abort; tile += npairs, ++local) {
+                const int a = local & 1;
+                const uint32_t use = local >> 1;
+                if (!mbar_wait(bar(2 * PSTAGES + 2 + a), (use & 1) ^ 1, s_abort)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(a * BN);
+                bool ok = true;
+                for (int k = 0; k < kblocks; ++k, ++kb) {
+                    const int s = kb % PSTAGES;
+                    if (!mbar_wait(bar(s), (kb / PSTAGES) & 1, s_abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = smem_desc_sw128(smemA(s)), bd = smem_desc_sw128(smemB(s));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        umma_f16_pair(d, ad + static_cast<uint64_t>(kk * 2), bd + static_cast<uint64_t>(kk * 2), idesc,
+                                      (k > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit_pair(bar(PSTAGES + s), 0x3);
+                }
+                if (!ok) {
+                    fail();
+                    break;
+                }
+                umma_commit_pair(bar(2 * PSTAGES + a), 0x3);
+            }
+            umma_commit_pair(bar(2 * PSTAGES + 4), 0x1);
+            mbar_wait(bar(2 * PSTAGES + 4), 0, s_abort, 1u << 22);
+            // Every TMA load counted on this CTA's full barriers has landed (both CTAs').
+            for (uint32_t i = (kb > PSTAGES ? kb - PSTAGES : 0); i < kb; ++i)
+                mbar_wait(bar(i % PSTAGES), (i / PSTAGES) & 1, s_abort, 1u << 22);
+        }
+    } else if (warp < 6) {
+        const int q = warp & 3;
+        const int row_in_cta = q * 32 + lane;
+        uint32_t local = 0;
+        unsigned char rs_ready_checked[kMaxRanks] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int tile = pair; tile < tiles && !*s_abort; tile += npairs, ++local) {
+            const int a = local & 1;
+            const uint32_t use = local >> 1;
+            if (!mbar_wait(bar(2 * PSTAGES + a), use & 1, s_abort)) {
+                if (lane == 0) fail();
+                break;
+            }
+            tc_fence_after();
+            const int rb = tile_rb(tile);
+            const int rb128 = rb * 2 + static_cast<int>(cta);
+            const int n0 = (tile % num_n) * BN;
+            const int row = rb128 * BM + row_in_cta;
+            __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
+            int owner = 0;
+            if (MODE == kModeReduceScatter) {
+                const int per = g.tp.ms / BM;
+                owner = rb128 / per;
+                if (owner != g.tp.rank && !rs_ready_checked[owner]) {
+                    if (lane == 0 && !wait_geq_sys(g.tp.rs_started + owner, g.tp.seq - 1, s_abort)) fail();
+                    __syncwarp();
+                    rs_ready_checked[owner] = 1;
+                }
+                const int local_row = (rb128 % per) * BM + row_in_cta;
+                crow = g.tp.rs_stage[owner] + ((size_t)g.tp.rank * g.tp.ms + local_row) * g.N;
+            }
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                __syncwarp();
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * BN + c),
+                                   v);
+                tmem_ld_wait();
+                const int col = n0 + c;
+                if (row >= g.M || col >= g.N) continue;
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    f[j] = __uint_as_float(v[j]);
+                    if (g.act == 1) f[j] = silu(f[j]);
+                }
+                if (col + 32 <= g.N && (reinterpret_cast<uintptr_t>(crow + col) & 15) == 0) {
+                    uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        dst[j] = make_uint4(pack_bf16x2(f[8 * j], f[8 * j + 1]), pack_bf16x2(f[8 * j + 2], f[8 * j + 3]),
+                                            pack_bf16x2(f[8 * j + 4], f[8 * j + 5]),
+                                            pack_bf16x2(f[8 * j + 6], f[8 * j + 7]));
+                    }
+                } else {
+                    for (int j = 0; j < 32 && col + j < g.N; ++j) crow[col + j] = __float2bfloat16_rn(f[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(bar(2 * PSTAGES + 2 + a), 0));
+            if (MODE == kModeReduceScatter && lane == 0) {
+                const int per = g.tp.ms / BM;
+                const int owner_tile = (rb128 % per) * num_n + (tile % num_n);
+                fence_sys();
+                red_add_sys(g.tp.rs_counters[owner] + owner_tile, 1ull);
+            }
+        }
+    } else {
+        comm_warps<MODE>(g, num_n, s_abort, s_comm_stop);
+    }
+    __syncthreads();
+    cluster_sync();  // the peer's shared memory and TMEM stay valid until both CTAs are done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -383,18 +620,30 @@ bool MakeMap(CUtensorMap* map, const void* base, int rows, int cols, int box_row
 
 template <int MODE>
 cudaError_t LaunchMode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tg, const Args& g, int grid,
-                       cudaStream_t stream) {
-    static bool attr_set[64] = {};
+                       bool pair, cudaStream_t stream) {
+    static bool attr_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(gemm_bf16_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (dev >= 0 && dev < 64 && !attr_set[pair][dev]) {
+        cudaError_t e = pair ? cudaFuncSetAttribute(gemm_bf16_pair_kernel<MODE>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes)
+                             : cudaFuncSetAttribute(gemm_bf16_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    kSmemBytes);
         if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
+        attr_set[pair][dev] = true;
     }
-    gemm_bf16_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tg, g);
+    if (pair) {
+        gemm_bf16_pair_kernel<MODE><<<grid & ~1, kThreads, kPSmemBytes, stream>>>(ta, tb, tg, g);
+    } else {
+        gemm_bf16_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tg, g);
+    }
     return cudaGetLastError();
+}
+
+// 2-SM tiles only with BCCL_GEMM_PAIR=1 (numerically verified, not yet faster than 1-SM tiles).
+bool UsePair() {
+    const char* v = std::getenv("BCCL_GEMM_PAIR");
+    return v != nullptr && v[0] == '1';
 }
 
 int NumSms() {
@@ -415,12 +664,14 @@ cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, 
         return cudaErrorInvalidValue;
     }
     CUtensorMap ta, tb;
-    if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, BN)) return cudaErrorInvalidValue;
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    int grid = std::min(tiles, NumSms());
+    if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, UsePair() ? BM : BN)) return cudaErrorInvalidValue;
+    const bool pair = UsePair();
+    const int tiles = ((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM)) * ((N + BN - 1) / BN);
+    int grid = std::min(pair ? 2 * tiles : tiles, NumSms());
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+    if (pair && grid < 2) grid = 2;
     Args g{static_cast<__nv_bfloat16*>(C), M, N, K, ldc, act, err, TpArgs{}};
-    return LaunchMode<kModePlain>(ta, tb, tb, g, grid, stream);
+    return LaunchMode<kModePlain>(ta, tb, tb, g, grid, pair, stream);
 }
 
 cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, const void* B, void* C, int M, int N,
@@ -431,19 +682,21 @@ cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, 
         return cudaErrorInvalidValue;
     }
     CUtensorMap ta, tb, tg;
-    const int grid = NumSms();
+    const bool pair = UsePair() && tp.ms % (2 * BM) == 0;
+    const int grid = NumSms() & ~1;
     TpArgs t = tp;
     t.contributors = grid;
     Args g{static_cast<__nv_bfloat16*>(C), M, N, K, N, act, err, t};
     if (mode == kModeAllGather) {
-        if (!MakeMap(&ta, A_local, tp.ms, K, BM) || !MakeMap(&tb, B, N, K, BN) || !MakeMap(&tg, A_gathered, M, K, BM)) {
+        if (!MakeMap(&ta, A_local, tp.ms, K, BM) || !MakeMap(&tb, B, N, K, pair ? BM : BN) ||
+            !MakeMap(&tg, A_gathered, M, K, BM)) {
             return cudaErrorInvalidValue;
         }
-        return LaunchMode<kModeAllGather>(ta, tb, tg, g, grid, stream);
+        return LaunchMode<kModeAllGather>(ta, tb, tg, g, grid, pair, stream);
     }
     if (mode == kModeReduceScatter) {
-        if (!MakeMap(&ta, A_local, M, K, BM) || !MakeMap(&tb, B, N, K, BN)) return cudaErrorInvalidValue;
-        return LaunchMode<kModeReduceScatter>(ta, tb, ta, g, grid, stream);
+        if (!MakeMap(&ta, A_local, M, K, BM) || !MakeMap(&tb, B, N, K, pair ? BM : BN)) return cudaErrorInvalidValue;
+        return LaunchMode<kModeReduceScatter>(ta, tb, ta, g, grid, pair, stream);
     }
     return cudaErrorInvalidValue;
 }
