@@ -265,6 +265,8 @@ int bcclTpGemmReduceScatter(bcclComm_t comm, const void* h, const void* w, void*
     return 0;
 }
 
+int bcclGemmUsesPair(void) { return bccl::GemmUsesPair() ? 1 : 0; }
+
 int bcclGemmCheckError(void) {
     int* err = GemmErrWord();
     if (err == nullptr) return -1;

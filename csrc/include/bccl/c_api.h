@@ -90,6 +90,8 @@ long bcclTraceDump(bcclComm_t comm, const char* path);
  * synchronises the current device and returns (and clears) the kernels' error word. */
 int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, void* stream);
 int bcclGemmCheckError(void);
+/* 1 when the GEMMs use 2-SM (cta_group::2) 256x256 tiles, 0 for 1-SM 128x256 tiles. */
+int bcclGemmUsesPair(void);
 
 /* Fused tensor-parallel GEMMs on a device communicator (bf16, one kernel each):
  *   bcclTpAllGatherGemm: y[nranks*ms, n] = act(AllGather(x[ms, k]) * w[n, k]^T)

@@ -36,6 +36,9 @@ struct TpArgs {
 // f32 accumulation in TMEM, bf16 output. act: 0 none, 1 SiLU. *err (device memory) becomes
 // non-zero if a bounded wait inside the kernel gave up. K must be a multiple of 8 (TMA row
 // pitch) and A/B 16-byte aligned; M, N and K need not be multiples of the tile sizes.
+// True when the GEMMs run on 2-SM (cta_group::2) 256x256 tiles instead of 1-SM 128x256 tiles.
+bool GemmUsesPair();
+
 cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, int* err,
                            int max_ctas, cudaStream_t stream);
 

@@ -380,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
 // ---------------------------------------------------------------------------------------
 // 2-SM variant: a CTA pair (cluster of 2) computes a 256x256 tile with tcgen05.mma.cta_group::2.
 // Each CTA TMA-loads its own 128 rows of A and its own 128 rows of B (N/2) into a 6-stage ring
-// and counts the bytes on the leader's full barrier; the leader's single MMA thread reads both
+// and its loads complete on the leader's full barrier, where the leader alone expects both CTAs'
+// bytes; the leader's single MMA thread reads both
 // CTAs' shared memory, and its commits arrive on both CTAs' barriers. Each CTA's TMEM holds its
 // 128 rows x 256 columns of the accumulator, so the epilogue is the same as the 1-SM kernel.
 // Per FLOP this moves a third less data from L2 into shared memory than 128x256 tiles. No load
@@ -409,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PSTAGES; ++s) {
-            mbar_init(bar(s), 2);
+            mbar_init(bar(s), 1);
             mbar_init(bar(PSTAGES + s), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -474,8 +475,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+                    // Only the leader arrives (locally, once for both CTAs' bytes): a remote
+                    // arrive with cluster-scope release per stage costs a memory barrier that
+                    // stalled the producers longer than the MMAs of a stage take.
                     const uint32_t lfull = mapa_shared(bar(s), 0);
-                    mbar_arrive_expect_tx_cluster(lfull, kPStageBytes);
+                    if (leader) mbar_arrive_expect_tx(bar(s), 2 * kPStageBytes);
                     tma_load_2d_pair(smemA(s), amap, lfull, k * BK, arow);
                     tma_load_2d_pair(smemB(s), &tmB, lfull, k * BK, n0);
                 }
@@ -640,10 +644,12 @@ cudaError_t LaunchMode(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return cudaGetLastError();
 }
 
-// 2-SM tiles only with BCCL_GEMM_PAIR=1 (numerically verified, not yet faster than 1-SM tiles).
+// BCCL_GEMM_PAIR=1 forces the 2-SM kernel, =0 the 1-SM kernel; otherwise kPairDefault decides.
+constexpr bool kPairDefault = true;
 bool UsePair() {
     const char* v = std::getenv("BCCL_GEMM_PAIR");
-    return v != nullptr && v[0] == '1';
+    if (v != nullptr && (v[0] == '0' || v[0] == '1')) return v[0] == '1';
+    return kPairDefault;
 }
 
 int NumSms() {
@@ -655,6 +661,8 @@ int NumSms() {
 
 }  // namespace
 }  // namespace gemm
+
+bool GemmUsesPair() { return gemm::UsePair(); }
 
 cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, int* err,
                            int max_ctas, cudaStream_t stream) {

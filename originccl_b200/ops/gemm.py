@@ -41,6 +41,11 @@ def gemm(a, w, activation: Optional[str] = None, out=None):
     return out
 
 
+def kernel_name(m: int = 0) -> str:
+    """Which kernel the GEMMs use: ``"pair_256x256"`` (2-SM, cta_group::2) or ``"single_128x256"``."""
+    return "pair_256x256" if _native.lib().bcclGemmUsesPair() else "single_128x256"
+
+
 def check_error() -> int:
     """Synchronises and returns the GEMM kernels' error word (0 = no bounded wait gave up)."""
     return int(_native.lib().bcclGemmCheckError())

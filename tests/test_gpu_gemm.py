@@ -13,14 +13,18 @@ def _need():
     return gemm
 
 
+@pytest.mark.parametrize("kernel", ["1", "0"], ids=["pair_256x256", "single_128x256"])
 @pytest.mark.parametrize("m,n,k,act", [
     (128, 256, 64, None),        # one tile, one k-block
     (256, 512, 1024, None),      # several tiles and k-blocks
     (300, 200, 136, "silu"),     # ragged M, N and K (TMA zero fill + masked stores)
     (1024, 3584, 2048, "silu"),  # TP up-projection shape (scaled down in K)
+    (384, 256, 64, None),        # an odd number of 2-SM row blocks (the last pair half-empty)
 ])
-def test_gemm_matches_fp32_reference(m, n, k, act):
+def test_gemm_matches_fp32_reference(m, n, k, act, kernel, monkeypatch):
     gemm = _need()
+    monkeypatch.setenv("BCCL_GEMM_PAIR", kernel)
+    assert gemm.kernel_name() == ("pair_256x256" if kernel == "1" else "single_128x256")
     torch.manual_seed(0)
     a = (torch.randn(m, k, device="cuda") * 0.5).bfloat16()
     w = (torch.randn(n, k, device="cuda") * 0.05).bfloat16()
