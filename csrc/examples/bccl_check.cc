@@ -1,0 +1,433 @@
+// bccl_check: a C++ program on the public bccl::Communicator API — the collective and P2P
+// check matrix and the AllReduce benchmark, run under bccl_run.
+//
+//   bccl_run -np 4 bccl_check check                 # host memory (shared memory / TCP)
+//   bccl_run -np 2 --gpus bccl_check check --device # GPU buffers (one GPU per rank)
+//   bccl_run -np 4 bccl_check bench --counts 32768,131072 --warmup 20 --iters 100
+//
+// check: every collective with exact-valued inputs (integers, and floats that are multiples of
+// 1/8), out of place and in place, a sentinel element after every output, nested groups,
+// Send/Recv around the ring and the contract cases (count 0 with null buffers, bad root,
+// null buffer). Rank 0 prints one JSON line: {"passed": P, "failed": F, ...}; exit status is
+// non-zero on any failure.
+// bench: int32 SUM AllReduce with rank r's element i = (r*7 + i) mod 1000 (checked), timed on
+// the host clock between barriers; the time per call is the max over ranks (an AllReduce of
+// the per-rank times with MAX), busbw = algbw * 2(N-1)/N. One JSON line per count.
+//
+// Parity: OriginCCL tests/test_common.cpp (case generator, oracle, sentinel, contract cases)
+// and tests/benchmark/test_allreduce_benchmark.cpp:341-421 (timing as max over ranks).
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "bccl/communicator.h"
+
+using bccl::Communicator;
+using bccl::DataType;
+using bccl::ReduceOp;
+
+namespace {
+
+int EnvInt(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return v ? std::atoi(v) : dflt;
+}
+
+bool ExchangeId(int rank, bccl::UniqueId* id, Communicator* comm) {
+    const char* path = std::getenv("BCCL_ID_FILE");
+    if (path == nullptr) {
+        std::fprintf(stderr, "BCCL_ID_FILE is not set (run under bccl_run)\n");
+        return false;
+    }
+    if (rank == 0) {
+        if (!comm->GetUniqueId(*id)) return false;
+        std::string tmp = std::string(path) + ".tmp";
+        {
+            std::ofstream f(tmp);
+            f << id->ip_addr << ":" << id->port;
+        }
+        return std::rename(tmp.c_str(), path) == 0;
+    }
+    auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    while (access(path, R_OK) != 0) {
+        if (std::chrono::steady_clock::now() > deadline) return false;
+        std::this_thread::sleep_for(std::chrono::milliseconds(5));
+    }
+    std::ifstream f(path);
+    std::string s;
+    f >> s;
+    size_t colon = s.rfind(':');
+    if (colon == std::string::npos) return false;
+    std::snprintf(id->ip_addr, sizeof(id->ip_addr), "%s", s.substr(0, colon).c_str());
+    id->port = static_cast<uint16_t>(std::atoi(s.substr(colon + 1).c_str()));
+    return true;
+}
+
+// Buffers live on the host or on the GPU; values are staged through host vectors.
+struct Mem {
+    bool device = false;
+    void* Alloc(size_t bytes) {
+        void* p = nullptr;
+        if (device) {
+            if (cudaMalloc(&p, std::max<size_t>(bytes, 16)) != cudaSuccess) return nullptr;
+        } else {
+            p = std::malloc(std::max<size_t>(bytes, 16));
+        }
+        return p;
+    }
+    void Free(void* p) {
+        if (device) cudaFree(p); else std::free(p);
+    }
+    void Put(void* dst, const void* src, size_t bytes) {
+        if (device) cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice); else std::memcpy(dst, src, bytes);
+    }
+    void Get(void* dst, const void* src, size_t bytes) {
+        if (device) cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost); else std::memcpy(dst, src, bytes);
+    }
+};
+
+template <typename T>
+T Value(int rank, size_t i) {
+    long v = static_cast<long>((rank * 7 + i * 13) % 97) - 48;  // small integers
+    if (std::is_floating_point<T>::value) return static_cast<T>(v / 8.0);
+    return static_cast<T>(v);
+}
+
+template <typename T>
+T Reduce(ReduceOp op, const std::vector<T>& xs, int n) {
+    double acc = xs[0];
+    for (size_t r = 1; r < xs.size(); ++r) {
+        if (op == ReduceOp::MAX) acc = std::max<double>(acc, xs[r]);
+        else if (op == ReduceOp::MIN) acc = std::min<double>(acc, xs[r]);
+        else acc += xs[r];
+    }
+    if (op == ReduceOp::AVG) acc = std::is_floating_point<T>::value ? acc / n : std::trunc(acc / n);
+    return static_cast<T>(acc);
+}
+
+struct Checker {
+    Communicator* comm;
+    Mem mem;
+    int rank, world;
+    int passed = 0, failed = 0;
+    std::vector<std::string> failures;
+
+    void Record(bool ok, const std::string& what) {
+        if (ok) {
+            ++passed;
+        } else {
+            ++failed;
+            if (failures.size() < 8) failures.push_back(what);
+        }
+    }
+
+    template <typename T>
+    void AllReduce(DataType dt, ReduceOp op, size_t n, bool in_place) {
+        std::vector<T> in(n), out(n + 1);
+        for (size_t i = 0; i < n; ++i) in[i] = Value<T>(rank, i);
+        void* s = mem.Alloc(n * sizeof(T));
+        void* d = in_place ? s : mem.Alloc((n + 1) * sizeof(T));
+        T sentinel = static_cast<T>(77);
+        std::vector<T> init(n + 1, sentinel);
+        if (!in_place) mem.Put(d, init.data(), (n + 1) * sizeof(T));
+        mem.Put(s, in.data(), n * sizeof(T));
+        bool ok = comm->AllReduce(s, d, n, dt, op);
+        mem.Get(out.data(), d, (in_place ? n : n + 1) * sizeof(T));
+        for (size_t i = 0; ok && i < n; ++i) {
+            std::vector<T> xs(world);
+            for (int r = 0; r < world; ++r) xs[r] = Value<T>(r, i);
+            ok = out[i] == Reduce<T>(op, xs, world);
+        }
+        if (ok && !in_place) ok = out[n] == sentinel;
+        if (ok && !in_place) {  // the input must come back unchanged
+            std::vector<T> back(n);
+            mem.Get(back.data(), s, n * sizeof(T));
+            ok = back == in;
+        }
+        Record(ok, "allreduce n=" + std::to_string(n) + " op=" + std::to_string(static_cast<int>(op)) +
+                       (in_place ? " in-place" : ""));
+        if (!in_place) mem.Free(d);
+        mem.Free(s);
+    }
+
+    void Broadcast(size_t n, int root) {
+        std::vector<float> buf(n);
+        for (size_t i = 0; i < n; ++i) buf[i] = rank == root ? Value<float>(root, i) : -1.0f;
+        void* b = mem.Alloc(n * sizeof(float));
+        mem.Put(b, buf.data(), n * sizeof(float));
+        bool ok = comm->Broadcast(b, n, DataType::FLOAT32, root);
+        mem.Get(buf.data(), b, n * sizeof(float));
+        for (size_t i = 0; ok && i < n; ++i) ok = buf[i] == Value<float>(root, i);
+        Record(ok, "broadcast n=" + std::to_string(n));
+        mem.Free(b);
+    }
+
+    void ReduceTo(size_t n, int root, ReduceOp op) {
+        std::vector<float> in(n), out(n, -5.0f);
+        for (size_t i = 0; i < n; ++i) in[i] = Value<float>(rank, i);
+        void* s = mem.Alloc(n * sizeof(float));
+        void* d = rank == root ? mem.Alloc(n * sizeof(float)) : nullptr;  // non-roots may pass null
+        mem.Put(s, in.data(), n * sizeof(float));
+        bool ok = comm->Reduce(s, d, n, DataType::FLOAT32, op, root);
+        if (rank == root) {
+            mem.Get(out.data(), d, n * sizeof(float));
+            for (size_t i = 0; ok && i < n; ++i) {
+                std::vector<float> xs(world);
+                for (int r = 0; r < world; ++r) xs[r] = Value<float>(r, i);
+                ok = out[i] == Reduce<float>(op, xs, world);
+            }
+            mem.Free(d);
+        }
+        Record(ok, "reduce n=" + std::to_string(n));
+        mem.Free(s);
+    }
+
+    void AllGather(size_t n) {
+        std::vector<int> in(n), out(n * world + 1, 77);
+        for (size_t i = 0; i < n; ++i) in[i] = Value<int>(rank, i);
+        void* s = mem.Alloc(n * sizeof(int));
+        void* d = mem.Alloc((n * world + 1) * sizeof(int));
+        mem.Put(s, in.data(), n * sizeof(int));
+        mem.Put(d, out.data(), out.size() * sizeof(int));
+        bool ok = comm->AllGather(s, d, n, DataType::INT32);
+        mem.Get(out.data(), d, out.size() * sizeof(int));
+        for (int r = 0; ok && r < world; ++r)
+            for (size_t i = 0; ok && i < n; ++i) ok = out[r * n + i] == Value<int>(r, i);
+        ok = ok && out[n * world] == 77;
+        Record(ok, "allgather n=" + std::to_string(n));
+        mem.Free(s);
+        mem.Free(d);
+    }
+
+    void ReduceScatter(size_t n) {
+        std::vector<int> in(n * world), out(n + 1, 77);
+        for (size_t i = 0; i < n * world; ++i) in[i] = Value<int>(rank, i);
+        void* s = mem.Alloc(in.size() * sizeof(int));
+        void* d = mem.Alloc((n + 1) * sizeof(int));
+        mem.Put(s, in.data(), in.size() * sizeof(int));
+        mem.Put(d, out.data(), out.size() * sizeof(int));
+        bool ok = comm->ReduceScatter(s, d, n, DataType::INT32, ReduceOp::SUM);
+        mem.Get(out.data(), d, out.size() * sizeof(int));
+        for (size_t i = 0; ok && i < n; ++i) {
+            int want = 0;
+            for (int r = 0; r < world; ++r) want += Value<int>(r, rank * n + i);
+            ok = out[i] == want;
+        }
+        ok = ok && out[n] == 77;
+        Record(ok, "reducescatter n=" + std::to_string(n));
+        mem.Free(s);
+        mem.Free(d);
+    }
+
+    // A nested group of four independent collectives; only the outer GroupEnd runs them.
+    void Group(size_t n) {
+        std::vector<void*> bufs;
+        std::vector<std::vector<float>> host(4, std::vector<float>(n));
+        for (int k = 0; k < 4; ++k) {
+            for (size_t i = 0; i < n; ++i) host[k][i] = Value<float>(rank + k, i);
+            void* b = mem.Alloc(n * sizeof(float));
+            mem.Put(b, host[k].data(), n * sizeof(float));
+            bufs.push_back(b);
+        }
+        comm->GroupStart();
+        comm->GroupStart();
+        bool ok = comm->AllReduce(bufs[0], bufs[0], n, DataType::FLOAT32, ReduceOp::SUM);
+        ok = ok && comm->AllReduce(bufs[1], bufs[1], n, DataType::FLOAT32, ReduceOp::MAX);
+        ok = ok && comm->GroupEnd();  // inner: must not execute
+        ok = ok && comm->AllReduce(bufs[2], bufs[2], n, DataType::FLOAT32, ReduceOp::MIN);
+        ok = ok && comm->Broadcast(bufs[3], n, DataType::FLOAT32, 0);
+        ok = comm->GroupEnd() && ok;
+        const ReduceOp ops[3] = {ReduceOp::SUM, ReduceOp::MAX, ReduceOp::MIN};
+        for (int k = 0; ok && k < 4; ++k) {
+            std::vector<float> out(n);
+            mem.Get(out.data(), bufs[k], n * sizeof(float));
+            for (size_t i = 0; ok && i < n; ++i) {
+                float want;
+                if (k < 3) {
+                    std::vector<float> xs(world);
+                    for (int r = 0; r < world; ++r) xs[r] = Value<float>(r + k, i);
+                    want = Reduce<float>(ops[k], xs, world);
+                } else {
+                    want = Value<float>(0 + k, i);
+                }
+                ok = out[i] == want;
+            }
+        }
+        Record(ok, "nested group n=" + std::to_string(n));
+        for (void* b : bufs) mem.Free(b);
+    }
+
+    void SendRecvRing(size_t n) {
+        if (world < 2) return;
+        const int next = (rank + 1) % world, prev = (rank + world - 1) % world;
+        std::vector<int> out(n), in(n, -1);
+        for (size_t i = 0; i < n; ++i) out[i] = Value<int>(rank, i);
+        void* s = mem.Alloc(n * sizeof(int));
+        void* d = mem.Alloc(n * sizeof(int));
+        mem.Put(s, out.data(), n * sizeof(int));
+        comm->GroupStart();
+        bool ok = comm->Send(s, n, DataType::INT32, next);
+        ok = ok && comm->Recv(d, n, DataType::INT32, prev);
+        ok = comm->GroupEnd() && ok;
+        mem.Get(in.data(), d, n * sizeof(int));
+        for (size_t i = 0; ok && i < n; ++i) ok = in[i] == Value<int>(prev, i);
+        Record(ok, "send/recv ring n=" + std::to_string(n));
+        mem.Free(s);
+        mem.Free(d);
+    }
+
+    void Contract() {
+        Record(comm->AllReduce(nullptr, nullptr, 0, DataType::FLOAT32, ReduceOp::SUM), "count 0 with null buffers");
+        void* b = mem.Alloc(64);
+        Record(!comm->Broadcast(b, 4, DataType::FLOAT32, world), "bad root rejected");
+        Record(!comm->AllReduce(nullptr, b, 4, DataType::FLOAT32, ReduceOp::SUM), "null send buffer rejected");
+        Record(!comm->Send(b, 4, DataType::FLOAT32, rank), "send to self rejected");
+        comm->GroupStart();
+        Record(!comm->Reduce(b, b, 4, DataType::FLOAT32, ReduceOp::SUM, -1), "bad root rejected inside a group");
+        Record(comm->GroupEnd(), "group with only rejected work ends cleanly");
+        mem.Free(b);
+    }
+};
+
+std::vector<size_t> ParseCounts(const std::string& s) {
+    std::vector<size_t> out;
+    std::stringstream ss(s);
+    std::string tok;
+    while (std::getline(ss, tok, ',')) out.push_back(static_cast<size_t>(std::atoll(tok.c_str())));
+    return out;
+}
+
+int RunBench(Communicator* comm, Mem mem, int rank, int world, const std::vector<size_t>& counts, int warmup,
+             int iters) {
+    int rc = 0;
+    for (size_t n : counts) {
+        std::vector<int> in(n), out(n);
+        for (size_t i = 0; i < n; ++i) in[i] = static_cast<int>((rank * 7 + i) % 1000);
+        void* s = mem.Alloc(n * sizeof(int));
+        void* d = mem.Alloc(n * sizeof(int));
+        mem.Put(s, in.data(), n * sizeof(int));
+        bool ok = true;
+        for (int w = 0; w < warmup && ok; ++w) ok = comm->AllReduce(s, d, n, DataType::INT32, ReduceOp::SUM);
+        mem.Get(out.data(), d, n * sizeof(int));
+        for (size_t i = 0; ok && i < n; ++i) {
+            long want = 0;
+            for (int r = 0; r < world; ++r) want += static_cast<long>((r * 7 + i) % 1000);
+            ok = out[i] == want;
+        }
+        ok = ok && comm->Barrier();
+        auto t0 = std::chrono::steady_clock::now();
+        for (int it = 0; it < iters && ok; ++it) ok = comm->AllReduce(s, d, n, DataType::INT32, ReduceOp::SUM);
+        double us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count() / iters;
+        double tmax = us;
+        void* tb = mem.Alloc(sizeof(double));
+        mem.Put(tb, &us, sizeof(double));
+        ok = ok && comm->AllReduce(tb, tb, 1, DataType::FLOAT64, ReduceOp::MAX);
+        mem.Get(&tmax, tb, sizeof(double));
+        mem.Free(tb);
+        const double bytes = static_cast<double>(n) * sizeof(int);
+        const double algbw = bytes / tmax / 1e3;  // GB/s
+        const double busbw = world > 1 ? algbw * 2.0 * (world - 1) / world : algbw;
+        if (rank == 0) {
+            std::printf("{\"op\": \"allreduce\", \"dtype\": \"int32\", \"path\": \"%s\", \"ranks\": %d, "
+                        "\"count\": %zu, \"bytes\": %.0f, \"time_us\": %.2f, \"algbw_gbs\": %.3f, "
+                        "\"busbw_gbs\": %.3f, \"check\": %s, \"warmup\": %d, \"iters\": %d}\n",
+                        mem.device ? "device" : "host", world, n, bytes, tmax, algbw, busbw, ok ? "true" : "false",
+                        warmup, iters);
+            std::fflush(stdout);
+        }
+        rc |= ok ? 0 : 1;
+        mem.Free(s);
+        mem.Free(d);
+    }
+    return rc;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    std::string mode = argc > 1 ? argv[1] : "check";
+    bool device = false;
+    std::vector<size_t> counts = {32768, 131072};
+    int warmup = 20, iters = 100, channels = 0;
+    for (int i = 2; i < argc; ++i) {
+        std::string a = argv[i];
+        if (a == "--device") device = true;
+        else if (a == "--counts" && i + 1 < argc) counts = ParseCounts(argv[++i]);
+        else if (a == "--warmup" && i + 1 < argc) warmup = std::atoi(argv[++i]);
+        else if (a == "--iters" && i + 1 < argc) iters = std::atoi(argv[++i]);
+        else if (a == "--channels" && i + 1 < argc) channels = std::atoi(argv[++i]);
+    }
+    const int rank = EnvInt("BCCL_RANK", 0), world = EnvInt("BCCL_WORLD_SIZE", 1);
+    Communicator comm;
+    bccl::CommConfig cfg;
+    cfg.rank = rank;
+    cfg.world_size = world;
+    cfg.n_channels = channels;
+    if (device) {
+        cfg.device = EnvInt("BCCL_DEVICE", EnvInt("BCCL_LOCAL_RANK", rank));
+        if (cudaSetDevice(cfg.device) != cudaSuccess) {
+            std::fprintf(stderr, "rank %d: no CUDA device %d\n", rank, cfg.device);
+            return 3;
+        }
+    }
+    if (!ExchangeId(rank, &cfg.unique_id, &comm) || !comm.Init(cfg)) {
+        std::fprintf(stderr, "rank %d: init failed\n", rank);
+        return 1;
+    }
+    Mem mem;
+    mem.device = device;
+    int rc = 0;
+    if (mode == "bench") {
+        rc = RunBench(&comm, mem, rank, world, counts, warmup, iters);
+    } else {
+        Checker c{&comm, mem, rank, world};
+        for (size_t n : {size_t(1), size_t(1000), size_t(32768 + 3)}) {
+            for (ReduceOp op : {ReduceOp::SUM, ReduceOp::MAX, ReduceOp::MIN, ReduceOp::AVG}) {
+                c.AllReduce<int>(DataType::INT32, op, n, false);
+                c.AllReduce<float>(DataType::FLOAT32, op, n, false);
+            }
+            c.AllReduce<double>(DataType::FLOAT64, ReduceOp::SUM, n, true);
+            c.AllReduce<long long>(DataType::INT64, ReduceOp::MAX, n, true);
+            c.Broadcast(n, world - 1);
+            c.ReduceTo(n, 1 % world, ReduceOp::SUM);
+            c.ReduceTo(n, 0, ReduceOp::MAX);
+            c.AllGather(n);
+            c.ReduceScatter(n);
+            c.Group(n);
+            c.SendRecvRing(n);
+        }
+        c.Contract();
+        int fails = c.failed, total_fail = 0;
+        void* fb = mem.Alloc(sizeof(int));
+        mem.Put(fb, &fails, sizeof(int));
+        if (!comm.AllReduce(fb, fb, 1, DataType::INT32, ReduceOp::SUM)) fails = -1;
+        mem.Get(&total_fail, fb, sizeof(int));
+        mem.Free(fb);
+        if (fails < 0) total_fail = world;
+        if (rank == 0) {
+            std::printf("{\"passed\": %d, \"failed\": %d, \"failed_all_ranks\": %d, \"ranks\": %d, \"path\": \"%s\"",
+                        c.passed, c.failed, total_fail, world, device ? "device" : "host");
+            std::printf(", \"failures\": [");
+            for (size_t i = 0; i < c.failures.size(); ++i)
+                std::printf("%s\"%s\"", i ? ", " : "", c.failures[i].c_str());
+            std::printf("]}\n");
+        } else if (c.failed) {
+            for (const std::string& f : c.failures) std::fprintf(stderr, "rank %d: FAILED %s\n", rank, f.c_str());
+        }
+        rc = total_fail == 0 ? 0 : 1;
+    }
+    comm.Finalize();
+    return rc;
+}

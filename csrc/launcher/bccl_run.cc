@@ -1,0 +1,170 @@
+// bccl_run: starts N ranks of a program on this machine, without MPI.
+//
+//   bccl_run -np 4 [--timeout SEC] [--id-file PATH] [--gpus] -- ./program args...
+//
+// Each child gets BCCL_RANK, BCCL_WORLD_SIZE, BCCL_LOCAL_RANK, BCCL_LOCAL_SIZE and BCCL_ID_FILE
+// (a fresh path in a private temp directory unless --id-file is given). Rank 0 creates the unique
+// id with Communicator::GetUniqueId and writes "ip:port" to that file (write to PATH.tmp, then
+// rename); the others wait for it. With --gpus, BCCL_DEVICE=<local rank> is exported too.
+// The launcher forwards SIGINT/SIGTERM to every child, and when one child fails (non-zero exit
+// or a signal) or the timeout expires it terminates the others (SIGTERM, then SIGKILL after 5 s)
+// and exits with the first failure's code. All children run in one process group of their own.
+//
+// Parity: the reference's tests are launched by `mpirun -np N` and broadcast the unique id with
+// MPI_Bcast (OriginCCL tests/test_common.cpp:465-477); MPI is not part of this library.
+#include <signal.h>
+#include <sys/stat.h>
+#include <sys/types.h>
+#include <sys/wait.h>
+#include <unistd.h>
+
+#include <cerrno>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace {
+
+volatile sig_atomic_t g_signal = 0;
+
+void OnSignal(int sig) { g_signal = sig; }
+
+int Usage() {
+    std::fprintf(stderr,
+                 "usage: bccl_run -np N [--timeout SEC] [--id-file PATH] [--gpus] -- program [args...]\n");
+    return 2;
+}
+
+// Signals the ranks' process group (which also reaches the ranks' own children), then any
+// rank that is not done in case it moved to another group.
+void KillAll(pid_t group, const std::vector<pid_t>& pids, const std::vector<bool>& done, int sig) {
+    if (group > 0) kill(-group, sig);
+    for (size_t i = 0; i < pids.size(); ++i)
+        if (!done[i]) kill(pids[i], sig);
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    int np = 0;
+    double timeout_s = 0;
+    bool gpus = false;
+    std::string id_file;
+    int i = 1;
+    for (; i < argc; ++i) {
+        std::string a = argv[i];
+        if (a == "--") {
+            ++i;
+            break;
+        }
+        if ((a == "-np" || a == "-n") && i + 1 < argc) {
+            np = std::atoi(argv[++i]);
+        } else if (a == "--timeout" && i + 1 < argc) {
+            timeout_s = std::atof(argv[++i]);
+        } else if (a == "--id-file" && i + 1 < argc) {
+            id_file = argv[++i];
+        } else if (a == "--gpus") {
+            gpus = true;
+        } else if (a[0] != '-') {
+            break;  // program without a "--" separator
+        } else {
+            return Usage();
+        }
+    }
+    if (np < 1 || i >= argc) return Usage();
+    char** prog = argv + i;
+
+    std::string tmpdir;
+    if (id_file.empty()) {
+        char tmpl[] = "/tmp/bccl_run.XXXXXX";
+        if (mkdtemp(tmpl) == nullptr) {
+            std::perror("bccl_run: mkdtemp");
+            return 1;
+        }
+        tmpdir = tmpl;
+        id_file = tmpdir + "/unique_id";
+    } else {
+        unlink(id_file.c_str());
+    }
+
+    struct sigaction sa;
+    std::memset(&sa, 0, sizeof(sa));
+    sa.sa_handler = OnSignal;
+    sigaction(SIGINT, &sa, nullptr);
+    sigaction(SIGTERM, &sa, nullptr);
+
+    std::vector<pid_t> pids(np, -1);
+    pid_t group = 0;
+    for (int r = 0; r < np; ++r) {
+        pid_t pid = fork();
+        if (pid < 0) {
+            std::perror("bccl_run: fork");
+            return 1;
+        }
+        if (pid == 0) {
+            setpgid(0, group);
+            setenv("BCCL_RANK", std::to_string(r).c_str(), 1);
+            setenv("BCCL_WORLD_SIZE", std::to_string(np).c_str(), 1);
+            setenv("BCCL_LOCAL_RANK", std::to_string(r).c_str(), 1);
+            setenv("BCCL_LOCAL_SIZE", std::to_string(np).c_str(), 1);
+            setenv("BCCL_ID_FILE", id_file.c_str(), 1);
+            if (gpus) setenv("BCCL_DEVICE", std::to_string(r).c_str(), 1);
+            execvp(prog[0], prog);
+            std::fprintf(stderr, "bccl_run: exec %s: %s\n", prog[0], std::strerror(errno));
+            _exit(127);
+        }
+        if (group == 0) group = pid;
+        setpgid(pid, group);
+        pids[r] = pid;
+    }
+
+    std::vector<bool> done(np, false);
+    int remaining = np, first_fail = 0;
+    bool terminating = false;
+    auto t0 = std::chrono::steady_clock::now();
+    auto term_at = t0;
+    bool killed = false;
+    while (remaining > 0) {
+        int status = 0;
+        pid_t pid = waitpid(-1, &status, WNOHANG);
+        if (pid > 0) {
+            for (int r = 0; r < np; ++r) {
+                if (pids[r] != pid) continue;
+                done[r] = true;
+                --remaining;
+                int code = WIFEXITED(status) ? WEXITSTATUS(status) : 128 + WTERMSIG(status);
+                if (code != 0 && first_fail == 0 && !terminating) {
+                    first_fail = code;
+                    std::fprintf(stderr, "bccl_run: rank %d exited with %d; stopping the others\n", r, code);
+                }
+            }
+            continue;
+        }
+        const double elapsed = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (!terminating && (first_fail != 0 || g_signal != 0 || (timeout_s > 0 && elapsed > timeout_s))) {
+            if (first_fail == 0) {
+                first_fail = g_signal != 0 ? 128 + g_signal : 124;
+                std::fprintf(stderr, "bccl_run: %s; stopping all ranks\n", g_signal ? "signal" : "timeout");
+            }
+            terminating = true;
+            term_at = std::chrono::steady_clock::now();
+            KillAll(group, pids, done, SIGTERM);
+        }
+        if (terminating && !killed && std::chrono::steady_clock::now() - term_at > std::chrono::seconds(5)) {
+            KillAll(group, pids, done, SIGKILL);
+            killed = true;
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(5));
+    }
+    if (terminating || first_fail != 0) kill(-group, SIGKILL);  // leftovers of failed ranks
+    if (!tmpdir.empty()) {
+        unlink(id_file.c_str());
+        unlink((id_file + ".tmp").c_str());
+        rmdir(tmpdir.c_str());
+    }
+    return first_fail;
+}

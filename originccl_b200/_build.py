@@ -39,7 +39,7 @@ def cutlass_include() -> Path | None:
 
 
 def _sources() -> tuple[list[Path], list[Path]]:
-    cc = sorted(p for p in CSRC.rglob("*.cc") if "tools" not in p.parts)
+    cc = sorted(p for p in CSRC.rglob("*.cc") if not {"launcher", "examples"} & set(p.parts))
     cu = sorted(CSRC.rglob("*.cu"))
     return cc, cu
 
@@ -75,11 +75,13 @@ def _ninja_file() -> str:
         "rule linkexe",
         "  command = $cxx -o $out $in -lpthread",
         "  description = LINK $out",
+        "rule linkexample",
+        f"  command = $cxx -o $out $in -L{LIBDIR} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} -lcudart "
+        f"-Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread",
+        "  description = LINK $out",
     ]
     objs = []
     for src in cc:
-        if src.parent.name == "tools":
-            continue
         obj = BUILD / (str(src.relative_to(CSRC)).replace("/", "_") + ".o")
         lines.append(f"build {obj}: cxx {src}")
         objs.append(obj)
@@ -88,11 +90,14 @@ def _ninja_file() -> str:
         lines.append(f"build {obj}: nvcc {src}")
         objs.append(obj)
     lines.append(f"build {LIBDIR / 'libbccl.so'}: link {' '.join(map(str, objs))}")
-    launcher = CSRC / "tools" / "bccl_run.cc"
-    if launcher.exists():
-        lobj = BUILD / "tools_bccl_run.cc.o"
-        lines.append(f"build {lobj}: cxx {launcher}")
-        lines.append(f"build {LIBDIR / 'bccl_run'}: linkexe {lobj}")
+    launcher = CSRC / "launcher" / "bccl_run.cc"
+    lobj = BUILD / "launcher_bccl_run.cc.o"
+    lines.append(f"build {lobj}: cxx {launcher}")
+    lines.append(f"build {LIBDIR / 'bccl_run'}: linkexe {lobj}")
+    for ex in sorted((CSRC / "examples").glob("*.cc")):
+        eobj = BUILD / f"examples_{ex.name}.o"
+        lines.append(f"build {eobj}: cxx {ex}")
+        lines.append(f"build {LIBDIR / ex.stem}: linkexample {eobj} | {LIBDIR / 'libbccl.so'}")
     return "\n".join(lines) + "\n"
 
 

@@ -402,6 +402,8 @@ def init_from_env(**kwargs) -> Communicator:
     """
     if "BCCL_RANK" in os.environ:
         rank, world = int(os.environ["BCCL_RANK"]), int(os.environ["BCCL_WORLD_SIZE"])
+        if "device" not in kwargs and "BCCL_DEVICE" in os.environ:  # bccl_run --gpus
+            kwargs["device"] = int(os.environ["BCCL_DEVICE"])
         path = os.environ["BCCL_ID_FILE"]
         comm = Communicator()
         if rank == 0:

@@ -1,0 +1,74 @@
+"""The C++ API end to end: the bccl_run launcher starting ranks of the bccl_check program
+(csrc/examples/bccl_check.cc), which uses bccl::Communicator directly (no Python in the ranks)."""
+import json
+import os
+import subprocess
+import time
+
+import pytest
+
+LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "originccl_b200", "_lib")
+RUN = os.path.join(LIB, "bccl_run")
+CHECK = os.path.join(LIB, "bccl_check")
+
+
+def _need_binaries():
+    if not (os.path.exists(RUN) and os.path.exists(CHECK)):
+        from originccl_b200 import _build
+        _build.build()
+
+
+def _run(args, timeout=180):
+    _need_binaries()
+    return subprocess.run([RUN] + args, capture_output=True, text=True, timeout=timeout)
+
+
+def _json_lines(out):
+    return [json.loads(line) for line in out.splitlines() if line.startswith("{")]
+
+
+@pytest.mark.parametrize("np_", [1, 2, 4])
+def test_cpp_check_matrix_host(np_):
+    r = _run(["-np", str(np_), "--timeout", "150", "--", CHECK, "check"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    res = _json_lines(r.stdout)[-1]
+    assert res["failed_all_ranks"] == 0 and res["passed"] >= 50 and res["ranks"] == np_
+
+
+def test_cpp_int32_allreduce_bench_host():
+    r = _run(["-np", "4", "--timeout", "150", "--", CHECK, "bench", "--counts", "32768,131072", "--warmup", "3",
+              "--iters", "10"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    recs = _json_lines(r.stdout)
+    assert [x["count"] for x in recs] == [32768, 131072]
+    assert all(x["check"] and x["busbw_gbs"] > 0 for x in recs)
+
+
+def test_launcher_stops_all_ranks_when_one_fails():
+    t0 = time.time()
+    r = _run(["-np", "3", "--", "sh", "-c", 'if [ "$BCCL_RANK" = 1 ]; then exit 7; fi; sleep 60'], timeout=60)
+    assert r.returncode == 7
+    assert time.time() - t0 < 30
+    assert "rank 1 exited with 7" in r.stderr
+
+
+def test_launcher_exports_rank_environment():
+    r = _run(["-np", "2", "--", "sh", "-c", 'echo "$BCCL_RANK/$BCCL_WORLD_SIZE/$BCCL_LOCAL_RANK ${BCCL_ID_FILE:+id}"'])
+    assert r.returncode == 0
+    assert sorted(r.stdout.split("\n")[:2]) == ["0/2/0 id", "1/2/1 id"]
+
+
+def test_launcher_timeout():
+    r = _run(["-np", "2", "--timeout", "1", "--", "sleep", "30"], timeout=60)
+    assert r.returncode == 124
+
+
+@pytest.mark.gpu
+def test_cpp_check_matrix_device_one_gpu():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    r = _run(["-np", "1", "--gpus", "--timeout", "150", "--", CHECK, "check", "--device"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    res = _json_lines(r.stdout)[-1]
+    assert res["failed_all_ranks"] == 0 and res["path"] == "device"
