@@ -1,5 +1,7 @@
 #include "bccl/communicator.h"
 
+#include <cstdio>
+
 #include <unistd.h>
 
 #include <algorithm>
@@ -10,6 +12,7 @@
 #include "core/env.h"
 #include "core/fdpass.h"
 #include "core/logger.h"
+#include "core/nvtx.h"
 #include "core/net.h"
 #include "core/planner.h"
 #include "device/device_engine.h"
@@ -247,6 +250,13 @@ bool Communicator::Flush() {
         return false;
     }
     if (!planner_->SortTasks(tasks, config_.rank, config_.world_size)) return false;
+    char range[48];
+    if (tasks.size() == 1) {
+        std::snprintf(range, sizeof(range), "bccl:%s", CollFuncName(tasks[0].func));
+    } else {
+        std::snprintf(range, sizeof(range), "bccl:group(%zu)", tasks.size());
+    }
+    NvtxRange nvtx(range);
     bool ok;
     if (device_) {
         cudaStream_t s = static_cast<cudaStream_t>(has_user_stream_ ? user_stream_ : device_->internal_stream());

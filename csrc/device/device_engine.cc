@@ -6,6 +6,7 @@
 #include "core/bootstrap.h"
 #include "core/env.h"
 #include "core/logger.h"
+#include "core/nvtx.h"
 #include <cuda_bf16.h>
 
 #include "kernels/gemm.h"
@@ -201,6 +202,7 @@ constexpr size_t kRsCountersOff = 16u << 10; // [own tiles] (<= 16K tiles)
 bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, int ms, int k, int n, int act,
                                    cudaStream_t stream) {
     if (!inited_) return false;
+    NvtxRange nvtx("bccl:AllGatherGemm");
     cudaSetDevice(device_);
     if (tp_err_ == nullptr) {
         CUDA_OK(cudaMalloc(&tp_err_, sizeof(int)), "cudaMalloc(tp err)");
@@ -236,6 +238,7 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
 bool DeviceEngine::TpGemmReduceScatter(const void* h, const void* w, void* out, int ms, int k, int n,
                                        cudaStream_t stream) {
     if (!inited_) return false;
+    NvtxRange nvtx("bccl:GemmReduceScatter");
     cudaSetDevice(device_);
     if (tp_err_ == nullptr) {
         CUDA_OK(cudaMalloc(&tp_err_, sizeof(int)), "cudaMalloc(tp err)");

@@ -9,7 +9,9 @@ Parity: the reference's AllReduce benchmark (OriginCCL tests/benchmark/test_allr
 113-421) sweeps sizes by a factor, validates, and reports busbw = algbw * 2(N-1)/N with the time
 taken as the max over ranks. Here every size is timed on the device with CUDA events (warm-up,
 then ``iters`` calls between barriers + synchronize), the max over ranks is reported, and the
-same buffers are timed through NCCL for comparison. Rank 0 prints one JSON line per size.
+same buffers are timed through NCCL for comparison. Before timing, every size is checked once
+against an fp64 reduction of the same inputs (``check`` in the record). Inputs are uniform in
+[-1, 1] from seed 1234+rank. Rank 0 prints one JSON line per size.
 """
 from __future__ import annotations
 
@@ -29,17 +31,155 @@ def parse_size(s: str) -> int:
     return int(float(s) * mult)
 
 
+def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, factor: int = 2, warmup: int = 20,
+              iters: int = 100, algo: str = "auto", inplace: bool = False, nccl: bool = True, redop: str = "sum",
+              seed: int = 1234, emit=print) -> list:
+    """Times ``op`` at every size from min_bytes to max_bytes (x factor) with this library and
+    with NCCL on the same buffers; returns (and emits on rank 0) one record per size."""
+    import torch
+    import torch.distributed as dist
+    from originccl_b200 import Algo, ReduceOp
+    from originccl_b200.utils.timing import busbw_factor
+
+    rank, world, local = comm.rank, comm.world_size, comm.device
+    dt = getattr(torch, dtype)
+    es = torch.empty((), dtype=dt).element_size()
+    algo_v = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS,
+              "ring": Algo.RING}[algo]
+    rop = {"sum": ReduceOp.SUM, "max": ReduceOp.MAX, "min": ReduceOp.MIN, "avg": ReduceOp.AVG}[redop]
+    nccl_op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
+               "avg": dist.ReduceOp.AVG}[redop]
+    barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
+
+    def timed(fn) -> float:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / iters], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) * 1e3  # microseconds
+
+    out = []
+    size = max(min_bytes, es)
+    g = torch.Generator(device="cuda").manual_seed(seed + rank)
+    while size <= max_bytes:
+        n = max(1, size // es)
+        # Per-rank payload convention (as nccl-tests): allreduce/broadcast/reduce move n elements;
+        # allgather gathers n per rank; reducescatter scatters n per rank (input world*n).
+        if op == "reducescatter":
+            x = (torch.rand(n * world, device="cuda", generator=g) * 2 - 1).to(dt)
+            y = torch.empty(n, device="cuda", dtype=dt)
+        elif op == "allgather":
+            x = (torch.rand(n, device="cuda", generator=g) * 2 - 1).to(dt)
+            y = torch.empty(n * world, device="cuda", dtype=dt)
+        else:
+            x = (torch.rand(n, device="cuda", generator=g) * 2 - 1).to(dt)
+            y = x if inplace else torch.empty_like(x)
+        if op == "allreduce":
+            ours = lambda: comm.all_reduce(x, rop, out=y, algo=algo_v)  # noqa: E731
+            ref = lambda: dist.all_reduce(y, op=nccl_op)  # noqa: E731
+            nbytes = n * es
+        elif op == "allgather":
+            ours = lambda: comm.all_gather(y, x)  # noqa: E731
+            ref = lambda: dist.all_gather_into_tensor(y, x)  # noqa: E731
+            nbytes = n * es * world
+        elif op == "reducescatter":
+            ours = lambda: comm.reduce_scatter(y, x, rop)  # noqa: E731
+            ref = lambda: dist.reduce_scatter_tensor(y, x, op=nccl_op)  # noqa: E731
+            nbytes = n * es * world
+        elif op == "broadcast":
+            ours = lambda: comm.broadcast(y, 0, src=x if rank == 0 else None, algo=algo_v)  # noqa: E731
+            ref = lambda: dist.broadcast(y, 0)  # noqa: E731
+            nbytes = n * es
+        else:
+            ours = lambda: comm.reduce(x, 0, rop, out=y, algo=algo_v)  # noqa: E731
+            ref = lambda: dist.reduce(y, 0, op=nccl_op)  # noqa: E731
+            nbytes = n * es
+        ok = _check(comm, op, x, rop, nccl_op, dtype)
+        t_ours = timed(ours)
+        used = comm.last_algorithm
+        t_nccl = timed(ref) if nccl else None
+        f = busbw_factor(op, world)
+        rec = {"op": op, "dtype": dtype, "redop": redop, "bytes": n * es, "ranks": world, "algo": used,
+               "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
+               "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok}
+        if t_nccl is not None:
+            rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
+                        "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
+        if rank == 0:
+            emit(json.dumps(rec))
+        out.append(rec)
+        del x, y
+        size *= factor
+    return out
+
+
+_RTOL = {"float32": 1e-5, "bfloat16": 8e-3, "float16": 1e-3, "int32": 0.0}
+
+
+def _check(comm, op: str, x, rop, nccl_op, dtype: str) -> bool:
+    """One out-of-place call of ``op`` on ``x`` against an fp64 NCCL reduction of the same inputs
+    (exact comparison for the data-movement ops); the verdict is agreed over all ranks."""
+    import torch
+    import torch.distributed as dist
+    rank, world = comm.rank, comm.world_size
+    n = x.numel()
+    x64 = x.double() if dtype != "int32" else x.long()
+    if op == "allreduce":
+        got = torch.empty_like(x)
+        comm.all_reduce(x, rop, out=got)
+        ref = x64.clone()
+        dist.all_reduce(ref, op=nccl_op)
+    elif op == "reducescatter":
+        m = n // world
+        got = torch.empty(m, dtype=x.dtype, device=x.device)
+        comm.reduce_scatter(got, x, rop)
+        ref = x64.clone()
+        dist.all_reduce(ref, op=nccl_op)
+        ref = ref[rank * m:(rank + 1) * m]
+    elif op == "reduce":
+        got = torch.empty_like(x)
+        comm.reduce(x, 0, rop, out=got)
+        ref = x64.clone()
+        dist.all_reduce(ref, op=nccl_op)
+        if rank != 0:  # only the root's output is defined
+            got = ref.to(x.dtype)
+    elif op == "allgather":
+        got = torch.empty(n * world, dtype=x.dtype, device=x.device)
+        comm.all_gather(got, x)
+        ref = torch.empty_like(got)
+        dist.all_gather_into_tensor(ref, x)
+    else:  # broadcast from root 0
+        got = torch.empty_like(x)
+        comm.broadcast(got, 0, src=x if rank == 0 else None)
+        ref = x.clone()
+        dist.broadcast(ref, 0)
+    rtol = _RTOL[dtype]
+    err = (got.double() - ref.double()).abs()
+    bound = rtol * (ref.double().abs() + world)
+    ok = torch.tensor([1 if bool((err <= bound).all()) else 0], device=x.device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return bool(ok.item())
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--op", default="allreduce",
                    choices=["allreduce", "allgather", "reducescatter", "broadcast", "reduce"])
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16", "float16", "int32"])
+    p.add_argument("--redop", default="sum", choices=["sum", "max", "min", "avg"])
     p.add_argument("--min-bytes", default="8")
     p.add_argument("--max-bytes", default="1G")
     p.add_argument("--factor", type=int, default=2)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--iters", type=int, default=100)
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls"])
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring"])
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--no-nccl", action="store_true")
     p.add_argument("--out", default="")
@@ -50,92 +190,27 @@ def main(argv=None) -> None:
 
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     import originccl_b200 as occl
-    from originccl_b200 import Algo
-    from originccl_b200.utils.timing import busbw_factor
 
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=300))
     comm = occl.init_from_store(dist.distributed_c10d._get_default_store(), rank, world, device=local)
-    dtype = getattr(torch, args.dtype)
-    es = torch.empty((), dtype=dtype).element_size()
-    algo = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS}[args.algo]
-    barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
-
-    def timed(fn) -> float:
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(args.iters):
-            fn()
-        e.record()
-        torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
-        t = torch.tensor([s.elapsed_time(e) / args.iters], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item()) * 1e3  # microseconds
-
     out_f = open(args.out, "a") if (args.out and rank == 0) else None
-    size = max(parse_size(args.min_bytes), es)
-    max_b = parse_size(args.max_bytes)
-    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    while size <= max_b:
-        n = max(1, size // es)
-        # Per-rank payload convention (as nccl-tests): allreduce/broadcast/reduce move n elements;
-        # allgather gathers n per rank; reducescatter scatters n per rank (input world*n).
-        if args.op == "reducescatter":
-            x = torch.rand(n * world, device="cuda", generator=g).to(dtype)
-            y = torch.empty(n, device="cuda", dtype=dtype)
-        elif args.op == "allgather":
-            x = torch.rand(n, device="cuda", generator=g).to(dtype)
-            y = torch.empty(n * world, device="cuda", dtype=dtype)
-        else:
-            x = torch.rand(n, device="cuda", generator=g).to(dtype)
-            y = x if args.inplace else torch.empty_like(x)
-        if args.op == "allreduce":
-            ours = lambda: comm.all_reduce(x, out=y, algo=algo)  # noqa: E731
-            ref = lambda: dist.all_reduce(y)  # noqa: E731
-            nbytes = n * es
-        elif args.op == "allgather":
-            ours = lambda: comm.all_gather(y, x)  # noqa: E731
-            ref = lambda: dist.all_gather_into_tensor(y, x)  # noqa: E731
-            nbytes = n * es * world
-        elif args.op == "reducescatter":
-            ours = lambda: comm.reduce_scatter(y, x)  # noqa: E731
-            ref = lambda: dist.reduce_scatter_tensor(y, x)  # noqa: E731
-            nbytes = n * es * world
-        elif args.op == "broadcast":
-            ours = lambda: comm.broadcast(y, 0, src=x if rank == 0 else None, algo=algo)  # noqa: E731
-            ref = lambda: dist.broadcast(y, 0)  # noqa: E731
-            nbytes = n * es
-        else:
-            ours = lambda: comm.reduce(x, 0, out=y, algo=algo)  # noqa: E731
-            ref = lambda: dist.reduce(y, 0)  # noqa: E731
-            nbytes = n * es
-        t_ours = timed(ours)
-        used = comm.last_algorithm
-        t_nccl = None if args.no_nccl else timed(ref)
-        f = busbw_factor(args.op, world)
-        rec = {"op": args.op, "dtype": args.dtype, "bytes": n * es, "ranks": world, "algo": used,
-               "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
-               "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": args.inplace}
-        if t_nccl is not None:
-            rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
-                        "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
-        if rank == 0:
-            line = json.dumps(rec)
-            print(line, flush=True)
-            if out_f:
-                out_f.write(line + "\n")
-                out_f.flush()
-        del x, y
-        size *= args.factor
+
+    def emit(line: str) -> None:
+        print(line, flush=True)
+        if out_f:
+            out_f.write(line + "\n")
+            out_f.flush()
+
+    run_sweep(comm, op=args.op, dtype=args.dtype, min_bytes=parse_size(args.min_bytes),
+              max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup, iters=args.iters,
+              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=emit)
     if out_f:
         out_f.close()
     comm.destroy()
-    barrier()
+    dist.barrier(device_ids=[local])
     dist.destroy_process_group()
 
 

@@ -89,3 +89,28 @@ def test_algorithm_table():
     assert choose(AR, 64 << 20, 2, True)[0] == TWOSHOT        # two ranks: push path
     assert choose(AG, 64 << 20, 8, True)[0] == ONESHOT
     assert choose(AR, 8, 8, True)[1] == 1
+
+
+def test_tuning_table_from_sweeps_is_loaded_by_the_planner(tmp_path, monkeypatch):
+    from originccl_b200.utils import tune
+    recs = []
+    for size, t_one, t_two, t_nvls in [(1024, 5.0, 9.0, 12.0), (65536, 8.0, 7.0, 9.0), (1 << 20, 30.0, 20.0, 15.0),
+                                        (1 << 24, 300.0, 120.0, 80.0)]:
+        for algo, t in (("oneshot", t_one), ("twoshot", t_two), ("nvls", t_nvls)):
+            recs.append({"op": "allreduce", "ranks": 4, "bytes": size, "algo": algo, "time_us": t, "check": True})
+    recs.append({"op": "allreduce", "ranks": 4, "bytes": 1 << 24, "algo": "oneshot", "time_us": 1.0, "check": False})
+    rows = tune.build_table(recs)
+    assert [(r[3], r[2]) for r in rows] == [("oneshot", int((1024 * 65536) ** 0.5)),
+                                             ("twoshot", int((65536 * (1 << 20)) ** 0.5)),
+                                             ("nvls", (1 << 64) - 1)]
+    path = tmp_path / "tuning.txt"
+    path.write_text(tune.format_table(rows))
+    monkeypatch.setenv("BCCL_TUNING_FILE", str(path))
+    lib = _native.lib()
+    algo, ctas = ctypes.c_int(), ctypes.c_int()
+
+    def choose(nbytes):
+        lib.bcclPlannerChoose(AR, F32, 0, nbytes, 4, 1, 0, ctypes.byref(algo), ctypes.byref(ctas))
+        return algo.value
+
+    assert [choose(n) for n in (512, 8192, 65536, 1 << 22, 1 << 30)] == [1, 1, 2, 3, 3]
