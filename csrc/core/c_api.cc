@@ -160,6 +160,20 @@ int bcclAllReduce(bcclComm_t comm, const void* send, void* recv, size_t count, i
     BCCL_SUBMIT(MakeTask(bccl::CollFunc::AllReduce, send, recv, count, dtype, op, 0, -1, scale, algo));
 }
 
+int bcclAllReduceMany(bcclComm_t comm, int n, const void* const* send, void* const* recv, const size_t* counts,
+                      int dtype, int op, float scale, int grouped, uintptr_t stream, int has_stream) {
+    if (comm == nullptr || n < 0 || (n > 0 && (send == nullptr || recv == nullptr || counts == nullptr))) return Fail();
+    ApplyStream(comm, stream, has_stream);
+    if (grouped) comm->comm.GroupStart();
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+        ok = comm->comm.Submit(MakeTask(bccl::CollFunc::AllReduce, send[i], recv[i], counts[i], dtype, op, 0, -1, scale,
+                                        0));
+    }
+    if (grouped) ok = comm->comm.GroupEnd() && ok;  // always leave the group
+    return ok ? 0 : Fail();
+}
+
 int bcclBroadcast(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int root, int algo,
                   uintptr_t stream, int has_stream) {
     BCCL_SUBMIT(MakeTask(bccl::CollFunc::Broadcast, send ? send : recv, recv, count, dtype, 0, root, -1, 1.0f, algo));

@@ -58,6 +58,12 @@ int bcclGroupEnd(bcclComm_t comm, uintptr_t stream, int has_stream);
 /* algo: 0 auto, 1 one-shot, 2 two-shot, 3 NVLS, 4 ring. */
 int bcclAllReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, float scale, int algo,
                   uintptr_t stream, int has_stream);
+/* n AllReduces (same dtype, op and scale) in one call: with grouped != 0 they form one group
+ * (GroupStart, n submissions, GroupEnd), so small ones run as a single batched kernel; with
+ * grouped == 0 each runs as its own operation, in order. Saves a call per tensor for callers
+ * that sync many tensors, e.g. gradient buckets. */
+int bcclAllReduceMany(bcclComm_t comm, int n, const void* const* send, void* const* recv, const size_t* counts,
+                      int dtype, int op, float scale, int grouped, uintptr_t stream, int has_stream);
 int bcclBroadcast(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int root, int algo,
                   uintptr_t stream, int has_stream);
 int bcclReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, int root, int algo,

@@ -68,6 +68,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclGroupStart": (c_int, [vp]),
         "bcclGroupEnd": (c_int, [vp, up, c_int]),
         "bcclAllReduce": (c_int, [vp, vp, vp, c_size, c_int, c_int, ctypes.c_float, c_int, up, c_int]),
+        "bcclAllReduceMany": (c_int, [vp, c_int, vp, vp, vp, c_int, c_int, ctypes.c_float, c_int, up, c_int]),
         "bcclBroadcast": (c_int, [vp, vp, vp, c_size, c_int, c_int, c_int, up, c_int]),
         "bcclReduce": (c_int, [vp, vp, vp, c_size, c_int, c_int, c_int, c_int, up, c_int]),
         "bcclAllGather": (c_int, [vp, vp, vp, c_size, c_int, up, c_int]),

@@ -305,6 +305,23 @@ class Communicator:
         self._check(self._lib.bcclRecv(self._h, _ptr(tensor), _numel(tensor), int(_dtype_of(tensor)), int(peer), s, has))
         return tensor
 
+    def batch(self, tensors: Sequence[Any], outs: Optional[Sequence[Any]] = None) -> "TensorBatch":
+        """Pointer arrays for :meth:`all_reduce_many`, built once for tensors that are synced often."""
+        return TensorBatch(tensors, outs)
+
+    def all_reduce_many(self, tensors: Any, op: ReduceOp = ReduceOp.SUM, *, scale: float = 1.0,
+                        grouped: bool = True, stream: Any = None) -> None:
+        """AllReduce of every tensor (in place, or into the batch's outputs) in ONE library call.
+
+        ``tensors`` is a list of same-dtype tensors or a :class:`TensorBatch`. With ``grouped`` the
+        calls form one GroupStart/GroupEnd batch (small tensors then run as one kernel); without,
+        each runs as its own operation in order.
+        """
+        b = tensors if isinstance(tensors, TensorBatch) else TensorBatch(tensors)
+        s, has = self._stream(stream)
+        self._check(self._lib.bcclAllReduceMany(self._h, b.n, b.send, b.recv, b.counts, int(b.dtype), int(op),
+                                                float(scale), int(grouped), s, has))
+
     # Raw-pointer entry points (device pointers or host addresses), for callers without tensors.
     def all_reduce_ptr(self, send: int, recv: int, count: int, dtype: DataType, op: ReduceOp = ReduceOp.SUM,
                        scale: float = 1.0, algo: Algo = Algo.AUTO, stream: Any = None) -> None:
@@ -360,6 +377,25 @@ class Communicator:
         if not ptr:
             raise BcclError(_native.last_error() or "symmetric allocation failed")
         return _tensor_from_ptr(ptr, shape, dtype, self.device)
+
+
+class TensorBatch:
+    """Send/recv pointer and count arrays of many same-dtype tensors (see Communicator.batch)."""
+
+    def __init__(self, tensors: Sequence[Any], outs: Optional[Sequence[Any]] = None) -> None:
+        tensors = list(tensors)
+        outs = tensors if outs is None else list(outs)
+        if len(outs) != len(tensors):
+            raise ValueError("outs must match tensors")
+        self.n = len(tensors)
+        self.dtype = _dtype_of(tensors[0]) if tensors else DataType.FLOAT32
+        for t in tensors:
+            if _dtype_of(t) != self.dtype:
+                raise TypeError("all tensors of a batch must have one dtype")
+        self.send = (ctypes.c_void_p * max(self.n, 1))(*[_ptr(t) for t in tensors])
+        self.recv = (ctypes.c_void_p * max(self.n, 1))(*[_ptr(t) for t in outs])
+        self.counts = (ctypes.c_size_t * max(self.n, 1))(*[_numel(t) for t in tensors])
+        self._keep = (tensors, outs)  # the pointers stay valid while the batch lives
 
 
 def _tensor_from_ptr(ptr: int, shape: Sequence[int], dtype: Any, device: int) -> Any:

@@ -135,6 +135,8 @@ class DataParallelSync:
         if self.on_gpu and stream is None:
             stream = torch.cuda.Stream(device=grads.device)
         self.stream = stream
+        self._bucket_batch = comm.batch([grads.bucket(i) for i in range(grads.num_buckets)])
+        self._small_batch = comm.batch(grads.small_tensors())
         self._hooks: list = []
         self._pending: List[int] = []
         self._next = 0
@@ -144,17 +146,14 @@ class DataParallelSync:
         """Launches every bucket, then the small tensors as one group, on ``stream`` (default: the
         current stream, so later work on it sees averaged gradients)."""
         s = stream if stream is not None else (torch.cuda.current_stream(self.grads.device) if self.on_gpu else None)
-        for i in range(self.grads.num_buckets):
-            self.comm.all_reduce(self.grads.bucket(i), ReduceOp.SUM, scale=self.scale, stream=s)
+        # One library call for all buckets (each its own AllReduce, in order) and one for the
+        # small tensors (one group, i.e. one batched kernel).
+        self.comm.all_reduce_many(self._bucket_batch, ReduceOp.SUM, scale=self.scale, grouped=False, stream=s)
         self._sync_small(s)
 
     def _sync_small(self, s) -> None:
-        small = self.grads.small_tensors()
-        if not small:
-            return
-        with self.comm.group(stream=s):
-            for t in small:
-                self.comm.all_reduce(t, ReduceOp.SUM, scale=self.scale)
+        if self._small_batch.n:
+            self.comm.all_reduce_many(self._small_batch, ReduceOp.SUM, scale=self.scale, grouped=True, stream=s)
 
     # ------------------------------------------------------------------ overlap with backward
     def attach(self) -> None:

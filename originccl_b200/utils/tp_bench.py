@@ -72,12 +72,33 @@ def main(argv=None) -> None:
     flops = 2 * 2.0 * args.tokens * args.hidden * (args.ffn // world)  # per rank, both GEMMs
     nvlink_bytes = 2 * (world - 1) * ms * args.hidden * 2  # AG in + RS out per rank, bf16
     roof_ms = max(flops / (args.gemm_peak_tflops * 1e12), nvlink_bytes / (args.nvlink_gbs * 1e9)) * 1e3
+    # Where the time goes: each fused op alone, the same GEMMs without communication (this
+    # library's kernel and cuBLAS) and the NCCL collectives alone.
+    from originccl_b200.ops import gemm as gemm_op
+    from originccl_b200.ops import tp as tp_op
+    xg = torch.empty(args.tokens, args.hidden, device="cuda", dtype=torch.bfloat16)
+    h = tp_op.all_gather_gemm(comm, x, mlp.w_up, "silu")
+    part = torch.empty(args.tokens, args.hidden, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(ms, args.hidden, device="cuda", dtype=torch.bfloat16)
+    bd = {
+        "ag_gemm_ms": timed(lambda: tp_op.all_gather_gemm(comm, x, mlp.w_up, "silu", out=h)),
+        "gemm_rs_ms": timed(lambda: tp_op.gemm_reduce_scatter(comm, h, mlp.w_down, out=out)),
+        "gemm_up_ours_ms": timed(lambda: gemm_op.gemm(xg, mlp.w_up, "silu", out=h)),
+        "gemm_down_ours_ms": timed(lambda: gemm_op.gemm(h, mlp.w_down, out=part)),
+        "gemm_up_cublas_ms": timed(lambda: torch.matmul(xg, mlp.w_up.t())),
+        "gemm_down_cublas_ms": timed(lambda: torch.matmul(h, mlp.w_down.t())),
+    }
+    if world > 1:
+        bd["nccl_allgather_ms"] = timed(lambda: dist.all_gather_into_tensor(xg, x))
+        bd["nccl_reducescatter_ms"] = timed(lambda: dist.reduce_scatter_tensor(out, part))
+    bd = {k: round(v, 4) for k, v in bd.items()}
     if rank == 0:
         print(json.dumps({"bench": "tp_mlp", "world": world, "tokens": args.tokens, "hidden": args.hidden,
                           "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
                           "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
                           "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
-                          "max_rel_diff_vs_reference": rel}), flush=True)
+                          "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(),
+                          "breakdown": bd}), flush=True)
     comm.destroy()
     if world > 1:
         dist.barrier(device_ids=[local])
