@@ -343,6 +343,9 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const int r = c.rank, n = c.nranks;
     const int kind = p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
     const bool sysf = (p.debug & 1) == 0;
+    // One-shot data flow: push (A stores into every peer's inbox) or, with debug bit 8, pull
+    // (A copies into this rank's own slot, B loads the peers' slots over NVLink).
+    const bool pull = (p.debug & 8) != 0;
     // Warp groups run their phases concurrently for NVLS (two local copies against one switch
     // phase); for the push kinds a single group measured faster (BCCL_PIPE_DEBUG bit 2 flips it).
     const bool split = (kind == kPipeNvls) != ((p.debug & 4) != 0);
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const int gtid = split ? (is_net ? threadIdx.x : threadIdx.x - half) : threadIdx.x;
     const int gnt = split ? half : blockDim.x;
     const bool do_net = !split || is_net, do_local = !split || !is_net;
-    if (threadIdx.x == 0) trace(c, 0, kTrBegin, 0);
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar0 & 0x7fffffffull));  // round field: barrier base
 
     auto geom = [&](int j, size_t* cbeg, size_t* clen, size_t* shard, size_t* s0, size_t* s1) {
         *cbeg = (size_t)j * p.chunk;
@@ -379,11 +382,16 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
         if (kind == kPipeOneShot) {
             if (s0 < s1) {
-                char* outs[kMaxRanks];
-                int no = 0;
-                for (int q = 0; q < n; ++q)
-                    if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
-                if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
+                if (pull) {  // stage into this rank's own slot; the peers read it over NVLink
+                    grp_copy(ts_region(c, r) + ((size_t)slot * n + r) * sb + s0, src + cbeg + s0, s1 - s0, tid, nt,
+                             false);
+                } else {
+                    char* outs[kMaxRanks];
+                    int no = 0;
+                    for (int q = 0; q < n; ++q)
+                        if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
+                    if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
+                }
             }
         } else if (kind == kPipeTwoShot) {
             for (int q = 0; q < n; ++q) {
@@ -408,8 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
             if (s0 < s1) {
                 const char* srcs[kMaxRanks];
                 char* mine = ts_region(c, r);
-                for (int q = 0; q < n; ++q)
-                    srcs[q] = (q == r) ? src + cbeg + s0 : mine + ((size_t)slot * n + q) * sb + s0;
+                for (int q = 0; q < n; ++q) {
+                    srcs[q] = (q == r) ? src + cbeg + s0
+                                       : (pull ? ts_region(c, q) : mine) + ((size_t)slot * n + q) * sb + s0;
+                }
                 char* outs[1] = {dst + cbeg + s0};
                 grp_reduce_multi<D, O>(outs, 1, srcs, n, r, s1 - s0, tid, nt, n, p.scale);
             }
@@ -474,6 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         }
         // ---- barrier t: both groups' writes are issued; fence + signal + wait.
         __syncthreads();
+        if (threadIdx.x == 0) trace(c, 0, kTrStaged, t);  // this CTA's phases of iteration t are issued
         const int tid = threadIdx.x;
         if (tid < n && tid != r) {
             if (sysf) fence_acq_rel_sys();

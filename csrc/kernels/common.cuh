@@ -355,7 +355,10 @@ __device__ __forceinline__ void cta_copy(void* dst, const void* src, size_t byte
 // dst[i] = epilogue(reduce_p srcs[p][i]) over `bytes` bytes, p in [0, n) in rank order
 // (identical order on every rank, so every rank produces bit-identical results).
 // srcs[p] with (cg_mask >> p) & 1 are read with ld.cg (written by another GPU).
-template <int D, int O>
+// NS bounds n (the register arrays' size); with NS <= 4 every thread keeps two vectors' loads
+// in flight (2n loads), which a CTA needs to approach its share of memory bandwidth when n is
+// small, while NS = 8 keeps one (8 loads) to stay within the register budget.
+template <int D, int O, int NS>
 __device__ __noinline__ void cta_reduce(void* dst, const void* const* srcs, int n, unsigned cg_mask, size_t bytes,
                                         int nranks, float scale) {
     using T = Ty<D>;
@@ -363,29 +366,56 @@ __device__ __noinline__ void cta_reduce(void* dst, const void* const* srcs, int 
     using Acc = typename T::Acc;
     using V = Vec<D>;
     constexpr int E = V::E;
+    constexpr int U = NS <= 4 ? 2 : 1;
     const size_t t = threadIdx.x, nt = blockDim.x;
     // Source pointers into registers (static indices below); unused slots alias source 0.
-    const char* sp[kMaxRanks];
+    const char* sp[NS];
 #pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p) sp[p] = static_cast<const char*>(srcs[p < n ? p : 0]);
+    for (int p = 0; p < NS; ++p) sp[p] = static_cast<const char*>(srcs[p < n ? p : 0]);
     uintptr_t mis = reinterpret_cast<uintptr_t>(dst);
 #pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p) mis |= reinterpret_cast<uintptr_t>(sp[p]);
+    for (int p = 0; p < NS; ++p) mis |= reinterpret_cast<uintptr_t>(sp[p]);
     const size_t nv = ((mis & 15) == 0) ? (bytes >> 4) : 0;
     const bool post = (O == kAvg) || scale != 1.0f;
-    for (size_t i = t; i < nv; i += nt) {
-        const size_t off = i << 4;
-        uint4 w[kMaxRanks];
+    size_t i = t;
+    for (; i + (U - 1) * nt < nv; i += U * nt) {
+        uint4 w[U][NS];
 #pragma unroll
-        for (int p = 0; p < kMaxRanks; ++p) {
-            if (p < n) w[p] = ((cg_mask >> p) & 1) ? ld_cg(sp[p] + off) : *reinterpret_cast<const uint4*>(sp[p] + off);
+        for (int u = 0; u < U; ++u) {
+            const size_t off = (i + u * nt) << 4;
+#pragma unroll
+            for (int p = 0; p < NS; ++p) {
+                if (p < n)
+                    w[u][p] = ((cg_mask >> p) & 1) ? ld_cg(sp[p] + off) : *reinterpret_cast<const uint4*>(sp[p] + off);
+            }
         }
-        Acc acc[E], x[E];
-        V::unpack(w[0], acc);
 #pragma unroll
-        for (int p = 1; p < kMaxRanks; ++p) {
+        for (int u = 0; u < U; ++u) {
+            Acc acc[E], x[E];
+            V::unpack(w[u][0], acc);
+#pragma unroll
+            for (int p = 1; p < NS; ++p) {
+                if (p < n) {
+                    V::unpack(w[u][p], x);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
+                }
+            }
+            if (post) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) acc[e] = epilogue<Acc>(O, acc[e], nranks, scale);
+            }
+            st_cg(static_cast<char*>(dst) + ((i + u * nt) << 4), V::pack(acc));
+        }
+    }
+    for (; i < nv; i += nt) {  // at most one vector per thread left
+        const size_t off = i << 4;
+        Acc acc[E], x[E];
+        V::unpack(((cg_mask & 1u) ? ld_cg(sp[0] + off) : *reinterpret_cast<const uint4*>(sp[0] + off)), acc);
+#pragma unroll
+        for (int p = 1; p < NS; ++p) {
             if (p < n) {
-                V::unpack(w[p], x);
+                V::unpack(((cg_mask >> p) & 1) ? ld_cg(sp[p] + off) : *reinterpret_cast<const uint4*>(sp[p] + off), x);
 #pragma unroll
                 for (int e = 0; e < E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
             }
@@ -403,7 +433,7 @@ __device__ __noinline__ void cta_reduce(void* dst, const void* const* srcs, int 
         const size_t off = done + j * sizeof(Bits);
         Acc acc = Acc(0);
 #pragma unroll
-        for (int p = 0; p < kMaxRanks; ++p) {
+        for (int p = 0; p < NS; ++p) {
             if (p < n) {
                 const Bits* e = reinterpret_cast<const Bits*>(sp[p] + off);
                 Bits b = ((cg_mask >> p) & 1) ? __ldcg(e) : *e;
@@ -414,14 +444,21 @@ __device__ __noinline__ void cta_reduce(void* dst, const void* const* srcs, int 
     }
 }
 
+template <int D, int O>
+__device__ __forceinline__ void cta_reduce_n(void* dst, const void* const* srcs, int n, unsigned cg_mask, size_t bytes,
+                                             int nranks, float scale) {
+    if (n <= 4) cta_reduce<D, O, 4>(dst, srcs, n, cg_mask, bytes, nranks, scale);
+    else cta_reduce<D, O, kMaxRanks>(dst, srcs, n, cg_mask, bytes, nranks, scale);
+}
+
 template <int D>
 __device__ __forceinline__ void cta_reduce_op(int op, void* dst, const void* const* srcs, int n, unsigned cg_mask,
                                               size_t bytes, int nranks, float scale) {
     switch (op) {
-    case kSum: cta_reduce<D, kSum>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
-    case kMax: cta_reduce<D, kMax>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
-    case kMin: cta_reduce<D, kMin>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
-    case kAvg: cta_reduce<D, kAvg>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
+    case kSum: cta_reduce_n<D, kSum>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
+    case kMax: cta_reduce_n<D, kMax>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
+    case kMin: cta_reduce_n<D, kMin>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
+    case kAvg: cta_reduce_n<D, kAvg>(dst, srcs, n, cg_mask, bytes, nranks, scale); break;
     default: break;
     }
 }

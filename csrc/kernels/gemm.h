@@ -25,7 +25,7 @@ struct TpArgs {
     const unsigned long long* ag_counters;    // here: [src][kTpMaxChunks]
     unsigned long long* ag_counters_peer[kMaxRanks];  // the same array on every rank
     // GEMM -> ReduceScatter
-    __nv_bfloat16* rs_stage[kMaxRanks];       // every rank's staging [nranks][ms][N] (this call's half)
+    __nv_bfloat16* rs_stage[kMaxRanks];       // every rank's partial product [M][N] (this call's half)
     unsigned long long* rs_counters[kMaxRanks];       // every rank's per-own-tile counters
     const unsigned long long* rs_started;     // here: [src] = last call index src started
     unsigned long long* rs_started_peer[kMaxRanks];

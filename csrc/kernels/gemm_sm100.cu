@@ -1,16 +1,22 @@
-// bf16 GEMM on the 5th-generation tensor cores: C[M,N] = act(A[M,K] * B[N,K]^T), f32 accumulate.
+// bf16 GEMM on the 5th-generation tensor cores: C[M,N] = act(A[M,K] * B[N,K]^T), f32 accumulate,
+// plus the two fused tensor-parallel modes (AllGather->GEMM and GEMM->ReduceScatter).
 //
-// Persistent, warp-specialised, one CTA per SM (192 threads):
-//   warp 0     TMA producer: 128x64 A and 256x64 B tiles (128-byte swizzle) into a 4-stage ring
-//   warp 1     allocates 512 TMEM columns; one thread issues tcgen05.mma (M=128, N=256, K=16)
-//              into one of two TMEM accumulators and tcgen05.commit's stage/accumulator barriers
+// Persistent, warp-specialised, one CTA per SM (320 threads):
+//   warp 0     TMA producer: A and B tiles (128-byte swizzle) into a ring of shared-memory stages
+//   warp 1     allocates 512 TMEM columns; one thread issues tcgen05.mma into one of two TMEM
+//              accumulators and tcgen05.commit's the stage/accumulator barriers
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quarter, optional
 //              SiLU, bf16 rounding, store to global
+//   warps 6-9  communication (fused modes only): push this rank's activation shard to every peer
+//              (AllGather), or pull and sum the partial tiles this rank owns (ReduceScatter)
+// Two kernels: 1-SM tiles of 128x256 (M=128 MMAs, 4 stages) and 2-SM tiles of 256x256 (a CTA pair
+// runs tcgen05.mma.cta_group::2; each CTA loads half of A and half of B, 6 stages), the default.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1. Every mbarrier
-// wait is bounded; a role that gives up raises a shared abort word that stops the others, the
-// MMA thread drains its in-flight MMAs and the producer its in-flight TMA loads before the
-// TMEM columns are freed, and the failure is recorded in the caller's error word.
-// The tile schedule walks N fastest so consecutive CTAs share an A row block in L2.
+// and flag wait is bounded; a role that gives up raises a shared abort word that stops the
+// others, the MMA thread drains its in-flight MMAs and the producer its in-flight TMA loads
+// before the TMEM columns are freed, and the failure is recorded in the caller's error word.
+// TMA reads only this GPU's memory, and no load uses cluster multicast.
+// The plain tile schedule walks N fastest so consecutive CTAs share an A row block in L2.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -88,6 +94,15 @@ __device__ __forceinline__ int ag_row_block(int i, const TpArgs& tp, int num_m, 
     return src * per + c;
 }
 
+// GEMM->ReduceScatter tile schedule: row blocks cycle through the owners (owner 0 chunk 0,
+// owner 1 chunk 0, ..., owner 0 chunk 1, ...), the same order on every rank, so every owner's
+// tiles complete (on all ranks at about the same time) all through the GEMM and its sums overlap
+// the math instead of piling up behind it.
+__device__ __forceinline__ int rs_row_block(int i, const TpArgs& tp, int block_rows = BM) {
+    const int per = tp.ms / block_rows;
+    return (i % tp.nranks) * per + i / tp.nranks;
+}
+
 // Communication warps of the fused modes (warps 6-9): AllGather pushes / ReduceScatter sums.
 template <int MODE>
 __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile int* s_abort, volatile int* s_comm_stop) {
@@ -138,27 +153,50 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
                 if (*s_comm_stop) break;
                 const int lrb = t / num_n, nb = t % num_n;
                 const int ncols = min(BN, g.N - nb * BN);
-                // 8 bf16 per thread-iteration; rows x ncols of the tile.
+                // 8 bf16 per vector; rows x ncols of the tile. kU vectors per thread per step, all
+                // N partials of all kU loaded before any is summed: enough loads in flight to
+                // cover memory latency with only four warps.
+                constexpr int kU = 4;
                 const int vec_per_row = ncols / 8;
-                for (int e = ctid; e < BM * vec_per_row; e += cnt_threads) {
-                    const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
-                    const int lrow = lrb * BM + rr;
-                    if (lrow >= g.tp.ms) continue;
-                    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                    for (int srcr = 0; srcr < g.tp.nranks; ++srcr) {
-                        const __nv_bfloat16* part =
-                            g.tp.rs_stage[g.tp.rank] + ((size_t)srcr * g.tp.ms + lrow) * g.N + nb * BN + cc;
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part));
-                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                const int total = BM * vec_per_row;
+                // Partials are pulled from every rank's staging ([M][N], this rank's rows):
+                // coalesced 16-byte loads over NVLink instead of scattered remote stores.
+                const size_t my_rows = (size_t)g.tp.rank * g.tp.ms * g.N;
+                for (int e0 = ctid; e0 < total; e0 += kU * cnt_threads) {
+                    uint4 v[kU][kMaxRanks];
+                    size_t off[kU];
+                    bool live[kU];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            acc[2 * j] += __uint_as_float(w[j] << 16);
-                            acc[2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
+                    for (int u = 0; u < kU; ++u) {
+                        const int e = e0 + u * cnt_threads;
+                        const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
+                        const int lrow = lrb * BM + rr;
+                        live[u] = e < total && lrow < g.tp.ms;
+                        off[u] = (size_t)lrow * g.N + nb * BN + cc;
+#pragma unroll
+                        for (int q = 0; q < kMaxRanks; ++q) {
+                            if (live[u] && q < g.tp.nranks)
+                                v[u][q] = __ldcg(reinterpret_cast<const uint4*>(g.tp.rs_stage[q] + my_rows + off[u]));
                         }
                     }
-                    uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
-                    *reinterpret_cast<uint4*>(g.tp.out + (size_t)lrow * g.N + nb * BN + cc) = o;
+#pragma unroll
+                    for (int u = 0; u < kU; ++u) {
+                        if (!live[u]) continue;
+                        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+                        for (int q = 0; q < kMaxRanks; ++q) {
+                            if (q >= g.tp.nranks) break;
+                            const uint32_t w[4] = {v[u][q].x, v[u][q].y, v[u][q].z, v[u][q].w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                acc[2 * j] += __uint_as_float(w[j] << 16);
+                                acc[2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
+                            }
+                        }
+                        uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                             pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+                        *reinterpret_cast<uint4*>(g.tp.out + off[u]) = o;
+                    }
                 }
             }
         }
@@ -210,7 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
     const int tiles = num_m * num_n;
     const int kblocks = (g.K + BK - 1) / BK;
     // Tile t -> (row block, column block); N walks fastest.
-    auto tile_rb = [&](int t) { return MODE == kModeAllGather ? ag_row_block(t / num_n, g.tp, num_m) : t / num_n; };
+    auto tile_rb = [&](int t) {
+        if (MODE == kModeAllGather) return ag_row_block(t / num_n, g.tp, num_m);
+        if (MODE == kModeReduceScatter) return rs_row_block(t / num_n, g.tp);
+        return t / num_n;
+    };
     auto fail = [&]() {
         *s_abort = 1;
         atomicExch(g.err, 1);
@@ -315,18 +357,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
             __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
             int owner = 0;
             if (MODE == kModeReduceScatter) {
-                // Partial tile goes to its owner's staging slot for this rank.
+                // The partial tile stays in this rank's own staging (g.C, [M][N]); its owner
+                // pulls it. The owner must have started the previous call (so it finished
+                // reading this parity's staging two calls ago) before the first overwrite.
                 const int per = g.tp.ms / BM;
                 owner = rb / per;
                 if (owner != g.tp.rank && !rs_ready_checked[owner]) {
-                    // The owner must have started the previous call (so it finished reading
-                    // this parity's staging two calls ago) before the first push to it.
                     if (lane == 0 && !wait_geq_sys(g.tp.rs_started + owner, g.tp.seq - 1, s_abort)) fail();
                     __syncwarp();
                     rs_ready_checked[owner] = 1;
                 }
-                const int local_row = (rb % per) * BM + row_in_tile;
-                crow = g.tp.rs_stage[owner] + ((size_t)g.tp.rank * g.tp.ms + local_row) * g.N;
             }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -439,7 +479,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int tiles = num_m * num_n;
     const int kblocks = (g.K + BK - 1) / BK;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    auto tile_rb = [&](int t) { return MODE == kModeAllGather ? ag_row_block(t / num_n, g.tp, num_m, PM) : t / num_n; };
+    auto tile_rb = [&](int t) {
+        if (MODE == kModeAllGather) return ag_row_block(t / num_n, g.tp, num_m, PM);
+        if (MODE == kModeReduceScatter) return rs_row_block(t / num_n, g.tp, PM);
+        return t / num_n;
+    };
     auto fail = [&]() {
         *s_abort = 1;
         atomicExch(g.err, 1);
@@ -549,7 +593,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int row = rb128 * BM + row_in_cta;
             __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
             int owner = 0;
-            if (MODE == kModeReduceScatter) {
+            if (MODE == kModeReduceScatter) {  // as in the 1-SM kernel: own staging, owner pulls
                 const int per = g.tp.ms / BM;
                 owner = rb128 / per;
                 if (owner != g.tp.rank && !rs_ready_checked[owner]) {
@@ -557,8 +601,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     rs_ready_checked[owner] = 1;
                 }
-                const int local_row = (rb128 % per) * BM + row_in_cta;
-                crow = g.tp.rs_stage[owner] + ((size_t)g.tp.rank * g.tp.ms + local_row) * g.N;
             }
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {

@@ -9,6 +9,10 @@
 //              its output -> barrier.
 // Slots form the same ring (indexed by DevState::nvls_round_seq) as the pipelined AllReduce,
 // so the two kinds of launch can follow each other.
+// No fence.proxy.alias between the multicast and unicast views of a slot: the system-scope
+// release/acquire of the barrier orders them (switch writes land in the owner's L2, and the
+// copy-out reads with ld.global.cg), as in the pipelined AllReduce; the alias fence cost tens
+// of microseconds per round with multicast traffic in flight.
 #include "kernels/common.cuh"
 #include "kernels/launch.h"
 
@@ -109,16 +113,12 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
             if (r == p.root) {
                 for (size_t off = lo + t * 16; off < hi; off += nt * 16) mm_st(mc + off, load_partial(src + off, hi - off));
             }
-            fence_proxy_alias();
             if (!cta_barrier(c, ++bar, j)) break;
-            fence_proxy_alias();
             if (lo < hi && r != p.root) cta_copy(dst + lo, uc + lo, hi - lo, true);
             if (lo < hi && r == p.root && dst != src) cta_copy(dst + lo, src + lo, hi - lo, false);
         } else {  // Reduce
             if (lo < hi) cta_copy(uc + lo, src + lo, hi - lo, false);
-            fence_proxy_alias();
             if (!cta_barrier(c, ++bar, 2 * j)) break;
-            fence_proxy_alias();
             if (r == p.root) {
                 for (size_t off = lo + t * 16; off < hi; off += nt * 16) {
                     V16<D> v;

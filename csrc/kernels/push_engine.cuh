@@ -151,7 +151,7 @@ __device__ __forceinline__ void push_engine_body(const DevComm& c, const WorkIte
                                                  size_t stream_bytes, size_t slot) {
     const uint64_t round0 = load_state_u64(&c.state->round_seq);
     const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
-    if (threadIdx.x == 0) trace(c, 0, kTrBegin, 0);
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar0 & 0x7fffffffull));  // round field: barrier base
     bool ok = true;
     int first = 0;  // first item that can still overlap this CTA's pieces (items are sorted)
     for (int j = 0; j < nrounds && ok; ++j) {
