@@ -24,9 +24,8 @@ constexpr int kMaxCtas = 256;
 constexpr size_t kCtrlBytes = 1u << 20;          // control region at the start of each UC buffer
 constexpr size_t kBarrierFlagsOff = 0;            // u64 [kMaxCtas][kMaxRanks]
 constexpr size_t kBarrierFlagsBytes = sizeof(uint64_t) * kMaxCtas * kMaxRanks;
-constexpr size_t kPipeReadyOff = 16u << 10;      // u64 [kMaxCtas][kMaxRanks], pipelined AllReduce
-constexpr size_t kPipeDoneOff = 32u << 10;       // u64 [kMaxCtas][kMaxRanks]
-constexpr size_t kPipeLocalOff = 48u << 10;      // u64 [kMaxCtas], same-GPU progress (finish -> stage)
+constexpr size_t kRingPostedOff = 16u << 10;     // u64 [kMaxCtas]: messages the ring predecessor posted here
+constexpr size_t kRingConsumedOff = 32u << 10;   // u64 [kMaxCtas]: messages the ring successor consumed
 constexpr size_t kTpFlagsOff = 64u << 10;         // u64 flags of the fused tensor-parallel kernels
 constexpr size_t kTpFlagsBytes = 256u << 10;
 constexpr size_t kAlign = 256;
@@ -59,6 +58,7 @@ struct DevState {
     unsigned long long tp_seq;       // fused tensor-parallel kernels: launches so far
     unsigned int tp_done;
     unsigned int pad2;
+    unsigned long long ring_seq;     // ring kernel: message numbers used so far (per CTA slot)
 };
 
 // One device trace record (written when tracing is on): who did what, when.
@@ -99,6 +99,7 @@ struct DevComm {
     unsigned int* trace_count;
     unsigned int trace_cap;
     unsigned int kernel_serial;     // host launch counter (trace labels only)
+    int spin_wait;                  // 1: flag waits poll without __nanosleep (BCCL_SPIN_WAIT)
 };
 
 // One collective in a push-engine launch. All byte offsets refer to the per-peer stream:

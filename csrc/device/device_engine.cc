@@ -88,6 +88,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     dc_.err = err_dev;
     dc_.abort = abort_dev;
     dc_.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
+    dc_.spin_wait = EnvInt("BCCL_SPIN_WAIT", 0) != 0 ? 1 : 0;
     dc_.data_bytes = data_bytes_;
     const long trace_cap = EnvInt("BCCL_TRACE", 0);
     if (trace_cap > 0) {
@@ -435,7 +436,10 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const int slots = PipeSlots();
     // Rounds of at least `min_chunk` bytes (each CTA then moves >= ~100 KB between fences),
     // about `rounds` of them so the software pipeline has something to overlap.
-    const unsigned long long rounds = static_cast<unsigned long long>(std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", 4)));
+    // Two rounds up to 16 MiB, four above (measured on 2 x B200: fewer, larger rounds win until
+    // the pipeline's fill and drain dominate).
+    const unsigned long long rounds = static_cast<unsigned long long>(
+        std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", bytes <= (16u << 20) ? 2 : 4)));
     const unsigned long long min_chunk = static_cast<unsigned long long>(EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20));
     auto pick_chunk = [&](unsigned long long cap) {
         unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, q);
@@ -445,7 +449,14 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const int debug = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
     int ctas = c.ctas;
     dc_.kernel_serial = ++kernel_serial_;
-    if (c.algo == Algo::kNvls) {
+    if (c.algo == Algo::kRing) {
+        // Messages of up to 128 KiB, small enough that every SM gets a channel.
+        const unsigned long long per = (bytes + static_cast<unsigned long long>(nranks_) * num_sms_ - 1) /
+                                       (static_cast<unsigned long long>(nranks_) * num_sms_);
+        const unsigned long long block = std::min<unsigned long long>(128u << 10, std::max<unsigned long long>(256, RoundUp(per, 256)));
+        e = LaunchRingAllReduce(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, block, ctas, stream);
+        last_algo_ = "ring";
+    } else if (c.algo == Algo::kNvls) {
         const unsigned long long slot = RoundDown(nvls_.bytes / slots, 256);
         const unsigned long long chunk = pick_chunk(slot);
         if (t.func == CollFunc::AllReduce) {
@@ -458,8 +469,9 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         last_algo_ = "nvls";
     } else {
         // Two ranks: a one-shot push moves the same NVLink bytes as two-shot with one
-        // reduction step per round instead of two.
-        int kind = nranks_ == 2 ? kPipeOneShot : kPipeTwoShot;
+        // reduction step per round instead of two; from 32 MiB the two-shot schedule measured
+        // faster (its rounds move half as much per phase).
+        int kind = (nranks_ == 2 && bytes < (32u << 20)) ? kPipeOneShot : kPipeTwoShot;
         const long forced_kind = EnvInt("BCCL_PIPE_KIND", -1);
         if (forced_kind == kPipeOneShot || forced_kind == kPipeTwoShot) kind = static_cast<int>(forced_kind);
         unsigned long long slot, chunk;
@@ -502,6 +514,8 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                              (t.func == CollFunc::Broadcast || NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
         AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
                                             t.algo != Algo::kAuto ? t.algo : forced_);
+        const bool ring = c.algo == Algo::kRing && t.func == CollFunc::AllReduce && nranks_ > 1;
+        if (ring) c.ctas = max_ctas_ > 0 ? std::min(num_sms_, max_ctas_) : num_sms_;
         if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls) {
             // Large-payload kernels: per-CTA barriers with the same CTA index on every rank, so
             // every CTA must be resident: at most one per SM.
@@ -512,7 +526,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
             long env_max = EnvInt("BCCL_MAX_CTAS", 0);
             if (env_max > 0) c.ctas = std::min<int>(c.ctas, static_cast<int>(env_max));
         }
-        if (nranks_ == 1 || c.algo == Algo::kOneShot || c.algo == Algo::kRing) {
+        if (nranks_ == 1 || c.algo == Algo::kOneShot || (c.algo == Algo::kRing && !ring)) {
             WorkItem w;
             w.src = t.send_buf;
             w.dst = t.recv_buf;

@@ -31,6 +31,10 @@ __device__ __forceinline__ uint64_t globaltimer() {
     return t;
 }
 
+__device__ __forceinline__ void st_relaxed_sys_flag(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -94,6 +98,8 @@ __device__ __forceinline__ void record_error(const DevComm& c, int code, int pee
     }
 }
 
+constexpr uint64_t kAbortCheckAfterNs = 1000000ull;
+
 // Spin until *flag >= target. Returns false (and records the error) on timeout or abort.
 // Polling uses relaxed loads with a short sleep between them (an acquire load per poll
 // invalidates the SM's L1 and stalls its memory pipeline, which slows every other warp of
@@ -107,14 +113,17 @@ __device__ __forceinline__ bool wait_flag_geq(const DevComm& c, const uint64_t* 
     const uint64_t t0 = globaltimer();
     uint32_t iter = 0;
     for (;;) {
-        __nanosleep(iter < 64 ? 32 : 256);
+        if (!c.spin_wait) __nanosleep(iter < 64 ? 32 : 256);
         if (ld_relaxed_sys(flag) >= target) {
             fence_acq_rel_sys();
             return true;
         }
         if ((++iter & 63u) == 0) {
             const uint64_t waited = globaltimer() - t0;
-            if (*c.abort != 0) {
+            // The abort word is host memory: a read crosses PCIe, and when the link has gone
+            // idle its wake-up stalls the reading thread for hundreds of microseconds. Only
+            // waits that already took over 1 ms look at it.
+            if (waited > kAbortCheckAfterNs && *c.abort != 0) {
                 record_error(c, kDevAborted, peer, phase, target, waited);
                 return false;
             }
@@ -144,7 +153,7 @@ __device__ __forceinline__ bool cta_barrier(const DevComm& c, uint64_t seq, int 
 // Called by every CTA once at the end of a launch: the last CTA advances the device-side
 // counters so the next launch (possibly a CUDA-graph replay) starts from fresh values.
 __device__ __forceinline__ void finish_launch(const DevComm& c, uint64_t rounds, uint64_t barriers,
-                                              uint64_t nvls_rounds) {
+                                              uint64_t nvls_rounds, uint64_t ring_msgs = 0) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -153,6 +162,7 @@ __device__ __forceinline__ void finish_launch(const DevComm& c, uint64_t rounds,
             c.state->round_seq += rounds;
             c.state->barrier_seq += barriers;
             c.state->nvls_round_seq += nvls_rounds;
+            c.state->ring_seq += ring_msgs;
             c.state->done_ctas = 0;
             __threadfence();
         }

@@ -39,6 +39,11 @@ cudaError_t LaunchBandwidthProbe(void* dst, const void* src, unsigned long long 
 cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long bytes, unsigned long long seg, int mode,
                              int nctas, cudaStream_t stream);
 
+// Ring AllReduce between neighbours (reduce-scatter then all-gather), `block` bytes per message
+// (multiple of 256), at most max_ctas channels.
+cudaError_t LaunchRingAllReduce(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
+                                int op, float scale, unsigned long long block, int max_ctas, cudaStream_t stream);
+
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.
 bool NvlsSupports(int dtype, int op);
 

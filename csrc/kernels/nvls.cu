@@ -111,7 +111,18 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
         char* dst = static_cast<char*>(p.dst) + cbeg;
         if (p.func == 1) {  // Broadcast
             if (r == p.root) {
-                for (size_t off = lo + t * 16; off < hi; off += nt * 16) mm_st(mc + off, load_partial(src + off, hi - off));
+                size_t off = lo + t * 16;
+                // Four 16-byte loads in flight per thread, then their multicast stores.
+                if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                    for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
+                        uint4 v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(src + off + u * nt * 16);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) mm_st(mc + off + u * nt * 16, v[u]);
+                    }
+                }
+                for (; off < hi; off += nt * 16) mm_st(mc + off, load_partial(src + off, hi - off));
             }
             if (!cta_barrier(c, ++bar, j)) break;
             if (lo < hi && r != p.root) cta_copy(dst + lo, uc + lo, hi - lo, true);
@@ -120,11 +131,32 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
             if (lo < hi) cta_copy(uc + lo, src + lo, hi - lo, false);
             if (!cta_barrier(c, ++bar, 2 * j)) break;
             if (r == p.root) {
-                for (size_t off = lo + t * 16; off < hi; off += nt * 16) {
+                constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
+                const bool post = p.op == kAvg || p.scale != 1.0f;
+                size_t off = lo + t * 16;
+                // Four switch reductions in flight per thread (each is a round trip through the
+                // switch to every GPU), then their stores.
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
+                        V16<D> v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(mc + off + u * nt * 16);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (post) {
+#pragma unroll
+                                for (int e = 0; e < E; ++e)
+                                    v[u].b[e] = Ty<D>::store(
+                                        epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v[u].b[e]), n, p.scale));
+                            }
+                            *reinterpret_cast<uint4*>(dst + off + u * nt * 16) = v[u].u;
+                        }
+                    }
+                }
+                for (; off < hi; off += nt * 16) {
                     V16<D> v;
                     v.u = red16<D, O>(mc + off);
-                    constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
-                    if (p.op == kAvg || p.scale != 1.0f) {
+                    if (post) {
 #pragma unroll
                         for (int e = 0; e < E; ++e)
                             v.b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v.b[e]), n, p.scale));

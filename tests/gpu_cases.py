@@ -78,7 +78,7 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
     dev = rank % torch.cuda.device_count()
     torch.cuda.set_device(dev)
     comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
-    algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS}
+    algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS, "ring": Algo.RING}
     ran = 0
     used = set()
     dtypes = ["float32", "bfloat16", "int32"] if quick else DTYPES
@@ -195,7 +195,7 @@ def run_mixed_sequence(rank: int, world: int, steps: int = 60) -> Dict:
     comm = occl.init_from_env(device=dev, timeout_ms=20000)  # async: enqueue back to back
     rng = random.Random(99)
     pending = []
-    algos = [Algo.AUTO, Algo.ONESHOT, Algo.TWOSHOT, Algo.NVLS]
+    algos = [Algo.AUTO, Algo.ONESHOT, Algo.TWOSHOT, Algo.NVLS, Algo.RING]
     for i in range(steps):
         n = rng.choice([3, 1000, 65536 + 7, 1 << 20, (5 << 20) + 11])
         kind = rng.choice(["ar", "ar", "ag", "rs", "bc", "red"])

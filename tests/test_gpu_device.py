@@ -37,8 +37,9 @@ def test_single_rank_large_multi_round():
 @pytest.mark.multigpu
 def test_two_rank_suite_all_algorithms():
     _need(2)
-    res = _mp.run(2, gpu_cases.run_suite, [1, 33, 65537, (3 << 20) + 5], ["oneshot", "twoshot", "nvls", "auto"],
+    res = _mp.run(2, gpu_cases.run_suite, [1, 33, 65537, (3 << 20) + 5], ["oneshot", "twoshot", "nvls", "ring", "auto"],
                   timeout=900)
+    assert "ring" in res[0]["algorithms"]
     assert res[0]["ran"] > 0
 
 
