@@ -41,14 +41,19 @@ CollFunc ParseFunc(const std::string& s) {
 std::vector<TuningRow> DefaultTable() {
     return {
         {CollFunc::AllReduce, 0, 256 << 10, Algo::kOneShot, 0},
+        // Two ranks (2 x B200): the switch reads the issuing GPU's own copy too, so NVLS moves
+        // 1.5*S per direction against S for the peer-to-peer kernels. Pipelined push up to
+        // 8 MiB, the ring (fine-grained neighbour flags) up to 96 MiB, two-shot above.
         {CollFunc::AllReduce, 2, 1 << 20, Algo::kOneShot, 0},
-        // Two ranks: the switch reads the issuing GPU's own copy too, so NVLS moves 1.5*S per
-        // direction against S for two-shot.
+        {CollFunc::AllReduce, 2, 8 << 20, Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 2, 96 << 20, Algo::kRing, 0},
         {CollFunc::AllReduce, 2, ~size_t(0), Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 0, 1 << 20, Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::Broadcast, 2, ~size_t(0), Algo::kOneShot, 0},
         {CollFunc::Broadcast, 0, 512 << 10, Algo::kOneShot, 0},
         {CollFunc::Broadcast, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::Reduce, 2, ~size_t(0), Algo::kOneShot, 0},
         {CollFunc::Reduce, 0, 512 << 10, Algo::kOneShot, 0},
         {CollFunc::Reduce, 0, ~size_t(0), Algo::kNvls, 0},
         {CollFunc::AllGather, 0, ~size_t(0), Algo::kOneShot, 0},

@@ -86,7 +86,11 @@ def test_algorithm_table():
     assert choose(AR, 8, 8, True)[0] == ONESHOT
     assert choose(AR, 64 << 20, 8, True)[0] == NVLS
     assert choose(AR, 64 << 20, 8, False)[0] == TWOSHOT       # no multicast -> two-shot
-    assert choose(AR, 64 << 20, 2, True)[0] == TWOSHOT        # two ranks: push path
+    assert choose(AR, 4 << 20, 2, True)[0] == TWOSHOT         # two ranks: pipelined push
+    assert choose(AR, 64 << 20, 2, True)[0] == 4              # two ranks, mid sizes: ring
+    assert choose(AR, 256 << 20, 2, True)[0] == TWOSHOT       # two ranks, large: two-shot
+    assert choose(BC, 256 << 20, 2, True)[0] == ONESHOT       # two ranks: no NVLS for Broadcast
+    assert choose(BC, 256 << 20, 8, True)[0] == NVLS
     assert choose(AG, 64 << 20, 8, True)[0] == ONESHOT
     assert choose(AR, 8, 8, True)[1] == 1
 
