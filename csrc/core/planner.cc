@@ -40,7 +40,6 @@ CollFunc ParseFunc(const std::string& s) {
 // payloads go to NVLS, which moves S*(1+1/N) bytes per direction instead of 2*S*(N-1)/N.
 std::vector<TuningRow> DefaultTable() {
     return {
-        {CollFunc::AllReduce, 0, 256 << 10, Algo::kOneShot, 0},
         // Two ranks (2 x B200): the switch reads the issuing GPU's own copy too, so NVLS moves
         // 1.5*S per direction against S for the peer-to-peer kernels. Pipelined push up to
         // 8 MiB, the ring (fine-grained neighbour flags) up to 96 MiB, two-shot above.
@@ -48,7 +47,10 @@ std::vector<TuningRow> DefaultTable() {
         {CollFunc::AllReduce, 2, 8 << 20, Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 2, 96 << 20, Algo::kRing, 0},
         {CollFunc::AllReduce, 2, ~size_t(0), Algo::kTwoShot, 0},
-        {CollFunc::AllReduce, 0, 1 << 20, Algo::kTwoShot, 0},
+        // Three or more ranks (8 x B200): one-shot up to 1 MiB, pipelined two-shot up to 8 MiB,
+        // NVLS above.
+        {CollFunc::AllReduce, 0, 1 << 20, Algo::kOneShot, 0},
+        {CollFunc::AllReduce, 0, 8 << 20, Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 0, ~size_t(0), Algo::kNvls, 0},
         {CollFunc::Broadcast, 2, ~size_t(0), Algo::kOneShot, 0},
         {CollFunc::Broadcast, 0, 512 << 10, Algo::kOneShot, 0},

@@ -436,10 +436,10 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const int slots = PipeSlots();
     // Rounds of at least `min_chunk` bytes (each CTA then moves >= ~100 KB between fences),
     // about `rounds` of them so the software pipeline has something to overlap.
-    // Two rounds up to 16 MiB, four above (measured on 2 x B200: fewer, larger rounds win until
-    // the pipeline's fill and drain dominate).
+    // Two rounds up to 64 MiB, four above (measured on 2 and 8 x B200: fewer, larger rounds win
+    // until the pipeline's fill and drain dominate).
     const unsigned long long rounds = static_cast<unsigned long long>(
-        std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", bytes <= (16u << 20) ? 2 : 4)));
+        std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", bytes <= (64u << 20) ? 2 : 4)));
     const unsigned long long min_chunk = static_cast<unsigned long long>(EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20));
     auto pick_chunk = [&](unsigned long long cap) {
         unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, q);

@@ -1,4 +1,4 @@
-"""Samples GPU clocks and throttle reasons with nvidia-smi while a timed region runs.
+"""Samples GPU clocks and throttle reasons while a timed region runs.
 
 Usage::
 
@@ -6,7 +6,10 @@ Usage::
         ...timed work...
     summary = cs.summary()   # {"sm_mhz": median under load, "sm_max_mhz": ..., "reasons": [...]}
 
-Reading clocks is all it does; it never changes a GPU setting.
+NVML (``pynvml``) is polled from a thread every ``interval_ms`` (default 2 ms), with one sample
+taken on entry and one on exit, so even a timed region of a few milliseconds is covered; without
+NVML it falls back to ``nvidia-smi -lms``. Reading clocks is all it does; it never changes a GPU
+setting.
 """
 from __future__ import annotations
 
@@ -17,40 +20,86 @@ import threading
 import time
 from typing import Dict, List, Optional
 
-_FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "utilization.gpu",
-           "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
-           "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
 _REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+# NVML clock-event (throttle) reason bits.
+_REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+_SMI_FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "utilization.gpu",
+               "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+               "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
 
 
 class ClockSampler:
-    def __init__(self, gpu_indices: Optional[List[int]] = None, interval_ms: int = 100) -> None:
+    def __init__(self, gpu_indices: Optional[List[int]] = None, interval_ms: float = 2.0) -> None:
         self.gpus = gpu_indices
         self.interval_ms = interval_ms
         self.samples: List[Dict] = []
-        self._proc: Optional[subprocess.Popen] = None
+        self.source = "none"
+        self._stop = threading.Event()
         self._thread: Optional[threading.Thread] = None
+        self._proc: Optional[subprocess.Popen] = None
+        self._nvml = None
+        self._handles: List = []
 
-    def __enter__(self) -> "ClockSampler":
+    # ------------------------------------------------------------------ NVML
+    def _nvml_start(self) -> bool:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+        except Exception:
+            return False
+        self._nvml = pynvml
+        idx = self.gpus if self.gpus is not None else list(range(pynvml.nvmlDeviceGetCount()))
+        try:
+            self._handles = [(i, pynvml.nvmlDeviceGetHandleByIndex(i)) for i in idx]
+        except Exception:
+            return False
+        self.source = "nvml"
+        self._nvml_sample()
+        self._thread = threading.Thread(target=self._nvml_loop, daemon=True)
+        self._thread.start()
+        return True
+
+    def _nvml_sample(self) -> None:
+        nv = self._nvml
+        for i, h in self._handles:
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                sm_max = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+                power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                util = float(nv.nvmlDeviceGetUtilizationRates(h).gpu)
+                get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                bits = int(get_reasons(h))
+            except Exception:
+                continue
+            self.samples.append({"index": i, "sm": sm, "sm_max": sm_max, "power": power, "util": util,
+                                 **{r: bool(bits & _REASON_BITS[r]) for r in _REASONS}})
+
+    def _nvml_loop(self) -> None:
+        while not self._stop.wait(self.interval_ms / 1000.0):
+            self._nvml_sample()
+
+    # ------------------------------------------------------------------ nvidia-smi fallback
+    def _smi_start(self) -> None:
         exe = shutil.which("nvidia-smi")
         if exe is None:
-            return self
-        cmd = [exe, f"--query-gpu={','.join(_FIELDS)}", "--format=csv,noheader,nounits", f"-lms={self.interval_ms}"]
+            return
+        cmd = [exe, f"--query-gpu={','.join(_SMI_FIELDS)}", "--format=csv,noheader,nounits",
+               f"-lms={max(int(self.interval_ms), 20)}"]
         try:
             self._proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self._proc = None
-            return self
-        self._thread = threading.Thread(target=self._reader, daemon=True)
+            return
+        self.source = "nvidia-smi"
+        self._thread = threading.Thread(target=self._smi_reader, daemon=True)
         self._thread.start()
         time.sleep(0.05)
-        return self
 
-    def _reader(self) -> None:
+    def _smi_reader(self) -> None:
         assert self._proc is not None and self._proc.stdout is not None
         for line in self._proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) != len(_FIELDS):
+            if len(parts) != len(_SMI_FIELDS):
                 continue
             try:
                 idx = int(parts[0])
@@ -58,6 +107,7 @@ class ClockSampler:
                 continue
             if self.gpus is not None and idx not in self.gpus:
                 continue
+
             def num(s: str) -> float:
                 try:
                     return float(s)
@@ -67,7 +117,16 @@ class ClockSampler:
                                  "util": num(parts[4]),
                                  **{r: parts[5 + i] == "Active" for i, r in enumerate(_REASONS)}})
 
+    # ------------------------------------------------------------------ context manager
+    def __enter__(self) -> "ClockSampler":
+        if self.gpus == []:
+            return self
+        if not self._nvml_start():
+            self._smi_start()
+        return self
+
     def __exit__(self, *exc) -> None:
+        self._stop.set()
         if self._proc is not None:
             self._proc.terminate()
             try:
@@ -76,13 +135,20 @@ class ClockSampler:
                 self._proc.kill()
         if self._thread is not None:
             self._thread.join(timeout=5)
+        if self._nvml is not None:
+            self._nvml_sample()
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self) -> Dict:
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
         loaded = [s for s in self.samples if s["util"] >= 50] or self.samples
         reasons = sorted({r for s in loaded for r in _REASONS if s[r]})
         return {"sm_mhz": statistics.median(s["sm"] for s in loaded),
                 "sm_max_mhz": max(s["sm_max"] for s in self.samples),
                 "power_w_max": max(s["power"] for s in self.samples),
-                "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded)}
+                "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded),
+                "source": self.source}

@@ -84,6 +84,8 @@ def test_algorithm_table():
 
     ONESHOT, TWOSHOT, NVLS = 1, 2, 3
     assert choose(AR, 8, 8, True)[0] == ONESHOT
+    assert choose(AR, 1 << 20, 8, True)[0] == ONESHOT
+    assert choose(AR, 4 << 20, 8, True)[0] == TWOSHOT
     assert choose(AR, 64 << 20, 8, True)[0] == NVLS
     assert choose(AR, 64 << 20, 8, False)[0] == TWOSHOT       # no multicast -> two-shot
     assert choose(AR, 4 << 20, 2, True)[0] == TWOSHOT         # two ranks: pipelined push
