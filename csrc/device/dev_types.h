@@ -73,7 +73,7 @@ struct TraceRecord {
 
 enum TraceEvent : unsigned short {
     kTrBegin = 1,     // kernel start
-    kTrStaged = 2,    // G1: round staged (copy-in / push done, flag sent)
+    kTrStaged = 2,    // a CTA issued its phases of a pipeline iteration (before the barrier)
     kTrReadyWait = 3, // G2: ready flags observed
     kTrReduced = 4,   // G2: reduce done, flag sent
     kTrDoneWait = 5,  // G3: reduced flags observed

@@ -367,14 +367,6 @@ void DeviceEngine::Abort() {
     if (abort_host_) *reinterpret_cast<volatile int*>(abort_host_) = 1;
 }
 
-const SymBuffer* DeviceEngine::FindSym(const void* p, size_t bytes) const {
-    const char* c = static_cast<const char*>(p);
-    for (const SymBuffer& b : user_bufs_) {
-        if (b.mc && c >= b.ptr[rank_] && c + bytes <= b.ptr[rank_] + b.bytes) return &b;
-    }
-    return nullptr;
-}
-
 void* DeviceEngine::SymAlloc(size_t bytes) {
     cudaSetDevice(device_);
     SymBuffer b;

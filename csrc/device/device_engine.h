@@ -75,7 +75,6 @@ public:
 private:
     bool FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream);
     bool LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream);
-    const SymBuffer* FindSym(const void* p, size_t bytes) const;
 
     int rank_ = 0;
     int nranks_ = 1;

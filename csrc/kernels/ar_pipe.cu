@@ -67,9 +67,6 @@ __device__ __forceinline__ void st_relaxed_gpu(uint64_t* p, uint64_t v) {
 }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
-__device__ __forceinline__ uint64_t* pipe_flag(char* uc_base, size_t off, int cta, int src) {
-    return reinterpret_cast<uint64_t*>(uc_base + off) + (size_t)cta * kMaxRanks + src;
-}
 
 // Group copy, `kUnroll` 16-byte vectors in flight per thread.
 __device__ __forceinline__ void grp_copy(char* d, const char* s, size_t bytes, int tid, int nt, bool cg) {

@@ -279,3 +279,44 @@ def run_tp(rank: int, world: int, ms: int = 256, k: int = 512, nf: int = 384, hd
         assert err2 < 3e-2, f"gemm_reduce_scatter call {c}: rel err {err2}"
     comm.destroy()
     return {"ag_err": worst_ag, "rs_err": worst_rs}
+
+
+def run_dp(rank: int, world: int, hidden: int = 256, steps: int = 2) -> Dict:
+    """Data-parallel sync on the GPU (buckets on a side stream during backward, small tensors
+    as one group) against gradients averaged locally from every rank's batch."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200.models import TinyLlamaStack
+    from originccl_b200.parallel.data_parallel import DataParallelSync, GradBuckets
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, timeout_ms=20000)
+
+    def grads_of(r: int):
+        m = TinyLlamaStack(hidden=hidden, ffn=3 * hidden, layers=2, seed=5).cuda()
+        g = torch.Generator(device="cuda").manual_seed(300 + r)
+        m(torch.randn(32, hidden, device="cuda", generator=g)).pow(2).mean().backward()
+        return {n: p.grad.detach().clone() for n, p in m.named_parameters()}
+
+    model = TinyLlamaStack(hidden=hidden, ffn=3 * hidden, layers=2, seed=5).cuda()
+    grads = GradBuckets(model.named_parameters(), bucket_bytes=64 << 10, small_bytes=4096)
+    dp = DataParallelSync(comm, grads)
+    dp.attach()
+    g = torch.Generator(device="cuda").manual_seed(300 + rank)
+    x = torch.randn(32, hidden, device="cuda", generator=g)
+    for _ in range(steps):
+        grads.zero_()
+        model(x).pow(2).mean().backward()
+        dp.finish()
+    torch.cuda.synchronize()
+    expect = [grads_of(r) for r in range(world)]
+    worst = 0.0
+    for n, p in model.named_parameters():
+        ref = sum(e[n] for e in expect) / world
+        err = ((p.grad - ref).abs().max() / ref.abs().max().clamp_min(1e-12)).item()
+        worst = max(worst, err)
+        assert err < 1e-4, f"{n}: relative error {err}"
+    comm.destroy()
+    return {"buckets": grads.num_buckets, "small": len(grads.small_idx), "worst": worst}

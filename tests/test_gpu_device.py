@@ -108,3 +108,10 @@ def test_tp_fused_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_tp, timeout=600)
     assert res[0]["rs_err"] < 3e-2
+
+
+@pytest.mark.multigpu
+def test_data_parallel_sync_two_ranks():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_dp, timeout=300)
+    assert res[0]["buckets"] > 1 and res[0]["small"] > 0
