@@ -4,6 +4,7 @@
 //   bccl_run -np 4 bccl_check check                 # host memory (shared memory / TCP)
 //   bccl_run -np 2 --gpus bccl_check check --device # GPU buffers (one GPU per rank)
 //   bccl_run -np 4 bccl_check bench --counts 32768,131072 --warmup 20 --iters 100
+//   bccl_run -np 4 bccl_check bench-group --messages 64 --message-bytes 262144
 //
 // check: every collective with exact-valued inputs (integers, and floats that are multiples of
 // 1/8), out of place and in place, a sentinel element after every output, nested groups,
@@ -354,13 +355,62 @@ int RunBench(Communicator* comm, Mem mem, int rank, int world, const std::vector
     return rc;
 }
 
+// Many small AllReduces in one group (the reference's --group-small benchmark,
+// tests/benchmark/test_allreduce_benchmark.cpp:423-490): messages per second, max over ranks.
+int RunGroupBench(Communicator* comm, Mem mem, int rank, int world, int nmsg, size_t bytes, int warmup, int iters) {
+    const size_t n = bytes / sizeof(float);
+    std::vector<void*> bufs;
+    std::vector<float> host(n);
+    for (int k = 0; k < nmsg; ++k) {
+        for (size_t i = 0; i < n; ++i) host[i] = Value<float>(rank + k, i);
+        void* b = mem.Alloc(n * sizeof(float));
+        mem.Put(b, host.data(), n * sizeof(float));
+        bufs.push_back(b);
+    }
+    auto one = [&]() {
+        comm->GroupStart();
+        bool ok = true;
+        for (int k = 0; k < nmsg && ok; ++k) ok = comm->AllReduce(bufs[k], bufs[k], n, DataType::FLOAT32, ReduceOp::MAX);
+        return comm->GroupEnd() && ok;
+    };
+    bool ok = true;
+    for (int w = 0; w < warmup && ok; ++w) ok = one();
+    // MAX of identical-per-rank inputs is idempotent: check the first buffer after the warm-up.
+    std::vector<float> out(n);
+    mem.Get(out.data(), bufs[0], n * sizeof(float));
+    for (size_t i = 0; ok && i < n; ++i) {
+        float want = Value<float>(0, i);
+        for (int r = 1; r < world; ++r) want = std::max(want, Value<float>(r, i));
+        ok = out[i] == want;
+    }
+    ok = ok && comm->Barrier();
+    auto t0 = std::chrono::steady_clock::now();
+    for (int it = 0; it < iters && ok; ++it) ok = one();
+    double us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count() / iters;
+    double tmax = us;
+    void* tb = mem.Alloc(sizeof(double));
+    mem.Put(tb, &us, sizeof(double));
+    ok = ok && comm->AllReduce(tb, tb, 1, DataType::FLOAT64, ReduceOp::MAX);
+    mem.Get(&tmax, tb, sizeof(double));
+    mem.Free(tb);
+    if (rank == 0) {
+        std::printf("{\"op\": \"allreduce_group\", \"path\": \"%s\", \"ranks\": %d, \"messages\": %d, "
+                    "\"bytes_per_message\": %zu, \"us_per_group\": %.1f, \"msgs_per_s\": %.0f, \"check\": %s}\n",
+                    mem.device ? "device" : "host", world, nmsg, bytes, tmax, nmsg / tmax * 1e6, ok ? "true" : "false");
+        std::fflush(stdout);
+    }
+    for (void* b : bufs) mem.Free(b);
+    return ok ? 0 : 1;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     std::string mode = argc > 1 ? argv[1] : "check";
     bool device = false;
     std::vector<size_t> counts = {32768, 131072};
-    int warmup = 20, iters = 100, channels = 0;
+    int warmup = 20, iters = 100, channels = 0, nmsg = 64;
+    size_t msg_bytes = 256u << 10;
     for (int i = 2; i < argc; ++i) {
         std::string a = argv[i];
         if (a == "--device") device = true;
@@ -368,6 +418,8 @@ int main(int argc, char** argv) {
         else if (a == "--warmup" && i + 1 < argc) warmup = std::atoi(argv[++i]);
         else if (a == "--iters" && i + 1 < argc) iters = std::atoi(argv[++i]);
         else if (a == "--channels" && i + 1 < argc) channels = std::atoi(argv[++i]);
+        else if (a == "--messages" && i + 1 < argc) nmsg = std::atoi(argv[++i]);
+        else if (a == "--message-bytes" && i + 1 < argc) msg_bytes = static_cast<size_t>(std::atoll(argv[++i]));
     }
     const int rank = EnvInt("BCCL_RANK", 0), world = EnvInt("BCCL_WORLD_SIZE", 1);
     Communicator comm;
@@ -391,6 +443,8 @@ int main(int argc, char** argv) {
     int rc = 0;
     if (mode == "bench") {
         rc = RunBench(&comm, mem, rank, world, counts, warmup, iters);
+    } else if (mode == "bench-group") {
+        rc = RunGroupBench(&comm, mem, rank, world, nmsg, msg_bytes, warmup, iters);
     } else {
         Checker c{&comm, mem, rank, world};
         for (size_t n : {size_t(1), size_t(1000), size_t(32768 + 3)}) {

@@ -71,6 +71,7 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     const long ncores = sysconf(_SC_NPROCESSORS_ONLN);
     n_channels_ = cfg.n_channels > 0 ? cfg.n_channels : 4;
     n_channels_ = std::max(1, std::min(n_channels_, 16));
+    split_bytes_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_HOST_SPLIT_BYTES", 1 << 20)));
     // The reference switches to its epoll executor when ranks outnumber cores
     // (src/communicator.cpp:37-45); here that choice drives how Send/Recv wait.
     std::string ex = EnvStr("BCCL_HOST_EXECUTOR", "");
@@ -575,9 +576,7 @@ bool HostEngine::ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t
     return true;
 }
 
-bool HostEngine::RunCollective(int ch, const CollTask& t) {
-    size_t e0, e1;
-    ChannelSlice(t.count, n_channels_, ch, &e0, &e1);
+bool HostEngine::RunSlice(int ch, const CollTask& t, size_t e0, size_t e1) {
     switch (t.func) {
     case CollFunc::AllReduce: return AllReduceSlice(ch, t, e0, e1, false);
     case CollFunc::Reduce: return AllReduceSlice(ch, t, e0, e1, true);
@@ -673,6 +672,7 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
         return false;
     }
     std::vector<CollTask> p2p;
+    std::vector<const CollTask*> work;
     for (const CollTask& t : sorted) {
         if (IsP2p(t.func)) {
             p2p.push_back(t);
@@ -690,10 +690,51 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
             }
             continue;
         }
-        const CollTask* tp = &t;
-        if (!RunOnChannels([this, tp](int ch) { return RunCollective(ch, *tp); })) return false;
+        work.push_back(&t);
+    }
+    if (!work.empty()) {
+        const std::vector<std::vector<WorkUnit>> plan = PlanChannels(work);
+        if (!RunOnChannels([this, &plan](int ch) {
+                for (const WorkUnit& u : plan[static_cast<size_t>(ch)])
+                    if (!RunSlice(ch, *u.task, u.e0, u.e1)) return false;
+                return true;
+            })) {
+            return false;
+        }
     }
     return RunP2p(p2p);
+}
+
+// The whole batch becomes one job per channel thread. A collective of at least
+// split_bytes_ (BCCL_HOST_SPLIT_BYTES, default 1 MiB) is cut into one slice per channel; a smaller one goes whole to the channel with
+// the fewest bytes so far (ties: lowest index). The plan depends only on the sorted task list,
+// which every rank builds identically, so channel c runs the same slices in the same order on
+// every rank and the per-channel barriers and connections line up. This is the reference's
+// dynamic executor's goal (many small collectives spread over the channels instead of each one
+// waking every channel) without its rank-0 in-band broadcast.
+std::vector<std::vector<HostEngine::WorkUnit>> HostEngine::PlanChannels(const std::vector<const CollTask*>& work) const {
+    std::vector<std::vector<WorkUnit>> plan(static_cast<size_t>(n_channels_));
+    std::vector<size_t> load(static_cast<size_t>(n_channels_), 0);
+    for (const CollTask* t : work) {
+        const size_t bytes = t->count * DataTypeSize(t->dtype);
+        if (bytes < split_bytes_ || n_channels_ == 1) {
+            size_t best = 0;
+            for (size_t c = 1; c < load.size(); ++c)
+                if (load[c] < load[best]) best = c;
+            plan[best].push_back({t, 0, t->count});
+            load[best] += bytes;
+            continue;
+        }
+        for (int ch = 0; ch < n_channels_; ++ch) {
+            size_t e0, e1;
+            ChannelSlice(t->count, n_channels_, ch, &e0, &e1);
+            if (e1 > e0) {
+                plan[static_cast<size_t>(ch)].push_back({t, e0, e1});
+                load[static_cast<size_t>(ch)] += (e1 - e0) * DataTypeSize(t->dtype);
+            }
+        }
+    }
+    return plan;
 }
 
 }  // namespace bccl

@@ -76,7 +76,13 @@ private:
         std::vector<char> scratch;                                // leader-private receive space
     };
 
-    bool RunCollective(int ch, const CollTask& t);
+    struct WorkUnit {
+        const CollTask* task;
+        size_t e0, e1;  // element range of this slice
+    };
+    std::vector<std::vector<WorkUnit>> PlanChannels(const std::vector<const CollTask*>& work) const;
+    size_t split_bytes_ = 1u << 20;
+    bool RunSlice(int ch, const CollTask& t, size_t e0, size_t e1);
     bool AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1, bool reduce_only);
     bool BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1);
     bool AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1);

@@ -72,3 +72,13 @@ def test_cpp_check_matrix_device_one_gpu():
     assert r.returncode == 0, r.stdout + r.stderr
     res = _json_lines(r.stdout)[-1]
     assert res["failed_all_ranks"] == 0 and res["path"] == "device"
+
+
+def test_cpp_group_benchmark_host_many_small_messages():
+    # The reference's --group-small case: many 256 KiB AllReduces in one group, spread over the
+    # channel threads by the host engine's planner.
+    r = _run(["-np", "3", "--timeout", "150", "--", CHECK, "bench-group", "--messages", "24",
+              "--message-bytes", "65536", "--warmup", "2", "--iters", "3"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    rec = _json_lines(r.stdout)[-1]
+    assert rec["check"] and rec["messages"] == 24 and rec["msgs_per_s"] > 0
