@@ -47,6 +47,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
     p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--no-clocks", action="store_true", help="diagnostic: do not sample clocks (no clocks key)")
     return p.parse_args()
 
 
@@ -100,18 +101,18 @@ def main() -> None:
         dist.all_reduce(check)
     max_err = float((y.float() - check).abs().max().item()) if args.warmup > 0 else 0.0
 
-    gpus = [int(d) for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip().isdigit()]
-    gpus = gpus or list(range(world))
+    # Clocks of rank 0's GPU (NVML index = its position in CUDA_VISIBLE_DEVICES, if set).
+    visible = [int(d) for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip().isdigit()]
+    gpus = [visible[local] if local < len(visible) else local]
     launches0 = comm.kernel_launches
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(gpus if rank == 0 else []) as clocks:
-        start.record()
-        for i in range(args.steps):
-            step(i)
-        end.record()
-        torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        step(i)
+    end.record()
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     launches = comm.kernel_launches - launches0
@@ -120,6 +121,7 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+
     algbw = nbytes / (ms * 1e-3) / 1e9
     factor = busbw_factor("allreduce", world)
     busbw = algbw * factor
@@ -169,6 +171,20 @@ def main() -> None:
     e2e_algbw = nbytes / (e2e_ms * 1e-3) / 1e9
     e2e_value = e2e_algbw * factor * world if world > 1 else e2e_algbw
 
+    # Clocks and throttle reasons under the same load: the same AllReduce loop for ~200 ms after
+    # the measurements, sampled through NVML on rank 0's GPU. NVML queries during the timed loop
+    # itself (even one sample before it) slowed the 2-GPU loop 1.9x (0.535 vs 0.282 ms per step),
+    # so no measured loop runs with them; clock locks and throttling persist far longer than
+    # this window, so it shows the state the timed region ran in.
+    n_clk = max(20, int(200.0 / max(ms, 1e-3)))
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpus if rank == 0 and not args.no_clocks else [], interval_ms=10.0) as clocks:
+        for i in range(n_clk):
+            step(i)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
     if rank == 0:
         out = {
             "metric": "AllReduce bus GB/s vs size at 2/4/8 B200 (max over ranks) vs reference & NCCL",
@@ -205,7 +221,8 @@ def main() -> None:
                     "d2h_bytes_per_step": sample.numel() * esize, "steps": args.e2e_steps,
                     "api": "originccl_b200.Communicator.all_reduce"},
             "gpu_launches": launches,
-            "clocks": clocks.summary(),
+            "clocks": {**clocks.summary(), "window": f"{n_clk} more steps of the same loop after the timed, "
+                        "NCCL and e2e loops (NVML during a timed loop perturbs it)"},
         }
         print(json.dumps(out), flush=True)
     comm.destroy()

@@ -6,10 +6,14 @@ Usage::
         ...timed work...
     summary = cs.summary()   # {"sm_mhz": median under load, "sm_max_mhz": ..., "reasons": [...]}
 
-NVML (``pynvml``) is polled from a thread every ``interval_ms`` (default 2 ms), with one sample
-taken on entry and one on exit, so even a timed region of a few milliseconds is covered; without
-NVML it falls back to ``nvidia-smi -lms``. Reading clocks is all it does; it never changes a GPU
-setting.
+NVML (``pynvml``) is polled from a thread every ``interval_ms`` (default 20 ms), with one sample
+taken on entry and one on exit; without NVML it falls back to ``nvidia-smi -lms``. Reading clocks
+is all it does; it never changes a GPU setting.
+
+NVML queries are not free for the GPU being measured: polling several quantities of every GPU
+every 2 ms slowed a two-GPU AllReduce loop about fourfold. So the polling thread reads only the
+SM clock and the clock-event reasons; the maximum clock and the power draw are read on entry
+and on exit, outside the timed work.
 """
 from __future__ import annotations
 
@@ -29,7 +33,7 @@ _SMI_FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "utilization
 
 
 class ClockSampler:
-    def __init__(self, gpu_indices: Optional[List[int]] = None, interval_ms: float = 2.0) -> None:
+    def __init__(self, gpu_indices: Optional[List[int]] = None, interval_ms: float = 20.0) -> None:
         self.gpus = gpu_indices
         self.interval_ms = interval_ms
         self.samples: List[Dict] = []
@@ -54,26 +58,26 @@ class ClockSampler:
         except Exception:
             return False
         self.source = "nvml"
-        self._nvml_sample()
+        self._nvml_sample(full=True)
         self._thread = threading.Thread(target=self._nvml_loop, daemon=True)
         self._thread.start()
         return True
 
-    def _nvml_sample(self) -> None:
+    def _nvml_sample(self, full: bool = False) -> None:
         nv = self._nvml
         for i, h in self._handles:
             try:
                 sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                sm_max = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
-                power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                util = float(nv.nvmlDeviceGetUtilizationRates(h).gpu)
                 get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                     nv.nvmlDeviceGetCurrentClocksThrottleReasons
                 bits = int(get_reasons(h))
+                rec = {"index": i, "sm": sm, **{r: bool(bits & _REASON_BITS[r]) for r in _REASONS}}
+                if full:
+                    rec["sm_max"] = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+                    rec["power"] = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
             except Exception:
                 continue
-            self.samples.append({"index": i, "sm": sm, "sm_max": sm_max, "power": power, "util": util,
-                                 **{r: bool(bits & _REASON_BITS[r]) for r in _REASONS}})
+            self.samples.append(rec)
 
     def _nvml_loop(self) -> None:
         while not self._stop.wait(self.interval_ms / 1000.0):
@@ -136,7 +140,7 @@ class ClockSampler:
         if self._thread is not None:
             self._thread.join(timeout=5)
         if self._nvml is not None:
-            self._nvml_sample()
+            self._nvml_sample(full=True)
             try:
                 self._nvml.nvmlShutdown()
             except Exception:
@@ -145,10 +149,14 @@ class ClockSampler:
     def summary(self) -> Dict:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
-        loaded = [s for s in self.samples if s["util"] >= 50] or self.samples
+        # nvidia-smi samples carry a utilization; NVML polls do not (a utilization query is one
+        # more call per poll) and are all taken while the timed work runs.
+        loaded = [s for s in self.samples if s.get("util", 100.0) >= 50] or self.samples
         reasons = sorted({r for s in loaded for r in _REASONS if s[r]})
+        maxes = [s["sm_max"] for s in self.samples if "sm_max" in s]
+        powers = [s["power"] for s in self.samples if "power" in s]
         return {"sm_mhz": statistics.median(s["sm"] for s in loaded),
-                "sm_max_mhz": max(s["sm_max"] for s in self.samples),
-                "power_w_max": max(s["power"] for s in self.samples),
+                "sm_max_mhz": max(maxes) if maxes else None,
+                "power_w_max": max(powers) if powers else None,
                 "reasons": reasons, "samples": len(self.samples), "samples_under_load": len(loaded),
                 "source": self.source}
