@@ -120,3 +120,9 @@ def test_tuning_table_from_sweeps_is_loaded_by_the_planner(tmp_path, monkeypatch
         return algo.value
 
     assert [choose(n) for n in (512, 8192, 65536, 1 << 22, 1 << 30)] == [1, 1, 2, 3, 3]
+
+
+def test_env_report_runs_without_a_gpu():
+    from originccl_b200.utils import env_report
+    r = env_report.report()
+    assert r["python"] and "bccl" in r and "topology" in r
