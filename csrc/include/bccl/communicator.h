@@ -10,6 +10,8 @@
 //   * count 0 succeeds with null buffers; Reduce's non-root recv may be null; AllGather's
 //     output is ordered by rank; ReduceScatter takes N*count inputs; in place is allowed;
 //   * AVG is SUM divided by the rank count.
+// A communicator is used by one thread at a time (like the reference's and NCCL's): calls from
+// several threads, e.g. from autograd hooks during backward, must not overlap.
 // Device communicators (CommConfig::device >= 0) take device pointers; with no stream in
 // the config every call blocks until its result is ready (the reference's contract); with
 // a stream, calls only enqueue (NCCL's contract) and errors surface on the next call or

@@ -124,7 +124,9 @@ class DataParallelSync:
     """Averages :class:`GradBuckets` over the ranks of ``comm`` (a :class:`~originccl_b200.Communicator`).
 
     All ranks must sync the same buckets in the same order; both :meth:`sync` and the hooks of
-    :meth:`attach` launch buckets strictly in index order.
+    :meth:`attach` launch buckets strictly in index order. The hooks run on the autograd thread
+    and call the communicator from there: do not use the same communicator from another thread
+    while backward runs.
     """
 
     def __init__(self, comm, grads: GradBuckets, *, average: bool = True, stream=None) -> None:

@@ -224,3 +224,29 @@ def run_init_only(rank: int, world: int) -> Dict:
     r = comm.rank
     comm.destroy()
     return {"rank": r}
+
+
+def run_many(rank: int, world: int) -> Dict:
+    """all_reduce_many: grouped and ungrouped batches of host tensors, against a local oracle."""
+    import torch
+    from originccl_b200 import ReduceOp, init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    sizes = [1, 7, 1000, 4096, 70000]
+    for grouped in (True, False):
+        for op in (ReduceOp.SUM, ReduceOp.MAX, ReduceOp.AVG):
+            xs = [torch.from_numpy(value(rank, n, "float32", seed=n + int(op))) for n in sizes]
+            batch = comm.batch(xs)
+            comm.all_reduce_many(batch, op, scale=1.0, grouped=grouped)
+            for n, x in zip(sizes, xs):
+                ref = reduce_ref({ReduceOp.SUM: "sum", ReduceOp.MAX: "max", ReduceOp.AVG: "avg"}[op],
+                                 [value(r, n, "float32", seed=n + int(op)) for r in range(world)], world)
+                assert np.allclose(x.numpy(), ref, rtol=1e-6, atol=1e-6), f"n={n} op={op} grouped={grouped}"
+    # out-of-place batch with a fused scale
+    xs = [torch.from_numpy(value(rank, n, "float32", seed=5)) for n in sizes]
+    outs = [torch.full((n,), 7.0) for n in sizes]
+    comm.all_reduce_many(comm.batch(xs, outs), ReduceOp.SUM, scale=0.5)
+    for n, o in zip(sizes, outs):
+        ref = reduce_ref("sum", [value(r, n, "float32", seed=5) for r in range(world)], world) * 0.5
+        assert np.allclose(o.numpy(), ref, rtol=1e-6), f"scaled n={n}"
+    comm.destroy()
+    return {"ok": True}

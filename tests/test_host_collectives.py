@@ -53,3 +53,8 @@ def test_p2p_across_logical_machines_tcp_epoll():
     res = _mp.run(4, host_cases.run_p2p, 2, "epoll", timeout=300)
     assert res[0]["transports"] == {1: "shm", 2: "tcp", 3: "tcp"}
     assert res[0]["executor"] == "epoll"
+
+
+def test_all_reduce_many_batches():
+    res = _mp.run(3, host_cases.run_many, timeout=240)
+    assert all(r["ok"] for r in res)
