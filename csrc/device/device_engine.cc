@@ -367,6 +367,18 @@ void DeviceEngine::Abort() {
     if (abort_host_) *reinterpret_cast<volatile int*>(abort_host_) = 1;
 }
 
+bool DeviceEngine::UserMulticast(const void* p, size_t bytes, char** mc) const {
+    const char* q = static_cast<const char*>(p);
+    for (const SymBuffer& b : user_bufs_) {
+        const char* base = b.ptr[rank_];
+        if (b.mc != nullptr && q >= base && q + bytes <= base + b.bytes) {
+            *mc = b.mc + (q - base);
+            return true;
+        }
+    }
+    return false;
+}
+
 void* DeviceEngine::SymAlloc(size_t bytes) {
     cudaSetDevice(device_);
     SymBuffer b;
@@ -508,6 +520,27 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                                             t.algo != Algo::kAuto ? t.algo : forced_);
         const bool ring = c.algo == Algo::kRing && t.func == CollFunc::AllReduce && nranks_ > 1;
         if (ring) c.ctas = max_ctas_ > 0 ? std::min(num_sms_, max_ctas_) : num_sms_;
+        // Symmetric (multicast-bound) user buffers on both sides: NVLS without staging.
+        char* send_mc = nullptr;
+        char* recv_mc = nullptr;
+        if (t.func == CollFunc::AllReduce && c.algo == Algo::kNvls && nranks_ > 1 && (bytes % 16) == 0 &&
+            EnvInt("BCCL_ZERO_COPY", 1) != 0 && UserMulticast(t.send_buf, bytes, &send_mc) &&
+            UserMulticast(t.recv_buf, bytes, &recv_mc)) {
+            if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+            int zc_ctas = static_cast<int>(std::min<size_t>(std::max<size_t>(bytes / (64u << 10), 8),
+                                                            static_cast<size_t>(num_sms_)));
+            if (max_ctas_ > 0) zc_ctas = std::min(zc_ctas, max_ctas_);
+            dc_.kernel_serial = ++kernel_serial_;
+            cudaError_t e = LaunchNvlsZeroCopy(dc_, send_mc, recv_mc, t.count, static_cast<int>(t.dtype),
+                                               static_cast<int>(t.op), t.scale, zc_ctas, stream);
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: zero-copy NVLS launch failed: %s", rank_, cudaGetErrorString(e));
+                return false;
+            }
+            launches_++;
+            last_algo_ = "nvls_zero_copy";
+            continue;
+        }
         if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls) {
             // Large-payload kernels: per-CTA barriers with the same CTA index on every rank, so
             // every CTA must be resident: at most one per SM.

@@ -56,6 +56,9 @@ public:
     // Collective allocation of memory every rank can address directly (NVLS-bound when
     // available); AllReduce on such a buffer in place skips the staging copies.
     void* SymAlloc(size_t bytes);
+    // Whether [p, p + bytes) lies in a multicast-bound symmetric user buffer; *mc = its
+    // multicast address.
+    bool UserMulticast(const void* p, size_t bytes, char** mc) const;
     bool SymFree(void* ptr);
 
     // Fused tensor-parallel GEMMs (bf16). x_local [ms,K] -> y [nranks*ms, n] = act(AllGather(x) * w^T)

@@ -44,6 +44,11 @@ cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long byte
 cudaError_t LaunchRingAllReduce(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
                                 int op, float scale, unsigned long long block, int max_ctas, cudaStream_t stream);
 
+// Zero-copy AllReduce on multicast-bound symmetric buffers (send_mc / recv_mc are the buffers'
+// multicast addresses at the caller's offset; bytes a multiple of 16).
+cudaError_t LaunchNvlsZeroCopy(const DevComm& c, const void* send_mc, void* recv_mc, unsigned long long count,
+                               int dtype, int op, float scale, int nctas, cudaStream_t stream);
+
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.
 bool NvlsSupports(int dtype, int op);
 

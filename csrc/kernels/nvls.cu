@@ -176,6 +176,75 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
     finish_launch(c, 0, (uint64_t)per_round * (uint64_t)p.nrounds, (uint64_t)p.nrounds);
 }
 
+// Zero-copy AllReduce on buffers bound to the multicast object (symmetric user buffers): no
+// staging. Rank r reduces its shard of every 16-byte vector straight from the send buffers of
+// all ranks (multimem.ld_reduce on the send buffer's multicast address) and stores the result
+// into every rank's receive buffer (multimem.st on the receive buffer's multicast address).
+// An entry barrier makes every rank's input ready before any rank reads it; the exit barrier
+// (system-scope release after the multicast stores) makes every output complete before any
+// rank's later work reads it. Both buffers sit at the same offset on every rank.
+struct ZcParams {
+    DevComm comm;
+    const char* send_mc;
+    char* recv_mc;
+    unsigned long long bytes;  // multiple of 16
+    int op;
+    float scale;
+};
+
+template <int D, int O>
+__global__ void __launch_bounds__(512, 1) nvls_zc_kernel(const __grid_constant__ ZcParams p) {
+    const DevComm& c = p.comm;
+    const int r = c.rank, n = c.nranks;
+    const uint64_t bar = load_state_u64(&c.state->barrier_seq);
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar & 0x7fffffffull));
+    bool ok = cta_barrier(c, bar + 1, 0);
+    if (ok) {
+        constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
+        const bool post = p.op == kAvg || p.scale != 1.0f;
+        const size_t nvec = p.bytes / 16;
+        const size_t per_rank = (nvec + n - 1) / n;
+        const size_t r0 = min(nvec, (size_t)r * per_rank), r1 = min(nvec, r0 + per_rank);
+        const size_t per_cta = (r1 - r0 + gridDim.x - 1) / gridDim.x;
+        const size_t c0 = min(r1, r0 + (size_t)blockIdx.x * per_cta), c1 = min(r1, c0 + per_cta);
+        const size_t t = threadIdx.x, nt = blockDim.x;
+        size_t i = c0 + t;
+        for (; i + 3 * nt < c1; i += 4 * nt) {  // four reductions in flight per thread
+            V16<D> v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(p.send_mc + (i + u * nt) * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (post) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        v[u].b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v[u].b[e]), n, p.scale));
+                }
+                mm_st(p.recv_mc + (i + u * nt) * 16, v[u].u);
+            }
+        }
+        for (; i < c1; i += nt) {
+            V16<D> v;
+            v.u = red16<D, O>(p.send_mc + i * 16);
+            if (post) {
+#pragma unroll
+                for (int e = 0; e < E; ++e)
+                    v.b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v.b[e]), n, p.scale));
+            }
+            mm_st(p.recv_mc + i * 16, v.u);
+        }
+        ok = cta_barrier(c, bar + 2, 1);
+    }
+    if (threadIdx.x == 0) trace(c, 0, kTrEnd, 0);
+    finish_launch(c, 0, 2, 0);
+}
+
+template <int D, int O>
+cudaError_t launch_zc(const ZcParams& p, int nctas, cudaStream_t s) {
+    nvls_zc_kernel<D, O><<<nctas, 512, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
 template <int D, int O>
 cudaError_t launch_t(const NvlsParams& p, int nctas, cudaStream_t s) {
     nvls_kernel<D, O><<<nctas, 512, 0, s>>>(p);
@@ -184,6 +253,42 @@ cudaError_t launch_t(const NvlsParams& p, int nctas, cudaStream_t s) {
 
 }  // namespace
 }  // namespace dev
+
+cudaError_t LaunchNvlsZeroCopy(const DevComm& c, const void* send_mc, void* recv_mc, unsigned long long count,
+                               int dtype, int op, float scale, int nctas, cudaStream_t stream) {
+    using namespace dev;
+    const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
+    if (nctas <= 0 || nctas > kMaxCtas || (bytes % 16) != 0 || ((reinterpret_cast<uintptr_t>(send_mc) |
+        reinterpret_cast<uintptr_t>(recv_mc)) & 15) != 0 || !NvlsSupports(dtype, op)) {
+        return cudaErrorInvalidValue;
+    }
+    ZcParams p;
+    p.comm = c;
+    p.send_mc = static_cast<const char*>(send_mc);
+    p.recv_mc = static_cast<char*>(recv_mc);
+    p.bytes = bytes;
+    p.op = op;
+    p.scale = scale;
+    const int o = (op == kAvg) ? kSum : op;
+#define ZC_CASE(D, O) \
+    if (dtype == D && o == O) return launch_zc<D, O>(p, nctas, stream);
+    ZC_CASE(kF32, kSum)
+    ZC_CASE(kF64, kSum)
+    ZC_CASE(kBF16, kSum)
+    ZC_CASE(kBF16, kMax)
+    ZC_CASE(kBF16, kMin)
+    ZC_CASE(kF16, kSum)
+    ZC_CASE(kF16, kMax)
+    ZC_CASE(kF16, kMin)
+    ZC_CASE(kI32, kSum)
+    ZC_CASE(kI32, kMax)
+    ZC_CASE(kI32, kMin)
+    ZC_CASE(kI64, kSum)
+    ZC_CASE(kI64, kMax)
+    ZC_CASE(kI64, kMin)
+#undef ZC_CASE
+    return cudaErrorNotSupported;
+}
 
 bool NvlsSupports(int dtype, int op) {
     using namespace dev;

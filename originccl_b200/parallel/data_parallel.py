@@ -36,11 +36,14 @@ class GradBuckets:
 
     ``params`` is an iterable of ``(name, nn.Parameter)`` or ``(name, shape)``. For parameters,
     ``.grad`` is set to a view into the flat storage, so autograd accumulates in place.
+    ``allocator(shape, dtype)`` provides the bucketed storage instead of ``torch.zeros``; with
+    ``comm.symmetric_empty`` the buckets live in multicast-bound memory and, where the planner
+    picks NVLS, are reduced in place without staging copies.
     """
 
     def __init__(self, params: Iterable[Tuple[str, Union[torch.nn.Parameter, Sequence[int]]]], *,
                  dtype: Optional[torch.dtype] = None, device=None, bucket_bytes: int = 25 << 20,
-                 small_bytes: int = 4096) -> None:
+                 small_bytes: int = 4096, allocator=None) -> None:
         items = list(params)
         if not items:
             raise ValueError("no parameters")
@@ -66,7 +69,11 @@ class GradBuckets:
         self.small_idx = [i for i, n in enumerate(numels) if n * es <= small_bytes]
         large = [i for i, n in enumerate(numels) if n * es > small_bytes]
         large.reverse()  # backward produces the last parameters' gradients first
-        self.flat = torch.zeros(sum(numels[i] for i in large), dtype=self.dtype, device=self.device)
+        n_large = sum(numels[i] for i in large)
+        if allocator is not None:  # e.g. comm.symmetric_empty: buckets the collectives read in place
+            self.flat = allocator((n_large,), self.dtype).zero_()
+        else:
+            self.flat = torch.zeros(n_large, dtype=self.dtype, device=self.device)
         self.small_flat = torch.zeros(sum(numels[i] for i in self.small_idx), dtype=self.dtype, device=self.device)
         self.views: List[torch.Tensor] = [torch.empty(0)] * len(items)
         self.offsets: List[int] = [0] * len(items)

@@ -30,6 +30,8 @@ def main(argv=None) -> int:
     p.add_argument("--small", type=int, default=256, help="number of 4 KiB tensors in the group")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--no-nccl", action="store_true")
+    p.add_argument("--symmetric", action="store_true",
+                   help="gradient buckets in the communicator's symmetric (multicast-bound) memory")
     args = p.parse_args(argv)
 
     import torch
@@ -52,7 +54,7 @@ def main(argv=None) -> int:
     cfg = LlamaConfig(layers=args.layers)
     shapes = param_shapes(cfg) + [(f"bias.{i}", (2048,)) for i in range(args.small)]
     grads = GradBuckets(shapes, dtype=torch.bfloat16, device=dev, bucket_bytes=int(args.bucket_mb * (1 << 20)),
-                        small_bytes=4096)
+                        small_bytes=4096, allocator=comm.symmetric_empty if args.symmetric else None)
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
     chunk = 1 << 28
     for lo in range(0, grads.flat.numel(), chunk):
@@ -114,9 +116,13 @@ def main(argv=None) -> int:
                 for t in small:
                     dist.all_reduce(t, op=dist.ReduceOp.AVG)
         t_small_nccl = timed(nccl_small)
+    from originccl_b200 import ReduceOp
+    comm.all_reduce(grads.bucket(0), ReduceOp.SUM, scale=1.0 / world)  # untimed: which kernel a bucket uses
+    bucket_algo = comm.last_algorithm
     nbytes = grads.numel * 2
     f = 2.0 * (world - 1) / world if world > 1 else 1.0
     rec = {"workload": "dp_grad_sync", "model": f"llama3-8b-shaped ({args.layers} layers)", "ranks": world,
+           "symmetric_buckets": args.symmetric, "bucket_algorithm": bucket_algo,
            "grad_values": grads.numel, "bucket_mb": args.bucket_mb, "buckets": nb, "small_tensors": len(small),
            "ms_per_sync": round(t_ours, 3), "busbw_gbs": round(nbytes / t_ours / 1e6 * f, 1),
            "launches_per_sync": launches, "small_group_us": round(t_small * 1e3, 2), "check_rel_err": worst,

@@ -320,3 +320,34 @@ def run_dp(rank: int, world: int, hidden: int = 256, steps: int = 2) -> Dict:
         assert err < 1e-4, f"{n}: relative error {err}"
     comm.destroy()
     return {"buckets": grads.num_buckets, "small": len(grads.small_idx), "worst": worst}
+
+
+def run_zero_copy(rank: int, world: int) -> Dict:
+    """AllReduce on symmetric (multicast-bound) buffers: the zero-copy NVLS kernel, in place and
+    out of place, against a float64 oracle."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import Algo, ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    if not comm.nvls_enabled:
+        comm.destroy()
+        return {"skipped": True}
+    used = set()
+    for dtype, n in (("float32", 4096), ("float32", (1 << 20) + 4), ("bfloat16", 3 << 18)):
+        td = getattr(torch, dtype)
+        inputs = [rank_input(r, n, dtype, seed=n) for r in range(world)]
+        src = comm.symmetric_empty((n,), td)
+        dst = comm.symmetric_empty((n,), td)
+        src.copy_(inputs[rank].cuda())
+        torch.cuda.synchronize()  # the communicator's own stream does not wait for torch's
+        comm.all_reduce(src, ReduceOp.SUM, out=dst, algo=Algo.NVLS)
+        used.add(comm.last_algorithm)
+        _close(dst, oracle("sum", inputs, world).to(td), dtype, f"zero-copy {dtype} n={n}")
+        comm.all_reduce(src, ReduceOp.AVG, algo=Algo.NVLS)  # in place
+        _close(src, oracle("avg", inputs, world).to(td), dtype, f"zero-copy in place {dtype} n={n}")
+    comm.destroy()
+    return {"algorithms": sorted(used)}
