@@ -52,6 +52,10 @@ inline void CpuRelax() {
 #endif
 }
 
+// How long an idle channel thread (and a caller waiting for the channels) spins before
+// blocking, when spinning is on: about the gap between back-to-back collectives.
+constexpr int kSpinUs = 200;
+
 // Elements [e0, e1) of channel ch when `count` elements are cut into n contiguous slices.
 void ChannelSlice(size_t count, int n, int ch, size_t* e0, size_t* e1) {
     size_t per = (count + static_cast<size_t>(n) - 1) / static_cast<size_t>(n);
@@ -72,6 +76,11 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     n_channels_ = cfg.n_channels > 0 ? cfg.n_channels : 4;
     n_channels_ = std::max(1, std::min(n_channels_, 16));
     split_bytes_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_HOST_SPLIT_BYTES", 1 << 20)));
+    {
+        const long cores = sysconf(_SC_NPROCESSORS_ONLN);
+        const long want = static_cast<long>(view.local_size) * (n_channels_ + 1);
+        spin_ = EnvInt("BCCL_HOST_SPIN", cores >= want ? 1 : 0) != 0;
+    }
     // The reference switches to its epoll executor when ranks outnumber cores
     // (src/communicator.cpp:37-45); here that choice drives how Send/Recv wait.
     std::string ex = EnvStr("BCCL_HOST_EXECUTOR", "");
@@ -227,13 +236,13 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
 void HostEngine::Finalize() {
     {
         std::lock_guard<std::mutex> lk(mu_);
-        stop_ = true;
+        stop_.store(true);
     }
     cv_job_.notify_all();
     for (auto& t : workers_)
         if (t.joinable()) t.join();
     workers_.clear();
-    stop_ = false;
+    stop_.store(false);
     chans_.clear();
     p2p_send_.clear();
     p2p_recv_.clear();
@@ -258,32 +267,51 @@ void HostEngine::WorkerLoop(int ch) {
     }
     uint64_t seen = 0;
     for (;;) {
-        std::function<bool(int)> job;
-        {
+        if (job_seq_.load(std::memory_order_acquire) == seen && !stop_.load(std::memory_order_acquire)) {
+            if (spin_) {
+                const auto until = Clock::now() + std::chrono::microseconds(kSpinUs);
+                for (uint32_t i = 0; job_seq_.load(std::memory_order_acquire) == seen && !stop_.load(); ++i) {
+                    CpuRelax();
+                    if ((i & 255u) == 255u && Clock::now() > until) break;
+                }
+            }
             std::unique_lock<std::mutex> lk(mu_);
-            cv_job_.wait(lk, [&] { return stop_ || job_seq_ != seen; });
-            if (stop_) return;
-            seen = job_seq_;
-            job = job_;
+            cv_job_.wait(lk, [&] { return stop_.load() || job_seq_.load() != seen; });
         }
-        bool ok = job(ch);
-        {
+        if (stop_.load()) return;
+        seen = job_seq_.load(std::memory_order_acquire);
+        // job_ was written before job_seq_ was bumped and is not rewritten until every channel
+        // finished this job, so reading it here needs no lock.
+        const std::function<bool(int)> job = job_;
+        if (!job(ch)) job_ok_.store(false);
+        if (job_pending_.fetch_sub(1, std::memory_order_acq_rel) == 1) {
             std::lock_guard<std::mutex> lk(mu_);
-            if (!ok) job_ok_ = false;
-            if (--job_pending_ == 0) cv_done_.notify_all();
+            cv_done_.notify_all();
         }
     }
 }
 
 bool HostEngine::RunOnChannels(const std::function<bool(int)>& fn) {
-    std::unique_lock<std::mutex> lk(mu_);
-    job_ = fn;
-    job_ok_ = true;
-    job_pending_ = n_channels_;
-    ++job_seq_;
+    {
+        std::lock_guard<std::mutex> lk(mu_);
+        job_ = fn;
+        job_ok_.store(true);
+        job_pending_.store(n_channels_);
+        job_seq_.fetch_add(1, std::memory_order_release);
+    }
     cv_job_.notify_all();
-    cv_done_.wait(lk, [&] { return job_pending_ == 0; });
-    return job_ok_;
+    if (spin_) {
+        const auto until = Clock::now() + std::chrono::microseconds(kSpinUs);
+        for (uint32_t i = 0; job_pending_.load(std::memory_order_acquire) != 0; ++i) {
+            CpuRelax();
+            if ((i & 255u) == 255u && Clock::now() > until) break;
+        }
+    }
+    if (job_pending_.load(std::memory_order_acquire) != 0) {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_done_.wait(lk, [&] { return job_pending_.load() == 0; });
+    }
+    return job_ok_.load();
 }
 
 bool HostEngine::Barrier(int ch) {

@@ -121,10 +121,13 @@ private:
     std::mutex mu_;
     std::condition_variable cv_job_, cv_done_;
     std::function<bool(int)> job_;
-    uint64_t job_seq_ = 0;
-    int job_pending_ = 0;
-    bool job_ok_ = true;
-    bool stop_ = false;
+    std::atomic<uint64_t> job_seq_{0};
+    std::atomic<int> job_pending_{0};
+    std::atomic<bool> job_ok_{true};
+    std::atomic<bool> stop_{false};
+    // Spin before blocking on the condition variables (dispatch and completion), when every
+    // channel thread and the caller of every local rank can have a core (BCCL_HOST_SPIN forces).
+    bool spin_ = false;
 };
 
 }  // namespace bccl
