@@ -1,4 +1,4 @@
-"""Headline benchmark: AllReduce bus bandwidth on B200 (headline size).
+"""Headline benchmark: AllReduce bus bandwidth on B200 (fp32, 128 MiB per rank).
 
 One step = one out-of-place fp32 SUM AllReduce of ``--bytes`` per rank through this library's
 device communicator. Launch with N=1 as ``python bench.py``; for N>1 under torchrun (one rank per

@@ -4,7 +4,7 @@ Run one rank per GPU::
 
     torchrun --nproc-per-node 8 -m originccl_b200.utils.dp_bench --steps 5 --warmup 3
 
-Workload (BASELINE config 5): every gradient of Llama-3-8B (8.03e9 bf16 values, 16 GB per rank)
+Workload: every gradient of Llama-3-8B (8.03e9 bf16 values, 16 GB per rank)
 in one flat buffer synced as 25 MiB buckets, each an AllReduce with the 1/world scale fused, plus
 256 bias-style gradients of 4 KiB synced as one GroupStart/GroupEnd batch. Gradients are
 normal(0, 1e-3) from seed 7+rank. The NCCL arm runs the same buckets with ``ReduceOp.AVG`` and the

@@ -1,4 +1,4 @@
-"""Mixed collectives on one node (BASELINE config 3): this library vs NCCL.
+"""Mixed collectives on one node: this library vs NCCL.
 
 Run one rank per GPU::
 

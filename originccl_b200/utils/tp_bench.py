@@ -1,4 +1,4 @@
-"""Tensor-parallel MLP benchmark: fused kernels vs NCCL + cuBLAS.
+"""Tensor-parallel Llama-style MLP benchmark: fused kernels vs NCCL + cuBLAS.
 
 ``torchrun --nproc-per-node 8 -m originccl_b200.utils.tp_bench`` runs X [tokens, hidden] sequence-
 sharded over the ranks through AllGather->GEMM(SiLU) and GEMM->ReduceScatter, random-init
