@@ -1,0 +1,184 @@
+"""A ``torch.distributed`` backend named ``"bccl"``: existing PyTorch code switches to this library
+with ``dist.init_process_group("bccl")`` (after ``import originccl_b200.torch_backend``).
+
+Collectives on CUDA tensors run on a device communicator for the current device (enqueued on the
+current stream, like NCCL), collectives on CPU tensors on a host communicator (shared memory
+between the processes of a machine, TCP between machines). Each communicator is created on the
+first collective that needs it; the unique id travels through the process group's store.
+Supported: all_reduce (SUM, AVG, MAX, MIN), broadcast, reduce, all_gather (list and tensor
+forms), reduce_scatter (list and tensor forms), their coalesced forms (one group, i.e. one
+batched kernel for small tensors), send / recv and barrier — the reference's operation set.
+AllToAll, gather and scatter, which the reference does not have, raise ``NotImplementedError``.
+DistributedDataParallel runs on it unchanged.
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import torch
+import torch.distributed as dist
+from torch._C._distributed_c10d import _create_work_from_future
+from torch.futures import Future
+
+from .comm import Communicator, ReduceOp, init_from_store
+
+_OPS = {
+    dist.ReduceOp.SUM: ReduceOp.SUM,
+    dist.ReduceOp.AVG: ReduceOp.AVG,
+    dist.ReduceOp.MAX: ReduceOp.MAX,
+    dist.ReduceOp.MIN: ReduceOp.MIN,
+}
+
+
+def _done(result) -> "dist.Work":
+    fut: Future = Future()
+    fut.set_result(result)
+    return _create_work_from_future(fut)
+
+
+class BcclProcessGroup(dist.ProcessGroup):
+    def __init__(self, store, rank: int, world_size: int, timeout) -> None:
+        super().__init__(rank, world_size)
+        self._store = store
+        self._timeout_ms = int(timeout.total_seconds() * 1000) if timeout is not None else 0
+        self._comms: Dict[str, Communicator] = {}
+
+    # ------------------------------------------------------------------ communicators
+    def _comm(self, t: torch.Tensor) -> Communicator:
+        key = f"cuda:{t.device.index}" if t.is_cuda else "cpu"
+        comm = self._comms.get(key)
+        if comm is None:
+            device = t.device.index if t.is_cuda else -1
+            comm = init_from_store(self._store, self.rank(), self.size(), key=f"bccl_pg_{key}", device=device,
+                                   timeout_ms=self._timeout_ms)
+            self._comms[key] = comm
+        return comm
+
+    @staticmethod
+    def _op(opts) -> ReduceOp:
+        if opts is None:
+            return ReduceOp.SUM
+        op = opts.reduceOp.op if hasattr(opts.reduceOp, "op") else opts.reduceOp
+        if op not in _OPS:
+            raise NotImplementedError(f"bccl: reduce op {op} is not supported (SUM, AVG, MAX, MIN are)")
+        return _OPS[op]
+
+    def getBackendName(self) -> str:
+        return "bccl"
+
+    def name(self) -> str:
+        return "bccl"
+
+    def destroy(self) -> None:
+        for c in self._comms.values():
+            c.destroy()
+        self._comms.clear()
+
+    # ------------------------------------------------------------------ collectives
+    def allreduce(self, tensors: List[torch.Tensor], opts=None):
+        op = self._op(opts)
+        if len(tensors) == 1:
+            self._comm(tensors[0]).all_reduce(tensors[0], op)
+        else:
+            self.allreduce_coalesced(tensors, opts)
+        return _done(tensors)
+
+    def allreduce_coalesced(self, tensors: List[torch.Tensor], opts=None):
+        op = self._op(opts)
+        comm = self._comm(tensors[0])
+        with comm.group():
+            for t in tensors:
+                comm.all_reduce(t, op)
+        return _done(tensors)
+
+    def broadcast(self, tensors: List[torch.Tensor], opts=None):
+        for t in tensors:
+            self._comm(t).broadcast(t, opts.rootRank if opts is not None else 0)
+        return _done(tensors)
+
+    def reduce(self, tensors: List[torch.Tensor], opts=None):
+        op = self._op(opts)
+        for t in tensors:
+            self._comm(t).reduce(t, opts.rootRank if opts is not None else 0, op, out=t)
+        return _done(tensors)
+
+    def _allgather_base(self, output: torch.Tensor, input: torch.Tensor, opts=None):
+        self._comm(input).all_gather(output, input.contiguous())
+        return _done([output])
+
+    def allgather(self, outputs: List[List[torch.Tensor]], inputs: List[torch.Tensor], opts=None):
+        for outs, inp in zip(outputs, inputs):
+            flat = torch.empty(self.size() * inp.numel(), dtype=inp.dtype, device=inp.device)
+            self._comm(inp).all_gather(flat, inp.contiguous())
+            for r, o in enumerate(outs):
+                o.copy_(flat[r * inp.numel():(r + 1) * inp.numel()].view_as(o))
+        return _done(outputs)
+
+    def allgather_into_tensor_coalesced(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor],
+                                        opts=None):
+        comm = self._comm(inputs[0])
+        with comm.group():
+            for o, i in zip(outputs, inputs):
+                comm.all_gather(o, i)
+        return _done(outputs)
+
+    def _reduce_scatter_base(self, output: torch.Tensor, input: torch.Tensor, opts=None):
+        self._comm(input).reduce_scatter(output, input.contiguous(), self._op(opts))
+        return _done([output])
+
+    def reduce_scatter(self, outputs: List[torch.Tensor], inputs: List[List[torch.Tensor]],
+                       opts=None):
+        op = self._op(opts)
+        for out, ins in zip(outputs, inputs):
+            flat = torch.cat([t.reshape(-1) for t in ins])
+            self._comm(out).reduce_scatter(out, flat, op)
+        return _done(outputs)
+
+    def reduce_scatter_tensor_coalesced(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor],
+                                        opts=None):
+        op = self._op(opts)
+        comm = self._comm(inputs[0])
+        with comm.group():
+            for o, i in zip(outputs, inputs):
+                comm.reduce_scatter(o, i, op)
+        return _done(outputs)
+
+    def send(self, tensors: List[torch.Tensor], dst: int, tag: int = 0):
+        for t in tensors:
+            self._comm(t).send(t, dst)
+        return _done(tensors)
+
+    def recv(self, tensors: List[torch.Tensor], src: int, tag: int = 0):
+        for t in tensors:
+            self._comm(t).recv(t, src)
+        return _done(tensors)
+
+    def barrier(self, opts=None):
+        if torch.cuda.is_available():
+            torch.cuda.current_stream().synchronize()
+        comm = next(iter(self._comms.values()), None)
+        if comm is None:
+            comm = self._comm(torch.empty(0))
+        comm.barrier()
+        return _done([])
+
+    # ------------------------------------------------------------------ not in the reference
+    def alltoall_base(self, *args, **kwargs):
+        raise NotImplementedError("bccl: AllToAll is not provided (the reference has no AllToAll)")
+
+    def alltoall(self, *args, **kwargs):
+        raise NotImplementedError("bccl: AllToAll is not provided (the reference has no AllToAll)")
+
+    def gather(self, *args, **kwargs):
+        raise NotImplementedError("bccl: gather is not provided")
+
+    def scatter(self, *args, **kwargs):
+        raise NotImplementedError("bccl: scatter is not provided")
+
+
+def _create(store, rank: int, world_size: int, timeout) -> BcclProcessGroup:
+    return BcclProcessGroup(store, rank, world_size, timeout)
+
+
+if "bccl" not in dist.Backend.backend_list:
+    dist.Backend.register_backend("bccl", _create, devices=["cpu", "cuda"])

@@ -1,0 +1,85 @@
+"""torch.distributed "bccl" backend cases (CPU tensors -> the host communicator)."""
+from __future__ import annotations
+
+import datetime
+import os
+from typing import Dict
+
+
+def _init(rank: int, world: int):
+    import torch.distributed as dist
+    import originccl_b200.torch_backend  # noqa: F401  (registers "bccl")
+    path = os.environ["BCCL_ID_FILE"] + ".torchstore"
+    dist.init_process_group("bccl", init_method=f"file://{path}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    return dist
+
+
+def run_collectives(rank: int, world: int) -> Dict:
+    import torch
+    dist = _init(rank, world)
+    for op, ref in ((dist.ReduceOp.SUM, sum(range(1, world + 1))), (dist.ReduceOp.MAX, world),
+                    (dist.ReduceOp.MIN, 1), (dist.ReduceOp.AVG, sum(range(1, world + 1)) / world)):
+        x = torch.full((33,), float(rank + 1))
+        dist.all_reduce(x, op=op)
+        assert torch.all(x == ref), (op, x[:3])
+    y = torch.arange(7.0) if rank == world - 1 else torch.zeros(7)
+    dist.broadcast(y, world - 1)
+    assert torch.equal(y, torch.arange(7.0))
+    z = torch.full((5,), float(rank))
+    dist.reduce(z, 0)
+    if rank == 0:
+        assert torch.all(z == sum(range(world)))
+    outs = [torch.empty(3) for _ in range(world)]
+    dist.all_gather(outs, torch.full((3,), float(rank)))
+    assert all(torch.all(o == r) for r, o in enumerate(outs))
+    flat = torch.empty(world * 4)
+    dist.all_gather_into_tensor(flat, torch.full((4,), float(rank)))
+    assert torch.equal(flat, torch.arange(world, dtype=torch.float32).repeat_interleave(4))
+    rs = torch.empty(2)
+    dist.reduce_scatter(rs, [torch.full((2,), float(r + rank)) for r in range(world)])
+    assert torch.all(rs == sum(q + rank for q in range(world)))
+    rt = torch.empty(3)
+    dist.reduce_scatter_tensor(rt, torch.arange(3.0 * world))
+    assert torch.equal(rt, world * torch.arange(3.0 * rank, 3.0 * (rank + 1)))
+    if world > 1:
+        nxt, prv = (rank + 1) % world, (rank - 1) % world
+        s = torch.full((9,), float(rank))
+        r = torch.empty(9)
+        ops = [dist.P2POp(dist.isend, s, nxt), dist.P2POp(dist.irecv, r, prv)]
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+        assert torch.all(r == prv)
+    dist.barrier()
+    try:
+        dist.all_to_all_single(torch.empty(world), torch.empty(world))
+        raised = False
+    except (NotImplementedError, RuntimeError):
+        raised = True
+    dist.destroy_process_group()
+    return {"alltoall_rejected": raised}
+
+
+def run_ddp(rank: int, world: int) -> Dict:
+    import torch
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    dist = _init(rank, world)
+
+    def make():
+        torch.manual_seed(0)
+        return torch.nn.Sequential(torch.nn.Linear(16, 64), torch.nn.ReLU(), torch.nn.Linear(64, 4))
+
+    model = make()
+    ddp = DDP(model, bucket_cap_mb=0.01)  # several buckets
+    x = torch.randn(8, 16, generator=torch.Generator().manual_seed(10 + rank))
+    ddp(x).pow(2).mean().backward()
+    ref = None
+    for r in range(world):
+        m = make()
+        m(torch.randn(8, 16, generator=torch.Generator().manual_seed(10 + r))).pow(2).mean().backward()
+        g = [p.grad for p in m.parameters()]
+        ref = g if ref is None else [a + b for a, b in zip(ref, g)]
+    worst = max((p.grad - r / world).abs().max().item() for p, r in zip(model.parameters(), ref))
+    assert worst < 1e-6, worst
+    dist.destroy_process_group()
+    return {"worst": worst}
