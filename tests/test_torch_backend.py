@@ -1,5 +1,7 @@
 """The torch.distributed "bccl" backend on CPU ranks: every supported collective through the
 torch API, and DistributedDataParallel training on it, against local references."""
+import os
+
 import pytest
 
 from tests import _mp, torch_backend_cases
@@ -16,3 +18,15 @@ def test_torch_collectives_on_bccl_backend(world):
 def test_ddp_on_bccl_backend():
     res = _mp.run(2, torch_backend_cases.run_ddp, timeout=240)
     assert all(r["worst"] < 1e-6 for r in res)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="CUDA path of the torch backend not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_ddp_cuda_on_bccl_backend():
+    import torch
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _mp.run(2, torch_backend_cases.run_ddp_cuda, timeout=300)
+    assert all(r["worst"] < 1e-4 for r in res)

@@ -83,3 +83,33 @@ def run_ddp(rank: int, world: int) -> Dict:
     assert worst < 1e-6, worst
     dist.destroy_process_group()
     return {"worst": worst}
+
+
+def run_ddp_cuda(rank: int, world: int) -> Dict:
+    """DDP on CUDA through the "bccl" backend (device communicator, current stream)."""
+    import torch
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    torch.cuda.set_device(rank % torch.cuda.device_count())
+    dist = _init(rank, world)
+
+    def make():
+        torch.manual_seed(0)
+        return torch.nn.Sequential(torch.nn.Linear(64, 256), torch.nn.ReLU(), torch.nn.Linear(256, 8)).cuda()
+
+    model = make()
+    ddp = DDP(model, bucket_cap_mb=0.05)
+    g = torch.Generator(device="cuda").manual_seed(10 + rank)
+    ddp(torch.randn(32, 64, device="cuda", generator=g)).pow(2).mean().backward()
+    torch.cuda.synchronize()
+    ref = None
+    for r in range(world):
+        m = make()
+        gr = torch.Generator(device="cuda").manual_seed(10 + r)
+        m(torch.randn(32, 64, device="cuda", generator=gr)).pow(2).mean().backward()
+        gl = [p.grad for p in m.parameters()]
+        ref = gl if ref is None else [a + b for a, b in zip(ref, gl)]
+    worst = max(((p.grad - r / world).abs().max() / (r / world).abs().max().clamp_min(1e-12)).item()
+                for p, r in zip(model.parameters(), ref))
+    assert worst < 1e-4, worst
+    dist.destroy_process_group()
+    return {"worst": worst}
