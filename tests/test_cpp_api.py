@@ -82,3 +82,14 @@ def test_cpp_group_benchmark_host_many_small_messages():
     assert r.returncode == 0, r.stdout + r.stderr
     rec = _json_lines(r.stdout)[-1]
     assert rec["check"] and rec["messages"] == 24 and rec["msgs_per_s"] > 0
+
+
+def test_python_launcher_runs_python_ranks():
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); import numpy as np, originccl_b200 as o; c = o.init_from_env(); "
+            "x = np.full(4, c.rank + 1.0, np.float32); c.all_reduce(x); assert (x == 3).all(); c.destroy()"
+            % os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    r = subprocess.run([sys.executable, "-m", "originccl_b200.run", "-np", "2", "--timeout", "60", "--",
+                        sys.executable, "-c", code], capture_output=True, text=True, timeout=120,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stdout + r.stderr
