@@ -387,6 +387,50 @@ bool HostEngine::LeaderExchange(int ch, const std::vector<int>& peers, const std
     }
 }
 
+// Ring AllReduce among the machine leaders over their TCP links (the reference's ring,
+// src/topology/topology_ring.cpp:255-290, between machines): `buf` holds this machine's partial
+// of `count` elements, cut into M blocks. Reduce-scatter: in step s, send block (m - s) to the
+// next leader and add block (m - s - 1) from the previous one; block (m + 1) is then complete
+// here and gets the AVG / scale epilogue. All-gather: pass the complete blocks around.
+bool HostEngine::LeaderRingAllReduce(int ch, char* buf, size_t count, DataType dt, ReduceOp op, float scale) {
+    const int M = view_.machine_count, m = view_.machine_index;
+    const int next = (m + 1) % M, prev = (m + M - 1) % M;
+    const size_t es = DataTypeSize(dt);
+    const size_t per = (count + static_cast<size_t>(M) - 1) / static_cast<size_t>(M);
+    auto blk = [&](int k, size_t* off, size_t* len) {
+        k = ((k % M) + M) % M;
+        *off = std::min(count, per * static_cast<size_t>(k));
+        *len = std::min(count, *off + per) - *off;
+    };
+    Channel& C = chans_[ch];
+    C.scratch.resize(per * es);
+    const ReduceOp partial = op == ReduceOp::AVG ? ReduceOp::SUM : op;
+    for (int s = 0; s < M - 1; ++s) {
+        size_t so, sl, ro, rl;
+        blk(m - s, &so, &sl);
+        blk(m - s - 1, &ro, &rl);
+        if (!LeaderExchange(ch, {next, prev}, {buf + so * es, nullptr}, {sl * es, 0}, {nullptr, C.scratch.data()},
+                            {0, rl * es})) {
+            return false;
+        }
+        const void* srcs[2] = {buf + ro * es, C.scratch.data()};
+        hostmath::Reduce(dt, partial, buf + ro * es, srcs, 2, rl, world_, 1.0f, false);
+    }
+    size_t fo, fl;
+    blk(m + 1, &fo, &fl);
+    hostmath::Finish(dt, op, buf + fo * es, buf + fo * es, fl, world_, scale);
+    for (int s = 0; s < M - 1; ++s) {
+        size_t so, sl, ro, rl;
+        blk(m + 1 - s, &so, &sl);
+        blk(m - s, &ro, &rl);
+        if (!LeaderExchange(ch, {next, prev}, {buf + so * es, nullptr}, {sl * es, 0}, {nullptr, buf + ro * es},
+                            {0, rl * es})) {
+            return false;
+        }
+    }
+    return true;
+}
+
 // Reduction family (AllReduce, and Reduce when reduce_only): intra-machine two-shot, then
 // leaders across machines.
 bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1, bool reduce_only) {
@@ -410,7 +454,10 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
             hostmath::Reduce(t.dtype, t.op, C.result + s0 * es, srcs, L, s1 - s0, world_, t.scale, M == 1);
         }
         if (!Barrier(ch)) return false;
-        if (M > 1 && leader) {
+        if (M > 2 && leader && !reduce_only) {
+            // Three or more machines: ring among the leaders (each sends 2(M-1)/M of the chunk).
+            if (!LeaderRingAllReduce(ch, C.result, clen, t.dtype, t.op, t.scale)) return false;
+        } else if (M > 1 && leader) {
             // Every leader receives the other machines' partials (Reduce: only the root's
             // leader needs them) and reduces all machines in machine order.
             std::vector<int> peers;

@@ -90,6 +90,7 @@ private:
     bool Barrier(int ch);
     // Leaders: send `send[m]` (bytes[m]) to machine m's leader and receive `recv[m]` from it,
     // for every m in `peers`, all concurrently.
+    bool LeaderRingAllReduce(int ch, char* buf, size_t count, DataType dt, ReduceOp op, float scale);
     bool LeaderExchange(int ch, const std::vector<int>& peers, const std::vector<const void*>& send,
                         const std::vector<size_t>& send_bytes, const std::vector<void*>& recv,
                         const std::vector<size_t>& recv_bytes);

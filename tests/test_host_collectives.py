@@ -58,3 +58,15 @@ def test_p2p_across_logical_machines_tcp_epoll():
 def test_all_reduce_many_batches():
     res = _mp.run(3, host_cases.run_many, timeout=240)
     assert all(r["ok"] for r in res)
+
+
+def test_four_logical_machines_leader_ring():
+    # Four machines of one rank each: AllReduce between machines runs the leaders' ring.
+    res = _mp.run(4, host_cases.run_matrix, [1, 5, 4099, 70001], ["float32", "int32", "float64"], 2, 1,
+                  timeout=300)
+    assert res[0]["machine_count"] == 4 and res[0]["leaders"] == [0, 1, 2, 3]
+
+
+def test_three_logical_machines_of_two_ranks():
+    res = _mp.run(6, host_cases.run_matrix, [3, 1000, 131072 + 7], ["float32", "int64"], 2, 2, timeout=400)
+    assert res[0]["machine_count"] == 3 and res[5]["local_ranks"] == [4, 5]
