@@ -52,6 +52,9 @@ inline void CpuRelax() {
 #endif
 }
 
+// Chunks from this size on go around the leaders' ring instead of the one-step exchange.
+constexpr size_t kLeaderRingBytes = 128u << 10;
+
 // How long an idle channel thread (and a caller waiting for the channels) spins before
 // blocking, when spinning is on: about the gap between back-to-back collectives.
 constexpr int kSpinUs = 200;
@@ -454,8 +457,11 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
             hostmath::Reduce(t.dtype, t.op, C.result + s0 * es, srcs, L, s1 - s0, world_, t.scale, M == 1);
         }
         if (!Barrier(ch)) return false;
-        if (M > 2 && leader && !reduce_only) {
-            // Three or more machines: ring among the leaders (each sends 2(M-1)/M of the chunk).
+        if (M > 2 && leader && !reduce_only && clen * es >= kLeaderRingBytes) {
+            // Three or more machines and a large chunk: ring among the leaders (each sends
+            // 2(M-1)/M of the chunk). Smaller chunks take the one-step exchange below, the
+            // latency-bound role the reference gives its tree below 128 KiB
+            // (src/planner.cpp:260-262).
             if (!LeaderRingAllReduce(ch, C.result, clen, t.dtype, t.op, t.scale)) return false;
         } else if (M > 1 && leader) {
             // Every leader receives the other machines' partials (Reduce: only the root's
