@@ -204,6 +204,11 @@ int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uint
 
 int bcclSynchronize(bcclComm_t comm) { return comm && comm->comm.Synchronize() ? 0 : Fail(); }
 int bcclBarrier(bcclComm_t comm) { return comm && comm->comm.Barrier() ? 0 : Fail(); }
+int bcclCommAbort(bcclComm_t comm) {
+    if (comm == nullptr) return Fail();
+    comm->comm.Abort();
+    return 0;
+}
 void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes) { return comm ? comm->comm.SymmetricAlloc(bytes) : nullptr; }
 int bcclSymmetricFree(bcclComm_t comm, void* ptr) { return comm && comm->comm.SymmetricFree(ptr) ? 0 : Fail(); }
 

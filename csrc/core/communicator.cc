@@ -378,6 +378,12 @@ bool Communicator::Synchronize() {
 void* Communicator::SymmetricAlloc(size_t bytes) { return device_ ? device_->SymAlloc(bytes) : nullptr; }
 bool Communicator::SymmetricFree(void* ptr) { return device_ ? device_->SymFree(ptr) : false; }
 bool Communicator::Barrier() { return bootstrap_ && bootstrap_->Barrier(); }
+
+void Communicator::Abort() {
+    failed_ = true;
+    if (device_) device_->Abort();
+    if (host_) host_->Abort();
+}
 bool Communicator::NvlsEnabled() const { return device_ && device_->nvls_enabled(); }
 const char* Communicator::LastAlgorithm() const { return device_ ? device_->last_algo() : "host"; }
 unsigned long long Communicator::KernelLaunches() const { return device_ ? device_->launches() : 0; }

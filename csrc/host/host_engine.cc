@@ -335,6 +335,10 @@ bool HostEngine::Barrier(int ch) {
             continue;
         }
         sched_yield();
+        if ((spins & 1023) == 0 && aborted_.load(std::memory_order_relaxed)) {
+            LOG_ERROR("rank %d: channel %d barrier aborted", rank_, ch);
+            return false;
+        }
         if ((spins & 1023) == 0 && Clock::now() > deadline) {
             LOG_ERROR("rank %d: channel %d barrier timed out after %d ms", rank_, ch, timeout_ms_);
             return false;
@@ -382,6 +386,10 @@ bool HostEngine::LeaderExchange(int ch, const std::vector<int>& peers, const std
                 if (ev) pf.push_back({chans_[ch].leader_links[peers[i]]->GetFd(), ev, 0});
             }
             poll(pf.data(), pf.size(), 50);
+            if (aborted_.load(std::memory_order_relaxed)) {
+                LOG_ERROR("rank %d: leader exchange on channel %d aborted", rank_, ch);
+                return false;
+            }
             if (Clock::now() > deadline) {
                 LOG_ERROR("rank %d: leader exchange on channel %d timed out", rank_, ch);
                 return false;
@@ -719,6 +727,11 @@ bool HostEngine::RunP2p(const std::vector<CollTask>& tasks) {
         }
         if (!ok || all) break;
         if (!progress) {
+            if (aborted_.load(std::memory_order_relaxed)) {
+                LOG_ERROR("rank %d: Send/Recv aborted", rank_);
+                ok = false;
+                break;
+            }
             if (Clock::now() > deadline) {
                 LOG_ERROR("rank %d: Send/Recv timed out after %d ms", rank_, timeout_ms_);
                 ok = false;

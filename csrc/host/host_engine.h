@@ -129,6 +129,11 @@ private:
     // Spin before blocking on the condition variables (dispatch and completion), when every
     // channel thread and the caller of every local rank can have a core (BCCL_HOST_SPIN forces).
     bool spin_ = false;
+    std::atomic<bool> aborted_{false};
+
+public:
+    // Makes every wait of the in-flight and later operations give up (thread-safe).
+    void Abort() { aborted_.store(true); }
 };
 
 }  // namespace bccl

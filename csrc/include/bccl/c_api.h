@@ -76,6 +76,10 @@ int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer
 int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
 int bcclSynchronize(bcclComm_t comm);
 int bcclBarrier(bcclComm_t comm);
+/* Aborts the communicator's operations in flight; callable from any thread (like ncclCommAbort).
+ * Host waits return at once, device waits within about a millisecond; afterwards only
+ * bcclCommFinalize / bcclCommDestroy are meaningful. */
+int bcclCommAbort(bcclComm_t comm);
 void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes);
 int bcclSymmetricFree(bcclComm_t comm, void* ptr);
 

@@ -18,6 +18,7 @@
 // in Synchronize().
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <memory>
 #include <mutex>
@@ -85,6 +86,10 @@ public:
     void* SymmetricAlloc(size_t bytes);
     bool SymmetricFree(void* ptr);
     bool Barrier();
+    // Stops the operations in flight from any thread: host waits return at once, device waits
+    // within ~1 ms (kernels record kDevAborted and return). The communicator stays in the error
+    // state; only Finalize is meaningful afterwards.
+    void Abort();
     bool IsDevice() const { return config_.device >= 0; }
     bool NvlsEnabled() const;
     const char* LastAlgorithm() const;
@@ -99,7 +104,7 @@ private:
 
     CommConfig config_;
     bool inited_ = false;
-    bool failed_ = false;
+    std::atomic<bool> failed_{false};
     int bootstrap_listen_fd_ = -1;
     int data_listen_fd_ = -1;
     bool have_unique_id_ = false;

@@ -86,6 +86,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclGemmBf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp]),
         "bcclGemmCheckError": (c_int, []),
         "bcclGemmUsesPair": (c_int, []),
+        "bcclCommAbort": (c_int, [vp]),
         "bcclTpAllGatherGemm": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, c_int, up, c_int]),
         "bcclTpGemmReduceScatter": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, up, c_int]),
         "bcclTraceDump": (ctypes.c_long, [vp, ctypes.c_char_p]),

@@ -362,6 +362,11 @@ class Communicator:
         """Writes the device trace (BCCL_TRACE=<records> at init) as Chrome-trace JSON."""
         return int(self._lib.bcclTraceDump(self._h, path.encode()))
 
+    def abort(self) -> None:
+        """Stops the operations in flight (callable from another thread): host waits return at
+        once, device waits within ~1 ms; the operation raises. Only destroy() is useful after."""
+        self._lib.bcclCommAbort(self._h)
+
     def barrier(self) -> None:
         """Host-side barrier over the bootstrap (no device work)."""
         self._check(self._lib.bcclBarrier(self._h))

@@ -250,3 +250,29 @@ def run_many(rank: int, world: int) -> Dict:
         assert np.allclose(o.numpy(), ref, rtol=1e-6), f"scaled n={n}"
     comm.destroy()
     return {"ok": True}
+
+
+def run_abort(rank: int, world: int) -> Dict:
+    """Rank 0 starts an AllReduce that rank 1 never joins; another thread aborts the communicator
+    after 0.3 s and the call must fail long before the 30 s timeout."""
+    import threading
+    import time
+
+    from originccl_b200 import BcclError, init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    elapsed = None
+    if rank == 0:
+        x = np.ones(1 << 16, np.float32)
+        timer = threading.Timer(0.3, comm.abort)
+        timer.start()
+        t0 = time.time()
+        try:
+            comm.all_reduce(x)
+            failed = False
+        except BcclError:
+            failed = True
+        elapsed = time.time() - t0
+        timer.join()
+        assert failed, "aborted AllReduce returned success"
+    comm.destroy()
+    return {"elapsed": elapsed}

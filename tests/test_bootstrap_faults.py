@@ -40,3 +40,8 @@ def test_shared_segment_never_arrives():
     res, dt = _run_with_fault(3, "segment_drop:0")
     assert not any(ok for ok, _ in res[1:]), res
     assert dt < 30
+
+
+def test_abort_stops_a_collective_a_peer_never_joins():
+    res = _mp.run(2, host_cases.run_abort, timeout=120)
+    assert res[0]["elapsed"] < 5.0
