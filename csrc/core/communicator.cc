@@ -15,6 +15,7 @@
 #include "core/nvtx.h"
 #include "core/net.h"
 #include "core/planner.h"
+#include "core/watchdog.h"
 #include "device/device_engine.h"
 #include "host/host_engine.h"
 
@@ -135,6 +136,13 @@ bool Communicator::Init(const CommConfig& cfg) {
     me.pid = static_cast<int>(getpid());
     bootstrap_.reset(new Bootstrap());
     if (!bootstrap_->Run(config_, me, bootstrap_listen_fd_, &all_nodes_)) return false;
+    if (cfg.world_size > 1 && EnvInt("BCCL_WATCHDOG", 1) != 0) {
+        watchdog_.reset(new Watchdog());
+        if (!watchdog_->Start(config_, bootstrap_listen_fd_, bootstrap_.get(), [this](int) { Abort(); })) {
+            watchdog_.reset();
+            return false;
+        }
+    }
 
     // Local and machine views: machines are numbered by first appearance of their hostname;
     // a machine's leader is its lowest rank.
@@ -197,6 +205,8 @@ bool Communicator::Init(const CommConfig& cfg) {
 
 void Communicator::Finalize() {
     std::lock_guard<std::mutex> lk(mu_);
+    if (watchdog_) watchdog_->Stop();  // goodbye first: this rank's teardown is not a failure
+    watchdog_.reset();
     if (device_) device_->Finalize();
     device_.reset();
     if (host_) host_->Finalize();

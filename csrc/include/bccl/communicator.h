@@ -34,6 +34,7 @@ class FdPasser;
 class Planner;
 class DeviceEngine;
 class HostEngine;
+class Watchdog;
 
 class Communicator {
 public:
@@ -113,6 +114,7 @@ private:
     std::unique_ptr<Planner> planner_;
     std::unique_ptr<DeviceEngine> device_;
     std::unique_ptr<HostEngine> host_;
+    std::unique_ptr<Watchdog> watchdog_;
     std::vector<NodeInfo> all_nodes_;
     int group_depth_ = 0;
     std::vector<CollTask> pending_;

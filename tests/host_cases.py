@@ -276,3 +276,32 @@ def run_abort(rank: int, world: int) -> Dict:
         assert failed, "aborted AllReduce returned success"
     comm.destroy()
     return {"elapsed": elapsed}
+
+
+_KEEP: List = []
+
+
+def run_rank_dies(rank: int, world: int) -> Dict:
+    """The last rank's process ends 0.5 s after init without finalizing; the others are in an
+    AllReduce that needs it and must get an error from the watchdog, long before the 30 s
+    timeout."""
+    import os
+    import threading
+    import time
+
+    from originccl_b200 import BcclError, init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    if rank == world - 1:
+        _KEEP.append(comm)  # no destroy(): the process just ends
+        threading.Timer(0.5, lambda: os._exit(3)).start()
+        return {"dies": True}
+    x = np.ones(1 << 16, np.float32)
+    t0 = time.time()
+    try:
+        comm.all_reduce(x)
+        failed = False
+    except BcclError:
+        failed = True
+    elapsed = time.time() - t0
+    assert failed, "AllReduce with a dead peer returned success"
+    return {"elapsed": elapsed}

@@ -45,3 +45,9 @@ def test_shared_segment_never_arrives():
 def test_abort_stops_a_collective_a_peer_never_joins():
     res = _mp.run(2, host_cases.run_abort, timeout=120)
     assert res[0]["elapsed"] < 5.0
+
+
+def test_watchdog_reports_a_rank_that_dies():
+    res = _mp.run(3, host_cases.run_rank_dies, timeout=120)
+    assert res[2]["dies"]
+    assert res[0]["elapsed"] < 10.0 and res[1]["elapsed"] < 10.0, res
