@@ -520,19 +520,42 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                                             t.algo != Algo::kAuto ? t.algo : forced_);
         const bool ring = c.algo == Algo::kRing && t.func == CollFunc::AllReduce && nranks_ > 1;
         if (ring) c.ctas = max_ctas_ > 0 ? std::min(num_sms_, max_ctas_) : num_sms_;
-        // Symmetric (multicast-bound) user buffers on both sides: NVLS without staging.
+        // Symmetric (multicast-bound) user buffers: NVLS without staging. AllReduce when the
+        // planner picks NVLS and both buffers are symmetric; AllGather when the output is,
+        // ReduceScatter when the input is (any size: one pass, two barriers).
         char* send_mc = nullptr;
         char* recv_mc = nullptr;
-        if (t.func == CollFunc::AllReduce && c.algo == Algo::kNvls && nranks_ > 1 && (bytes % 16) == 0 &&
-            EnvInt("BCCL_ZERO_COPY", 1) != 0 && UserMulticast(t.send_buf, bytes, &send_mc) &&
-            UserMulticast(t.recv_buf, bytes, &recv_mc)) {
+        const size_t all_bytes = bytes * static_cast<size_t>(nranks_);
+        bool zc = false;
+        const void* zc_send = nullptr;
+        void* zc_recv = nullptr;
+        if (nranks_ > 1 && (bytes % 16) == 0 && nvls_.mc != nullptr && EnvInt("BCCL_ZERO_COPY", 1) != 0) {
+            if (t.func == CollFunc::AllReduce && c.algo == Algo::kNvls && UserMulticast(t.send_buf, bytes, &send_mc) &&
+                UserMulticast(t.recv_buf, bytes, &recv_mc)) {
+                zc = true;
+                zc_send = send_mc;
+                zc_recv = recv_mc;
+            } else if (t.func == CollFunc::AllGather && UserMulticast(t.recv_buf, all_bytes, &recv_mc)) {
+                zc = true;
+                zc_send = t.send_buf;
+                zc_recv = recv_mc;
+            } else if (t.func == CollFunc::ReduceScatter && NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)) &&
+                       UserMulticast(t.send_buf, all_bytes, &send_mc)) {
+                zc = true;
+                zc_send = send_mc;
+                zc_recv = t.recv_buf;
+            }
+        }
+        if (zc) {
             if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
-            int zc_ctas = static_cast<int>(std::min<size_t>(std::max<size_t>(bytes / (64u << 10), 8),
+            const size_t moved = t.func == CollFunc::AllReduce ? bytes : all_bytes;
+            int zc_ctas = static_cast<int>(std::min<size_t>(std::max<size_t>(moved / (64u << 10), 8),
                                                             static_cast<size_t>(num_sms_)));
             if (max_ctas_ > 0) zc_ctas = std::min(zc_ctas, max_ctas_);
             dc_.kernel_serial = ++kernel_serial_;
-            cudaError_t e = LaunchNvlsZeroCopy(dc_, send_mc, recv_mc, t.count, static_cast<int>(t.dtype),
-                                               static_cast<int>(t.op), t.scale, zc_ctas, stream);
+            cudaError_t e = LaunchNvlsZeroCopy(dc_, static_cast<int>(t.func), zc_send, zc_recv, t.count,
+                                               static_cast<int>(t.dtype), static_cast<int>(t.op), t.scale, zc_ctas,
+                                               stream);
             if (e != cudaSuccess) {
                 LOG_ERROR("rank %d: zero-copy NVLS launch failed: %s", rank_, cudaGetErrorString(e));
                 return false;

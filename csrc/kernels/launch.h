@@ -44,9 +44,11 @@ cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long byte
 cudaError_t LaunchRingAllReduce(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
                                 int op, float scale, unsigned long long block, int max_ctas, cudaStream_t stream);
 
-// Zero-copy AllReduce on multicast-bound symmetric buffers (send_mc / recv_mc are the buffers'
-// multicast addresses at the caller's offset; bytes a multiple of 16).
-cudaError_t LaunchNvlsZeroCopy(const DevComm& c, const void* send_mc, void* recv_mc, unsigned long long count,
+// Zero-copy collectives on multicast-bound symmetric buffers (func 0 AllReduce: send and recv
+// are multicast addresses; 3 AllGather: send local, recv multicast; 4 ReduceScatter: send
+// multicast, recv local). count is the payload (AllReduce) or per-rank block (AllGather,
+// ReduceScatter) in elements; its bytes must be a multiple of 16.
+cudaError_t LaunchNvlsZeroCopy(const DevComm& c, int func, const void* send, void* recv, unsigned long long count,
                                int dtype, int op, float scale, int nctas, cudaStream_t stream);
 
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.

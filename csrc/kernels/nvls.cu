@@ -176,18 +176,23 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
     finish_launch(c, 0, (uint64_t)per_round * (uint64_t)p.nrounds, (uint64_t)p.nrounds);
 }
 
-// Zero-copy AllReduce on buffers bound to the multicast object (symmetric user buffers): no
-// staging. Rank r reduces its shard of every 16-byte vector straight from the send buffers of
-// all ranks (multimem.ld_reduce on the send buffer's multicast address) and stores the result
-// into every rank's receive buffer (multimem.st on the receive buffer's multicast address).
-// An entry barrier makes every rank's input ready before any rank reads it; the exit barrier
-// (system-scope release after the multicast stores) makes every output complete before any
-// rank's later work reads it. Both buffers sit at the same offset on every rank.
+// Zero-copy collectives on buffers bound to the multicast object (symmetric user buffers), no
+// staging:
+//   AllReduce:     rank r reduces its shard of every 16-byte vector straight from all ranks' send
+//                  buffers (multimem.ld_reduce on the send buffer's multicast address) and stores
+//                  it into every rank's receive buffer (multimem.st on its multicast address);
+//   ReduceScatter: rank r reduces its own block from all ranks' send buffers into its output;
+//   AllGather:     rank r stores its input block into every rank's receive buffer at block r.
+// An entry barrier makes every rank's input (and free output) ready before any rank touches
+// them; the exit barrier (system-scope release after the multicast stores) makes every output
+// complete, and every input read, before any rank's later work. Symmetric buffers sit at the
+// same offset on every rank.
 struct ZcParams {
     DevComm comm;
-    const char* send_mc;
-    char* recv_mc;
-    unsigned long long bytes;  // multiple of 16
+    const char* send;   // AllReduce, ReduceScatter: the send buffer's multicast address; AllGather: local input
+    char* recv;         // AllReduce, AllGather: the receive buffer's multicast address; ReduceScatter: local output
+    unsigned long long bytes;  // AllReduce: payload; AllGather / ReduceScatter: per-rank block; multiple of 16
+    int func;           // 0 AllReduce, 3 AllGather, 4 ReduceScatter (CollFunc values)
     int op;
     float scale;
 };
@@ -199,20 +204,43 @@ __global__ void __launch_bounds__(512, 1) nvls_zc_kernel(const __grid_constant__
     const uint64_t bar = load_state_u64(&c.state->barrier_seq);
     if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar & 0x7fffffffull));
     bool ok = cta_barrier(c, bar + 1, 0);
-    if (ok) {
+    if (ok && p.func == 3) {  // AllGather: this rank's block into every rank's output
+        const size_t nvec = p.bytes / 16;
+        const size_t per_cta = (nvec + gridDim.x - 1) / gridDim.x;
+        const size_t c0 = min(nvec, (size_t)blockIdx.x * per_cta), c1 = min(nvec, c0 + per_cta);
+        char* out = p.recv + (size_t)r * p.bytes;
+        size_t i = c0 + threadIdx.x;
+        for (; i + 3 * blockDim.x < c1; i += 4 * blockDim.x) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(p.send + (i + u * blockDim.x) * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) mm_st(out + (i + u * blockDim.x) * 16, v[u]);
+        }
+        for (; i < c1; i += blockDim.x) mm_st(out + i * 16, *reinterpret_cast<const uint4*>(p.send + i * 16));
+        ok = cta_barrier(c, bar + 2, 1);
+    } else if (ok) {
         constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
         const bool post = p.op == kAvg || p.scale != 1.0f;
+        const bool rs = p.func == 4;  // ReduceScatter: reduce this rank's block into local memory
         const size_t nvec = p.bytes / 16;
-        const size_t per_rank = (nvec + n - 1) / n;
-        const size_t r0 = min(nvec, (size_t)r * per_rank), r1 = min(nvec, r0 + per_rank);
+        const size_t per_rank = rs ? nvec : (nvec + n - 1) / n;
+        const size_t r0 = rs ? 0 : min(nvec, (size_t)r * per_rank), r1 = min(nvec, r0 + per_rank);
+        const char* in = rs ? p.send + (size_t)r * p.bytes : p.send;
         const size_t per_cta = (r1 - r0 + gridDim.x - 1) / gridDim.x;
         const size_t c0 = min(r1, r0 + (size_t)blockIdx.x * per_cta), c1 = min(r1, c0 + per_cta);
         const size_t t = threadIdx.x, nt = blockDim.x;
+        // AllReduce: multicast store of the reduced vector to every rank; ReduceScatter: plain
+        // store to this rank's output.
+        auto put = [&](size_t idx, const uint4& val) {
+            if (rs) *reinterpret_cast<uint4*>(p.recv + idx * 16) = val;
+            else mm_st(p.recv + idx * 16, val);
+        };
         size_t i = c0 + t;
         for (; i + 3 * nt < c1; i += 4 * nt) {  // four reductions in flight per thread
             V16<D> v[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(p.send_mc + (i + u * nt) * 16);
+            for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(in + (i + u * nt) * 16);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 if (post) {
@@ -220,18 +248,18 @@ __global__ void __launch_bounds__(512, 1) nvls_zc_kernel(const __grid_constant__
                     for (int e = 0; e < E; ++e)
                         v[u].b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v[u].b[e]), n, p.scale));
                 }
-                mm_st(p.recv_mc + (i + u * nt) * 16, v[u].u);
+                put(i + u * nt, v[u].u);
             }
         }
         for (; i < c1; i += nt) {
             V16<D> v;
-            v.u = red16<D, O>(p.send_mc + i * 16);
+            v.u = red16<D, O>(in + i * 16);
             if (post) {
 #pragma unroll
                 for (int e = 0; e < E; ++e)
                     v.b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v.b[e]), n, p.scale));
             }
-            mm_st(p.recv_mc + i * 16, v.u);
+            put(i, v.u);
         }
         ok = cta_barrier(c, bar + 2, 1);
     }
@@ -254,21 +282,24 @@ cudaError_t launch_t(const NvlsParams& p, int nctas, cudaStream_t s) {
 }  // namespace
 }  // namespace dev
 
-cudaError_t LaunchNvlsZeroCopy(const DevComm& c, const void* send_mc, void* recv_mc, unsigned long long count,
+cudaError_t LaunchNvlsZeroCopy(const DevComm& c, int func, const void* send, void* recv, unsigned long long count,
                                int dtype, int op, float scale, int nctas, cudaStream_t stream) {
     using namespace dev;
     const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
-    if (nctas <= 0 || nctas > kMaxCtas || (bytes % 16) != 0 || ((reinterpret_cast<uintptr_t>(send_mc) |
-        reinterpret_cast<uintptr_t>(recv_mc)) & 15) != 0 || !NvlsSupports(dtype, op)) {
+    if (nctas <= 0 || nctas > kMaxCtas || (bytes % 16) != 0 ||
+        ((reinterpret_cast<uintptr_t>(send) | reinterpret_cast<uintptr_t>(recv)) & 15) != 0 ||
+        (func != 0 && func != 3 && func != 4) || (func != 3 && !NvlsSupports(dtype, op))) {
         return cudaErrorInvalidValue;
     }
     ZcParams p;
     p.comm = c;
-    p.send_mc = static_cast<const char*>(send_mc);
-    p.recv_mc = static_cast<char*>(recv_mc);
+    p.send = static_cast<const char*>(send);
+    p.recv = static_cast<char*>(recv);
     p.bytes = bytes;
+    p.func = func;
     p.op = op;
     p.scale = scale;
+    if (func == 3) return launch_zc<kF32, kSum>(p, nctas, stream);  // data movement only
     const int o = (op == kAvg) ? kSum : op;
 #define ZC_CASE(D, O) \
     if (dtype == D && o == O) return launch_zc<D, O>(p, nctas, stream);

@@ -323,8 +323,9 @@ def run_dp(rank: int, world: int, hidden: int = 256, steps: int = 2) -> Dict:
 
 
 def run_zero_copy(rank: int, world: int) -> Dict:
-    """AllReduce on symmetric (multicast-bound) buffers: the zero-copy NVLS kernel, in place and
-    out of place, against a float64 oracle."""
+    """Collectives on symmetric (multicast-bound) buffers through the zero-copy NVLS kernel:
+    AllReduce in place and out of place, AllGather into a symmetric output, ReduceScatter from a
+    symmetric input, against a float64 oracle."""
     import torch
 
     import originccl_b200 as occl
@@ -349,5 +350,24 @@ def run_zero_copy(rank: int, world: int) -> Dict:
         _close(dst, oracle("sum", inputs, world).to(td), dtype, f"zero-copy {dtype} n={n}")
         comm.all_reduce(src, ReduceOp.AVG, algo=Algo.NVLS)  # in place
         _close(src, oracle("avg", inputs, world).to(td), dtype, f"zero-copy in place {dtype} n={n}")
+    # AllGather into a symmetric output, ReduceScatter from a symmetric input.
+    for dtype, n in (("float32", 1024), ("bfloat16", 5 << 16)):
+        td = getattr(torch, dtype)
+        blocks = [rank_input(r, n, dtype, seed=n + 1) for r in range(world)]
+        gathered = comm.symmetric_empty((world * n,), td)
+        mine = blocks[rank].cuda()
+        torch.cuda.synchronize()
+        comm.all_gather(gathered, mine)
+        used.add(comm.last_algorithm)
+        _close(gathered, torch.cat(blocks).to(td), dtype, f"zero-copy all_gather {dtype} n={n}")
+        full = [rank_input(r, world * n, dtype, seed=n + 2) for r in range(world)]
+        src = comm.symmetric_empty((world * n,), td)
+        src.copy_(full[rank].cuda())
+        torch.cuda.synchronize()
+        shard = torch.empty(n, dtype=td, device="cuda")
+        comm.reduce_scatter(shard, src, ReduceOp.SUM)
+        used.add(comm.last_algorithm)
+        want = oracle("sum", full, world)[rank * n:(rank + 1) * n].to(td)
+        _close(shard, want, dtype, f"zero-copy reduce_scatter {dtype} n={n}")
     comm.destroy()
     return {"algorithms": sorted(used)}

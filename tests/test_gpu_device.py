@@ -122,7 +122,7 @@ def test_data_parallel_sync_two_ranks():
 @pytest.mark.multigpu
 @pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
                     reason="zero-copy NVLS kernel not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
-def test_zero_copy_nvls_allreduce_two_ranks():
+def test_zero_copy_nvls_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_zero_copy, timeout=300)
     assert res[0].get("skipped") or res[0]["algorithms"] == ["nvls_zero_copy"]
