@@ -5,6 +5,7 @@
 //   bccl_run -np 2 --gpus bccl_check check --device # GPU buffers (one GPU per rank)
 //   bccl_run -np 4 bccl_check bench --counts 32768,131072 --warmup 20 --iters 100
 //   bccl_run -np 4 bccl_check bench-group --messages 64 --message-bytes 262144
+//   bccl_run -np 32 bccl_check check --ranks-per-machine 8   # four logical machines
 //
 // check: every collective with exact-valued inputs (integers, and floats that are multiples of
 // 1/8), out of place and in place, a sentinel element after every output, nested groups,
@@ -14,6 +15,10 @@
 // bench: int32 SUM AllReduce with rank r's element i = (r*7 + i) mod 1000 (checked), timed on
 // the host clock between barriers; the time per call is the max over ranks (an AllReduce of
 // the per-rank times with MAX), busbw = algbw * 2(N-1)/N. One JSON line per count.
+//
+// --ranks-per-machine K injects the hostname "logical-machine-<rank / K>" through
+// CommConfig::get_hostname, as OriginCCL tests/regression/test_multi_machine.cpp:14-20 does, so
+// one host runs the shared-memory, leader-exchange and TCP paths of several machines.
 //
 // Parity: OriginCCL tests/test_common.cpp (case generator, oracle, sentinel, contract cases)
 // and tests/benchmark/test_allreduce_benchmark.cpp:341-421 (timing as max over ranks).
@@ -132,6 +137,23 @@ struct Checker {
             ++failed;
             if (failures.size() < 8) failures.push_back(what);
         }
+    }
+
+    // The communicator's view of machines when ranks are grouped K per (logical) machine in
+    // rank order (K = world when every rank shares one host).
+    void View(int per_machine) {
+        const int k = per_machine > 0 ? std::min(per_machine, world) : world;
+        const int machine = rank / k, machines = (world + k - 1) / k;
+        const int first = machine * k, size = std::min(k, world - first);
+        std::vector<int> locals, leaders;
+        for (int r = first; r < first + size; ++r) locals.push_back(r);
+        for (int m = 0; m < machines; ++m) leaders.push_back(m * k);
+        Record(comm->GetRank() == rank && comm->GetWorldSize() == world, "view: rank/world");
+        Record(comm->GetMachineIndex() == machine && comm->GetMachineCount() == machines, "view: machines");
+        Record(comm->IsSingleMachine() == (machines == 1), "view: single machine");
+        Record(comm->GetLocalRank() == rank - first && comm->GetLocalSize() == size, "view: local rank/size");
+        Record(comm->GetLocalRanks() == locals, "view: local ranks");
+        Record(comm->GetMachineLeaders() == leaders, "view: machine leaders");
     }
 
     template <typename T>
@@ -405,11 +427,14 @@ int RunGroupBench(Communicator* comm, Mem mem, int rank, int world, int nmsg, si
 
 }  // namespace
 
+std::string g_logical_host;
+std::string LogicalHost() { return g_logical_host; }
+
 int main(int argc, char** argv) {
     std::string mode = argc > 1 ? argv[1] : "check";
     bool device = false;
     std::vector<size_t> counts = {32768, 131072};
-    int warmup = 20, iters = 100, channels = 0, nmsg = 64;
+    int warmup = 20, iters = 100, channels = 0, nmsg = 64, per_machine = 0;
     size_t msg_bytes = 256u << 10;
     for (int i = 2; i < argc; ++i) {
         std::string a = argv[i];
@@ -420,6 +445,7 @@ int main(int argc, char** argv) {
         else if (a == "--channels" && i + 1 < argc) channels = std::atoi(argv[++i]);
         else if (a == "--messages" && i + 1 < argc) nmsg = std::atoi(argv[++i]);
         else if (a == "--message-bytes" && i + 1 < argc) msg_bytes = static_cast<size_t>(std::atoll(argv[++i]));
+        else if (a == "--ranks-per-machine" && i + 1 < argc) per_machine = std::atoi(argv[++i]);
     }
     const int rank = EnvInt("BCCL_RANK", 0), world = EnvInt("BCCL_WORLD_SIZE", 1);
     Communicator comm;
@@ -427,6 +453,10 @@ int main(int argc, char** argv) {
     cfg.rank = rank;
     cfg.world_size = world;
     cfg.n_channels = channels;
+    if (per_machine > 0) {
+        g_logical_host = "logical-machine-" + std::to_string(rank / per_machine);
+        cfg.get_hostname = LogicalHost;
+    }
     if (device) {
         cfg.device = EnvInt("BCCL_DEVICE", EnvInt("BCCL_LOCAL_RANK", rank));
         if (cudaSetDevice(cfg.device) != cudaSuccess) {
@@ -447,6 +477,7 @@ int main(int argc, char** argv) {
         rc = RunGroupBench(&comm, mem, rank, world, nmsg, msg_bytes, warmup, iters);
     } else {
         Checker c{&comm, mem, rank, world};
+        c.View(per_machine);
         for (size_t n : {size_t(1), size_t(1000), size_t(32768 + 3)}) {
             for (ReduceOp op : {ReduceOp::SUM, ReduceOp::MAX, ReduceOp::MIN, ReduceOp::AVG}) {
                 c.AllReduce<int>(DataType::INT32, op, n, false);
@@ -471,8 +502,9 @@ int main(int argc, char** argv) {
         mem.Free(fb);
         if (fails < 0) total_fail = world;
         if (rank == 0) {
-            std::printf("{\"passed\": %d, \"failed\": %d, \"failed_all_ranks\": %d, \"ranks\": %d, \"path\": \"%s\"",
-                        c.passed, c.failed, total_fail, world, device ? "device" : "host");
+            std::printf("{\"passed\": %d, \"failed\": %d, \"failed_all_ranks\": %d, \"ranks\": %d, \"machines\": %d, "
+                        "\"path\": \"%s\"",
+                        c.passed, c.failed, total_fail, world, comm.GetMachineCount(), device ? "device" : "host");
             std::printf(", \"failures\": [");
             for (size_t i = 0; i < c.failures.size(); ++i)
                 std::printf("%s\"%s\"", i ? ", " : "", c.failures[i].c_str());

@@ -27,12 +27,22 @@ def _json_lines(out):
     return [json.loads(line) for line in out.splitlines() if line.startswith("{")]
 
 
-@pytest.mark.parametrize("np_", [1, 2, 4])
-def test_cpp_check_matrix_host(np_):
-    r = _run(["-np", str(np_), "--timeout", "150", "--", CHECK, "check"])
+# The reference's levels run 4, 8 and 32 ranks (tests/test_common.cpp:28-39); its multi-machine
+# test groups ranks into logical machines by hostname (tests/regression/test_multi_machine.cpp).
+@pytest.mark.parametrize("np_,per_machine,machines", [
+    (1, 0, 1), (2, 0, 1), (4, 0, 1),    # one machine, level 0
+    (8, 0, 1),                          # level 1
+    (32, 8, 4),                         # level 2: four logical machines of eight ranks
+    (8, 3, 3),                          # uneven machines (3 + 3 + 2)
+    (4, 1, 4),                          # one rank per machine: every exchange over TCP
+])
+def test_cpp_check_matrix_host(np_, per_machine, machines):
+    extra = ["--ranks-per-machine", str(per_machine)] if per_machine else []
+    r = _run(["-np", str(np_), "--timeout", "150", "--", CHECK, "check"] + extra)
     assert r.returncode == 0, r.stdout + r.stderr
     res = _json_lines(r.stdout)[-1]
-    assert res["failed_all_ranks"] == 0 and res["passed"] >= 50 and res["ranks"] == np_
+    assert res["failed_all_ranks"] == 0 and res["passed"] >= 56 and res["ranks"] == np_
+    assert res["machines"] == machines
 
 
 def test_cpp_int32_allreduce_bench_host():
