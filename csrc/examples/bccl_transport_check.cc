@@ -11,7 +11,7 @@
 //     a TCP socket is bidirectional;
 //   * boundaries: 1 B .. 5 MiB around powers of two and the 2 MiB ring capacity, byte-exact,
 //     with progress monotone and done <=> progress == size;
-//   * back-pressure: a send to a receiver that does not read for 200 ms stalls without error,
+//   * back-pressure: a send to a receiver that does not read for 400 ms stalls without error,
 //     then completes when the receiver drains (8 MiB over the 2 MiB ring; 64 MiB over TCP, whose
 //     loopback socket buffers can absorb several MiB);
 //   * close: after the peer closes, TCP reports an error to the receiver once the stream is
@@ -58,7 +58,15 @@ std::vector<size_t> BoundarySizes() {
     return s;
 }
 
-size_t BackPressureBytes(bool tcp) { return tcp ? size_t(64) << 20 : size_t(8) << 20; }
+size_t BackPressureBytes(bool tcp) { return tcp ? size_t(16) << 20 : size_t(8) << 20; }
+
+// Loopback TCP autotunes its buffers up to the system maximum, which on some hosts absorbs the
+// whole back-pressure message; fixed 256 KiB socket buffers on both ends make the stall certain.
+void CapSocketBuffers(int fd) {
+    const int bytes = 256 << 10;
+    setsockopt(fd, SOL_SOCKET, SO_SNDBUF, &bytes, sizeof(bytes));
+    setsockopt(fd, SOL_SOCKET, SO_RCVBUF, &bytes, sizeof(bytes));
+}
 
 uint8_t Pattern(size_t size, size_t i) { return static_cast<uint8_t>((i * 131 + size * 7 + (i >> 9)) & 0xff); }
 
@@ -127,8 +135,8 @@ int Receiver(Transport* t, bool tcp) {
             }
         }
     }
-    // Back-pressure: do not read for 200 ms, then drain.
-    std::this_thread::sleep_for(std::chrono::milliseconds(200));
+    // Back-pressure: do not read for 400 ms (the sender watches for 100 ms), then drain.
+    std::this_thread::sleep_for(std::chrono::milliseconds(400));
     const size_t bp = BackPressureBytes(tcp);
     std::vector<uint8_t> buf(bp);
     if (!Drive(t, false, buf.data(), bp, 20000, &why)) return bad + 1;
@@ -178,6 +186,7 @@ int Run(bool tcp) {
         if (tcp) {
             int fd = bccl::net::Accept(listen_fd, 10000);
             if (fd < 0) _exit(3);
+            CapSocketBuffers(fd);
             t.reset(new TcpTransport(fd));
         } else {
             t.reset(new ShmRingTransport(ctrl, ring, kRingBytes, /*producer=*/false));
@@ -189,6 +198,7 @@ int Run(bool tcp) {
     if (tcp) {
         int fd = bccl::net::Connect("127.0.0.1", port, 10000);
         if (fd < 0) return 2;
+        CapSocketBuffers(fd);
         tx.reset(new TcpTransport(fd));
         rep.Check(tx->GetFd() >= 0 && tx->GetPollEvents(true) == POLLOUT && tx->GetPollEvents(false) == POLLIN,
                   "tcp exposes its fd with POLLOUT/POLLIN");
@@ -206,16 +216,19 @@ int Run(bool tcp) {
     }
     std::string why;
     uint8_t z = 0;
-    rep.Check(Drive(tx.get(), true, &z, 0, 1000, &why), "zero-size send done at once");
-    for (size_t size : BoundarySizes()) {
-        std::vector<uint8_t> buf(size);
-        for (size_t i = 0; i < size; ++i) buf[i] = Pattern(size, i);
-        rep.Check(Drive(tx.get(), true, buf.data(), size, 20000, &why), "send " + std::to_string(size) + ": " + why);
-    }
-    // Back-pressure: while the receiver sleeps, progress must stall below the message size.
+    // The back-pressure message is prepared first, so the sender's stall window below starts as
+    // soon as the last boundary message is handed over, well inside the receiver's pause (even
+    // when an instrumented build makes filling 16 MiB slow).
     const size_t bp = BackPressureBytes(tcp);
     std::vector<uint8_t> buf(bp);
     for (size_t i = 0; i < bp; ++i) buf[i] = Pattern(bp, i);
+    rep.Check(Drive(tx.get(), true, &z, 0, 1000, &why), "zero-size send done at once");
+    for (size_t size : BoundarySizes()) {
+        std::vector<uint8_t> msg(size);
+        for (size_t i = 0; i < size; ++i) msg[i] = Pattern(size, i);
+        rep.Check(Drive(tx.get(), true, msg.data(), size, 20000, &why), "send " + std::to_string(size) + ": " + why);
+    }
+    // Back-pressure: while the receiver sleeps, progress must stall below the message size.
     size_t progress = 0;
     bool done = false, ok = true;
     auto until = Clock::now() + std::chrono::milliseconds(100);

@@ -101,6 +101,75 @@ def _ninja_file() -> str:
     return "\n".join(lines) + "\n"
 
 
+SANITIZERS = {
+    "asan": "-fsanitize=address,undefined -fno-sanitize-recover=undefined -fno-omit-frame-pointer",
+    "tsan": "-fsanitize=thread -fno-omit-frame-pointer",
+}
+
+
+def _sanitized_ninja_file(kind: str) -> str:
+    """Host C++ of the library, the launcher and the examples rebuilt with a sanitizer; the CUDA
+    objects of the regular build are linked in unchanged (kernels are not instrumented)."""
+    cc, cu = _sources()
+    out = ROOT / "build" / f"san-{kind}"
+    nccl = nccl_include()
+    incs = f"-I{CSRC} -I{CSRC / 'include'} -I{CUDA_HOME / 'include'}"
+    if nccl:
+        incs += f" -I{nccl}"
+    san = SANITIZERS[kind]
+    cxxflags = f"-O1 -g -std=c++17 -fPIC -Wall -Wno-unused-parameter -Wno-missing-field-initializers {san} {incs}"
+    lines = [
+        "ninja_required_version = 1.5",
+        f"cxxflags = {cxxflags}",
+        "rule cxx",
+        "  command = g++ -MMD -MF $out.d $cxxflags -c $in -o $out",
+        "  depfile = $out.d",
+        "  deps = gcc",
+        "  description = CXX $out",
+        "rule link",
+        f"  command = g++ {san} -shared -o $out $in -L{CUDA_HOME / 'lib64'} -lcudart_static -ldl -lpthread -lrt",
+        "  description = LINK $out",
+        "rule linkexe",
+        f"  command = g++ {san} -o $out $in -L{out} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} "
+        f"-lcudart -Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread",
+        "  description = LINK $out",
+    ]
+    objs = []
+    for src in cc:
+        obj = out / (str(src.relative_to(CSRC)).replace("/", "_") + ".o")
+        lines.append(f"build {obj}: cxx {src}")
+        objs.append(str(obj))
+    objs += [str(BUILD / (str(src.relative_to(CSRC)).replace("/", "_") + ".o")) for src in cu]
+    lines.append(f"build {out / 'libbccl.so'}: link {' '.join(objs)}")
+    for ex in sorted((CSRC / "examples").glob("*.cc")):
+        eobj = out / f"examples_{ex.name}.o"
+        lines.append(f"build {eobj}: cxx {ex}")
+        lines.append(f"build {out / ex.stem}: linkexe {eobj} | {out / 'libbccl.so'}")
+    return "\n".join(lines) + "\n"
+
+
+def build_sanitized(kind: str, verbose: bool = False) -> Path:
+    """Builds libbccl.so and the example programs (bccl_check, bccl_transport_check) with
+    AddressSanitizer + UndefinedBehaviorSanitizer (``"asan"``) or ThreadSanitizer (``"tsan"``)
+    into build/san-<kind>/ and returns that folder. Used by the CPU tests of the host path; run
+    the programs under the regular ``bccl_run`` launcher."""
+    if kind not in SANITIZERS:
+        raise ValueError(f"unknown sanitizer {kind!r} (asan, tsan)")
+    build(verbose)  # the CUDA objects are shared with the regular build
+    out = ROOT / "build" / f"san-{kind}"
+    out.mkdir(parents=True, exist_ok=True)
+    ninja_path = out / "build.ninja"
+    content = _sanitized_ninja_file(kind)
+    if not ninja_path.exists() or ninja_path.read_text() != content:
+        ninja_path.write_text(content)
+    ninja = shutil.which("ninja") or str(Path(sys.executable).parent / "ninja")
+    res = subprocess.run([ninja, "-C", str(out)] + (["-v"] if verbose else []), capture_output=not verbose,
+                         text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"sanitized build ({kind}) failed:\n{((res.stdout or '') + (res.stderr or ''))[-8000:]}")
+    return out
+
+
 def build(verbose: bool = False) -> Path:
     """Compiles everything (incrementally) and returns the path of libbccl.so."""
     BUILD.mkdir(parents=True, exist_ok=True)
@@ -121,4 +190,8 @@ def build(verbose: bool = False) -> Path:
 
 
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    kinds = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--sanitize=")]
+    for k in kinds:
+        print(build_sanitized(k, verbose="-v" in sys.argv))
+    if not kinds:
+        print(build(verbose="-v" in sys.argv))
