@@ -17,7 +17,6 @@ from __future__ import annotations
 
 import argparse
 import datetime
-import json
 import os
 import sys
 
@@ -30,6 +29,7 @@ def main(argv=None) -> int:
     p.add_argument("--small", type=int, default=256, help="number of 4 KiB tensors in the group")
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--no-nccl", action="store_true")
+    p.add_argument("--out", default="", help="also append the record to this JSON-lines file")
     p.add_argument("--symmetric", action="store_true",
                    help="gradient buckets in the communicator's symmetric (multicast-bound) memory")
     args = p.parse_args(argv)
@@ -130,8 +130,9 @@ def main(argv=None) -> int:
     if t_nccl is not None:
         rec.update({"nccl_ms_per_sync": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e6 * f, 1),
                     "speedup_vs_nccl": round(t_nccl / t_ours, 3), "nccl_small_group_us": round(t_small_nccl * 1e3, 2)})
-    if rank == 0:
-        print(json.dumps(rec), flush=True)
+    from originccl_b200.utils.results import ResultLog
+    with ResultLog("dp_bench", args.out, enabled=rank == 0) as log:
+        log(rec)
     comm.destroy()
     barrier()
     dist.destroy_process_group()

@@ -12,7 +12,6 @@ square one.
 from __future__ import annotations
 
 import argparse
-import json
 import os
 import sys
 
@@ -36,10 +35,14 @@ def main(argv=None) -> int:
     p.add_argument("--shapes", default="8192x3584x8192:silu,8192x8192x3584,4096x4096x4096",
                    help="comma list of MxNxK[:silu]")
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
     args = p.parse_args(argv)
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     import torch
     from originccl_b200.ops import gemm
+    from originccl_b200.utils.results import ResultLog
+
+    log = ResultLog("gemm_bench", args.out)
 
     torch.cuda.set_device(0)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -61,9 +64,10 @@ def main(argv=None) -> int:
         ours = _time(lambda: gemm.gemm(a, w, act, out=y), args.iters)
         cub = _time(lambda: torch.matmul(a, w.t()), args.iters)
         fl = 2.0 * m * n * k
-        print(json.dumps({"shape": spec, "kernel": gemm.kernel_name(m), "ours_ms": round(ours, 4),
-                          "ours_tflops": round(fl / ours / 1e9, 1), "cublas_ms": round(cub, 4),
-                          "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": round(err, 5), "ok": ok}), flush=True)
+        log({"shape": spec, "kernel": gemm.kernel_name(m), "ours_ms": round(ours, 4),
+             "ours_tflops": round(fl / ours / 1e9, 1), "cublas_ms": round(cub, 4),
+             "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": round(err, 5), "ok": ok})
+    log.close()
     return rc
 
 

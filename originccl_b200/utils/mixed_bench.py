@@ -34,6 +34,7 @@ def main(argv=None) -> int:
     p.add_argument("--group-bytes", default="4K,64K,1M")
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--iters", type=int, default=100)
+    p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
     args = p.parse_args(argv)
 
     import torch
@@ -53,7 +54,8 @@ def main(argv=None) -> int:
     barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
     parts = set(args.parts.split(","))
     lo, hi = parse_size(args.min_bytes), parse_size(args.max_bytes)
-    emit = lambda line: print(line, flush=True)  # noqa: E731
+    from originccl_b200.utils.results import ResultLog
+    emit = ResultLog("mixed_bench", args.out, enabled=rank == 0)
     common = dict(factor=args.factor, warmup=args.warmup, iters=args.iters, seed=42, emit=emit)
     all_ok = True
 

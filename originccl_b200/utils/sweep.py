@@ -182,7 +182,7 @@ def main(argv=None) -> None:
     p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring"])
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--no-nccl", action="store_true")
-    p.add_argument("--out", default="")
+    p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
     args = p.parse_args(argv)
 
     import torch
@@ -196,19 +196,13 @@ def main(argv=None) -> None:
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=300))
     comm = occl.init_from_store(dist.distributed_c10d._get_default_store(), rank, world, device=local)
-    out_f = open(args.out, "a") if (args.out and rank == 0) else None
-
-    def emit(line: str) -> None:
-        print(line, flush=True)
-        if out_f:
-            out_f.write(line + "\n")
-            out_f.flush()
+    from originccl_b200.utils.results import ResultLog
+    log = ResultLog("sweep", args.out, enabled=rank == 0)
 
     run_sweep(comm, op=args.op, dtype=args.dtype, min_bytes=parse_size(args.min_bytes),
               max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup, iters=args.iters,
-              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=emit)
-    if out_f:
-        out_f.close()
+              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log)
+    log.close()
     comm.destroy()
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()

@@ -10,7 +10,6 @@ from __future__ import annotations
 
 import argparse
 import datetime
-import json
 import os
 import sys
 
@@ -24,6 +23,7 @@ def main(argv=None) -> None:
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--gemm-peak-tflops", type=float, default=1383.8, help="measured sustained cuBLAS bf16 peak")
     p.add_argument("--nvlink-gbs", type=float, default=770.0)
+    p.add_argument("--out", default="", help="also append the record to this JSON-lines file")
     args = p.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -92,13 +92,14 @@ def main(argv=None) -> None:
         bd["nccl_allgather_ms"] = timed(lambda: dist.all_gather_into_tensor(xg, x))
         bd["nccl_reducescatter_ms"] = timed(lambda: dist.reduce_scatter_tensor(out, part))
     bd = {k: round(v, 4) for k, v in bd.items()}
-    if rank == 0:
-        print(json.dumps({"bench": "tp_mlp", "world": world, "tokens": args.tokens, "hidden": args.hidden,
-                          "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
-                          "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
-                          "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
-                          "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(),
-                          "breakdown": bd}), flush=True)
+    from originccl_b200.utils.results import ResultLog
+    with ResultLog("tp_bench", args.out, enabled=rank == 0) as log:
+        log({"bench": "tp_mlp", "world": world, "tokens": args.tokens, "hidden": args.hidden,
+             "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
+             "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
+             "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
+             "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(),
+             "breakdown": bd})
     comm.destroy()
     if world > 1:
         dist.barrier(device_ids=[local])
