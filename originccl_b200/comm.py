@@ -248,7 +248,13 @@ class Communicator:
 
     # ---------------------------------------------------------------- streams
     def _stream(self, stream: Any = None) -> tuple:
-        if self.device < 0 or (self.blocking and stream is None):
+        if self.device < 0:
+            return 0, 0
+        if self.blocking and stream is None:
+            import torch
+            if torch.cuda.is_current_stream_capturing():
+                raise BcclError("a blocking communicator runs on its own stream and waits on the host, so it "
+                                "cannot be captured into a CUDA graph; use a stream-ordered one (blocking=False)")
             return 0, 0
         if stream is None:
             import torch

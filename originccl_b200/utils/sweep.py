@@ -11,7 +11,9 @@ taken as the max over ranks. Here every size is timed on the device with CUDA ev
 then ``iters`` calls between barriers + synchronize), the max over ranks is reported, and the
 same buffers are timed through NCCL for comparison. Before timing, every size is checked once
 against an fp64 reduction of the same inputs (``check`` in the record). Inputs are uniform in
-[-1, 1] from seed 1234+rank. Rank 0 prints one JSON line per size.
+[-1, 1] from seed 1234+rank. Rank 0 prints one JSON line per size. ``--graph K`` times CUDA-graph
+replays of K captured calls instead of eager calls (both libraries), which removes the host's
+launch path from small-message latency.
 """
 from __future__ import annotations
 
@@ -33,9 +35,13 @@ def parse_size(s: str) -> int:
 
 def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, factor: int = 2, warmup: int = 20,
               iters: int = 100, algo: str = "auto", inplace: bool = False, nccl: bool = True, redop: str = "sum",
-              seed: int = 1234, emit=print) -> list:
+              seed: int = 1234, emit=print, graph: int = 0) -> list:
     """Times ``op`` at every size from min_bytes to max_bytes (x factor) with this library and
-    with NCCL on the same buffers; returns (and emits on rank 0) one record per size."""
+    with NCCL on the same buffers; returns (and emits on rank 0) one record per size.
+
+    ``graph`` > 0 captures that many back-to-back calls into one CUDA graph (for both
+    libraries) and times graph replays instead of eager calls: the per-call time then excludes
+    the host's launch path, as nccl-tests' ``-G`` does."""
     import torch
     import torch.distributed as dist
     from originccl_b200 import Algo, ReduceOp
@@ -52,6 +58,15 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
     barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
 
     def timed(fn) -> float:
+        if graph > 0:
+            from originccl_b200.utils.graphs import capture, time_replays
+            g = capture(fn, repeat=graph, warmup=warmup)
+            g.replay()  # one untimed replay
+            us = time_replays(g, max(1, iters // graph), graph, sync=barrier)
+            t = torch.tensor([us], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            del g
+            return float(t.item())
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
@@ -108,7 +123,8 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
         f = busbw_factor(op, world)
         rec = {"op": op, "dtype": dtype, "redop": redop, "bytes": n * es, "ranks": world, "algo": used,
                "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
-               "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok}
+               "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok,
+               "graph": graph}
         if t_nccl is not None:
             rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
                         "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
@@ -183,6 +199,8 @@ def main(argv=None) -> None:
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--no-nccl", action="store_true")
     p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
+    p.add_argument("--graph", type=int, default=0,
+                   help="capture this many calls per CUDA graph and time replays (0: eager calls)")
     args = p.parse_args(argv)
 
     import torch
@@ -201,7 +219,7 @@ def main(argv=None) -> None:
 
     run_sweep(comm, op=args.op, dtype=args.dtype, min_bytes=parse_size(args.min_bytes),
               max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup, iters=args.iters,
-              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log)
+              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log, graph=args.graph)
     log.close()
     comm.destroy()
     dist.barrier(device_ids=[local])

@@ -371,3 +371,67 @@ def run_zero_copy(rank: int, world: int) -> Dict:
         _close(shard, want, dtype, f"zero-copy reduce_scatter {dtype} n={n}")
     comm.destroy()
     return {"algorithms": sorted(used)}
+
+
+def run_graph(rank: int, world: int) -> Dict:
+    """Collectives captured into CUDA graphs and replayed: a small AllReduce (push engine), a
+    group of three collectives (one batched kernel) and a large AllReduce (pipelined kernels),
+    each replayed several times with new input values written between replays; every replay is
+    checked against the float64 oracle. Replays run without the host, so this also checks that
+    the device-side sequence numbers carry the cross-rank synchronisation."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import ReduceOp
+    from originccl_b200.utils.graphs import capture
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, timeout_ms=20000)  # stream-ordered
+    small, large = 3000, (24 << 20) // 4 + 12
+    x = torch.empty(small, device="cuda")
+    y = torch.empty(small, device="cuda")
+    a = torch.empty(1000, device="cuda")
+    g_in = torch.empty(777, device="cuda")
+    g_out = torch.empty(777 * world, device="cuda")
+    rs_in = torch.empty(512 * world, device="cuda")
+    rs_out = torch.empty(512, device="cuda")
+    big = torch.empty(large, device="cuda")
+    big_out = torch.empty(large, device="cuda")
+
+    def fill(seed: int):
+        ins = {}
+        for k, (name, t, n) in enumerate((("x", x, small), ("a", a, 1000), ("g", g_in, 777),
+                                          ("rs", rs_in, 512 * world), ("big", big, large))):
+            per_rank = [rank_input(r, n, "float32", seed=seed * 10 + k) for r in range(world)]
+            t.copy_(per_rank[rank].cuda())
+            ins[name] = per_rank
+        return ins
+
+    def step():
+        comm.all_reduce(x, ReduceOp.SUM, out=y)
+        with comm.group():
+            comm.all_reduce(a, ReduceOp.MAX)
+            comm.all_gather(g_out, g_in)
+            comm.reduce_scatter(rs_out, rs_in, ReduceOp.SUM)
+        comm.all_reduce(big, ReduceOp.SUM, out=big_out, scale=0.5)
+
+    fill(0)
+    graph = capture(step, repeat=1, warmup=2)
+    launches = comm.kernel_launches
+    for it in range(1, 5):
+        ins = fill(it)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        comm.synchronize()  # reports device-side failures of the replay
+        _close(y, oracle("sum", ins["x"], world), "float32", f"graph replay {it}: small all_reduce")
+        _close(a, oracle("max", ins["a"], world), "float32", f"graph replay {it}: grouped all_reduce max")
+        _close(g_out, torch.cat(ins["g"]), "float32", f"graph replay {it}: grouped all_gather")
+        _close(rs_out, oracle("sum", ins["rs"], world)[rank * 512:(rank + 1) * 512], "float32",
+               f"graph replay {it}: grouped reduce_scatter")
+        _close(big_out, oracle("sum", ins["big"], world) * 0.5, "float32", f"graph replay {it}: large all_reduce")
+    host_launches = comm.kernel_launches - launches  # replays do not go through the library
+    del graph
+    comm.destroy()
+    return {"replays": 4, "host_launches_during_replays": host_launches}

@@ -126,3 +126,20 @@ def test_zero_copy_nvls_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_zero_copy, timeout=300)
     assert res[0].get("skipped") or res[0]["algorithms"] == ["nvls_zero_copy"]
+
+
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="CUDA-graph replay not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_cuda_graph_replay_single_rank():
+    _need(1)
+    res = _mp.run(1, gpu_cases.run_graph, timeout=300)
+    assert res[0]["replays"] == 4 and res[0]["host_launches_during_replays"] == 0
+
+
+@pytest.mark.multigpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="CUDA-graph replay not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_cuda_graph_replay_two_ranks():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_graph, timeout=300)
+    assert all(r["host_launches_during_replays"] == 0 for r in res)
