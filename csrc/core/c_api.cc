@@ -211,6 +211,10 @@ int bcclCommAbort(bcclComm_t comm) {
 }
 void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes) { return comm ? comm->comm.SymmetricAlloc(bytes) : nullptr; }
 int bcclSymmetricFree(bcclComm_t comm, void* ptr) { return comm && comm->comm.SymmetricFree(ptr) ? 0 : Fail(); }
+int bcclCommRegister(bcclComm_t comm, void* ptr, size_t bytes) {
+    return comm && comm->comm.RegisterBuffer(ptr, bytes) ? 0 : Fail();
+}
+int bcclCommDeregister(bcclComm_t comm, void* ptr) { return comm && comm->comm.DeregisterBuffer(ptr) ? 0 : Fail(); }
 
 int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms) {
     if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1;

@@ -387,6 +387,8 @@ bool Communicator::Synchronize() {
 
 void* Communicator::SymmetricAlloc(size_t bytes) { return device_ ? device_->SymAlloc(bytes) : nullptr; }
 bool Communicator::SymmetricFree(void* ptr) { return device_ ? device_->SymFree(ptr) : false; }
+bool Communicator::RegisterBuffer(void* ptr, size_t bytes) { return device_ ? device_->RegisterBuffer(ptr, bytes) : true; }
+bool Communicator::DeregisterBuffer(void* ptr) { return device_ ? device_->DeregisterBuffer(ptr) : true; }
 bool Communicator::Barrier() { return bootstrap_ && bootstrap_->Barrier(); }
 
 void Communicator::Abort() {

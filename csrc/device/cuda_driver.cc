@@ -47,6 +47,7 @@ const DriverApi* Driver() {
         Load("cuMulticastUnbind", &api.cuMulticastUnbind);
         Load("cuMulticastGetGranularity", &api.cuMulticastGetGranularity);
         Load("cuTensorMapEncodeTiled", &api.cuTensorMapEncodeTiled);
+        Load("cuMemGetAddressRange", &api.cuMemGetAddressRange);
         api.loaded = ok;
         if (!ok) LOG_WARN("CUDA driver entry points unavailable (no driver?)");
     });

@@ -7,6 +7,7 @@
 #include "core/env.h"
 #include "core/logger.h"
 #include "core/nvtx.h"
+#include "device/cuda_driver.h"
 #include <cuda_bf16.h>
 
 #include "kernels/gemm.h"
@@ -120,6 +121,9 @@ void DeviceEngine::Finalize() {
     if (bs_ != nullptr && bs_->ready()) bs_->Barrier();
     for (SymBuffer& b : user_bufs_) sm_.Free(&b);
     user_bufs_.clear();
+    reg_bufs_.clear();
+    for (auto& m : ipc_maps_) cudaIpcCloseMemHandle(m.second.base);
+    ipc_maps_.clear();
     for (SymBuffer& b : tp_xg_) sm_.Free(&b);
     for (SymBuffer& b : tp_rs_) sm_.Free(&b);
     tp_xg_bytes_ = tp_rs_bytes_ = 0;
@@ -400,6 +404,145 @@ bool DeviceEngine::SymFree(void* ptr) {
     return false;
 }
 
+namespace {
+
+// What each rank contributes to a registration: its allocation's IPC handle, where the buffer
+// sits in it, and the sizes (checked for agreement).
+struct RegBlob {
+    uint32_t ok;
+    uint32_t pad;
+    cudaIpcMemHandle_t handle;
+    uint64_t offset;      // buffer - allocation base
+    uint64_t bytes;       // registered bytes
+    uint64_t alloc_size;  // allocation size
+};
+
+}  // namespace
+
+bool DeviceEngine::RegisterBuffer(void* ptr, size_t bytes) {
+    if (!inited_) return false;
+    cudaSetDevice(device_);
+    RegBlob mine;
+    std::memset(&mine, 0, sizeof(mine));
+    mine.bytes = bytes;
+    const DriverApi* d = Driver();
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    bool ok = ptr != nullptr && bytes > 0 && d != nullptr && d->cuMemGetAddressRange != nullptr &&
+              d->cuMemGetAddressRange(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) == CUDA_SUCCESS;
+    if (ok) {
+        mine.offset = reinterpret_cast<uintptr_t>(ptr) - base;
+        mine.alloc_size = size;
+        ok = mine.offset + bytes <= size;
+    }
+    if (ok && nranks_ > 1) {
+        cudaError_t e = cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base));
+        if (e != cudaSuccess) {
+            LOG_ERROR("rank %d: register: no CUDA IPC handle for %p (%s); memory from cuMemCreate (symmetric "
+                      "allocations, expandable segments) cannot be registered",
+                      rank_, ptr, cudaGetErrorString(e));
+            cudaGetLastError();
+            ok = false;
+        }
+    }
+    mine.ok = ok ? 1 : 0;
+    std::vector<uint8_t> blob(sizeof(mine));
+    std::memcpy(blob.data(), &mine, sizeof(mine));
+    std::vector<std::vector<uint8_t>> all;
+    if (!bs_->AllGather(blob, &all) || static_cast<int>(all.size()) != nranks_) return false;
+    std::vector<RegBlob> info(nranks_);
+    bool agree = true;
+    for (int q = 0; q < nranks_; ++q) {
+        if (all[q].size() != sizeof(RegBlob)) return false;
+        std::memcpy(&info[q], all[q].data(), sizeof(RegBlob));
+        agree = agree && info[q].ok == 1 && info[q].bytes == bytes;
+    }
+    if (!agree) {
+        LOG_ERROR("rank %d: register: a rank could not export its buffer or the sizes differ", rank_);
+        return false;
+    }
+    RegBuffer rb;
+    rb.bytes = bytes;
+    rb.ptr[rank_] = static_cast<char*>(ptr);
+    bool opened = true;
+    for (int q = 0; q < nranks_ && opened; ++q) {
+        if (q == rank_) continue;
+        std::string key(reinterpret_cast<const char*>(&info[q].handle), sizeof(cudaIpcMemHandle_t));
+        auto it = ipc_maps_.find(key);
+        if (it == ipc_maps_.end()) {
+            void* pb = nullptr;
+            cudaError_t e = cudaIpcOpenMemHandle(&pb, info[q].handle, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: register: cannot map rank %d's buffer (%s)", rank_, q, cudaGetErrorString(e));
+                cudaGetLastError();
+                opened = false;
+                break;
+            }
+            it = ipc_maps_.emplace(key, IpcMapping{pb, 0}).first;
+        }
+        it->second.refs++;
+        rb.ipc[q] = key;
+        rb.ptr[q] = static_cast<char*>(it->second.base) + info[q].offset;
+    }
+    // Every rank keeps the registration only if every rank mapped every peer.
+    std::vector<uint8_t> flag(1, opened ? 1 : 0);
+    std::vector<std::vector<uint8_t>> flags;
+    bool all_ok = bs_->AllGather(flag, &flags);
+    for (const auto& f : flags) all_ok = all_ok && !f.empty() && f[0] == 1;
+    if (!all_ok) {
+        for (int q = 0; q < nranks_; ++q) {
+            if (!rb.ipc[q].empty()) ReleaseIpc(rb.ipc[q]);
+        }
+        return false;
+    }
+    reg_bufs_.push_back(rb);
+    return true;
+}
+
+void DeviceEngine::ReleaseIpc(const std::string& key) {
+    auto it = ipc_maps_.find(key);
+    if (it == ipc_maps_.end()) return;
+    if (--it->second.refs <= 0) {
+        cudaIpcCloseMemHandle(it->second.base);
+        ipc_maps_.erase(it);
+    }
+}
+
+bool DeviceEngine::DeregisterBuffer(void* ptr) {
+    for (size_t i = 0; i < reg_bufs_.size(); ++i) {
+        if (reg_bufs_[i].ptr[rank_] != ptr) continue;
+        cudaSetDevice(device_);
+        cudaDeviceSynchronize();
+        if (!bs_->Barrier()) return false;  // no peer still reads or writes through the mapping
+        for (int q = 0; q < nranks_; ++q) {
+            if (!reg_bufs_[i].ipc[q].empty()) ReleaseIpc(reg_bufs_[i].ipc[q]);
+        }
+        reg_bufs_.erase(reg_bufs_.begin() + static_cast<long>(i));
+        return true;
+    }
+    LOG_ERROR("rank %d: deregister: %p is not a registered buffer", rank_, ptr);
+    return false;
+}
+
+bool DeviceEngine::PeerPointers(const void* p, size_t bytes, char* (&peers)[kMaxRanks]) const {
+    const char* q = static_cast<const char*>(p);
+    for (const RegBuffer& b : reg_bufs_) {
+        const char* base = b.ptr[rank_];
+        if (q >= base && q + bytes <= base + b.bytes) {
+            for (int r = 0; r < nranks_; ++r) peers[r] = b.ptr[r] + (q - base);
+            return true;
+        }
+    }
+    for (const SymBuffer& b : user_bufs_) {
+        const char* base = b.ptr[rank_];
+        if (q >= base && q + bytes <= base + b.bytes) {
+            for (int r = 0; r < nranks_; ++r) peers[r] = b.ptr[r] + (q - base);
+            return true;
+        }
+    }
+    return false;
+}
+
 bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream) {
     if (batch->empty()) return true;
     // The push engine owns the first half of the UC data region (two halves x N sources).
@@ -545,6 +688,44 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                 zc_send = send_mc;
                 zc_recv = t.recv_buf;
             }
+        }
+        // Registered or symmetric buffers at the same place on every rank: AllReduce /
+        // AllGather / ReduceScatter over peer memory without staging, for payloads of at least
+        // BCCL_P2P_ZC_MIN_BYTES (the batched push kernel stays better for small ones).
+        char* in_peers[kMaxRanks] = {};
+        char* out_peers[kMaxRanks] = {};
+        bool p2p_zc = false;
+        if (!zc && nranks_ > 1 && (bytes % 16) == 0 && EnvInt("BCCL_ZERO_COPY", 1) != 0 &&
+            (t.func == CollFunc::AllReduce ? bytes : all_bytes) >=
+                static_cast<size_t>(EnvInt("BCCL_P2P_ZC_MIN_BYTES", 1 << 20))) {
+            if (t.func == CollFunc::AllReduce) {
+                p2p_zc = PeerPointers(t.send_buf, bytes, in_peers) && PeerPointers(t.recv_buf, bytes, out_peers);
+            } else if (t.func == CollFunc::AllGather) {
+                p2p_zc = PeerPointers(t.recv_buf, all_bytes, out_peers);
+                for (int q = 0; q < nranks_; ++q) in_peers[q] = const_cast<char*>(static_cast<const char*>(t.send_buf));
+            } else if (t.func == CollFunc::ReduceScatter) {
+                p2p_zc = PeerPointers(t.send_buf, all_bytes, in_peers);
+                for (int q = 0; q < nranks_; ++q) out_peers[q] = static_cast<char*>(t.recv_buf);
+            }
+        }
+        if (p2p_zc) {
+            if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+            const size_t moved = t.func == CollFunc::AllReduce ? bytes : all_bytes;
+            int ctas = static_cast<int>(std::min<size_t>(std::max<size_t>(moved / (32u << 10), 8),
+                                                         static_cast<size_t>(num_sms_)));
+            if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
+            long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+            if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
+            dc_.kernel_serial = ++kernel_serial_;
+            cudaError_t e = LaunchP2pZeroCopy(dc_, static_cast<int>(t.func), in_peers, out_peers, t.count,
+                                              static_cast<int>(t.dtype), static_cast<int>(t.op), t.scale, ctas, stream);
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: zero-copy peer launch failed: %s", rank_, cudaGetErrorString(e));
+                return false;
+            }
+            launches_++;
+            last_algo_ = "p2p_zero_copy";
+            continue;
         }
         if (zc) {
             if (!FlushBatch(&batch, &stream_bytes, stream)) return false;

@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <map>
+#include <string>
 #include <vector>
 
 #include "bccl/types.h"
@@ -60,6 +62,15 @@ public:
     // multicast address.
     bool UserMulticast(const void* p, size_t bytes, char** mc) const;
     bool SymFree(void* ptr);
+    // Registration of existing device memory (cudaMalloc'd, e.g. PyTorch tensors); collective:
+    // every rank passes its own buffer of the same size, registrations in the same order. The
+    // peers map it with CUDA IPC (one mapping per allocation, shared by the registrations that
+    // fall in it). A collective whose buffers lie in registered or symmetric memory, at the same
+    // offset of the same registration on every rank, then runs over peer memory without staging.
+    bool RegisterBuffer(void* ptr, size_t bytes);
+    bool DeregisterBuffer(void* ptr);
+    // Every rank's address of [p, p + bytes) when it lies in registered or symmetric memory.
+    bool PeerPointers(const void* p, size_t bytes, char* (&peers)[kMaxRanks]) const;
 
     // Fused tensor-parallel GEMMs (bf16). x_local [ms,K] -> y [nranks*ms, n] = act(AllGather(x) * w^T)
     // with w [n,K]; h [nranks*ms, K] -> out [ms, n] = this rank's rows of sum_ranks(h * w^T).
@@ -91,6 +102,18 @@ private:
     SymBuffer uc_;
     SymBuffer nvls_;
     std::vector<SymBuffer> user_bufs_;
+    struct RegBuffer {
+        char* ptr[kMaxRanks] = {};  // every rank's registered buffer, mapped here
+        size_t bytes = 0;
+        std::string ipc[kMaxRanks];  // the peers' IPC handles (keys of ipc_maps_)
+    };
+    std::vector<RegBuffer> reg_bufs_;
+    struct IpcMapping {
+        void* base = nullptr;
+        int refs = 0;
+    };
+    std::map<std::string, IpcMapping> ipc_maps_;  // a peer's allocation, opened once
+    void ReleaseIpc(const std::string& key);
     DevState* state_ = nullptr;
     ErrorRecord* err_host_ = nullptr;
     int* abort_host_ = nullptr;

@@ -82,6 +82,10 @@ int bcclBarrier(bcclComm_t comm);
 int bcclCommAbort(bcclComm_t comm);
 void* bcclSymmetricAlloc(bcclComm_t comm, size_t bytes);
 int bcclSymmetricFree(bcclComm_t comm, void* ptr);
+/* Collective registration of existing device memory for zero-copy collectives (like
+ * ncclCommRegister); every rank passes its own buffer of the same size. */
+int bcclCommRegister(bcclComm_t comm, void* ptr, size_t bytes);
+int bcclCommDeregister(bcclComm_t comm, void* ptr);
 
 /* Failure-detection self-test: runs a kernel whose bounded wait can never be satisfied and
  * returns the error code it recorded (1 = timeout) or -1 if it could not run. */

@@ -86,6 +86,13 @@ public:
     // Device communicators: collective allocation of peer-addressable memory.
     void* SymmetricAlloc(size_t bytes);
     bool SymmetricFree(void* ptr);
+    // Device communicators: collective registration of existing device memory (e.g. a
+    // cudaMalloc'd gradient buffer); every rank registers its own buffer of the same size, in the
+    // same order. AllReduce / AllGather / ReduceScatter of at least 1 MiB whose buffers lie in
+    // registered memory, at the same offset on every rank, then read and write the peers'
+    // buffers directly instead of staging. Host communicators accept and ignore it.
+    bool RegisterBuffer(void* ptr, size_t bytes);
+    bool DeregisterBuffer(void* ptr);
     bool Barrier();
     // Stops the operations in flight from any thread: host waits return at once, device waits
     // within ~1 ms (kernels record kDevAborted and return). The communicator stays in the error

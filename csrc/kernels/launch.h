@@ -51,6 +51,13 @@ cudaError_t LaunchRingAllReduce(const DevComm& c, const void* src, void* dst, un
 cudaError_t LaunchNvlsZeroCopy(const DevComm& c, int func, const void* send, void* recv, unsigned long long count,
                                int dtype, int op, float scale, int nctas, cudaStream_t stream);
 
+// Zero-copy collectives over peer memory (func 0 AllReduce, 3 AllGather, 4 ReduceScatter):
+// in[q] / out[q] are rank q's input / output as mapped on this GPU (AllGather reads only
+// in[rank], ReduceScatter writes only out[rank]); count as for LaunchNvlsZeroCopy; bytes and
+// every pointer 16-byte aligned.
+cudaError_t LaunchP2pZeroCopy(const DevComm& c, int func, const char* const* in, char* const* out,
+                              unsigned long long count, int dtype, int op, float scale, int nctas, cudaStream_t stream);
+
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.
 bool NvlsSupports(int dtype, int op);
 

@@ -79,6 +79,8 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclBarrier": (c_int, [vp]),
         "bcclSymmetricAlloc": (vp, [vp, c_size]),
         "bcclSymmetricFree": (c_int, [vp, vp]),
+        "bcclCommRegister": (c_int, [vp, vp, c_size]),
+        "bcclCommDeregister": (c_int, [vp, vp]),
         "bcclPlannerSort": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_size),
                                     ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                                     ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),

@@ -115,6 +115,12 @@ def _numel(buf: Any) -> int:
     return int(buf.size)
 
 
+def _nbytes(buf: Any) -> int:
+    if type(buf).__module__.startswith("torch"):
+        return buf.numel() * buf.element_size()
+    return int(buf.nbytes)
+
+
 class Communicator:
     """One rank's communicator (see module docstring)."""
 
@@ -388,6 +394,31 @@ class Communicator:
         if not ptr:
             raise BcclError(_native.last_error() or "symmetric allocation failed")
         return _tensor_from_ptr(ptr, shape, dtype, self.device)
+
+    def register(self, tensor: Any) -> Any:
+        """Collective: lets the peers address ``tensor``'s memory (CUDA IPC) so that AllReduce,
+        AllGather and ReduceScatter of at least 1 MiB on it (or on a view at the same offset on
+        every rank) run without staging copies. Every rank registers its own tensor of the same
+        size, in the same order; deregister before the memory is freed. Host communicators
+        ignore it. Returns ``tensor``."""
+        self._check(self._lib.bcclCommRegister(self._h, _ptr(tensor), _nbytes(tensor)))
+        return tensor
+
+    def deregister(self, tensor: Any) -> None:
+        """Collective: undoes ``register`` (waits for the device and for every rank)."""
+        self._check(self._lib.bcclCommDeregister(self._h, _ptr(tensor)))
+
+    @contextlib.contextmanager
+    def registered(self, *tensors: Any):
+        """``with comm.registered(a, b): ...`` registers the tensors for the block."""
+        done = []
+        try:
+            for t in tensors:
+                done.append(self.register(t))
+            yield tensors
+        finally:
+            for t in reversed(done):
+                self.deregister(t)
 
 
 class TensorBatch:

@@ -19,6 +19,9 @@ Two ways to use it::
 
     dp.attach()                     # or overlap with backward: buckets launch as they fill
     loss.backward(); dp.finish()
+
+``DataParallelSync(comm, grads, register=True)`` lets the peers address the bucket storage, so
+each bucket is reduced over NVLink peer memory in one kernel without staging copies.
 """
 from __future__ import annotations
 
@@ -136,9 +139,16 @@ class DataParallelSync:
     while backward runs.
     """
 
-    def __init__(self, comm, grads: GradBuckets, *, average: bool = True, stream=None) -> None:
+    def __init__(self, comm, grads: GradBuckets, *, average: bool = True, stream=None,
+                 register: bool = False) -> None:
         self.comm = comm
         self.grads = grads
+        # register=True: the peers map the bucket storage (CUDA IPC), so every bucket is reduced
+        # in place over peer memory without staging copies (collective; call close() before the
+        # gradients are freed).
+        self.registered = bool(register) and grads.device.type == "cuda" and comm.world_size > 1
+        if self.registered:
+            comm.register(grads.flat)
         self.scale = 1.0 / comm.world_size if average else 1.0
         self.on_gpu = grads.device.type == "cuda"
         if self.on_gpu and stream is None:
@@ -149,6 +159,13 @@ class DataParallelSync:
         self._hooks: list = []
         self._pending: List[int] = []
         self._next = 0
+
+    def close(self) -> None:
+        """Collective when registered: releases the peers' mappings of the bucket storage."""
+        self.detach()
+        if self.registered:
+            self.comm.deregister(self.grads.flat)
+            self.registered = False
 
     # ------------------------------------------------------------------ after-backward sync
     def sync(self, stream=None) -> None:

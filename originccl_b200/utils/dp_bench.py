@@ -32,6 +32,8 @@ def main(argv=None) -> int:
     p.add_argument("--out", default="", help="also append the record to this JSON-lines file")
     p.add_argument("--symmetric", action="store_true",
                    help="gradient buckets in the communicator's symmetric (multicast-bound) memory")
+    p.add_argument("--register", action="store_true",
+                   help="register the gradient storage with the communicator (zero-copy over peer memory)")
     args = p.parse_args(argv)
 
     import torch
@@ -61,7 +63,7 @@ def main(argv=None) -> int:
         seg = grads.flat[lo:lo + chunk]
         seg.copy_(torch.randn(seg.numel(), device=dev, generator=gen) * 1e-3)
     grads.small_flat.copy_(torch.randn(grads.small_flat.numel(), device=dev, generator=gen) * 1e-3)
-    dp = DataParallelSync(comm, grads)
+    dp = DataParallelSync(comm, grads, register=args.register)
     small = grads.small_tensors()
     nb = grads.num_buckets
 
@@ -122,7 +124,7 @@ def main(argv=None) -> int:
     nbytes = grads.numel * 2
     f = 2.0 * (world - 1) / world if world > 1 else 1.0
     rec = {"workload": "dp_grad_sync", "model": f"llama3-8b-shaped ({args.layers} layers)", "ranks": world,
-           "symmetric_buckets": args.symmetric, "bucket_algorithm": bucket_algo,
+           "symmetric_buckets": args.symmetric, "registered_buckets": args.register, "bucket_algorithm": bucket_algo,
            "grad_values": grads.numel, "bucket_mb": args.bucket_mb, "buckets": nb, "small_tensors": len(small),
            "ms_per_sync": round(t_ours, 3), "busbw_gbs": round(nbytes / t_ours / 1e6 * f, 1),
            "launches_per_sync": launches, "small_group_us": round(t_small * 1e3, 2), "check_rel_err": worst,
@@ -133,6 +135,7 @@ def main(argv=None) -> int:
     from originccl_b200.utils.results import ResultLog
     with ResultLog("dp_bench", args.out, enabled=rank == 0) as log:
         log(rec)
+    dp.close()
     comm.destroy()
     barrier()
     dist.destroy_process_group()

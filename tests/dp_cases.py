@@ -25,7 +25,7 @@ def run_dp_sync(rank: int, world: int, mode: str, bucket_bytes: int) -> Dict:
     comm = init_from_env(n_channels=2, timeout_ms=30000)
     model = TinyLlamaStack(hidden=hidden, ffn=3 * hidden, layers=2, seed=7)
     grads = GradBuckets(model.named_parameters(), bucket_bytes=bucket_bytes, small_bytes=1024)
-    dp = DataParallelSync(comm, grads)
+    dp = DataParallelSync(comm, grads, register=True)  # registration: a no-op for host memory
     if mode == "attach":
         dp.attach()
     g = torch.Generator().manual_seed(100 + rank)
@@ -44,5 +44,6 @@ def run_dp_sync(rank: int, world: int, mode: str, bucket_bytes: int) -> Dict:
         worst = max(worst, (p.grad - ref).abs().max().item())
         assert torch.allclose(p.grad, ref, rtol=1e-5, atol=1e-6), f"{n}: max diff {(p.grad - ref).abs().max()}"
     out = {"buckets": grads.num_buckets, "small": len(grads.small_idx), "worst": worst}
+    dp.close()
     comm.destroy()
     return out

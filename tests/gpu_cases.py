@@ -435,3 +435,63 @@ def run_graph(rank: int, world: int) -> Dict:
     del graph
     comm.destroy()
     return {"replays": 4, "host_launches_during_replays": host_launches}
+
+
+def run_registered(rank: int, world: int) -> Dict:
+    """Ordinary PyTorch CUDA tensors registered with the communicator (CUDA IPC): AllReduce
+    (out of place, in place, AVG, bf16 with a scale), AllGather, ReduceScatter and views of one
+    registered flat buffer at the same offsets on every rank (gradient buckets) run over peer
+    memory without staging; checked against the float64 oracle, with a sentinel after each
+    output. Below the size threshold the staged kernels run on the same buffers."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    used = set()
+    n = (3 << 20) // 4 + 8                   # 3 MiB of fp32, above the 1 MiB threshold
+    ins = [rank_input(r, n, "float32", seed=5) for r in range(world)]
+    x = ins[rank].cuda()
+    y = torch.full((n + 4,), 77.0, device="cuda")  # 16-byte sentinel tail
+    comm.register(x)
+    comm.register(y)
+    comm.all_reduce(x, ReduceOp.SUM, out=y[:n])
+    used.add(comm.last_algorithm)
+    _close(y[:n], oracle("sum", ins, world), "float32", "registered all_reduce")
+    assert bool((y[n:] == 77.0).all()), "registered all_reduce wrote past the output"
+    comm.all_reduce(x, ReduceOp.AVG)           # in place
+    _close(x, oracle("avg", ins, world), "float32", "registered all_reduce in place avg")
+    # AllGather into / ReduceScatter from registered buffers.
+    m = (1 << 20) // 4
+    blocks = [rank_input(r, m, "float32", seed=6) for r in range(world)]
+    gathered = torch.empty(world * m, device="cuda")
+    comm.register(gathered)
+    comm.all_gather(gathered, blocks[rank].cuda())
+    used.add(comm.last_algorithm)
+    _close(gathered, torch.cat(blocks), "float32", "registered all_gather")
+    full = [rank_input(r, world * m, "float32", seed=7) for r in range(world)]
+    rs_in = full[rank].cuda()
+    comm.register(rs_in)
+    shard = torch.empty(m, device="cuda")
+    comm.reduce_scatter(shard, rs_in, ReduceOp.MAX)
+    used.add(comm.last_algorithm)
+    _close(shard, oracle("max", full, world)[rank * m:(rank + 1) * m], "float32", "registered reduce_scatter max")
+    # bf16 buckets: views of one registered flat buffer, scaled mean as in gradient sync.
+    nb, per = 4, (1 << 20)
+    grads = [rank_input(r, nb * per, "bfloat16", seed=8) for r in range(world)]
+    flat = grads[rank].cuda()
+    comm.register(flat)
+    for b in range(nb):
+        comm.all_reduce(flat[b * per:(b + 1) * per], ReduceOp.SUM, scale=1.0 / world)
+        used.add(comm.last_algorithm)
+    _close(flat, (oracle("sum", grads, world) / world).to(torch.bfloat16), "bfloat16", "registered bf16 buckets")
+    # A small message on registered memory still takes the batched push kernel.
+    comm.all_reduce(flat[:256], ReduceOp.MAX)
+    small_algo = comm.last_algorithm
+    for t in (flat, rs_in, gathered, y, x):
+        comm.deregister(t)
+    comm.destroy()
+    return {"algorithms": sorted(used), "small_algorithm": small_algo}

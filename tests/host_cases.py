@@ -143,6 +143,10 @@ def run_contract(rank: int, world: int) -> Dict:
     assert np.all(y == world * (world + 1) / 2)
     # Reduce: a non-root may pass a null recv buffer
     assert lib.bcclReduce(h, p, null if rank != 0 else p, 8, 0, 0, 0, 0, 0, 0) == 0
+    # Buffer registration is a device feature; host communicators accept and ignore it.
+    with comm.registered(x, y):
+        comm.all_reduce(x, out=y)
+    assert np.all(y == world * (world + 1) / 2)
     comm.destroy()
     return {"rejected": rej}
 

@@ -143,3 +143,12 @@ def test_cuda_graph_replay_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_graph, timeout=300)
     assert all(r["host_launches_during_replays"] == 0 for r in res)
+
+
+@pytest.mark.multigpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="registered-buffer zero-copy kernels not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_registered_buffers_zero_copy_two_ranks():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_registered, timeout=300)
+    assert res[0]["algorithms"] == ["p2p_zero_copy"] and res[0]["small_algorithm"] == "oneshot"
