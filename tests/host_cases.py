@@ -174,7 +174,8 @@ def run_groups(rank: int, world: int) -> Dict:
 
 def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str = "") -> Dict:
     """Ring exchange in a group, FIFO for a repeated peer, a mixed 10-op group, typed messages
-    around the ring-buffer capacity, and the transport each pair uses."""
+    around the ring-buffer capacity, a 1 MiB-per-peer mesh with receives out of order, and the
+    transport each pair uses."""
     import os
     if executor:
         os.environ["BCCL_HOST_EXECUTOR"] = executor
@@ -215,6 +216,20 @@ def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str 
     for q in range(world):
         if q != rank:
             assert np.all(mesh_out[q] == 100 * q + rank), "mesh exchange"
+    # Full mesh of 256K int32 (1 MiB) per peer in one group, receives issued in the reverse of
+    # the send order (the reference's out-of-order source and mesh cases, test_p2p.cpp:63-78,
+    # 264-314).
+    big = 1 << 18
+    peers = [q for q in range(world) if q != rank]
+    big_in = {q: np.arange(big, dtype=np.int32) + 1000 * rank + q for q in peers}
+    big_out = {q: np.zeros(big, np.int32) for q in peers}
+    with comm.group():
+        for q in peers:
+            comm.send(big_in[q], q)
+        for q in reversed(peers):
+            comm.recv(big_out[q], q)
+    for q in peers:
+        assert np.array_equal(big_out[q], np.arange(big, dtype=np.int32) + 1000 * q + rank), "1 MiB mesh"
     kinds = {q: comm.p2p_transport(q) for q in range(world) if q != rank}
     ex = comm.host_executor
     comm.destroy()
