@@ -68,12 +68,32 @@ void ChannelSlice(size_t count, int n, int ch, size_t* e0, size_t* e1) {
 
 }  // namespace
 
+// Every rank as its own machine: all exchanges then go over TCP (BCCL_DISABLE_SHM).
+static MachineView SplitView(int rank, int world) {
+    MachineView v;
+    v.local_rank = 0;
+    v.local_size = 1;
+    v.local_ranks = {rank};
+    v.machine_index = rank;
+    v.machine_count = world;
+    for (int p = 0; p < world; ++p) {
+        v.machine_leaders.push_back(p);
+        v.machine_of.push_back(p);
+        v.local_index_of.push_back(0);
+        v.machine_ranks.push_back({p});
+    }
+    return v;
+}
+
 bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const std::vector<NodeInfo>& nodes,
                       const MachineView& view, int data_listen_fd) {
     rank_ = cfg.rank;
     listen_fd_ = data_listen_fd;
     world_ = cfg.world_size;
-    view_ = view;
+    // BCCL_DISABLE_SHM=1 (the reference's OCCL_DISABLE_SHM, src/communicator.cpp:47-60): ranks on
+    // one host talk over TCP as if each were a machine of its own. Only the engine's routing
+    // changes; the communicator's machine view stays the host's.
+    view_ = EnvFlag("BCCL_DISABLE_SHM") ? SplitView(cfg.rank, cfg.world_size) : view;
     timeout_ms_ = cfg.timeout_ms > 0 ? cfg.timeout_ms : static_cast<int>(EnvInt("BCCL_TIMEOUT_MS", 30000));
     const long ncores = sysconf(_SC_NPROCESSORS_ONLN);
     n_channels_ = cfg.n_channels > 0 ? cfg.n_channels : 4;

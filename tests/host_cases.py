@@ -324,3 +324,13 @@ def run_rank_dies(rank: int, world: int) -> Dict:
     elapsed = time.time() - t0
     assert failed, "AllReduce with a dead peer returned success"
     return {"elapsed": elapsed}
+
+
+def run_without_shm(rank: int, world: int, part: str) -> Dict:
+    """BCCL_DISABLE_SHM=1: the collective matrix ("matrix") or the P2P cases ("p2p") with every
+    exchange over TCP, while the communicator still reports one machine."""
+    import os
+    os.environ["BCCL_DISABLE_SHM"] = "1"
+    if part == "matrix":
+        return run_matrix(rank, world, [5, 40000], ["float32", "int64"])
+    return run_p2p(rank, world)

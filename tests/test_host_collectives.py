@@ -70,3 +70,10 @@ def test_four_logical_machines_leader_ring():
 def test_three_logical_machines_of_two_ranks():
     res = _mp.run(6, host_cases.run_matrix, [3, 1000, 131072 + 7], ["float32", "int64"], 2, 2, timeout=400)
     assert res[0]["machine_count"] == 3 and res[5]["local_ranks"] == [4, 5]
+
+
+def test_disable_shm_runs_everything_over_tcp():
+    res = _mp.run(4, host_cases.run_without_shm, "matrix", timeout=300)
+    assert res[0]["ran"] > 0 and res[0]["single"]  # the view stays one machine
+    res = _mp.run(4, host_cases.run_without_shm, "p2p", timeout=300)
+    assert set(res[0]["transports"].values()) == {"tcp"}
