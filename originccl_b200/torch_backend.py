@@ -9,7 +9,8 @@ Supported: all_reduce (SUM, AVG, MAX, MIN), broadcast, reduce, all_gather (list 
 forms), reduce_scatter (list and tensor forms), their coalesced forms (one group, i.e. one
 batched kernel for small tensors), send / recv and barrier — the reference's operation set.
 AllToAll, gather and scatter, which the reference does not have, raise ``NotImplementedError``.
-DistributedDataParallel runs on it unchanged.
+DistributedDataParallel runs on it unchanged; :class:`AllReduceHook` is a DDP communication hook
+that fuses the gradient mean into the AllReduce and registers large bucket buffers for zero-copy.
 """
 from __future__ import annotations
 
@@ -174,6 +175,56 @@ class BcclProcessGroup(dist.ProcessGroup):
 
     def scatter(self, *args, **kwargs):
         raise NotImplementedError("bccl: scatter is not provided")
+
+
+class AllReduceHook:
+    """DistributedDataParallel communication hook for the "bccl" backend::
+
+        hook = AllReduceHook()
+        ddp.register_comm_hook(dist.group.WORLD, hook)   # state: the bccl process group (or None)
+
+    Each gradient bucket is averaged by ONE AllReduce with the 1/world scale fused into the
+    kernel's store (DDP's default hook divides the bucket first, an extra pass over it). On CUDA,
+    bucket buffers of at least ``min_bytes`` are registered with the communicator the first time
+    they are seen, so their AllReduce reads and writes the peers' buffers directly (no staging).
+    Every rank sees the same buckets in the same order, which keeps registration collective; DDP
+    keeps its bucket buffers between iterations, so this happens once per buffer. ``close()``
+    deregisters them (collective)."""
+
+    def __init__(self, process_group: "BcclProcessGroup" = None, *, register: bool = True,
+                 min_bytes: int = 1 << 20) -> None:
+        self.process_group = process_group
+        self.register = register
+        self.min_bytes = min_bytes
+        self._registered: Dict[tuple, tuple] = {}  # (ptr, bytes) -> (communicator, tensor)
+        self.__name__ = self.__qualname__ = "bccl_allreduce_hook"  # DDP logs the hook's name
+
+    def _pg(self, state) -> "BcclProcessGroup":
+        for cand in (state, self.process_group, dist.distributed_c10d._get_default_group()):
+            if isinstance(cand, BcclProcessGroup):
+                return cand
+        raise TypeError("AllReduceHook needs the 'bccl' process group")
+
+    # No annotations: DDP compares them against the objects themselves, and this module's are
+    # strings (postponed evaluation).
+    def __call__(self, state, bucket):
+        t = bucket.buffer()
+        comm = self._pg(state)._comm(t)
+        nbytes = t.numel() * t.element_size()
+        if self.register and t.is_cuda and comm.world_size > 1 and nbytes >= self.min_bytes:
+            key = (t.data_ptr(), nbytes)
+            if key not in self._registered:
+                comm.register(t)
+                self._registered[key] = (comm, t)  # keeps the buffer alive while registered
+        comm.all_reduce(t, ReduceOp.SUM, scale=1.0 / comm.world_size)
+        fut: Future = Future()
+        fut.set_result(t)
+        return fut
+
+    def close(self) -> None:
+        for comm, t in self._registered.values():
+            comm.deregister(t)
+        self._registered.clear()
 
 
 def _create(store, rank: int, world_size: int, timeout) -> BcclProcessGroup:

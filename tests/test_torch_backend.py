@@ -15,8 +15,9 @@ def test_torch_collectives_on_bccl_backend(world):
     assert all(r["alltoall_rejected"] for r in res)
 
 
-def test_ddp_on_bccl_backend():
-    res = _mp.run(2, torch_backend_cases.run_ddp, timeout=240)
+@pytest.mark.parametrize("hook", [False, True])
+def test_ddp_on_bccl_backend(hook):
+    res = _mp.run(2, torch_backend_cases.run_ddp, hook, timeout=240)
     assert all(r["worst"] < 1e-6 for r in res)
 
 
@@ -28,5 +29,6 @@ def test_ddp_cuda_on_bccl_backend():
     import torch
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    res = _mp.run(2, torch_backend_cases.run_ddp_cuda, timeout=300)
-    assert all(r["worst"] < 1e-4 for r in res)
+    for hook in (False, True):
+        res = _mp.run(2, torch_backend_cases.run_ddp_cuda, hook, timeout=300)
+        assert all(r["worst"] < 1e-4 for r in res)

@@ -60,7 +60,7 @@ def run_collectives(rank: int, world: int) -> Dict:
     return {"alltoall_rejected": raised}
 
 
-def run_ddp(rank: int, world: int) -> Dict:
+def run_ddp(rank: int, world: int, hook: bool = False) -> Dict:
     import torch
     from torch.nn.parallel import DistributedDataParallel as DDP
     dist = _init(rank, world)
@@ -71,6 +71,9 @@ def run_ddp(rank: int, world: int) -> Dict:
 
     model = make()
     ddp = DDP(model, bucket_cap_mb=0.01)  # several buckets
+    if hook:
+        from originccl_b200.torch_backend import AllReduceHook
+        ddp.register_comm_hook(dist.group.WORLD, AllReduceHook())
     x = torch.randn(8, 16, generator=torch.Generator().manual_seed(10 + rank))
     ddp(x).pow(2).mean().backward()
     ref = None
@@ -85,8 +88,9 @@ def run_ddp(rank: int, world: int) -> Dict:
     return {"worst": worst}
 
 
-def run_ddp_cuda(rank: int, world: int) -> Dict:
-    """DDP on CUDA through the "bccl" backend (device communicator, current stream)."""
+def run_ddp_cuda(rank: int, world: int, hook: bool = False) -> Dict:
+    """DDP on CUDA through the "bccl" backend (device communicator, current stream); with
+    ``hook`` through AllReduceHook (fused mean; buckets of >= 64 KiB registered, zero-copy)."""
     import torch
     from torch.nn.parallel import DistributedDataParallel as DDP
     torch.cuda.set_device(rank % torch.cuda.device_count())
@@ -98,8 +102,16 @@ def run_ddp_cuda(rank: int, world: int) -> Dict:
 
     model = make()
     ddp = DDP(model, bucket_cap_mb=0.05)
+    h = None
+    if hook:
+        from originccl_b200.torch_backend import AllReduceHook
+        h = AllReduceHook(min_bytes=64 << 10)
+        ddp.register_comm_hook(dist.group.WORLD, h)
     g = torch.Generator(device="cuda").manual_seed(10 + rank)
-    ddp(torch.randn(32, 64, device="cuda", generator=g)).pow(2).mean().backward()
+    for _ in range(2 if hook else 1):  # the second step reuses the registered buckets
+        model.zero_grad(set_to_none=False)
+        ddp(torch.randn(32, 64, device="cuda", generator=torch.Generator(device="cuda").manual_seed(10 + rank))
+            ).pow(2).mean().backward()
     torch.cuda.synchronize()
     ref = None
     for r in range(world):
@@ -111,5 +123,7 @@ def run_ddp_cuda(rank: int, world: int) -> Dict:
     worst = max(((p.grad - r / world).abs().max() / (r / world).abs().max().clamp_min(1e-12)).item()
                 for p, r in zip(model.parameters(), ref))
     assert worst < 1e-4, worst
+    if h is not None:
+        h.close()
     dist.destroy_process_group()
     return {"worst": worst}
