@@ -38,6 +38,8 @@ struct P2pZcParams {
     float scale;
 };
 
+static_assert(sizeof(P2pZcParams) <= 32764, "kernel parameter limit");
+
 // Loads vectors [v0, v1) (16 bytes each, at byte offset src_off) from n sources, reduces them
 // and stores the result at dst_off into nd destinations. NS bounds n; U vectors per thread are
 // in flight (U * n loads): with every SM's 512 threads loading, that is megabytes in flight,

@@ -34,6 +34,9 @@ struct PushParams {
     WorkItem items[MAXI];
 };
 
+// Kernel parameters are limited to 32764 bytes (CUDA 12.1+ on sm_70 and later).
+static_assert(sizeof(PushParams<kPushMaxItems>) <= 32764, "push-engine work list exceeds the kernel parameter limit");
+
 template <int MAXI>
 __global__ void __launch_bounds__(512, 1) push_engine_kernel(const __grid_constant__ PushParams<MAXI> p) {
     push_engine_body(p.comm, p.items, p.nitems, p.nrounds, p.stream_bytes, p.slot_bytes);
