@@ -117,7 +117,9 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     const int L = view_.local_size;
     const size_t hdr = 4096;
     const size_t bar_bytes = AlignUp(sizeof(ShmBarrier) * static_cast<size_t>(n_channels_), 4096);
-    const size_t chan_bytes = static_cast<size_t>(world_ + 1) * slot_bytes_;
+    // Two buffer sets per channel (slots of every rank + a result area), used by alternate chunks.
+    const size_t set_bytes = static_cast<size_t>(world_ + 1) * slot_bytes_;
+    const size_t chan_bytes = 2 * set_bytes;
     const size_t ring_stride = sizeof(ShmRingCtrl) + AlignUp(ring_bytes_, 64);
     seg_bytes_ = hdr + bar_bytes + chan_bytes * static_cast<size_t>(n_channels_) +
                  ring_stride * static_cast<size_t>(L) * static_cast<size_t>(L);
@@ -163,8 +165,12 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     chans_.resize(n_channels_);
     for (int c = 0; c < n_channels_; ++c) {
         chans_[c].barrier = reinterpret_cast<ShmBarrier*>(base + hdr) + c;
-        chans_[c].slots = base + hdr + bar_bytes + chan_bytes * static_cast<size_t>(c);
-        chans_[c].result = chans_[c].slots + static_cast<size_t>(world_) * slot_bytes_;
+        for (int k = 0; k < 2; ++k) {
+            chans_[c].set_slots[k] = base + hdr + bar_bytes + chan_bytes * static_cast<size_t>(c) + set_bytes * k;
+            chans_[c].set_result[k] = chans_[c].set_slots[k] + static_cast<size_t>(world_) * slot_bytes_;
+        }
+        chans_[c].slots = chans_[c].set_slots[0];
+        chans_[c].result = chans_[c].set_result[0];
     }
     char* rings = base + hdr + bar_bytes + chan_bytes * static_cast<size_t>(n_channels_);
     p2p_send_.resize(world_);
@@ -314,15 +320,17 @@ void HostEngine::WorkerLoop(int ch) {
     }
 }
 
-bool HostEngine::RunOnChannels(const std::function<bool(int)>& fn) {
+bool HostEngine::RunOnChannels(const std::function<bool(int)>& fn, int inline_ch) {
     {
         std::lock_guard<std::mutex> lk(mu_);
-        job_ = fn;
+        // Channel inline_ch runs on the calling thread; its worker only reports in.
+        job_ = [&fn, inline_ch](int ch) { return ch == inline_ch ? true : fn(ch); };
         job_ok_.store(true);
         job_pending_.store(n_channels_);
         job_seq_.fetch_add(1, std::memory_order_release);
     }
     cv_job_.notify_all();
+    if (inline_ch >= 0 && !fn(inline_ch)) job_ok_.store(false);
     if (spin_) {
         const auto until = Clock::now() + std::chrono::microseconds(kSpinUs);
         for (uint32_t i = 0; job_pending_.load(std::memory_order_acquire) != 0; ++i) {
@@ -474,6 +482,7 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
     const char* src = static_cast<const char*>(t.send_buf);
     char* dst = static_cast<char*>(t.recv_buf);
     for (size_t off = e0; off < e1; off += chunk) {
+        NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         memcpy(Slot(ch, rank_), src + off * es, clen * es);
         if (!Barrier(ch)) return false;
@@ -520,7 +529,6 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
         }
         if (M > 1 && !Barrier(ch)) return false;
         if (!reduce_only || rank_ == t.root) memcpy(dst + off * es, C.result, clen * es);
-        if (!Barrier(ch)) return false;
     }
     return true;
 }
@@ -534,6 +542,7 @@ bool HostEngine::BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1)
     char* buf = static_cast<char*>(t.recv_buf);
     const char* in = static_cast<const char*>(t.send_buf ? t.send_buf : t.recv_buf);
     for (size_t off = e0; off < e1; off += chunk) {
+        NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         if (rank_ == t.root) memcpy(C.result, in + off * es, clen * es);
         if (!Barrier(ch)) return false;
@@ -562,7 +571,6 @@ bool HostEngine::BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1)
         }
         if (M > 1 && !Barrier(ch)) return false;
         if (rank_ != t.root || buf != in) memcpy(buf + off * es, C.result, clen * es);
-        if (!Barrier(ch)) return false;
     }
     return true;
 }
@@ -574,6 +582,7 @@ bool HostEngine::AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1)
     const char* src = static_cast<const char*>(t.send_buf);
     char* dst = static_cast<char*>(t.recv_buf);
     for (size_t off = e0; off < e1; off += chunk) {
+        NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         memcpy(Slot(ch, rank_), src + off * es, clen * es);
         if (!Barrier(ch)) return false;
@@ -623,7 +632,6 @@ bool HostEngine::AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1)
             const char* in = (q == rank_) ? src + off * es : Slot(ch, q);
             if (out != in) memcpy(out, in, clen * es);
         }
-        if (!Barrier(ch)) return false;
     }
     return true;
 }
@@ -636,6 +644,7 @@ bool HostEngine::ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t
     const char* src = static_cast<const char*>(t.send_buf);
     char* dst = static_cast<char*>(t.recv_buf);
     for (size_t off = e0; off < e1; off += chunk) {
+        NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         const size_t sub = clen * es;
         // My slot holds [world][clen]: sub-chunk s is my contribution to rank s's output.
@@ -680,7 +689,6 @@ bool HostEngine::ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t
         }
         if (M > 1 && !Barrier(ch)) return false;
         memcpy(dst + off * es, C.result + static_cast<size_t>(rank_) * sub, sub);
-        if (!Barrier(ch)) return false;
     }
     return true;
 }
@@ -808,11 +816,25 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
     }
     if (!work.empty()) {
         const std::vector<std::vector<WorkUnit>> plan = PlanChannels(work);
-        if (!RunOnChannels([this, &plan](int ch) {
-                for (const WorkUnit& u : plan[static_cast<size_t>(ch)])
-                    if (!RunSlice(ch, *u.task, u.e0, u.e1)) return false;
-                return true;
-            })) {
+        auto run = [this, &plan](int ch) {
+            for (const WorkUnit& u : plan[static_cast<size_t>(ch)])
+                if (!RunSlice(ch, *u.task, u.e0, u.e1)) return false;
+            return true;
+        };
+        int busy = 0, last = -1;
+        for (int ch = 0; ch < n_channels_; ++ch) {
+            if (!plan[static_cast<size_t>(ch)].empty()) {
+                ++busy;
+                last = ch;
+            }
+        }
+        // One busy channel (a small collective, or a small group): run it on this thread, with
+        // no hand-off to a worker. Otherwise the workers run the others while this thread runs
+        // the last one. The per-channel barriers are in shared memory, so which thread of a rank
+        // runs a channel does not matter to the other ranks.
+        if (busy == 1) {
+            if (!run(last)) return false;
+        } else if (!RunOnChannels(run, last)) {
             return false;
         }
     }

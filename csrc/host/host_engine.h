@@ -68,10 +68,17 @@ public:
     const char* executor_name() const { return epoll_ ? "epoll" : "polling"; }
 
 private:
+    // Chunks alternate between two buffer sets. A chunk's buffers are last read within that
+    // chunk, and every chunk crosses at least one barrier after its first write, so when a rank
+    // starts chunk k (having passed chunk k-1's first barrier) every rank has finished chunk
+    // k-2, the previous user of the same set: no barrier is needed at the end of a chunk.
     struct Channel {
         ShmBarrier* barrier = nullptr;
-        char* slots = nullptr;   // [world][slot_bytes]
-        char* result = nullptr;  // [slot_bytes]
+        char* slots = nullptr;   // current set: [world][slot_bytes]
+        char* result = nullptr;  // current set: [slot_bytes]
+        char* set_slots[2] = {nullptr, nullptr};
+        char* set_result[2] = {nullptr, nullptr};
+        unsigned chunks = 0;     // chunks started on this channel (same count on every rank)
         std::vector<std::unique_ptr<TcpTransport>> leader_links;  // per machine (leaders only)
         std::vector<char> scratch;                                // leader-private receive space
     };
@@ -95,9 +102,18 @@ private:
                         const std::vector<size_t>& send_bytes, const std::vector<void*>& recv,
                         const std::vector<size_t>& recv_bytes);
     bool RunP2p(const std::vector<CollTask>& tasks);
-    bool RunOnChannels(const std::function<bool(int)>& fn);
+    // Runs fn(ch) for every channel on the channel threads and waits; channel inline_ch (if >= 0)
+    // runs on the calling thread instead.
+    bool RunOnChannels(const std::function<bool(int)>& fn, int inline_ch = -1);
     void WorkerLoop(int ch);
     char* Slot(int ch, int rank) { return chans_[ch].slots + static_cast<size_t>(rank) * slot_bytes_; }
+    // Switches channel ch to the other buffer set; called at the start of every chunk.
+    void NextBuffers(int ch) {
+        Channel& c = chans_[ch];
+        const unsigned k = c.chunks++ & 1u;
+        c.slots = c.set_slots[k];
+        c.result = c.set_result[k];
+    }
 
     int rank_ = 0;
     int world_ = 1;
