@@ -484,13 +484,21 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
     for (size_t off = e0; off < e1; off += chunk) {
         NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
-        memcpy(Slot(ch, rank_), src + off * es, clen * es);
-        if (!Barrier(ch)) return false;
         const size_t share = (clen + L - 1) / L;
         const size_t s0 = std::min(clen, share * li), s1 = std::min(clen, s0 + share);
+        // Every share but this rank's own goes to the slot; this rank reduces its own share
+        // reading its input in place.
+        char* mine = Slot(ch, rank_);
+        if (s0 > 0) memcpy(mine, src + off * es, s0 * es);
+        if (clen > s1) memcpy(mine + s1 * es, src + (off + s1) * es, (clen - s1) * es);
+        if (!Barrier(ch)) return false;
         if (s1 > s0) {
             const void* srcs[64];
-            for (int i = 0; i < L; ++i) srcs[i] = Slot(ch, view_.local_ranks[i]) + s0 * es;
+            for (int i = 0; i < L; ++i) {
+                const int q = view_.local_ranks[i];
+                srcs[i] = q == rank_ ? static_cast<const void*>(src + (off + s0) * es)
+                                     : static_cast<const void*>(Slot(ch, q) + s0 * es);
+            }
             hostmath::Reduce(t.dtype, t.op, C.result + s0 * es, srcs, L, s1 - s0, world_, t.scale, M == 1);
         }
         if (!Barrier(ch)) return false;
