@@ -81,7 +81,7 @@ int DefaultCtas(Algo algo, size_t bytes) {
 
 }  // namespace
 
-Planner::Planner() : table_(DefaultTable()) {
+Planner::Planner() : table_(DefaultTable()), env_max_ctas_(EnvInt("BCCL_MAX_CTAS", 0)) {
     std::string path = EnvStr("BCCL_TUNING_FILE", "");
     if (!path.empty() && !LoadTuningFile(path)) {
         LOG_WARN("planner: could not load tuning file %s, keeping the built-in table", path.c_str());
@@ -240,8 +240,7 @@ AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_
         algo = Algo::kOneShot;
     }
     if (ctas <= 0) ctas = DefaultCtas(algo, bytes);
-    long env_max = EnvInt("BCCL_MAX_CTAS", 0);
-    if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
+    if (env_max_ctas_ > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max_ctas_));
     if (max_ctas > 0) ctas = std::min(ctas, max_ctas);
     c.algo = algo;
     c.ctas = std::max(1, ctas);

@@ -59,6 +59,7 @@ public:
 
 private:
     std::vector<TuningRow> table_;
+    long env_max_ctas_ = 0;  // BCCL_MAX_CTAS, read at construction
 };
 
 }  // namespace bccl

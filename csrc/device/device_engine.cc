@@ -25,8 +25,6 @@ namespace {
         }                                                                                \
     } while (0)
 
-// Staging ring depth of the pipelined kernels (BCCL_PIPE_SLOTS); every rank must agree.
-int PipeSlots() { return static_cast<int>(std::max<long>(3, std::min<long>(16, EnvInt("BCCL_PIPE_SLOTS", 3)))); }
 
 size_t RoundDown(size_t x, size_t a) { return x / a * a; }
 size_t RoundUp(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -90,6 +88,16 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     dc_.abort = abort_dev;
     dc_.timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
     dc_.spin_wait = EnvInt("BCCL_SPIN_WAIT", 0) != 0 ? 1 : 0;
+    // Knobs of the per-call path, read once here (a getenv per call costs microseconds of a
+    // small collective's latency). Every rank must agree on the pipeline ones.
+    knob_max_ctas_ = EnvInt("BCCL_MAX_CTAS", 0);
+    knob_zero_copy_ = EnvInt("BCCL_ZERO_COPY", 1) != 0;
+    knob_p2p_zc_min_ = static_cast<size_t>(std::max<long>(16, EnvInt("BCCL_P2P_ZC_MIN_BYTES", 1 << 20)));
+    knob_pipe_slots_ = static_cast<int>(std::max<long>(3, std::min<long>(16, EnvInt("BCCL_PIPE_SLOTS", 3))));
+    knob_pipe_rounds_ = EnvInt("BCCL_PIPE_ROUNDS", 0);
+    knob_pipe_min_chunk_ = EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20);
+    knob_pipe_debug_ = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
+    knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     dc_.data_bytes = data_bytes_;
     const long trace_cap = EnvInt("BCCL_TRACE", 0);
     if (trace_cap > 0) {
@@ -558,7 +566,7 @@ bool DeviceEngine::FlushBatch(std::vector<WorkItem>* batch, unsigned long long* 
         unsigned long long bytes = last.stream_off + RoundUp(last.count * DataTypeSize(static_cast<DataType>(last.dtype)), 16);
         int ctas = PushCtas(std::min<unsigned long long>(bytes, slot), num_sms_);
         if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
-        long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+        const long env_max = knob_max_ctas_;
         if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
         dc_.kernel_serial = ++kernel_serial_;
         cudaError_t e = LaunchPushEngine(dc_, part.data(), static_cast<int>(n), bytes, slot, ctas, stream);
@@ -580,20 +588,20 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const int dt = static_cast<int>(t.dtype), op = static_cast<int>(t.op);
     const size_t bytes = t.count * DataTypeSize(t.dtype);
     const unsigned long long q = 16ull * nranks_;
-    const int slots = PipeSlots();
+    const int slots = knob_pipe_slots_;
     // Rounds of at least `min_chunk` bytes (each CTA then moves >= ~100 KB between fences),
     // about `rounds` of them so the software pipeline has something to overlap.
     // Two rounds up to 64 MiB, four above (measured on 2 and 8 x B200: fewer, larger rounds win
     // until the pipeline's fill and drain dominate).
     const unsigned long long rounds = static_cast<unsigned long long>(
-        std::max<long>(1, EnvInt("BCCL_PIPE_ROUNDS", bytes <= (64u << 20) ? 2 : 4)));
-    const unsigned long long min_chunk = static_cast<unsigned long long>(EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20));
+        std::max<long>(1, knob_pipe_rounds_ > 0 ? knob_pipe_rounds_ : (bytes <= (64u << 20) ? 2 : 4)));
+    const unsigned long long min_chunk = static_cast<unsigned long long>(knob_pipe_min_chunk_);
     auto pick_chunk = [&](unsigned long long cap) {
         unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, q);
         want = std::max<unsigned long long>(want, RoundUp(min_chunk, q));
         return std::max<unsigned long long>(q, std::min<unsigned long long>(want, RoundDown(cap, q)));
     };
-    const int debug = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
+    const int debug = knob_pipe_debug_;
     int ctas = c.ctas;
     dc_.kernel_serial = ++kernel_serial_;
     if (c.algo == Algo::kRing) {
@@ -619,7 +627,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         // reduction step per round instead of two; from 32 MiB the two-shot schedule measured
         // faster (its rounds move half as much per phase).
         int kind = (nranks_ == 2 && bytes < (32u << 20)) ? kPipeOneShot : kPipeTwoShot;
-        const long forced_kind = EnvInt("BCCL_PIPE_KIND", -1);
+        const long forced_kind = knob_pipe_kind_;
         if (forced_kind == kPipeOneShot || forced_kind == kPipeTwoShot) kind = static_cast<int>(forced_kind);
         unsigned long long slot, chunk;
         if (kind == kPipeOneShot) {
@@ -672,7 +680,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         bool zc = false;
         const void* zc_send = nullptr;
         void* zc_recv = nullptr;
-        if (nranks_ > 1 && (bytes % 16) == 0 && nvls_.mc != nullptr && EnvInt("BCCL_ZERO_COPY", 1) != 0) {
+        if (nranks_ > 1 && (bytes % 16) == 0 && nvls_.mc != nullptr && knob_zero_copy_) {
             if (t.func == CollFunc::AllReduce && c.algo == Algo::kNvls && UserMulticast(t.send_buf, bytes, &send_mc) &&
                 UserMulticast(t.recv_buf, bytes, &recv_mc)) {
                 zc = true;
@@ -695,9 +703,8 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         char* in_peers[kMaxRanks] = {};
         char* out_peers[kMaxRanks] = {};
         bool p2p_zc = false;
-        if (!zc && nranks_ > 1 && (bytes % 16) == 0 && EnvInt("BCCL_ZERO_COPY", 1) != 0 &&
-            (t.func == CollFunc::AllReduce ? bytes : all_bytes) >=
-                static_cast<size_t>(EnvInt("BCCL_P2P_ZC_MIN_BYTES", 1 << 20))) {
+        if (!zc && nranks_ > 1 && (bytes % 16) == 0 && knob_zero_copy_ && (!reg_bufs_.empty() || !user_bufs_.empty()) &&
+            (t.func == CollFunc::AllReduce ? bytes : all_bytes) >= knob_p2p_zc_min_) {
             if (t.func == CollFunc::AllReduce) {
                 p2p_zc = PeerPointers(t.send_buf, bytes, in_peers) && PeerPointers(t.recv_buf, bytes, out_peers);
             } else if (t.func == CollFunc::AllGather) {
@@ -714,7 +721,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
             int ctas = static_cast<int>(std::min<size_t>(std::max<size_t>(moved / (32u << 10), 8),
                                                          static_cast<size_t>(num_sms_)));
             if (max_ctas_ > 0) ctas = std::min(ctas, max_ctas_);
-            long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+            const long env_max = knob_max_ctas_;
             if (env_max > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max));
             dc_.kernel_serial = ++kernel_serial_;
             cudaError_t e = LaunchP2pZeroCopy(dc_, static_cast<int>(t.func), in_peers, out_peers, t.count,
@@ -752,7 +759,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
                                                          static_cast<size_t>(num_sms_)));
             c.ctas = std::min(want, kMaxCtas);
             if (max_ctas_ > 0) c.ctas = std::min(c.ctas, max_ctas_);
-            long env_max = EnvInt("BCCL_MAX_CTAS", 0);
+            const long env_max = knob_max_ctas_;
             if (env_max > 0) c.ctas = std::min<int>(c.ctas, static_cast<int>(env_max));
         }
         if (nranks_ == 1 || c.algo == Algo::kOneShot || (c.algo == Algo::kRing && !ring)) {

@@ -96,6 +96,15 @@ private:
     int max_ctas_ = 0;
     int num_sms_ = 148;
     Algo forced_ = Algo::kAuto;
+    // Environment knobs of the per-call path, read at Init.
+    long knob_max_ctas_ = 0;
+    bool knob_zero_copy_ = true;
+    size_t knob_p2p_zc_min_ = 1u << 20;
+    int knob_pipe_slots_ = 3;
+    long knob_pipe_rounds_ = 0;  // 0: by size
+    long knob_pipe_min_chunk_ = 4 << 20;
+    int knob_pipe_debug_ = 0;
+    long knob_pipe_kind_ = -1;
     const Planner* planner_ = nullptr;
     Bootstrap* bs_ = nullptr;
     SymmetricMemory sm_;
