@@ -289,6 +289,7 @@ int bcclTpGemmReduceScatter(bcclComm_t comm, const void* h, const void* w, void*
 }
 
 int bcclGemmUsesPair(void) { return bccl::GemmUsesPair() ? 1 : 0; }
+int bcclGemmTileWidth(int m, int n) { return bccl::GemmTileWidth(m, n); }
 
 int bcclGemmCheckError(void) {
     int* err = GemmErrWord();

@@ -106,6 +106,8 @@ int bcclGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int
 int bcclGemmCheckError(void);
 /* 1 when the GEMMs use 2-SM (cta_group::2) 256x256 tiles, 0 for 1-SM 128x256 tiles. */
 int bcclGemmUsesPair(void);
+/* Columns of C per tile for an m x n GEMM (256, or 224 with BCCL_GEMM_BN=224|auto on 2-SM tiles). */
+int bcclGemmTileWidth(int m, int n);
 
 /* Fused tensor-parallel GEMMs on a device communicator (bf16, one kernel each):
  *   bcclTpAllGatherGemm: y[nranks*ms, n] = act(AllGather(x[ms, k]) * w[n, k]^T)

@@ -38,6 +38,9 @@ struct TpArgs {
 // pitch) and A/B 16-byte aligned; M, N and K need not be multiples of the tile sizes.
 // True when the GEMMs run on 2-SM (cta_group::2) 256x256 tiles instead of 1-SM 128x256 tiles.
 bool GemmUsesPair();
+// Tile width (columns of C per tile) the GEMMs use for an M x N product: 256, or 224 for 2-SM
+// tiles when BCCL_GEMM_BN=224 (or =auto and narrower tiles fill the last wave better).
+int GemmTileWidth(int M, int N);
 
 cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, int* err,
                            int max_ctas, cudaStream_t stream);

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 
 #include "kernels/gemm.h"
 #include "kernels/sm100.cuh"
@@ -104,7 +105,8 @@ __device__ __forceinline__ int rs_row_block(int i, const TpArgs& tp, int block_r
 }
 
 // Communication warps of the fused modes (warps 6-9): AllGather pushes / ReduceScatter sums.
-template <int MODE>
+// TBN: the GEMM's tile width (the ReduceScatter tiles this rank owns are TBN columns wide).
+template <int MODE, int TBN = BN>
 __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile int* s_abort, volatile int* s_comm_stop) {
     auto fail = [&]() {
         *s_abort = 1;
@@ -152,7 +154,7 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
                 asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
                 if (*s_comm_stop) break;
                 const int lrb = t / num_n, nb = t % num_n;
-                const int ncols = min(BN, g.N - nb * BN);
+                const int ncols = min(TBN, g.N - nb * TBN);
                 // 8 bf16 per vector; rows x ncols of the tile. kU vectors per thread per step, all
                 // N partials of all kU loaded before any is summed: enough loads in flight to
                 // cover memory latency with only four warps.
@@ -172,7 +174,7 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
                         const int rr = e / vec_per_row, cc = (e % vec_per_row) * 8;
                         const int lrow = lrb * BM + rr;
                         live[u] = e < total && lrow < g.tp.ms;
-                        off[u] = (size_t)lrow * g.N + nb * BN + cc;
+                        off[u] = (size_t)lrow * g.N + nb * TBN + cc;
 #pragma unroll
                         for (int q = 0; q < kMaxRanks; ++q) {
                             if (live[u] && q < g.tp.nranks)
@@ -426,14 +428,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_bf16_kernel(const __grid_con
 // 128 rows x 256 columns of the accumulator, so the epilogue is the same as the 1-SM kernel.
 // Per FLOP this moves a third less data from L2 into shared memory than 128x256 tiles. No load
 // uses cluster multicast.
+//
+// PBN, the tile width, is 256 or 224. Narrower tiles exist for wave quantisation: with 74 CTA
+// pairs, N = 3584 (a TP=8 shard of a 28672-wide FFN) gives 14 columns of 256-wide tiles, e.g.
+// 448 tiles = 6.05 waves for M = 8192, so the seventh wave is nearly empty; 224-wide tiles make
+// 512 tiles = 6.9 waves. Each CTA holds PBN/2 rows of B (a multiple of the 8-row swizzle atom).
 constexpr int PSTAGES = 6;
-constexpr int kPStageBytes = 2 * (BM * BK * 2);  // 16 KiB of A + 16 KiB of B per CTA
-constexpr int kPSmemBytes = PSTAGES * kPStageBytes + 1024 + 256;
+template <int PBN>
+constexpr int PStageBytes() { return BM * BK * 2 + (PBN / 2) * BK * 2; }  // A rows + this CTA's half of B
+template <int PBN>
+constexpr int PSmemBytes() { return PSTAGES * PStageBytes<PBN>() + 1024 + 256; }
+static_assert(PStageBytes<224>() % 1024 == 0 && PStageBytes<256>() % 1024 == 0, "stages must keep 1 KiB alignment");
+static_assert(PSmemBytes<256>() <= 227 * 1024, "shared memory");
 
-template <int MODE>
+template <int MODE, int PBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmG, const __grid_constant__ Args g) {
+    static_assert(PBN % 32 == 0 && PBN <= 256 && (PBN / 2) % 8 == 0, "tile width");
+    constexpr int kPStageBytes = PStageBytes<PBN>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PSTAGES * kPStageBytes);
@@ -475,7 +488,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int PM = 2 * BM;  // rows per pair tile
-    const int num_m = (g.M + PM - 1) / PM, num_n = (g.N + BN - 1) / BN;
+    const int num_m = (g.M + PM - 1) / PM, num_n = (g.N + PBN - 1) / PBN;
     const int tiles = num_m * num_n;
     const int kblocks = (g.K + BK - 1) / BK;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -494,7 +507,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t kb = 0;
             for (int tile = pair; tile < tiles && !*s_abort; tile += npairs) {
                 const int rb = tile_rb(tile);
-                const int n0 = (tile % num_n) * BN + static_cast<int>(cta) * BM;  // this CTA's half of N
+                const int n0 = (tile % num_n) * PBN + static_cast<int>(cta) * (PBN / 2);  // this CTA's half of N
                 const CUtensorMap* amap = &tmA;
                 int arow = rb * PM + static_cast<int>(cta) * BM;
                 if (MODE == kModeAllGather) {
@@ -535,7 +548,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
-            const uint32_t idesc = idesc_bf16_f32(2 * BM, BN);
+            const uint32_t idesc = idesc_bf16_f32(2 * BM, PBN);
             uint32_t kb = 0, local = 0;
             for (int tile = pair; tile < tiles && !*s_abort; tile += npairs, ++local) {
                 const int a = local & 1;
@@ -545,7 +558,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(a * BN);
+                const uint32_t d = tmem_base + static_cast<uint32_t>(a * PBN);
                 bool ok = true;
                 for (int k = 0; k < kblocks; ++k, ++kb) {
                     const int s = kb % PSTAGES;
@@ -589,7 +602,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int rb = tile_rb(tile);
             const int rb128 = rb * 2 + static_cast<int>(cta);
-            const int n0 = (tile % num_n) * BN;
+            const int n0 = (tile % num_n) * PBN;
             const int row = rb128 * BM + row_in_cta;
             __nv_bfloat16* crow = g.C + static_cast<size_t>(row) * g.ldc;
             int owner = 0;
@@ -603,10 +616,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = 0; c < PBN; c += 32) {
                 __syncwarp();
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * BN + c),
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * PBN + c),
                                    v);
                 tmem_ld_wait();
                 const int col = n0 + c;
@@ -640,7 +653,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        comm_warps<MODE>(g, num_n, s_abort, s_comm_stop);
+        comm_warps<MODE, PBN>(g, num_n, s_abort, s_comm_stop);
     }
     __syncthreads();
     cluster_sync();  // the peer's shared memory and TMEM stay valid until both CTAs are done
@@ -666,24 +679,50 @@ bool MakeMap(CUtensorMap* map, const void* base, int rows, int cols, int box_row
 
 template <int MODE>
 cudaError_t LaunchMode(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tg, const Args& g, int grid,
-                       bool pair, cudaStream_t stream) {
-    static bool attr_set[2][64] = {};
+                       bool pair, int pbn, cudaStream_t stream) {
+    static bool attr_set[3][64] = {};
+    const int which = !pair ? 0 : (pbn == 224 ? 2 : 1);
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[pair][dev]) {
-        cudaError_t e = pair ? cudaFuncSetAttribute(gemm_bf16_pair_kernel<MODE>,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes)
-                             : cudaFuncSetAttribute(gemm_bf16_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    kSmemBytes);
+    if (dev >= 0 && dev < 64 && !attr_set[which][dev]) {
+        cudaError_t e = which == 0 ? cudaFuncSetAttribute(gemm_bf16_kernel<MODE>,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
+                        : which == 1 ? cudaFuncSetAttribute(gemm_bf16_pair_kernel<MODE, 256>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, PSmemBytes<256>())
+                                     : cudaFuncSetAttribute(gemm_bf16_pair_kernel<MODE, 224>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, PSmemBytes<224>());
         if (e != cudaSuccess) return e;
-        attr_set[pair][dev] = true;
+        attr_set[which][dev] = true;
     }
-    if (pair) {
-        gemm_bf16_pair_kernel<MODE><<<grid & ~1, kThreads, kPSmemBytes, stream>>>(ta, tb, tg, g);
+    if (which == 1) {
+        gemm_bf16_pair_kernel<MODE, 256><<<grid & ~1, kThreads, PSmemBytes<256>(), stream>>>(ta, tb, tg, g);
+    } else if (which == 2) {
+        gemm_bf16_pair_kernel<MODE, 224><<<grid & ~1, kThreads, PSmemBytes<224>(), stream>>>(ta, tb, tg, g);
     } else {
         gemm_bf16_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, tg, g);
     }
     return cudaGetLastError();
+}
+
+// Tile width of the 2-SM kernel: BCCL_GEMM_BN=256 or 224 forces one; "auto" picks the one with
+// the smaller ceil(tiles / pairs) * width (waves times the work of a tile; ties keep 256).
+// The default is 256 until the 224-wide kernel has been measured on a B200.
+int ChoosePairBN(int M, int N, int pairs) {
+    const char* v = std::getenv("BCCL_GEMM_BN");
+    if (v != nullptr && std::strcmp(v, "224") == 0) return 224;
+    if (v == nullptr || std::strcmp(v, "auto") != 0) return 256;
+    const long rows = (M + 2 * BM - 1) / (2 * BM);
+    long best_cost = -1;
+    int best = 256;
+    for (int bn : {256, 224}) {
+        const long tiles = rows * ((N + bn - 1) / bn);
+        const long cost = (tiles + pairs - 1) / pairs * bn;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 // BCCL_GEMM_PAIR=1 forces the 2-SM kernel, =0 the 1-SM kernel; otherwise kPairDefault decides.
@@ -706,6 +745,8 @@ int NumSms() {
 
 bool GemmUsesPair() { return gemm::UsePair(); }
 
+int GemmTileWidth(int M, int N) { return gemm::UsePair() ? gemm::ChoosePairBN(M, N, gemm::NumSms() / 2) : gemm::BN; }
+
 cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, int K, int ldc, int act, int* err,
                            int max_ctas, cudaStream_t stream) {
     using namespace gemm;
@@ -714,14 +755,15 @@ cudaError_t LaunchGemmBf16(const void* A, const void* B, void* C, int M, int N, 
         return cudaErrorInvalidValue;
     }
     CUtensorMap ta, tb;
-    if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, UsePair() ? BM : BN)) return cudaErrorInvalidValue;
     const bool pair = UsePair();
-    const int tiles = ((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM)) * ((N + BN - 1) / BN);
+    const int pbn = pair ? ChoosePairBN(M, N, (max_ctas > 0 ? std::min(max_ctas, NumSms()) : NumSms()) / 2) : BN;
+    if (!MakeMap(&ta, A, M, K, BM) || !MakeMap(&tb, B, N, K, pair ? pbn / 2 : BN)) return cudaErrorInvalidValue;
+    const int tiles = ((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM)) * ((N + pbn - 1) / pbn);
     int grid = std::min(pair ? 2 * tiles : tiles, NumSms());
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
     if (pair && grid < 2) grid = 2;
     Args g{static_cast<__nv_bfloat16*>(C), M, N, K, ldc, act, err, TpArgs{}};
-    return LaunchMode<kModePlain>(ta, tb, tb, g, grid, pair, stream);
+    return LaunchMode<kModePlain>(ta, tb, tb, g, grid, pair, pbn, stream);
 }
 
 cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, const void* B, void* C, int M, int N,
@@ -738,15 +780,17 @@ cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, 
     t.contributors = grid;
     Args g{static_cast<__nv_bfloat16*>(C), M, N, K, N, act, err, t};
     if (mode == kModeAllGather) {
-        if (!MakeMap(&ta, A_local, tp.ms, K, BM) || !MakeMap(&tb, B, N, K, pair ? BM : BN) ||
+        const int pbn = pair ? ChoosePairBN(M, N, grid / 2) : BN;
+        if (!MakeMap(&ta, A_local, tp.ms, K, BM) || !MakeMap(&tb, B, N, K, pair ? pbn / 2 : BN) ||
             !MakeMap(&tg, A_gathered, M, K, BM)) {
             return cudaErrorInvalidValue;
         }
-        return LaunchMode<kModeAllGather>(ta, tb, tg, g, grid, pair, stream);
+        return LaunchMode<kModeAllGather>(ta, tb, tg, g, grid, pair, pbn, stream);
     }
     if (mode == kModeReduceScatter) {
+        // 256-wide tiles only: the owners' tile counters are laid out for them.
         if (!MakeMap(&ta, A_local, M, K, BM) || !MakeMap(&tb, B, N, K, pair ? BM : BN)) return cudaErrorInvalidValue;
-        return LaunchMode<kModeReduceScatter>(ta, tb, ta, g, grid, pair, stream);
+        return LaunchMode<kModeReduceScatter>(ta, tb, ta, g, grid, pair, 256, stream);
     }
     return cudaErrorInvalidValue;
 }

@@ -88,6 +88,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclGemmBf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp]),
         "bcclGemmCheckError": (c_int, []),
         "bcclGemmUsesPair": (c_int, []),
+        "bcclGemmTileWidth": (c_int, [c_int, c_int]),
         "bcclCommAbort": (c_int, [vp]),
         "bcclTpAllGatherGemm": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, c_int, up, c_int]),
         "bcclTpGemmReduceScatter": (c_int, [vp, vp, vp, vp, c_int, c_int, c_int, up, c_int]),

@@ -41,9 +41,13 @@ def gemm(a, w, activation: Optional[str] = None, out=None):
     return out
 
 
-def kernel_name(m: int = 0) -> str:
-    """Which kernel the GEMMs use: ``"pair_256x256"`` (2-SM, cta_group::2) or ``"single_128x256"``."""
-    return "pair_256x256" if _native.lib().bcclGemmUsesPair() else "single_128x256"
+def kernel_name(m: int = 0, n: int = 0) -> str:
+    """Which kernel an m x n GEMM uses: ``"pair_256x256"`` / ``"pair_256x224"`` (2-SM,
+    cta_group::2) or ``"single_128x256"``."""
+    lib = _native.lib()
+    if not lib.bcclGemmUsesPair():
+        return "single_128x256"
+    return f"pair_256x{lib.bcclGemmTileWidth(int(m), int(n))}"
 
 
 def check_error() -> int:

@@ -64,7 +64,7 @@ def main(argv=None) -> int:
         ours = _time(lambda: gemm.gemm(a, w, act, out=y), args.iters)
         cub = _time(lambda: torch.matmul(a, w.t()), args.iters)
         fl = 2.0 * m * n * k
-        log({"shape": spec, "kernel": gemm.kernel_name(m), "ours_ms": round(ours, 4),
+        log({"shape": spec, "kernel": gemm.kernel_name(m, n), "ours_ms": round(ours, 4),
              "ours_tflops": round(fl / ours / 1e9, 1), "cublas_ms": round(cub, 4),
              "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": round(err, 5), "ok": ok})
     log.close()

@@ -98,7 +98,7 @@ def main(argv=None) -> None:
              "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
              "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
              "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
-             "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(),
+             "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(args.tokens, args.ffn // world),
              "breakdown": bd})
     comm.destroy()
     if world > 1:

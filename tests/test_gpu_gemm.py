@@ -34,3 +34,26 @@ def test_gemm_matches_fp32_reference(m, n, k, act, kernel, monkeypatch):
     if act == "silu":
         ref = torch.nn.functional.silu(ref)
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+
+
+@pytest.mark.skipif(__import__("os").environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="224-wide 2-SM tiles not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+@pytest.mark.parametrize("m,n,k,act", [
+    (256, 224, 64, None),        # one tile
+    (300, 200, 136, "silu"),     # ragged in every dimension
+    (1024, 3584, 2048, "silu"),  # 16 full column tiles
+    (512, 1000, 320, None),      # a partial last column tile
+])
+def test_gemm_224_wide_tiles_match_fp32_reference(m, n, k, act, monkeypatch):
+    gemm = _need()
+    monkeypatch.setenv("BCCL_GEMM_PAIR", "1")
+    monkeypatch.setenv("BCCL_GEMM_BN", "224")
+    torch.manual_seed(1)
+    a = (torch.randn(m, k, device="cuda") * 0.5).bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.05).bfloat16()
+    y = gemm.gemm(a, w, act)
+    assert gemm.check_error() == 0
+    ref = a.float() @ w.float().t()
+    if act == "silu":
+        ref = torch.nn.functional.silu(ref)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())

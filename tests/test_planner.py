@@ -126,3 +126,22 @@ def test_env_report_runs_without_a_gpu():
     from originccl_b200.utils import env_report
     r = env_report.report()
     assert r["python"] and "bccl" in r and "topology" in r
+
+
+def test_gemm_tile_width_choice(monkeypatch):
+    """2-SM GEMM tile width: 256 by default; BCCL_GEMM_BN=auto takes 224-wide tiles where they
+    fill the last wave of 74 CTA pairs better (N = 3584: 448 -> 512 tiles, 7 waves either way),
+    and keeps 256 where they do not (runs without a GPU: 148 SMs assumed)."""
+    from originccl_b200.ops import gemm
+    monkeypatch.setenv("BCCL_GEMM_PAIR", "1")
+    monkeypatch.delenv("BCCL_GEMM_BN", raising=False)
+    assert gemm.kernel_name(8192, 3584) == "pair_256x256"
+    monkeypatch.setenv("BCCL_GEMM_BN", "auto")
+    assert gemm.kernel_name(8192, 3584) == "pair_256x224"
+    assert gemm.kernel_name(16384, 3584) == "pair_256x224"
+    assert gemm.kernel_name(8192, 8192) == "pair_256x256"
+    assert gemm.kernel_name(4096, 4096) == "pair_256x256"
+    monkeypatch.setenv("BCCL_GEMM_BN", "224")
+    assert gemm.kernel_name(4096, 4096) == "pair_256x224"
+    monkeypatch.setenv("BCCL_GEMM_PAIR", "0")
+    assert gemm.kernel_name(8192, 3584) == "single_128x256"
