@@ -79,39 +79,50 @@ class UniqueId:
         return UniqueId(ip, int(port))
 
 
-def _dtype_of(buf: Any) -> DataType:
-    mod = type(buf).__module__
-    if mod.startswith("torch"):
+_DTYPE_CACHE: dict = {}  # torch / numpy dtype object -> DataType
+
+
+def _resolve_dtype(buf: Any) -> DataType:
+    if type(buf).__module__.startswith("torch"):
         import torch
         table = {torch.float32: DataType.FLOAT32, torch.float64: DataType.FLOAT64, torch.int32: DataType.INT32,
                  torch.int64: DataType.INT64, torch.bfloat16: DataType.BF16, torch.float16: DataType.FP16}
-        if buf.dtype not in table:
-            raise TypeError(f"unsupported dtype {buf.dtype}")
-        return table[buf.dtype]
-    import numpy as np
-    table = {np.dtype(np.float32): DataType.FLOAT32, np.dtype(np.float64): DataType.FLOAT64,
-             np.dtype(np.int32): DataType.INT32, np.dtype(np.int64): DataType.INT64,
-             np.dtype(np.float16): DataType.FP16}
+    else:
+        import numpy as np
+        table = {np.dtype(np.float32): DataType.FLOAT32, np.dtype(np.float64): DataType.FLOAT64,
+                 np.dtype(np.int32): DataType.INT32, np.dtype(np.int64): DataType.INT64,
+                 np.dtype(np.float16): DataType.FP16}
     if buf.dtype not in table:
         raise TypeError(f"unsupported dtype {buf.dtype}")
     return table[buf.dtype]
 
 
+def _dtype_of(buf: Any) -> DataType:
+    # Per-call path of every collective: one dict lookup once a dtype has been seen.
+    dt = buf.dtype
+    v = _DTYPE_CACHE.get(dt)
+    if v is None:
+        v = _DTYPE_CACHE[dt] = _resolve_dtype(buf)
+    return v
+
+
 def _ptr(buf: Any) -> Optional[int]:
     if buf is None:
         return None
-    if type(buf).__module__.startswith("torch"):
+    data_ptr = getattr(buf, "data_ptr", None)  # torch tensors
+    if data_ptr is not None:
         if not buf.is_contiguous():
             raise ValueError("tensors must be contiguous")
-        return buf.data_ptr()
+        return data_ptr()
     if not buf.flags["C_CONTIGUOUS"]:
         raise ValueError("arrays must be C-contiguous")
     return buf.ctypes.data
 
 
 def _numel(buf: Any) -> int:
-    if type(buf).__module__.startswith("torch"):
-        return buf.numel()
+    numel = getattr(buf, "numel", None)
+    if callable(numel):
+        return numel()
     return int(buf.size)
 
 
@@ -119,6 +130,20 @@ def _nbytes(buf: Any) -> int:
     if type(buf).__module__.startswith("torch"):
         return buf.numel() * buf.element_size()
     return int(buf.nbytes)
+
+
+_RAW_STREAM = None
+
+
+def _current_raw_stream(device: int) -> int:
+    """The current torch CUDA stream of ``device`` as a raw handle (without building a Stream
+    object on every call)."""
+    global _RAW_STREAM
+    if _RAW_STREAM is None:
+        import torch
+        raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+        _RAW_STREAM = raw if raw is not None else (lambda d: torch.cuda.current_stream(d).cuda_stream)
+    return int(_RAW_STREAM(device))
 
 
 class Communicator:
@@ -263,8 +288,7 @@ class Communicator:
                                 "cannot be captured into a CUDA graph; use a stream-ordered one (blocking=False)")
             return 0, 0
         if stream is None:
-            import torch
-            stream = torch.cuda.current_stream(self.device)
+            return _current_raw_stream(self.device), 1
         handle = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
         return int(handle), 1
 
