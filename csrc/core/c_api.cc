@@ -227,8 +227,8 @@ double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int
 }
 
 long bcclTraceDump(bcclComm_t comm, const char* path) {
-    if (comm == nullptr || comm->comm.device_engine() == nullptr) return -1;
-    return comm->comm.device_engine()->DumpTrace(path);
+    if (comm == nullptr || path == nullptr) return -1;
+    return comm->comm.DumpTrace(path);
 }
 
 namespace {

@@ -391,6 +391,12 @@ bool Communicator::RegisterBuffer(void* ptr, size_t bytes) { return device_ ? de
 bool Communicator::DeregisterBuffer(void* ptr) { return device_ ? device_->DeregisterBuffer(ptr) : true; }
 bool Communicator::Barrier() { return bootstrap_ && bootstrap_->Barrier(); }
 
+long Communicator::DumpTrace(const char* path) {
+    if (device_) return device_->DumpTrace(path);
+    if (host_) return host_->DumpTrace(path);
+    return -1;
+}
+
 void Communicator::Abort() {
     failed_ = true;
     if (device_) device_->Abort();

@@ -112,6 +112,7 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     if (slot_bytes_ == 0) slot_bytes_ = std::max<size_t>(64u << 10, (8u << 20) / static_cast<size_t>(std::max(world_, 1)));
     slot_bytes_ = AlignUp(slot_bytes_, 256);
     ring_bytes_ = static_cast<size_t>(EnvInt("BCCL_HOST_RING_BYTES", 1 << 20));
+    trace_cap_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_TRACE", 0)));
 
     // ---- shared segment of this machine
     const int L = view_.local_size;
@@ -353,6 +354,7 @@ bool HostEngine::Barrier(int ch) {
     if (b->count.fetch_add(1, std::memory_order_acq_rel) == n - 1) {
         b->count.store(0, std::memory_order_relaxed);
         b->gen.store(g + 1, std::memory_order_release);
+        Mark(ch, kTrBarrier);
         return true;
     }
     auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms_);
@@ -372,6 +374,7 @@ bool HostEngine::Barrier(int ch) {
             return false;
         }
     }
+    Mark(ch, kTrBarrier);
     return true;
 }
 
@@ -491,6 +494,7 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
         char* mine = Slot(ch, rank_);
         if (s0 > 0) memcpy(mine, src + off * es, s0 * es);
         if (clen > s1) memcpy(mine + s1 * es, src + (off + s1) * es, (clen - s1) * es);
+        Mark(ch, kTrCopyIn);
         if (!Barrier(ch)) return false;
         if (s1 > s0) {
             const void* srcs[64];
@@ -501,6 +505,7 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
             }
             hostmath::Reduce(t.dtype, t.op, C.result + s0 * es, srcs, L, s1 - s0, world_, t.scale, M == 1);
         }
+        Mark(ch, kTrReduce);
         if (!Barrier(ch)) return false;
         if (M > 2 && leader && !reduce_only && clen * es >= kLeaderRingBytes) {
             // Three or more machines and a large chunk: ring among the leaders (each sends
@@ -535,8 +540,10 @@ bool HostEngine::AllReduceSlice(int ch, const CollTask& t, size_t e0, size_t e1,
                 hostmath::Reduce(t.dtype, t.op, C.result, srcs.data(), M, clen, world_, t.scale, true);
             }
         }
+        if (M > 1 && leader) Mark(ch, kTrExchange);
         if (M > 1 && !Barrier(ch)) return false;
         if (!reduce_only || rank_ == t.root) memcpy(dst + off * es, C.result, clen * es);
+        Mark(ch, kTrCopyOut);
     }
     return true;
 }
@@ -553,6 +560,7 @@ bool HostEngine::BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1)
         NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         if (rank_ == t.root) memcpy(C.result, in + off * es, clen * es);
+        Mark(ch, kTrCopyIn);
         if (!Barrier(ch)) return false;
         if (M > 1 && view_.local_rank == 0) {
             std::vector<int> peers;
@@ -576,9 +584,11 @@ bool HostEngine::BroadcastSlice(int ch, const CollTask& t, size_t e0, size_t e1)
                 }
             }
             if (!LeaderExchange(ch, peers, sends, sb, recvs, rb)) return false;
+            Mark(ch, kTrExchange);
         }
         if (M > 1 && !Barrier(ch)) return false;
         if (rank_ != t.root || buf != in) memcpy(buf + off * es, C.result, clen * es);
+        Mark(ch, kTrCopyOut);
     }
     return true;
 }
@@ -593,6 +603,7 @@ bool HostEngine::AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1)
         NextBuffers(ch);
         const size_t clen = std::min(chunk, e1 - off);
         memcpy(Slot(ch, rank_), src + off * es, clen * es);
+        Mark(ch, kTrCopyIn);
         if (!Barrier(ch)) return false;
         if (M > 1 && view_.local_rank == 0) {
             // Exchange whole machines' slots; a machine's ranks are not contiguous in
@@ -633,6 +644,7 @@ bool HostEngine::AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1)
                 if (!LeaderExchange(ch, p1, s1, sb1, r1, rb1)) return false;
                 i = j;
             }
+            Mark(ch, kTrExchange);
         }
         if (M > 1 && !Barrier(ch)) return false;
         for (int q = 0; q < world_; ++q) {
@@ -640,6 +652,7 @@ bool HostEngine::AllGatherSlice(int ch, const CollTask& t, size_t e0, size_t e1)
             const char* in = (q == rank_) ? src + off * es : Slot(ch, q);
             if (out != in) memcpy(out, in, clen * es);
         }
+        Mark(ch, kTrCopyOut);
     }
     return true;
 }
@@ -658,12 +671,14 @@ bool HostEngine::ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t
         // My slot holds [world][clen]: sub-chunk s is my contribution to rank s's output.
         for (int s = 0; s < world_; ++s)
             memcpy(Slot(ch, rank_) + static_cast<size_t>(s) * sub, src + (static_cast<size_t>(s) * t.count + off) * es, sub);
+        Mark(ch, kTrCopyIn);
         if (!Barrier(ch)) return false;
         for (int s = li; s < world_; s += L) {
             const void* srcs[64];
             for (int i = 0; i < L; ++i) srcs[i] = Slot(ch, view_.local_ranks[i]) + static_cast<size_t>(s) * sub;
             hostmath::Reduce(t.dtype, t.op, C.result + static_cast<size_t>(s) * sub, srcs, L, clen, world_, t.scale, M == 1);
         }
+        Mark(ch, kTrReduce);
         if (!Barrier(ch)) return false;
         if (M > 1 && view_.local_rank == 0) {
             // Send machine m the partials of its ranks; receive our ranks' partials from every machine.
@@ -694,22 +709,60 @@ bool HostEngine::ReduceScatterSlice(int ch, const CollTask& t, size_t e0, size_t
                 }
                 hostmath::Reduce(t.dtype, t.op, C.result + static_cast<size_t>(mine[k]) * sub, srcs.data(), M, clen, world_, t.scale, true);
             }
+            Mark(ch, kTrExchange);
         }
         if (M > 1 && !Barrier(ch)) return false;
         memcpy(dst + off * es, C.result + static_cast<size_t>(rank_) * sub, sub);
+        Mark(ch, kTrCopyOut);
     }
     return true;
 }
 
 bool HostEngine::RunSlice(int ch, const CollTask& t, size_t e0, size_t e1) {
-    switch (t.func) {
-    case CollFunc::AllReduce: return AllReduceSlice(ch, t, e0, e1, false);
-    case CollFunc::Reduce: return AllReduceSlice(ch, t, e0, e1, true);
-    case CollFunc::Broadcast: return BroadcastSlice(ch, t, e0, e1);
-    case CollFunc::AllGather: return AllGatherSlice(ch, t, e0, e1);
-    case CollFunc::ReduceScatter: return ReduceScatterSlice(ch, t, e0, e1);
-    default: return false;
+    if (trace_cap_) {
+        chans_[ch].trace_func = static_cast<uint16_t>(t.func);
+        chans_[ch].trace_slice++;
+        Mark(ch, kTrSliceBegin);
     }
+    bool ok = false;
+    switch (t.func) {
+    case CollFunc::AllReduce: ok = AllReduceSlice(ch, t, e0, e1, false); break;
+    case CollFunc::Reduce: ok = AllReduceSlice(ch, t, e0, e1, true); break;
+    case CollFunc::Broadcast: ok = BroadcastSlice(ch, t, e0, e1); break;
+    case CollFunc::AllGather: ok = AllGatherSlice(ch, t, e0, e1); break;
+    case CollFunc::ReduceScatter: ok = ReduceScatterSlice(ch, t, e0, e1); break;
+    default: break;
+    }
+    Mark(ch, kTrSliceEnd);
+    return ok;
+}
+
+long HostEngine::DumpTrace(const char* path) {
+    if (trace_cap_ == 0) return -1;
+    FILE* f = fopen(path, "w");
+    if (f == nullptr) return -1;
+    // The phase that ends at an event, by event.
+    static const char* kPhase[] = {"?", "idle", "copy_in", "barrier_wait", "reduce", "leader_exchange", "copy_out",
+                                   "tail"};
+    fprintf(f, "{\"traceEvents\":[\n");
+    long n = 0;
+    for (int ch = 0; ch < n_channels_; ++ch) {
+        std::vector<TraceRec>& tr = chans_[ch].trace;
+        for (size_t i = 1; i < tr.size(); ++i) {
+            const TraceRec& a = tr[i - 1];
+            const TraceRec& b = tr[i];
+            if (b.event == kTrSliceBegin || b.slice != a.slice) continue;  // between slices: idle
+            fprintf(f, "%s{\"name\":\"%s\",\"ph\":\"X\",\"ts\":%.3f,\"dur\":%.3f,\"pid\":%d,\"tid\":%d,"
+                       "\"args\":{\"op\":\"%s\",\"slice\":%u}}\n",
+                    n ? "," : "", kPhase[b.event < 8 ? b.event : 0], a.t_ns / 1000.0, (b.t_ns - a.t_ns) / 1000.0, rank_,
+                    ch, CollFuncName(static_cast<CollFunc>(b.func)), b.slice);
+            ++n;
+        }
+        tr.clear();
+    }
+    fprintf(f, "]}\n");
+    fclose(f);
+    return n;
 }
 
 bool HostEngine::RunP2p(const std::vector<CollTask>& tasks) {

@@ -18,6 +18,7 @@
 #pragma once
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <functional>
 #include <memory>
@@ -66,8 +67,30 @@ public:
     int n_channels() const { return n_channels_; }
     const char* p2p_transport_name(int peer) const;
     const char* executor_name() const { return epoll_ ? "epoll" : "polling"; }
+    // Host trace (BCCL_TRACE=<events per channel>): writes the phases recorded so far (copy-in,
+    // barrier waits, reduction, leader exchange, copy-out) as Chrome-trace duration events, one
+    // track per channel, and clears them. Call while no collective runs. Returns events written.
+    long DumpTrace(const char* path);
+
+    enum TraceEvent : uint16_t { kTrSliceBegin = 1, kTrCopyIn, kTrBarrier, kTrReduce, kTrExchange, kTrCopyOut, kTrSliceEnd };
 
 private:
+    struct TraceRec {
+        uint64_t t_ns;
+        uint16_t event;
+        uint16_t func;
+        uint32_t slice;
+    };
+    size_t trace_cap_ = 0;  // events kept per channel; 0 = tracing off
+    void Mark(int ch, TraceEvent ev) {
+        if (trace_cap_ == 0) return;
+        Channel& c = chans_[ch];
+        if (c.trace.size() < trace_cap_)
+            c.trace.push_back({static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                   std::chrono::steady_clock::now().time_since_epoch()).count()),
+                               static_cast<uint16_t>(ev), c.trace_func, c.trace_slice});
+    }
+
     // Chunks alternate between two buffer sets. A chunk's buffers are last read within that
     // chunk, and every chunk crosses at least one barrier after its first write, so when a rank
     // starts chunk k (having passed chunk k-1's first barrier) every rank has finished chunk
@@ -81,6 +104,9 @@ private:
         unsigned chunks = 0;     // chunks started on this channel (same count on every rank)
         std::vector<std::unique_ptr<TcpTransport>> leader_links;  // per machine (leaders only)
         std::vector<char> scratch;                                // leader-private receive space
+        std::vector<TraceRec> trace;                              // BCCL_TRACE (this channel's thread only)
+        uint16_t trace_func = 0;
+        uint32_t trace_slice = 0;
     };
 
     struct WorkUnit {

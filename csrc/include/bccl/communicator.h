@@ -106,6 +106,10 @@ public:
     const char* HostExecutorName() const;
     const Planner& planner() const { return *planner_; }
     DeviceEngine* device_engine() { return device_.get(); }
+    // With BCCL_TRACE=<records> at Init: writes the recorded device events (device
+    // communicators) or host channel phases (host communicators) as Chrome-trace JSON and
+    // clears them. Returns the number of events, or -1 when tracing is off.
+    long DumpTrace(const char* path);
 
 private:
     bool Flush();

@@ -395,7 +395,10 @@ class Communicator:
         self._check(self._lib.bcclSynchronize(self._h))
 
     def dump_trace(self, path: str) -> int:
-        """Writes the device trace (BCCL_TRACE=<records> at init) as Chrome-trace JSON."""
+        """Writes the trace recorded since the last dump (BCCL_TRACE=<records> at init) as
+        Chrome-trace JSON: per-CTA kernel events on device communicators, per-channel phases
+        (copy-in, barrier waits, reduction, leader exchange, copy-out) on host ones. Returns
+        the number of events, -1 when tracing is off."""
         return int(self._lib.bcclTraceDump(self._h, path.encode()))
 
     def abort(self) -> None:

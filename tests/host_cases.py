@@ -334,3 +334,31 @@ def run_without_shm(rank: int, world: int, part: str) -> Dict:
     if part == "matrix":
         return run_matrix(rank, world, [5, 40000], ["float32", "int64"])
     return run_p2p(rank, world)
+
+
+def run_trace(rank: int, world: int, out_dir: str) -> Dict:
+    """BCCL_TRACE on a host communicator: every collective's channel phases become Chrome-trace
+    duration events (one track per channel) in the file dump_trace writes."""
+    import json
+    import os
+    os.environ["BCCL_TRACE"] = "100000"
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    big = np.ones(1 << 20, np.float32)         # 4 MiB: split over both channels
+    out = np.empty_like(big)
+    comm.all_reduce(big, out=out)
+    g = np.empty(world * 1000, np.int32)
+    comm.all_gather(g, np.full(1000, rank, np.int32))
+    with comm.group():
+        for _ in range(3):
+            comm.all_reduce(np.ones(10, np.float64), out=np.empty(10))
+    path = os.path.join(out_dir, f"trace_{rank}.json")
+    n = comm.dump_trace(path)
+    again = comm.dump_trace(path + ".2")        # cleared by the first dump
+    comm.destroy()
+    with open(path) as f:
+        events = json.load(f)["traceEvents"]
+    assert n == len(events) > 0 and again == 0
+    assert all(e["ph"] == "X" and e["dur"] >= 0 and e["pid"] == rank for e in events)
+    return {"names": sorted({e["name"] for e in events}), "tracks": sorted({e["tid"] for e in events}),
+            "ops": sorted({e["args"]["op"] for e in events})}

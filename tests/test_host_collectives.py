@@ -77,3 +77,10 @@ def test_disable_shm_runs_everything_over_tcp():
     assert res[0]["ran"] > 0 and res[0]["single"]  # the view stays one machine
     res = _mp.run(4, host_cases.run_without_shm, "p2p", timeout=300)
     assert set(res[0]["transports"].values()) == {"tcp"}
+
+
+def test_host_trace_records_channel_phases(tmp_path):
+    res = _mp.run(2, host_cases.run_trace, str(tmp_path), timeout=120)
+    for r in res:
+        assert {"copy_in", "barrier_wait", "reduce", "copy_out"} <= set(r["names"])
+        assert r["tracks"] == [0, 1] and {"allreduce", "allgather"} <= set(r["ops"])
