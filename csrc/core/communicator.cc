@@ -5,6 +5,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 
@@ -90,10 +91,25 @@ bool Communicator::GetUniqueId(UniqueId& unique_id) {
         LOG_ERROR("GetUniqueId called twice on the same communicator");
         return false;
     }
+    // BCCL_MASTER=<addr>:<port> (set by a multi-node launcher): the id is known in advance, so
+    // rank 0 listens on that port and announces that address; no id file is exchanged.
+    uint16_t want = 0;
+    std::string ip;
+    if (const char* m = std::getenv("BCCL_MASTER")) {
+        const std::string ms(m);
+        const size_t colon = ms.rfind(':');
+        const long p = colon == std::string::npos ? -1 : std::atol(ms.c_str() + colon + 1);
+        if (p <= 0 || p > 65535) {
+            LOG_ERROR("BCCL_MASTER must be <address>:<port>, got '%s'", m);
+            return false;
+        }
+        want = static_cast<uint16_t>(p);
+        ip = ms.substr(0, colon);
+    }
     uint16_t port = 0;
-    bootstrap_listen_fd_ = net::Listen(0, &port);
+    bootstrap_listen_fd_ = net::Listen(want, &port);
     if (bootstrap_listen_fd_ < 0) return false;
-    std::string ip = net::LocalIpAddress();
+    if (ip.empty()) ip = net::LocalIpAddress();
     memset(&unique_id, 0, sizeof(unique_id));
     strncpy(unique_id.ip_addr, ip.c_str(), sizeof(unique_id.ip_addr) - 1);
     unique_id.port = port;

@@ -52,6 +52,15 @@ int EnvInt(const char* name, int dflt) {
 }
 
 bool ExchangeId(int rank, bccl::UniqueId* id, Communicator* comm) {
+    if (const char* m = std::getenv("BCCL_MASTER")) {  // multi-node launch: the id is known
+        if (rank == 0) return comm->GetUniqueId(*id);
+        std::string s(m);
+        size_t colon = s.rfind(':');
+        if (colon == std::string::npos) return false;
+        std::snprintf(id->ip_addr, sizeof(id->ip_addr), "%s", s.substr(0, colon).c_str());
+        id->port = static_cast<uint16_t>(std::atoi(s.substr(colon + 1).c_str()));
+        return true;
+    }
     const char* path = std::getenv("BCCL_ID_FILE");
     if (path == nullptr) {
         std::fprintf(stderr, "BCCL_ID_FILE is not set (run under bccl_run)\n");

@@ -1,6 +1,11 @@
 // bccl_run: starts N ranks of a program on this machine, without MPI.
 //
 //   bccl_run -np 4 [--timeout SEC] [--id-file PATH] [--gpus] -- ./program args...
+//   bccl_run -np 8 --nnodes 2 --node-rank K --master ADDR:PORT [--gpus] -- ./program args...
+//
+// Multi-node (one bccl_run per node, like torchrun): node K runs global ranks K*np .. K*np+np-1
+// of nnodes*np; BCCL_MASTER=ADDR:PORT is exported instead of an id file, and global rank 0
+// (on node 0, whose address ADDR must be) listens on PORT for the bootstrap.
 //
 // Each child gets BCCL_RANK, BCCL_WORLD_SIZE, BCCL_LOCAL_RANK, BCCL_LOCAL_SIZE and BCCL_ID_FILE
 // (a fresh path in a private temp directory unless --id-file is given). Rank 0 creates the unique
@@ -35,7 +40,8 @@ void OnSignal(int sig) { g_signal = sig; }
 
 int Usage() {
     std::fprintf(stderr,
-                 "usage: bccl_run -np N [--timeout SEC] [--id-file PATH] [--gpus] -- program [args...]\n");
+                 "usage: bccl_run -np N [--timeout SEC] [--id-file PATH] [--gpus]\n"
+                 "                [--nnodes M --node-rank K --master ADDR:PORT] -- program [args...]\n");
     return 2;
 }
 
@@ -50,10 +56,10 @@ void KillAll(pid_t group, const std::vector<pid_t>& pids, const std::vector<bool
 }  // namespace
 
 int main(int argc, char** argv) {
-    int np = 0;
+    int np = 0, nnodes = 1, node_rank = 0;
     double timeout_s = 0;
     bool gpus = false;
-    std::string id_file;
+    std::string id_file, master;
     int i = 1;
     for (; i < argc; ++i) {
         std::string a = argv[i];
@@ -69,17 +75,29 @@ int main(int argc, char** argv) {
             id_file = argv[++i];
         } else if (a == "--gpus") {
             gpus = true;
+        } else if (a == "--nnodes" && i + 1 < argc) {
+            nnodes = std::atoi(argv[++i]);
+        } else if (a == "--node-rank" && i + 1 < argc) {
+            node_rank = std::atoi(argv[++i]);
+        } else if (a == "--master" && i + 1 < argc) {
+            master = argv[++i];
         } else if (a[0] != '-') {
             break;  // program without a "--" separator
         } else {
             return Usage();
         }
     }
-    if (np < 1 || i >= argc) return Usage();
+    if (np < 1 || i >= argc || nnodes < 1 || node_rank < 0 || node_rank >= nnodes) return Usage();
+    if (nnodes > 1 && master.find(':') == std::string::npos) {
+        std::fprintf(stderr, "bccl_run: --nnodes > 1 needs --master ADDR:PORT\n");
+        return 2;
+    }
     char** prog = argv + i;
 
     std::string tmpdir;
-    if (id_file.empty()) {
+    if (!master.empty()) {
+        // no id file: the ranks find rank 0 at the master address
+    } else if (id_file.empty()) {
         char tmpl[] = "/tmp/bccl_run.XXXXXX";
         if (mkdtemp(tmpl) == nullptr) {
             std::perror("bccl_run: mkdtemp");
@@ -107,11 +125,15 @@ int main(int argc, char** argv) {
         }
         if (pid == 0) {
             setpgid(0, group);
-            setenv("BCCL_RANK", std::to_string(r).c_str(), 1);
-            setenv("BCCL_WORLD_SIZE", std::to_string(np).c_str(), 1);
+            setenv("BCCL_RANK", std::to_string(node_rank * np + r).c_str(), 1);
+            setenv("BCCL_WORLD_SIZE", std::to_string(nnodes * np).c_str(), 1);
             setenv("BCCL_LOCAL_RANK", std::to_string(r).c_str(), 1);
             setenv("BCCL_LOCAL_SIZE", std::to_string(np).c_str(), 1);
-            setenv("BCCL_ID_FILE", id_file.c_str(), 1);
+            if (!master.empty()) {
+                setenv("BCCL_MASTER", master.c_str(), 1);
+            } else {
+                setenv("BCCL_ID_FILE", id_file.c_str(), 1);
+            }
             if (gpus) setenv("BCCL_DEVICE", std::to_string(r).c_str(), 1);
             execvp(prog[0], prog);
             std::fprintf(stderr, "bccl_run: exec %s: %s\n", prog[0], std::strerror(errno));

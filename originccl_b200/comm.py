@@ -502,15 +502,20 @@ def init_from_env(**kwargs) -> Communicator:
     """Creates a communicator from the launcher's environment.
 
     ``bccl_run`` exports BCCL_RANK / BCCL_WORLD_SIZE / BCCL_ID_FILE (rank 0 writes the unique
-    id to the file, the others wait for it). Under torchrun (RANK / WORLD_SIZE set) the id goes
+    id to the file, the others wait for it), or, across nodes, BCCL_MASTER=<addr>:<port> (rank 0
+    listens there, the others connect to it). Under torchrun (RANK / WORLD_SIZE set) the id goes
     through the default torch.distributed store when a process group exists.
     """
     if "BCCL_RANK" in os.environ:
         rank, world = int(os.environ["BCCL_RANK"]), int(os.environ["BCCL_WORLD_SIZE"])
         if "device" not in kwargs and "BCCL_DEVICE" in os.environ:  # bccl_run --gpus
             kwargs["device"] = int(os.environ["BCCL_DEVICE"])
-        path = os.environ["BCCL_ID_FILE"]
         comm = Communicator()
+        master = os.environ.get("BCCL_MASTER")  # multi-node launch: rank 0 listens there
+        if master:
+            uid = comm.get_unique_id() if rank == 0 else UniqueId.from_bytes(master.encode())
+            return comm.init(rank, world, uid, **kwargs)
+        path = os.environ["BCCL_ID_FILE"]
         if rank == 0:
             uid = comm.get_unique_id()
             tmp = path + ".tmp"

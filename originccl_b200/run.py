@@ -1,6 +1,7 @@
 """Starts N ranks of a command on this machine through the ``bccl_run`` launcher (no MPI).
 
     python -m originccl_b200.run -np 4 [--gpus] [--timeout SEC] -- python my_script.py args...
+    python -m originccl_b200.run -np 8 --nnodes 2 --node-rank K --master ADDR:PORT -- ...   # per node
 
 Each rank gets BCCL_RANK / BCCL_WORLD_SIZE / BCCL_LOCAL_RANK / BCCL_ID_FILE (and BCCL_DEVICE with
 ``--gpus``); ``originccl_b200.init_from_env()`` picks them up. The exit status is the first failing

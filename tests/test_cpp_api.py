@@ -103,3 +103,43 @@ def test_python_launcher_runs_python_ranks():
                         sys.executable, "-c", code], capture_output=True, text=True, timeout=120,
                        cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+def _free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("program", ["cpp", "python"])
+def test_multi_node_launch(program):
+    """Two launcher instances ("nodes") started like torchrun: --nnodes 2 --node-rank K --master
+    ADDR:PORT; no id file, rank 0 listens on the master port. The ranks group into two logical
+    machines (hostname injection), so the collectives cross them over TCP."""
+    import sys
+    _need_binaries()
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    port = _free_port()
+    if program == "cpp":
+        prog = [CHECK, "check", "--ranks-per-machine", "2"]
+    else:
+        code = ("import sys; sys.path.insert(0, %r); import numpy as np, originccl_b200 as o; "
+                "c = o.init_from_env(logical_machine_size=2); x = np.full(4, c.rank + 1.0, np.float32); "
+                "c.all_reduce(x); assert (x == 10).all(), x; assert c.machine_count == 2; "
+                "import os; os.write(1, ('rank %%d of %%d\\n' %% (c.rank, c.world_size)).encode()); c.destroy()"
+                % root)
+        prog = [sys.executable, "-c", code]
+    procs = [subprocess.Popen([RUN, "-np", "2", "--nnodes", "2", "--node-rank", str(k), "--master",
+                               f"127.0.0.1:{port}", "--timeout", "120", "--"] + prog,
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, cwd=root)
+             for k in (0, 1)]
+    outs = [p.communicate(timeout=180) for p in procs]
+    for p, (out, err) in zip(procs, outs):
+        assert p.returncode == 0, out + err
+    if program == "cpp":
+        res = _json_lines(outs[0][0])[-1]
+        assert res["failed_all_ranks"] == 0 and res["ranks"] == 4 and res["machines"] == 2
+    else:
+        assert sorted(l for o, _ in outs for l in o.splitlines() if l.startswith("rank")) == \
+            [f"rank {r} of 4" for r in range(4)]
