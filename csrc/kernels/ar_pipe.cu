@@ -46,7 +46,8 @@ struct PipeParams {
     int op;
     float scale;
     int nvls;   // PipeKind
-    int debug;  // BCCL_PIPE_DEBUG bits (experiments): 1 no sys fences, 2 no alias fences, 4 serialise groups
+    int debug;  // BCCL_PIPE_DEBUG bits (experiments): 1 no system fence before the barrier flags,
+                // 4 flip the warp-group split, 8 one-shot pulls instead of pushing
 };
 
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     // (A copies into this rank's own slot, B loads the peers' slots over NVLink).
     const bool pull = (p.debug & 8) != 0;
     // Warp groups run their phases concurrently for NVLS (two local copies against one switch
-    // phase); for the push kinds a single group measured faster (BCCL_PIPE_DEBUG bit 2 flips it).
+    // phase); for the push kinds a single group measured faster (BCCL_PIPE_DEBUG bit 4 flips it).
     const bool split = (kind == kPipeNvls) != ((p.debug & 4) != 0);
     const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
     const uint64_t round0 = kind == kPipeNvls ? load_state_u64(&c.state->nvls_round_seq)
