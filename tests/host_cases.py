@@ -88,6 +88,7 @@ def run_matrix(rank: int, world: int, counts: List[int], dtypes: List[str], n_ch
             # allgather (rank order) and reducescatter (N*count input)
             g = _out(n * world, dtype)
             comm.all_gather(g[:n * world], x)
+            keep.append(x)
             _check(g, np.concatenate(ins), n * world, f"allgather {dtype} n={n}")
             rs_in = [value(r, n * world, dtype, n + 7) for r in range(world)]
             rs = _out(n, dtype)
@@ -362,3 +363,104 @@ def run_trace(rank: int, world: int, out_dir: str) -> Dict:
     assert all(e["ph"] == "X" and e["dur"] >= 0 and e["pid"] == rank for e in events)
     return {"names": sorted({e["name"] for e in events}), "tracks": sorted({e["tid"] for e in events}),
             "ops": sorted({e["args"]["op"] for e in events})}
+
+
+def run_fuzz(rank: int, world: int, seed: int, n_ops: int, logical_machine_size: int = 0) -> Dict:
+    """A random sequence of operations that every rank draws from the same seed: collectives of
+    every kind, dtype and op, counts from 0 to a few MiB (odd ones included), in place and out of
+    place, random roots, alone or in (nested) groups mixed with Send/Recv around the ring. Every
+    result is checked against the oracle, with sentinels, and inputs must come back unchanged."""
+    from originccl_b200 import ReduceOp, init_from_env
+    comm = init_from_env(n_channels=3, logical_machine_size=logical_machine_size, timeout_ms=60000)
+    rng = np.random.default_rng(seed)  # identical on every rank
+    checks = []                        # deferred until the group that holds the op has run
+    keep = []                          # buffers must live until their group has run
+    done = 0
+
+    def draw_count():
+        return int(rng.choice([0, 1, 3, 17, 1000, 4097, 65537, 300001, 1 << 20]))
+
+    def one(i: int, grouped: bool):
+        kind = str(rng.choice(["allreduce", "reduce", "broadcast", "allgather", "reducescatter", "sendrecv"]))
+        dtype = str(rng.choice(["float32", "float64", "int32", "int64"]))
+        op = str(rng.choice(list(OPS)))
+        n = draw_count()
+        root = int(rng.integers(0, world))
+        inplace = bool(rng.integers(0, 2))
+        tag = f"op {i} {kind} {dtype} {op} n={n} root={root} inplace={inplace}"
+        ins = [value(r, n, dtype, seed * 1000 + i) for r in range(world)]
+        if kind == "allreduce":
+            x = ins[rank].copy()
+            if inplace:
+                comm.all_reduce(x, ReduceOp(OPS[op]))
+                checks.append(lambda: _check(np.append(x, SENTINEL).astype(x.dtype), reduce_ref(op, ins, world), n, tag))
+            else:
+                y = _out(n, dtype)
+                comm.all_reduce(x, ReduceOp(OPS[op]), out=y[:n])
+                checks.append(lambda: (_check(y, reduce_ref(op, ins, world), n, tag),
+                                       np.testing.assert_array_equal(x, ins[rank], err_msg=tag + " input")))
+        elif kind == "reduce":
+            x = ins[rank].copy()
+            y = _out(n, dtype)
+            comm.reduce(x, root, ReduceOp(OPS[op]), out=y[:n] if rank == root else None)
+            keep.append(x)
+            if rank == root:
+                checks.append(lambda: _check(y, reduce_ref(op, ins, world), n, tag))
+        elif kind == "broadcast":
+            y = _out(n, dtype)
+            y[:n] = ins[rank] if rank == root else 0
+            comm.broadcast(y[:n], root)
+            checks.append(lambda: _check(y, ins[root], n, tag))
+        elif kind == "allgather":
+            g = _out(n * world, dtype)
+            x = ins[rank].copy()
+            comm.all_gather(g[:n * world], x)
+            keep.append(x)
+            checks.append(lambda: _check(g, np.concatenate(ins), n * world, tag))
+        elif kind == "reducescatter":
+            full = [value(r, n * world, dtype, seed * 1000 + i + 7) for r in range(world)]
+            x = full[rank].copy()
+            y = _out(n, dtype)
+            comm.reduce_scatter(y[:n], x, ReduceOp(OPS[op]))
+            keep.append(x)
+            checks.append(lambda: _check(y, reduce_ref(op, full, world)[rank * n:(rank + 1) * n], n, tag))
+        else:
+            if world == 1:
+                return
+            nxt, prv = (rank + 1) % world, (rank - 1) % world
+            s = ins[rank].copy()
+            r = _out(n, dtype)
+            if grouped:
+                comm.send(s, nxt)
+                comm.recv(r[:n], prv)
+            else:
+                with comm.group():
+                    comm.send(s, nxt)
+                    comm.recv(r[:n], prv)
+            checks.append(lambda: _check(r, ins[prv], n, tag))
+            keep.append(s)
+
+    i = 0
+    while i < n_ops:
+        mode = int(rng.integers(0, 3))
+        if mode == 0:  # alone
+            one(i, False)
+            i += 1
+        else:          # a group of 2-6 ops, nested once when mode == 2
+            k = int(rng.integers(2, 7))
+            comm.group_start()
+            if mode == 2:
+                comm.group_start()
+            for _ in range(k):
+                one(i, True)
+                i += 1
+            if mode == 2:
+                comm.group_end()  # inner: runs nothing
+            comm.group_end()
+        for c in checks:
+            c()
+        done += len(checks)
+        checks.clear()
+        keep.clear()
+    comm.destroy()
+    return {"checked": done}

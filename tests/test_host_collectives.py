@@ -84,3 +84,9 @@ def test_host_trace_records_channel_phases(tmp_path):
     for r in res:
         assert {"copy_in", "barrier_wait", "reduce", "copy_out"} <= set(r["names"])
         assert r["tracks"] == [0, 1] and {"allreduce", "allgather"} <= set(r["ops"])
+
+
+@pytest.mark.parametrize("world,machine,seed", [(3, 0, 11), (4, 2, 12), (5, 2, 13)])
+def test_random_operation_sequences(world, machine, seed):
+    res = _mp.run(world, host_cases.run_fuzz, seed, 120, machine, timeout=600)
+    assert all(r["checked"] >= 60 for r in res)
