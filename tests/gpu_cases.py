@@ -495,3 +495,111 @@ def run_registered(rank: int, world: int) -> Dict:
         comm.deregister(t)
     comm.destroy()
     return {"algorithms": sorted(used), "small_algorithm": small_algo}
+
+
+def run_fuzz(rank: int, world: int, seed: int, n_ops: int) -> Dict:
+    """Device counterpart of the host path's random sequences: every rank draws the same
+    sequence of collectives (kind, dtype, op, size up to 48 MiB, root, algorithm, in place or
+    not, alone or in groups with Send/Recv) and checks each result against the float64 oracle
+    with a sentinel after every output. Buffers stay alive until their group has run."""
+    import numpy as np
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import Algo, ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=30000)
+    rng = np.random.default_rng(seed)
+    algos = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS, "ring": Algo.RING}
+    checks, keep, used = [], [], set()
+    done = 0
+
+    def one(i: int, grouped: bool):
+        kind = str(rng.choice(["allreduce", "reduce", "broadcast", "allgather", "reducescatter", "sendrecv"]))
+        dtype = str(rng.choice(["float32", "bfloat16", "float16", "int32", "int64", "float64"]))
+        op = str(rng.choice(list(OPS)))
+        if dtype == "float16" and op == "avg":
+            op = "sum"
+        n = int(rng.choice([0, 1, 5, 1000, 4099, 65536 + 8, 300001, 1 << 20, (6 << 20) + 4, 12 << 20]))
+        root = int(rng.integers(0, world))
+        algo = str(rng.choice(list(algos))) if not grouped else "auto"
+        inplace = bool(rng.integers(0, 2))
+        td = _torch_dtype(dtype)
+        tag = f"op {i} {kind} {dtype} {op} n={n} root={root} algo={algo} inplace={inplace}"
+        ins = [rank_input(r, n, dtype, seed=seed * 1000 + i) for r in range(world)]
+        x = ins[rank].cuda()
+        out = torch.full((n + 1,), 7, dtype=td, device="cuda")
+        keep.extend([x, out])
+        sentinel = lambda: (out[n].item() == 7) or (_ for _ in ()).throw(AssertionError(tag + ": wrote past the end"))  # noqa: E731
+        if kind == "broadcast" and rank == root:
+            out[:n].copy_(x)
+        # The communicator runs on its own stream: inputs written on torch's stream must be done.
+        torch.cuda.synchronize()
+        if kind == "allreduce":
+            if inplace:
+                comm.all_reduce(x, ReduceOp(OPS[op]), algo=algos[algo])
+                checks.append(lambda: _close(x, oracle(op, ins, world).to(td), dtype, tag))
+            else:
+                comm.all_reduce(x, ReduceOp(OPS[op]), out=out[:n], algo=algos[algo])
+                checks.append(lambda: (_close(out[:n], oracle(op, ins, world).to(td), dtype, tag), sentinel()))
+        elif kind == "reduce":
+            comm.reduce(x, root, ReduceOp(OPS[op]), out=out[:n] if rank == root else None, algo=algos[algo])
+            if rank == root:
+                checks.append(lambda: (_close(out[:n], oracle(op, ins, world).to(td), dtype, tag), sentinel()))
+        elif kind == "broadcast":
+            comm.broadcast(out[:n], root, algo=algos[algo])
+            checks.append(lambda: (_close(out[:n], ins[root].to(td), dtype, tag), sentinel()))
+        elif kind == "allgather":
+            g = torch.full((n * world + 1,), 7, dtype=td, device="cuda")
+            keep.append(g)
+            torch.cuda.synchronize()
+            comm.all_gather(g[:n * world], x)
+            checks.append(lambda: (_close(g[:n * world], torch.cat(ins).to(td), dtype, tag),
+                                   (g[n * world].item() == 7) or (_ for _ in ()).throw(AssertionError(tag))))
+        elif kind == "reducescatter":
+            full = [rank_input(r, n * world, dtype, seed=seed * 1000 + i + 7) for r in range(world)]
+            xi = full[rank].cuda()
+            keep.append(xi)
+            torch.cuda.synchronize()
+            comm.reduce_scatter(out[:n], xi, ReduceOp(OPS[op]))
+            checks.append(lambda: (_close(out[:n], oracle(op, full, world)[rank * n:(rank + 1) * n].to(td), dtype, tag),
+                                   sentinel()))
+        elif world > 1:
+            nxt, prv = (rank + 1) % world, (rank - 1) % world
+            if grouped:
+                comm.send(x, nxt)
+                comm.recv(out[:n], prv)
+            else:
+                with comm.group():
+                    comm.send(x, nxt)
+                    comm.recv(out[:n], prv)
+            checks.append(lambda: (_close(out[:n], ins[prv].to(td), dtype, tag), sentinel()))
+
+    i = 0
+    while i < n_ops:
+        mode = int(rng.integers(0, 3))
+        if mode == 0:
+            one(i, False)
+            i += 1
+            used.add(comm.last_algorithm)
+        else:
+            k = int(rng.integers(2, 7))
+            comm.group_start()
+            if mode == 2:
+                comm.group_start()
+            for _ in range(k):
+                one(i, True)
+                i += 1
+            if mode == 2:
+                comm.group_end()
+            comm.group_end()
+        torch.cuda.synchronize()
+        for c in checks:
+            c()
+        done += len(checks)
+        checks.clear()
+        keep.clear()
+    comm.destroy()
+    return {"checked": done, "algorithms": sorted(used)}

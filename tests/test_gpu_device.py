@@ -152,3 +152,12 @@ def test_registered_buffers_zero_copy_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_registered, timeout=300)
     assert res[0]["algorithms"] == ["p2p_zero_copy"] and res[0]["small_algorithm"] == "oneshot"
+
+
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="random device sequences not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+@pytest.mark.parametrize("world", [1, 2])
+def test_random_device_operation_sequences(world):
+    _need(world)
+    res = _mp.run(world, gpu_cases.run_fuzz, 5 + world, 60, timeout=600)
+    assert all(r["checked"] >= 30 for r in res)
