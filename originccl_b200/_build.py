@@ -80,6 +80,11 @@ def _ninja_file() -> str:
         "rule linkexe",
         "  command = $cxx -o $out $in -lpthread",
         "  description = LINK $out",
+        "rule cc",
+        f"  command = gcc -MMD -MF $out.d -O2 -g -std=c11 -Wall -Wextra -pedantic -I{CSRC / 'include'} -c $in -o $out",
+        "  depfile = $out.d",
+        "  deps = gcc",
+        "  description = CC $out",
         "rule linkexample",
         f"  command = $cxx -o $out $in -L{LIBDIR} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} -lcudart "
         f"-Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread",
@@ -104,6 +109,10 @@ def _ninja_file() -> str:
     for ex in sorted((CSRC / "examples").glob("*.cc")):
         eobj = BUILD / f"examples_{ex.name}.o"
         lines.append(f"build {eobj}: cxx {ex}")
+        lines.append(f"build {LIBDIR / ex.stem}: linkexample {eobj} | {LIBDIR / 'libbccl.so'}")
+    for ex in sorted((CSRC / "examples").glob("*.c")):  # C callers of the C interface
+        eobj = BUILD / f"examples_{ex.name}.o"
+        lines.append(f"build {eobj}: cc {ex}")
         lines.append(f"build {LIBDIR / ex.stem}: linkexample {eobj} | {LIBDIR / 'libbccl.so'}")
     return "\n".join(lines) + "\n"
 

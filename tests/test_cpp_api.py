@@ -143,3 +143,17 @@ def test_multi_node_launch(program):
     else:
         assert sorted(l for o, _ in outs for l in o.splitlines() if l.startswith("rank")) == \
             [f"rank {r} of 4" for r in range(4)]
+
+
+@pytest.mark.parametrize("np_", [1, 3])
+def test_c_interface_from_c11(np_):
+    """csrc/examples/bccl_c_example.c: the C header compiled as C11 (-pedantic) and the library
+    driven from plain C: AllReduce, a grouped AllGather + ReduceScatter, Send/Recv."""
+    prog = os.path.join(LIB, "bccl_c_example")
+    if not os.path.exists(prog):
+        from originccl_b200 import _build
+        _build.build()
+    r = _run(["-np", str(np_), "--timeout", "60", "--", prog])
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert sorted(l for l in r.stdout.splitlines() if l.startswith("rank")) == \
+        sorted(f"rank {q} of {np_}: ok" for q in range(np_))
