@@ -19,6 +19,7 @@ struct TpArgs {
     int ms;                                   // rows per rank (multiple of 128)
     unsigned long long seq;                   // call index, 1-based, same on every rank
     int contributors;                         // CTAs per rank that bump each counter (set by the launcher)
+    int push_threads;                         // AllGather: threads per CTA that push (set by the launcher)
     // AllGather -> GEMM
     const void* x_local;                      // this rank's shard [ms, K]
     void* xg[kMaxRanks];                      // every rank's gathered-X buffer (this call's half)

@@ -120,11 +120,14 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
             const size_t chunk_bytes = (size_t)BM * g.K * 2;
             const size_t slice = ((chunk_bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
             const size_t lo = min(chunk_bytes, (size_t)blockIdx.x * slice), hi = min(chunk_bytes, lo + slice);
+            // Only the first push_threads threads push (fewer pushing warps leave more issue slots
+            // to the epilogue warps on the same SM); the others just keep the barrier company.
+            const int pushers = g.tp.push_threads > 0 ? min(g.tp.push_threads, cnt_threads) : cnt_threads;
             // No waits here: the loop always runs to the end (uniform named barriers).
             for (int c = 0; c < per; ++c) {
                 const char* srcp = reinterpret_cast<const char*>(g.tp.x_local) + (size_t)c * chunk_bytes;
                 const size_t dst_off = ((size_t)g.tp.rank * per + c) * chunk_bytes;
-                for (size_t o = lo + (size_t)ctid * 16; o < hi; o += (size_t)cnt_threads * 16) {
+                for (size_t o = lo + (size_t)ctid * 16; ctid < pushers && o < hi; o += (size_t)pushers * 16) {
                     const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
                     for (int q = 0; q < g.tp.nranks; ++q) {
                         if (q == g.tp.rank) continue;
@@ -778,6 +781,9 @@ cudaError_t LaunchTpGemm(int mode, const void* A_local, const void* A_gathered, 
     const int grid = NumSms() & ~1;
     TpArgs t = tp;
     t.contributors = grid;
+    // BCCL_TP_PUSH_WARPS (1-4): communication warps that push the activation shard (default 4).
+    const char* pw = std::getenv("BCCL_TP_PUSH_WARPS");
+    t.push_threads = 32 * std::max(1, std::min(4, pw != nullptr ? std::atoi(pw) : 4));
     Args g{static_cast<__nv_bfloat16*>(C), M, N, K, N, act, err, t};
     if (mode == kModeAllGather) {
         const int pbn = pair ? ChoosePairBN(M, N, grid / 2) : BN;
