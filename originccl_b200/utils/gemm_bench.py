@@ -36,6 +36,9 @@ def main(argv=None) -> int:
                    help="comma list of MxNxK[:silu]")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
+    p.add_argument("--variants", default="",
+                   help="also time (and check) each shape under these environment variants, e.g. "
+                        "'BCCL_GEMM_BN=224,BCCL_GEMM_BN=auto,BCCL_GEMM_PAIR=0'")
     args = p.parse_args(argv)
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     import torch
@@ -64,9 +67,30 @@ def main(argv=None) -> int:
         ours = _time(lambda: gemm.gemm(a, w, act, out=y), args.iters)
         cub = _time(lambda: torch.matmul(a, w.t()), args.iters)
         fl = 2.0 * m * n * k
+        variants = {}
+        for var in filter(None, args.variants.split(",")):
+            key, _, val = var.partition("=")
+            saved = os.environ.get(key)
+            os.environ[key] = val
+            yv = gemm.gemm(a, w, act)
+            refv = a.float() @ w.float().t()
+            if act:
+                refv = torch.nn.functional.silu(refv)
+            errv = ((yv.float() - refv).abs().max() / refv.abs().max()).item()
+            del refv
+            okv = errv < 2e-2 and gemm.check_error() == 0
+            rc |= 0 if okv else 1
+            tv = _time(lambda: gemm.gemm(a, w, act, out=yv), args.iters)
+            variants[var] = {"kernel": gemm.kernel_name(m, n), "ms": round(tv, 4),
+                             "tflops": round(fl / tv / 1e9, 1), "ok": okv}
+            if saved is None:
+                os.environ.pop(key, None)
+            else:
+                os.environ[key] = saved
         log({"shape": spec, "kernel": gemm.kernel_name(m, n), "ours_ms": round(ours, 4),
              "ours_tflops": round(fl / ours / 1e9, 1), "cublas_ms": round(cub, 4),
-             "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": round(err, 5), "ok": ok})
+             "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": round(err, 5), "ok": ok,
+             "variants": variants})
     log.close()
     return rc
 

@@ -24,6 +24,9 @@ def main(argv=None) -> None:
     p.add_argument("--gemm-peak-tflops", type=float, default=1383.8, help="measured sustained cuBLAS bf16 peak")
     p.add_argument("--nvlink-gbs", type=float, default=770.0)
     p.add_argument("--out", default="", help="also append the record to this JSON-lines file")
+    p.add_argument("--variants", default="",
+                   help="also time the fused MLP under each environment variant, e.g. "
+                        "'BCCL_GEMM_BN=auto,BCCL_TP_PUSH_WARPS=2,BCCL_GEMM_BN=auto;BCCL_TP_PUSH_WARPS=2'")
     args = p.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -92,6 +95,20 @@ def main(argv=None) -> None:
         bd["nccl_allgather_ms"] = timed(lambda: dist.all_gather_into_tensor(xg, x))
         bd["nccl_reducescatter_ms"] = timed(lambda: dist.reduce_scatter_tensor(out, part))
     bd = {k: round(v, 4) for k, v in bd.items()}
+    # Knob variants (read by the kernels' launchers at every call, so they apply in-process).
+    variants = {}
+    for spec in filter(None, args.variants.split(",")):
+        saved = {}
+        for kv in spec.split(";"):
+            k, _, v = kv.partition("=")
+            saved[k] = os.environ.get(k)
+            os.environ[k] = v
+        variants[spec] = round(timed(lambda: mlp(x)), 4)
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     from originccl_b200.utils.results import ResultLog
     with ResultLog("tp_bench", args.out, enabled=rank == 0) as log:
         log({"bench": "tp_mlp", "world": world, "tokens": args.tokens, "hidden": args.hidden,
@@ -99,7 +116,7 @@ def main(argv=None) -> None:
              "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
              "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
              "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(args.tokens, args.ffn // world),
-             "breakdown": bd})
+             "breakdown": bd, "variants_ms": variants})
     comm.destroy()
     if world > 1:
         dist.barrier(device_ids=[local])
