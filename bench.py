@@ -48,6 +48,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-clocks", action="store_true", help="diagnostic: do not sample clocks (no clocks key)")
+    p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
+                   help="plain torch tensors (default); the same tensors registered with the communicator "
+                        "(zero-copy over peer memory); or symmetric multicast-bound allocations (zero-copy NVLS)")
     return p.parse_args()
 
 
@@ -88,6 +91,15 @@ def main() -> None:
     # Two rotating inputs + output: 3 x 128 MiB on every rank, larger than the 126 MB L2.
     xs = [(torch.rand(count, device="cuda", generator=g) * 2 - 1).to(dtype) for _ in range(2)]
     y = torch.empty(count, device="cuda", dtype=dtype)
+    if args.buffers == "symmetric" and world > 1:
+        sym = [comm.symmetric_empty((count,), dtype) for _ in range(3)]
+        for dst, src in zip(sym, xs):
+            dst.copy_(src)
+        torch.cuda.synchronize()
+        xs, y = sym[:2], sym[2]
+    elif args.buffers == "registered" and world > 1:
+        for t_ in (*xs, y):
+            comm.register(t_)
 
     def step(i: int) -> None:
         comm.all_reduce(xs[i & 1], out=y)
@@ -198,6 +210,7 @@ def main() -> None:
             "scaling": "weak",
             "vs_baseline": round(value / REFERENCE_WHOLE_JOB_GBS, 2),
             "dtype": {"float32": "fp32", "bfloat16": "bf16"}[args.dtype],
+            "buffers": args.buffers,
             "data": "synthetic (uniform [-1,1), seed 1234+rank)",
             "config": {
                 "model": f"AllReduce SUM out-of-place, {args.dtype}",
@@ -208,6 +221,7 @@ def main() -> None:
                 "busbw_gbs_per_rank": round(busbw, 2),
                 "algbw_gbs": round(algbw, 2),
                 "algorithm": comm.last_algorithm,
+                "buffers": args.buffers,
                 "nvls": comm.nvls_enabled,
                 "l2": "inputs larger than L2: two rotating 128 MiB inputs + a 128 MiB output per rank",
                 "n1_semantics": ("N=1 has no bus (factor 2(N-1)/N = 0); value is the algbw of the single-rank "
