@@ -110,7 +110,7 @@ bool Communicator::GetUniqueId(UniqueId& unique_id) {
     bootstrap_listen_fd_ = net::Listen(want, &port);
     if (bootstrap_listen_fd_ < 0) return false;
     if (ip.empty()) ip = net::LocalIpAddress();
-    memset(&unique_id, 0, sizeof(unique_id));
+    unique_id = UniqueId{};
     strncpy(unique_id.ip_addr, ip.c_str(), sizeof(unique_id.ip_addr) - 1);
     unique_id.port = port;
     have_unique_id_ = true;
