@@ -464,3 +464,31 @@ def run_fuzz(rank: int, world: int, seed: int, n_ops: int, logical_machine_size:
         keep.clear()
     comm.destroy()
     return {"checked": done}
+
+
+def run_bf16_fp16_torch(rank: int, world: int) -> Dict:
+    """bf16 and fp16 on the host path, as torch CPU tensors: the reduction widens to fp32 and
+    rounds once (round to nearest even), so results equal the fp32 sum rounded to the type.
+    Inputs are multiples of 1/8 in [-8, 8) (exact in both types); sums of a few of them too,
+    and AVG / scale results are compared against the same rounding of the fp32 value."""
+    import torch
+
+    from originccl_b200 import ReduceOp, init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    checked = 0
+    for dt in (torch.bfloat16, torch.float16):
+        for n in (1, 7, 4097, 300001):
+            ins = [torch.from_numpy(value(r, n, "float32", n + 3)) for r in range(world)]
+            x = ins[rank].to(dt)
+            for op, scale in (("sum", 1.0), ("max", 1.0), ("min", 1.0), ("avg", 1.0), ("sum", 0.25)):
+                if dt == torch.float16 and op == "avg":
+                    continue
+                y = torch.full((n + 1,), 77.0, dtype=dt)
+                comm.all_reduce(x, ReduceOp(OPS[op]), out=y[:n], scale=scale)
+                ref = torch.from_numpy(reduce_ref(op, [a.numpy() for a in ins], world).astype(np.float32))
+                exp = (ref * scale).to(dt)
+                assert torch.equal(y[:n], exp), f"{dt} {op} scale={scale} n={n}: {(y[:n] != exp).nonzero()[:3]}"
+                assert y[n].item() == 77.0
+                checked += 1
+    comm.destroy()
+    return {"checked": checked}

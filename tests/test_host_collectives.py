@@ -90,3 +90,8 @@ def test_host_trace_records_channel_phases(tmp_path):
 def test_random_operation_sequences(world, machine, seed):
     res = _mp.run(world, host_cases.run_fuzz, seed, 120, machine, timeout=600)
     assert all(r["checked"] >= 60 for r in res)
+
+
+def test_bf16_fp16_on_host_tensors():
+    res = _mp.run(3, host_cases.run_bf16_fp16_torch, timeout=180)
+    assert all(r["checked"] == 36 for r in res)
