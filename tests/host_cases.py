@@ -88,7 +88,6 @@ def run_matrix(rank: int, world: int, counts: List[int], dtypes: List[str], n_ch
             # allgather (rank order) and reducescatter (N*count input)
             g = _out(n * world, dtype)
             comm.all_gather(g[:n * world], x)
-            keep.append(x)
             _check(g, np.concatenate(ins), n * world, f"allgather {dtype} n={n}")
             rs_in = [value(r, n * world, dtype, n + 7) for r in range(world)]
             rs = _out(n, dtype)
