@@ -209,8 +209,24 @@ bool Communicator::Init(const CommConfig& cfg) {
         v.local_index_of.assign(cfg.world_size, 0);
         for (const auto& mr : machine_ranks)
             for (size_t i = 0; i < mr.size(); ++i) v.local_index_of[mr[i]] = static_cast<int>(i);
+        CommConfig hc = config_;
+        if (hc.n_channels <= 0) {
+            // Up to 4 channels (the reference's default), fewer where this machine's ranks would
+            // otherwise run more busy channel threads than it has cores (each rank's calling
+            // thread runs one channel itself); every rank takes the minimum, since the channel
+            // plan must be the same everywhere.
+            const long cores = std::max(1L, sysconf(_SC_NPROCESSORS_ONLN));
+            const int want = static_cast<int>(std::max(1L, std::min(4L, cores / std::max(1, local_size_))));
+            std::vector<uint8_t> mine(1, static_cast<uint8_t>(want));
+            std::vector<std::vector<uint8_t>> all;
+            if (!bootstrap_->AllGather(mine, &all)) return false;
+            int agreed = want;
+            for (const auto& a : all)
+                if (!a.empty()) agreed = std::min<int>(agreed, a[0]);
+            hc.n_channels = std::max(1, agreed);
+        }
         host_.reset(new HostEngine());
-        if (!host_->Init(config_, bootstrap_.get(), fdpass_.get(), all_nodes_, v, data_listen_fd_)) {
+        if (!host_->Init(hc, bootstrap_.get(), fdpass_.get(), all_nodes_, v, data_listen_fd_)) {
             host_.reset();
             return false;
         }
