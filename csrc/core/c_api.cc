@@ -137,6 +137,11 @@ const char* bcclCommLastAlgorithm(bcclComm_t comm) { return comm ? comm->comm.La
 unsigned long long bcclCommKernelLaunches(bcclComm_t comm) { return comm ? comm->comm.KernelLaunches() : 0; }
 const char* bcclCommP2pTransport(bcclComm_t comm, int peer) { return comm ? comm->comm.P2pTransportName(peer) : ""; }
 const char* bcclCommHostExecutor(bcclComm_t comm) { return comm ? comm->comm.HostExecutorName() : ""; }
+unsigned long long bcclCommHostZeroCopyTransfers(bcclComm_t comm, int* enabled) {
+    if (comm == nullptr) return 0;
+    if (enabled) *enabled = comm->comm.HostZeroCopyP2p() ? 1 : 0;
+    return comm->comm.HostZeroCopyTransfers();
+}
 
 int bcclGroupStart(bcclComm_t comm) {
     if (comm == nullptr) return Fail();

@@ -442,5 +442,7 @@ const char* Communicator::P2pTransportName(int peer) const {
     return device_ ? "nccl" : "none";
 }
 const char* Communicator::HostExecutorName() const { return host_ ? host_->executor_name() : "cuda-stream"; }
+bool Communicator::HostZeroCopyP2p() const { return host_ && host_->zero_copy_p2p(); }
+unsigned long long Communicator::HostZeroCopyTransfers() const { return host_ ? host_->zero_copy_transfers() : 0; }
 
 }  // namespace bccl

@@ -4,9 +4,11 @@
 #include <sched.h>
 #include <sys/epoll.h>
 #include <sys/mman.h>
+#include <sys/uio.h>
 #include <unistd.h>
 
 #include <algorithm>
+#include <cerrno>
 #include <chrono>
 #include <cstring>
 #include <map>
@@ -33,6 +35,26 @@ struct SegHeader {
     uint64_t ring_bytes;
     uint64_t world;
 };
+
+// Single-copy Send/Recv within a machine (cross-memory attach): each local rank publishes its pid
+// and the address of a probe word here; acks[i][j] counts the zero-copy messages rank j (local
+// index) has finished reading from rank i.
+struct CmaInfo {
+    int32_t pid;
+    int32_t pad;
+    uint64_t probe_addr;
+    uint64_t pad2[2];
+};
+constexpr uint64_t kCmaMagic = 0xBCC1C0DE5E4D0001ull;
+// What the sender puts in the ring instead of the payload: where the receiver reads it.
+struct CmaDesc {
+    uint64_t magic;
+    int64_t pid;
+    uint64_t addr;
+    uint64_t bytes;
+};
+size_t CmaInfoOff() { return 64; }
+size_t CmaAcksOff(int L) { return (CmaInfoOff() + sizeof(CmaInfo) * static_cast<size_t>(L) + 63) / 64 * 64; }
 
 struct LinkHello {
     uint32_t magic;
@@ -116,7 +138,9 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
 
     // ---- shared segment of this machine
     const int L = view_.local_size;
-    const size_t hdr = 4096;
+    // Header page(s): SegHeader, the ranks' CmaInfo, the zero-copy acks[L][L].
+    const size_t hdr = AlignUp(CmaAcksOff(L) + sizeof(uint64_t) * static_cast<size_t>(L) * static_cast<size_t>(L), 4096);
+    cma_bytes_ = static_cast<size_t>(std::max<long>(1, EnvInt("BCCL_HOST_ZC_BYTES", 256 << 10)));
     const size_t bar_bytes = AlignUp(sizeof(ShmBarrier) * static_cast<size_t>(n_channels_), 4096);
     // Two buffer sets per channel (slots of every rank + a result area), used by alternate chunks.
     const size_t set_bytes = static_cast<size_t>(world_ + 1) * slot_bytes_;
@@ -163,6 +187,7 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
         return false;
     }
     char* base = static_cast<char*>(seg_);
+    if (!SetupCma(bs)) return false;
     chans_.resize(n_channels_);
     for (int c = 0; c < n_channels_; ++c) {
         chans_[c].barrier = reinterpret_cast<ShmBarrier*>(base + hdr) + c;
@@ -260,6 +285,41 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
     for (int c = 0; c < n_channels_; ++c) workers_.emplace_back(&HostEngine::WorkerLoop, this, c);
     if (!bs->Barrier()) return false;
     inited_ = true;
+    return true;
+}
+
+// Zero-copy Send/Recv between ranks of this machine: enabled when every local rank can read
+// every other's memory with process_vm_readv (same user, no ptrace restriction), checked by
+// reading each peer's published probe word; the decision is agreed over all ranks.
+bool HostEngine::SetupCma(Bootstrap* bs) {
+    const int L = view_.local_size;
+    char* base = static_cast<char*>(seg_);
+    auto* info = reinterpret_cast<CmaInfo*>(base + CmaInfoOff());
+    cma_acks_ = reinterpret_cast<std::atomic<uint64_t>*>(base + CmaAcksOff(L));
+    cma_probe_ = kCmaMagic ^ static_cast<uint64_t>(rank_);
+    info[view_.local_rank].pid = static_cast<int32_t>(getpid());
+    info[view_.local_rank].probe_addr = reinterpret_cast<uint64_t>(&cma_probe_);
+    cma_sent_.assign(static_cast<size_t>(world_), 0);
+    const bool enabled = EnvInt("BCCL_HOST_CMA", 1) != 0;
+    if (!bs->Barrier()) return false;  // every rank's info is published
+    bool ok = enabled;
+    for (int i = 0; ok && i < L; ++i) {
+        if (i == view_.local_rank) continue;
+        uint64_t v = 0;
+        struct iovec mine = {&v, sizeof(v)};
+        struct iovec theirs = {reinterpret_cast<void*>(info[i].probe_addr), sizeof(v)};
+        ok = process_vm_readv(info[i].pid, &mine, 1, &theirs, 1, 0) == static_cast<ssize_t>(sizeof(v)) &&
+             v == (kCmaMagic ^ static_cast<uint64_t>(view_.local_ranks[i]));
+    }
+    // Every rank reports whether it can read all of its local peers (trivially when it has none).
+    std::vector<uint8_t> flag(1, ok ? 1 : 0);
+    std::vector<std::vector<uint8_t>> all;
+    if (!bs->AllGather(flag, &all)) return false;
+    cma_ = enabled && L > 1;
+    for (const auto& a : all) cma_ = cma_ && !a.empty() && a[0] == 1;
+    if (enabled && L > 1 && !cma_) {
+        LOG_INFO("rank %d: single-copy Send/Recv unavailable (process_vm_readv refused)", rank_);
+    }
     return true;
 }
 
@@ -767,15 +827,34 @@ long HostEngine::DumpTrace(const char* path) {
 
 bool HostEngine::RunP2p(const std::vector<CollTask>& tasks) {
     // FIFO per (peer, direction): only the head op of each queue is active.
+    // Messages of at least cma_bytes_ to a rank of this machine go single-copy: the sender
+    // writes a CmaDesc into the ring instead of the payload and completes once the receiver has
+    // acked; the receiver reads the descriptor, copies the payload straight out of the sender's
+    // buffer (process_vm_readv) and acks. Both sides take the same decision from the size.
     struct Op {
         const CollTask* t;
         size_t progress;
+        int state;        // zero-copy: 0 descriptor in flight, 1 waiting for the ack / copying
+        uint64_t target;  // zero-copy send: the ack count that completes it
+        CmaDesc desc;
     };
     std::map<std::pair<int, int>, std::vector<Op>> queues;
     for (const CollTask& t : tasks) {
         if (t.count == 0) continue;
-        queues[{t.peer, t.func == CollFunc::Send ? 0 : 1}].push_back({&t, 0});
+        Op op{&t, 0, 0, 0, {}};
+        if (t.func == CollFunc::Send) {
+            op.desc = {kCmaMagic, static_cast<int64_t>(getpid()), reinterpret_cast<uint64_t>(t.send_buf),
+                       t.count * DataTypeSize(t.dtype)};
+        }
+        queues[{t.peer, t.func == CollFunc::Send ? 0 : 1}].push_back(op);
     }
+    auto zero_copy = [&](const CollTask& t, size_t bytes) {
+        return cma_ && bytes >= cma_bytes_ && view_.machine_of[t.peer] == view_.machine_index;
+    };
+    auto acks = [&](int sender, int receiver) -> std::atomic<uint64_t>& {
+        return cma_acks_[static_cast<size_t>(view_.local_index_of[sender]) * static_cast<size_t>(view_.local_size) +
+                         static_cast<size_t>(view_.local_index_of[receiver])];
+    };
     std::map<std::pair<int, int>, size_t> head;
     for (auto& kv : queues) head[kv.first] = 0;
     int ep = -1;
@@ -798,15 +877,55 @@ bool HostEngine::RunP2p(const std::vector<CollTask>& tasks) {
                 }
                 size_t before = op.progress;
                 bool done = false;
-                bool r = kv.first.second == 0 ? tr->TrySend(t.send_buf, bytes, &op.progress, &done)
-                                              : tr->TryRecv(t.recv_buf, bytes, &op.progress, &done);
+                const bool send = kv.first.second == 0;
+                bool r = true;
+                if (!zero_copy(t, bytes)) {
+                    r = send ? tr->TrySend(t.send_buf, bytes, &op.progress, &done)
+                             : tr->TryRecv(t.recv_buf, bytes, &op.progress, &done);
+                } else if (op.state == 0) {  // the descriptor goes through the ring, in FIFO order
+                    bool sent = false;
+                    r = send ? tr->TrySend(&op.desc, sizeof(CmaDesc), &op.progress, &sent)
+                             : tr->TryRecv(&op.desc, sizeof(CmaDesc), &op.progress, &sent);
+                    if (r && sent) {
+                        op.state = 1;
+                        if (send) op.target = ++cma_sent_[static_cast<size_t>(t.peer)];
+                    }
+                }
+                if (r && zero_copy(t, bytes) && op.state == 1) {
+                    if (send) {
+                        done = acks(rank_, t.peer).load(std::memory_order_acquire) >= op.target;
+                    } else if (op.desc.magic != kCmaMagic || op.desc.bytes != bytes) {
+                        LOG_ERROR("rank %d: zero-copy message from rank %d does not match the receive (%llu vs %zu bytes)",
+                                  rank_, t.peer, static_cast<unsigned long long>(op.desc.bytes), bytes);
+                        r = false;
+                    } else {
+                        size_t got = 0;
+                        while (r && got < bytes) {
+                            struct iovec mine = {static_cast<char*>(t.recv_buf) + got, bytes - got};
+                            struct iovec theirs = {reinterpret_cast<char*>(op.desc.addr) + got, bytes - got};
+                            const ssize_t k = process_vm_readv(static_cast<pid_t>(op.desc.pid), &mine, 1, &theirs, 1, 0);
+                            if (k <= 0) {
+                                LOG_ERROR("rank %d: zero-copy read from rank %d failed: %s", rank_, t.peer, strerror(errno));
+                                r = false;
+                            } else {
+                                got += static_cast<size_t>(k);
+                            }
+                        }
+                        if (r) {
+                            acks(t.peer, rank_).fetch_add(1, std::memory_order_release);
+                            cma_transfers_.fetch_add(1, std::memory_order_relaxed);
+                            done = true;
+                        }
+                    }
+                    progress |= done;
+                }
                 if (!r) {
                     ok = false;
                     break;
                 }
                 progress |= op.progress != before;
                 if (!done) {
-                    if (tr->GetFd() < 0) need_poll_shm = true;
+                    if (tr->GetFd() < 0 || zero_copy(t, bytes)) need_poll_shm = true;
                     break;
                 }
                 ++h;

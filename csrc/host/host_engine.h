@@ -67,6 +67,8 @@ public:
     int n_channels() const { return n_channels_; }
     const char* p2p_transport_name(int peer) const;
     const char* executor_name() const { return epoll_ ? "epoll" : "polling"; }
+    bool zero_copy_p2p() const { return cma_; }
+    unsigned long long zero_copy_transfers() const { return cma_transfers_.load(); }
     // Host trace (BCCL_TRACE=<events per channel>): writes the phases recorded so far (copy-in,
     // barrier waits, reduction, leader exchange, copy-out) as Chrome-trace duration events, one
     // track per channel, and clears them. Call while no collective runs. Returns events written.
@@ -158,6 +160,15 @@ private:
     std::vector<std::unique_ptr<Transport>> p2p_send_;  // per peer
     std::vector<std::unique_ptr<Transport>> p2p_recv_;  // per peer (same object for TCP)
     std::vector<std::shared_ptr<TcpTransport>> p2p_tcp_;
+    // Single-copy Send/Recv within a machine (messages of at least cma_bytes_): the receiver
+    // reads the sender's buffer with process_vm_readv; the sender completes when acked.
+    bool SetupCma(Bootstrap* bs);
+    bool cma_ = false;
+    size_t cma_bytes_ = 256u << 10;
+    uint64_t cma_probe_ = 0;
+    std::atomic<uint64_t>* cma_acks_ = nullptr;  // [sender local][receiver local], in the segment
+    std::vector<uint64_t> cma_sent_;             // per peer: zero-copy messages sent
+    std::atomic<uint64_t> cma_transfers_{0};     // completed zero-copy receives (statistics)
 
     // Channel worker pool.
     std::vector<std::thread> workers_;

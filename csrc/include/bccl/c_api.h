@@ -51,6 +51,9 @@ const char* bcclCommLastAlgorithm(bcclComm_t comm);
 unsigned long long bcclCommKernelLaunches(bcclComm_t comm);
 const char* bcclCommP2pTransport(bcclComm_t comm, int peer);
 const char* bcclCommHostExecutor(bcclComm_t comm);
+/* Host communicators: single-copy Send/Recv between ranks of a machine (*enabled) and the number
+ * of such messages this rank has received. */
+unsigned long long bcclCommHostZeroCopyTransfers(bcclComm_t comm, int* enabled);
 
 int bcclGroupStart(bcclComm_t comm);
 int bcclGroupEnd(bcclComm_t comm, uintptr_t stream, int has_stream);

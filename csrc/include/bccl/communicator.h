@@ -104,6 +104,10 @@ public:
     unsigned long long KernelLaunches() const;
     const char* P2pTransportName(int peer) const;
     const char* HostExecutorName() const;
+    // Host communicators: whether large Send/Recv within a machine go single-copy (cross-memory
+    // attach), and how many such messages this rank has received.
+    bool HostZeroCopyP2p() const;
+    unsigned long long HostZeroCopyTransfers() const;
     const Planner& planner() const { return *planner_; }
     DeviceEngine* device_engine() { return device_.get(); }
     // With BCCL_TRACE=<records> at Init: writes the recorded device events (device

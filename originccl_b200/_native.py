@@ -65,6 +65,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclCommKernelLaunches": (ctypes.c_ulonglong, [vp]),
         "bcclCommP2pTransport": (ctypes.c_char_p, [vp, c_int]),
         "bcclCommHostExecutor": (ctypes.c_char_p, [vp]),
+        "bcclCommHostZeroCopyTransfers": (ctypes.c_ulonglong, [vp, ctypes.POINTER(c_int)]),
         "bcclGroupStart": (c_int, [vp]),
         "bcclGroupEnd": (c_int, [vp, up, c_int]),
         "bcclAllReduce": (c_int, [vp, vp, vp, c_size, c_int, c_int, ctypes.c_float, c_int, up, c_int]),

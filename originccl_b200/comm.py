@@ -277,6 +277,14 @@ class Communicator:
     def host_executor(self) -> str:
         return self._lib.bcclCommHostExecutor(self._h).decode()
 
+    @property
+    def host_zero_copy(self) -> tuple:
+        """(enabled, messages received): single-copy Send/Recv between ranks of one machine
+        (host communicators; messages of at least BCCL_HOST_ZC_BYTES, default 256 KiB)."""
+        en = ctypes.c_int(0)
+        n = int(self._lib.bcclCommHostZeroCopyTransfers(self._h, ctypes.byref(en)))
+        return bool(en.value), n
+
     # ---------------------------------------------------------------- streams
     def _stream(self, stream: Any = None) -> tuple:
         if self.device < 0:

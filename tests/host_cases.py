@@ -172,13 +172,15 @@ def run_groups(rank: int, world: int) -> Dict:
     return {"inner_untouched": inner_untouched}
 
 
-def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str = "") -> Dict:
+def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str = "", cma: str = "") -> Dict:
     """Ring exchange in a group, FIFO for a repeated peer, a mixed 10-op group, typed messages
     around the ring-buffer capacity, a 1 MiB-per-peer mesh with receives out of order, and the
     transport each pair uses."""
     import os
     if executor:
         os.environ["BCCL_HOST_EXECUTOR"] = executor
+    if cma:
+        os.environ["BCCL_HOST_CMA"] = cma
     from originccl_b200 import init_from_env
     comm = init_from_env(n_channels=2, logical_machine_size=logical_machine_size, timeout_ms=30000)
     nxt, prv = (rank + 1) % world, (rank - 1) % world
@@ -232,8 +234,9 @@ def run_p2p(rank: int, world: int, logical_machine_size: int = 0, executor: str 
         assert np.array_equal(big_out[q], np.arange(big, dtype=np.int32) + 1000 * q + rank), "1 MiB mesh"
     kinds = {q: comm.p2p_transport(q) for q in range(world) if q != rank}
     ex = comm.host_executor
+    zc = comm.host_zero_copy
     comm.destroy()
-    return {"transports": kinds, "executor": ex}
+    return {"transports": kinds, "executor": ex, "zero_copy": zc}
 
 
 def run_init_only(rank: int, world: int) -> Dict:

@@ -47,6 +47,14 @@ def test_single_rank():
 def test_p2p_shared_memory():
     res = _mp.run(4, host_cases.run_p2p, timeout=300)
     assert set(res[0]["transports"].values()) == {"shm"}
+    # Messages of 256 KiB and more went single-copy (process_vm_readv) where the host allows it.
+    enabled, received = res[0]["zero_copy"]
+    assert not enabled or received == 5  # 2 ring messages of 4 and 20 MiB + three 1 MiB mesh messages
+
+
+def test_p2p_shared_memory_without_zero_copy():
+    res = _mp.run(3, host_cases.run_p2p, 0, "", "0", timeout=300)
+    assert all(r["zero_copy"] == (False, 0) for r in res)
 
 
 def test_p2p_across_logical_machines_tcp_epoll():
