@@ -502,6 +502,7 @@ int main(int argc, char** argv) {
             c.Group(n);
             c.SendRecvRing(n);
         }
+        c.SendRecvRing(300001);  // above the host path's single-copy threshold (256 KiB)
         c.Contract();
         int fails = c.failed, total_fail = 0;
         void* fb = mem.Alloc(sizeof(int));
