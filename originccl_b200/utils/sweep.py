@@ -35,13 +35,16 @@ def parse_size(s: str) -> int:
 
 def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, factor: int = 2, warmup: int = 20,
               iters: int = 100, algo: str = "auto", inplace: bool = False, nccl: bool = True, redop: str = "sum",
-              seed: int = 1234, emit=print, graph: int = 0) -> list:
+              seed: int = 1234, emit=print, graph: int = 0, buffers: str = "plain") -> list:
     """Times ``op`` at every size from min_bytes to max_bytes (x factor) with this library and
     with NCCL on the same buffers; returns (and emits on rank 0) one record per size.
 
     ``graph`` > 0 captures that many back-to-back calls into one CUDA graph (for both
     libraries) and times graph replays instead of eager calls: the per-call time then excludes
-    the host's launch path, as nccl-tests' ``-G`` does."""
+    the host's launch path, as nccl-tests' ``-G`` does. ``buffers`` = ``"registered"`` registers
+    this library's buffers with the communicator (zero-copy over peer memory) and
+    ``"symmetric"`` allocates them in symmetric memory (zero-copy NVLS); NCCL uses plain copies
+    of them."""
     import torch
     import torch.distributed as dist
     from originccl_b200 import Algo, ReduceOp
@@ -83,6 +86,7 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
     out = []
     size = max(min_bytes, es)
     g = torch.Generator(device="cuda").manual_seed(seed + rank)
+    sym = [None, None]  # symmetric buffers (buffers="symmetric"), allocated on first use
     while size <= max_bytes:
         n = max(1, size // es)
         # Per-rank payload convention (as nccl-tests): allreduce/broadcast/reduce move n elements;
@@ -96,6 +100,21 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
         else:
             x = (torch.rand(n, device="cuda", generator=g) * 2 - 1).to(dt)
             y = x if inplace else torch.empty_like(x)
+        registered = []
+        if buffers == "symmetric" and world > 1:
+            # Views at the start of two symmetric buffers sized once for the largest point (every
+            # rank uses the same offsets, as the zero-copy kernels require).
+            if sym[0] is None:
+                cap = max(1, max_bytes // es) * world
+                sym[0], sym[1] = comm.symmetric_empty((cap,), dt), comm.symmetric_empty((cap,), dt)
+            xs_, ys_ = sym[0][:x.numel()], sym[1][:y.numel()]
+            xs_.copy_(x)
+            torch.cuda.synchronize()
+            x, y = xs_, (xs_ if inplace and op not in ("reducescatter", "allgather") else ys_)
+        elif buffers == "registered" and world > 1:
+            for t_ in ({id(x): x, id(y): y}).values():
+                comm.register(t_)
+                registered.append(t_)
         if op == "allreduce":
             ours = lambda: comm.all_reduce(x, rop, out=y, algo=algo_v)  # noqa: E731
             ref = lambda: dist.all_reduce(y, op=nccl_op)  # noqa: E731
@@ -124,13 +143,15 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
         rec = {"op": op, "dtype": dtype, "redop": redop, "bytes": n * es, "ranks": world, "algo": used,
                "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
                "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok,
-               "graph": graph}
+               "graph": graph, "buffers": buffers}
         if t_nccl is not None:
             rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
                         "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
         if rank == 0:
             emit(json.dumps(rec))
         out.append(rec)
+        for t_ in registered:
+            comm.deregister(t_)
         del x, y
         size *= factor
     return out
@@ -199,6 +220,8 @@ def main(argv=None) -> None:
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--no-nccl", action="store_true")
     p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
+    p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
+                   help="this library's buffers: plain tensors, registered tensors or symmetric memory")
     p.add_argument("--graph", type=int, default=0,
                    help="capture this many calls per CUDA graph and time replays (0: eager calls)")
     args = p.parse_args(argv)
@@ -219,7 +242,7 @@ def main(argv=None) -> None:
 
     run_sweep(comm, op=args.op, dtype=args.dtype, min_bytes=parse_size(args.min_bytes),
               max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup, iters=args.iters,
-              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log, graph=args.graph)
+              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log, graph=args.graph, buffers=args.buffers)
     log.close()
     comm.destroy()
     dist.barrier(device_ids=[local])
