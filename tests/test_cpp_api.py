@@ -157,3 +157,25 @@ def test_c_interface_from_c11(np_):
     assert r.returncode == 0, r.stdout + r.stderr
     assert sorted(l for l in r.stdout.splitlines() if l.startswith("rank")) == \
         sorted(f"rank {q} of {np_}: ok" for q in range(np_))
+
+
+@pytest.mark.parametrize("args", [
+    ["--op", "allreduce", "--dtype", "bf16", "--redop", "avg"],
+    ["--op", "allgather", "--dtype", "f16"],
+    ["--op", "reducescatter", "--dtype", "i32", "--redop", "max"],
+    ["--op", "broadcast", "--dtype", "f64", "--root", "2", "--inplace"],
+    ["--op", "reduce", "--dtype", "i64", "--redop", "min", "--root", "1"],
+    ["--op", "sendrecv", "--dtype", "f32"],
+])
+def test_perf_tool_host(args):
+    """bccl_perf (the reference's size-sweep benchmark for every collective) on host buffers:
+    every size is validated before it is timed and reported as a JSON line."""
+    perf = os.path.join(LIB, "bccl_perf")
+    if not os.path.exists(perf):
+        from originccl_b200 import _build
+        _build.build()
+    r = _run(["-np", "3", "--timeout", "120", "--", perf, "-b", "4", "-e", "2M", "-f", "8", "-w", "1", "-n", "3",
+              "--json"] + args)
+    assert r.returncode == 0, r.stdout + r.stderr
+    recs = _json_lines(r.stdout)
+    assert len(recs) >= 6 and all(x["check"] and x["time_us"] > 0 and x["ranks"] == 3 for x in recs)
