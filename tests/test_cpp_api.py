@@ -179,3 +179,18 @@ def test_perf_tool_host(args):
     assert r.returncode == 0, r.stdout + r.stderr
     recs = _json_lines(r.stdout)
     assert len(recs) >= 6 and all(x["check"] and x["time_us"] > 0 and x["ranks"] == 3 for x in recs)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="bccl_perf --device not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+@pytest.mark.parametrize("op", ["allreduce", "allgather", "reducescatter", "broadcast", "reduce"])
+def test_perf_tool_device_one_gpu(op):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    r = _run(["-np", "1", "--gpus", "--timeout", "120", "--", os.path.join(LIB, "bccl_perf"), "--device", "--op", op,
+              "--dtype", "bf16", "-b", "4", "-e", "64M", "-f", "16", "-w", "2", "-n", "5", "--json"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    recs = _json_lines(r.stdout)
+    assert len(recs) >= 6 and all(x["check"] and x["path"] == "device" for x in recs)
