@@ -6,6 +6,7 @@
 //   bccl_run -np 4 bccl_check bench --counts 32768,131072 --warmup 20 --iters 100
 //   bccl_run -np 4 bccl_check bench-group --messages 64 --message-bytes 262144
 //   bccl_run -np 32 bccl_check check --ranks-per-machine 8   # four logical machines
+//   bccl_run -np 4 bccl_check fuzz --seed 3 --ops 60          # random checked sequence
 //
 // check: every collective with exact-valued inputs (integers, and floats that are multiples of
 // 1/8), out of place and in place, a sentinel element after every output, nested groups,
@@ -31,6 +32,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <random>
 #include <sstream>
 #include <string>
 #include <thread>
@@ -443,7 +445,7 @@ int main(int argc, char** argv) {
     std::string mode = argc > 1 ? argv[1] : "check";
     bool device = false;
     std::vector<size_t> counts = {32768, 131072};
-    int warmup = 20, iters = 100, channels = 0, nmsg = 64, per_machine = 0;
+    int warmup = 20, iters = 100, channels = 0, nmsg = 64, per_machine = 0, fuzz_seed = 1, fuzz_ops = 50;
     size_t msg_bytes = 256u << 10;
     for (int i = 2; i < argc; ++i) {
         std::string a = argv[i];
@@ -455,6 +457,8 @@ int main(int argc, char** argv) {
         else if (a == "--messages" && i + 1 < argc) nmsg = std::atoi(argv[++i]);
         else if (a == "--message-bytes" && i + 1 < argc) msg_bytes = static_cast<size_t>(std::atoll(argv[++i]));
         else if (a == "--ranks-per-machine" && i + 1 < argc) per_machine = std::atoi(argv[++i]);
+        else if (a == "--seed" && i + 1 < argc) fuzz_seed = std::atoi(argv[++i]);
+        else if (a == "--ops" && i + 1 < argc) fuzz_ops = std::atoi(argv[++i]);
     }
     const int rank = EnvInt("BCCL_RANK", 0), world = EnvInt("BCCL_WORLD_SIZE", 1);
     Communicator comm;
@@ -484,6 +488,47 @@ int main(int argc, char** argv) {
         rc = RunBench(&comm, mem, rank, world, counts, warmup, iters);
     } else if (mode == "bench-group") {
         rc = RunGroupBench(&comm, mem, rank, world, nmsg, msg_bytes, warmup, iters);
+    } else if (mode == "fuzz") {
+        // A random sequence of checked operations, the same on every rank (one seed): every
+        // collective and dtype, SUM/MAX/MIN/AVG, in place or not, sizes from 1 element to a few
+        // MiB (so channel splitting, alternating buffer sets and single-copy Send/Recv all run),
+        // groups and Send/Recv around the ring. Meant for the sanitizer builds.
+        Checker c{&comm, mem, rank, world};
+        std::mt19937_64 rng(static_cast<uint64_t>(fuzz_seed));
+        const size_t sizes[] = {1, 17, 1000, 4097, 40000, 300001, 1u << 20};
+        const ReduceOp ops[] = {ReduceOp::SUM, ReduceOp::MAX, ReduceOp::MIN, ReduceOp::AVG};
+        for (int k = 0; k < fuzz_ops; ++k) {
+            const size_t n = sizes[rng() % 7];
+            const ReduceOp op = ops[rng() % 4];
+            const int root = static_cast<int>(rng() % static_cast<uint64_t>(world));
+            const bool in_place = rng() % 2 == 0;
+            switch (rng() % 9) {
+            case 0: c.AllReduce<int>(DataType::INT32, op, n, in_place); break;
+            case 1: c.AllReduce<float>(DataType::FLOAT32, op, n, in_place); break;
+            case 2: c.AllReduce<double>(DataType::FLOAT64, op, n, in_place); break;
+            case 3: c.AllReduce<long long>(DataType::INT64, op, n, in_place); break;
+            case 4: c.Broadcast(n, root); break;
+            case 5: c.ReduceTo(n, root, op == ReduceOp::AVG ? ReduceOp::SUM : op); break;
+            case 6: c.AllGather(n); break;
+            case 7: c.ReduceScatter(n); break;
+            default: (rng() % 2 ? c.Group(n) : c.SendRecvRing(n)); break;
+            }
+        }
+        int fails = c.failed, total_fail = 0;
+        void* fb = mem.Alloc(sizeof(int));
+        mem.Put(fb, &fails, sizeof(int));
+        if (!comm.AllReduce(fb, fb, 1, DataType::INT32, ReduceOp::SUM)) fails = -1;
+        mem.Get(&total_fail, fb, sizeof(int));
+        mem.Free(fb);
+        if (fails < 0) total_fail = world;
+        if (rank == 0) {
+            std::printf("{\"fuzz_ops\": %d, \"passed\": %d, \"failed_all_ranks\": %d, \"ranks\": %d, \"failures\": [",
+                        fuzz_ops, c.passed, total_fail, world);
+            for (size_t i = 0; i < c.failures.size(); ++i)
+                std::printf("%s\"%s\"", i ? ", " : "", c.failures[i].c_str());
+            std::printf("]}\n");
+        }
+        rc = total_fail == 0 ? 0 : 1;
     } else {
         Checker c{&comm, mem, rank, world};
         c.View(per_machine);

@@ -29,6 +29,8 @@ CASES = [
     ["-np", "4", "--", "{bin}/bccl_check", "bench", "--counts", "1000,300000,3000000", "--warmup", "2", "--iters", "5"],
     ["-np", "4", "--", "{bin}/bccl_check", "bench-group", "--messages", "64", "--message-bytes", "65536", "--warmup",
      "2", "--iters", "5"],
+    ["-np", "4", "--", "{bin}/bccl_check", "fuzz", "--seed", "7", "--ops", "40"],
+    ["-np", "6", "--", "{bin}/bccl_check", "fuzz", "--seed", "8", "--ops", "30", "--ranks-per-machine", "2"],
 ]
 
 
