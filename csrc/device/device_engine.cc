@@ -680,7 +680,11 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         bool zc = false;
         const void* zc_send = nullptr;
         void* zc_recv = nullptr;
-        if (nranks_ > 1 && (bytes % 16) == 0 && nvls_.mc != nullptr && knob_zero_copy_) {
+        // Zero-copy kernels move 16-byte vectors: sizes and addresses must be 16-byte aligned
+        // (otherwise the staged kernels below run).
+        const bool aligned16 = (bytes % 16) == 0 && ((reinterpret_cast<uintptr_t>(t.send_buf) |
+                                                      reinterpret_cast<uintptr_t>(t.recv_buf)) & 15) == 0;
+        if (nranks_ > 1 && aligned16 && nvls_.mc != nullptr && knob_zero_copy_) {
             if (t.func == CollFunc::AllReduce && c.algo == Algo::kNvls && UserMulticast(t.send_buf, bytes, &send_mc) &&
                 UserMulticast(t.recv_buf, bytes, &recv_mc)) {
                 zc = true;
@@ -703,7 +707,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         char* in_peers[kMaxRanks] = {};
         char* out_peers[kMaxRanks] = {};
         bool p2p_zc = false;
-        if (!zc && nranks_ > 1 && (bytes % 16) == 0 && knob_zero_copy_ && (!reg_bufs_.empty() || !user_bufs_.empty()) &&
+        if (!zc && nranks_ > 1 && aligned16 && knob_zero_copy_ && (!reg_bufs_.empty() || !user_bufs_.empty()) &&
             (t.func == CollFunc::AllReduce ? bytes : all_bytes) >= knob_p2p_zc_min_) {
             if (t.func == CollFunc::AllReduce) {
                 p2p_zc = PeerPointers(t.send_buf, bytes, in_peers) && PeerPointers(t.recv_buf, bytes, out_peers);
