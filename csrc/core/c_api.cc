@@ -100,6 +100,22 @@ int bcclCommDestroy(bcclComm_t comm) {
     return 0;
 }
 
+int bcclCommSplit(bcclComm_t comm, int color, int key, bcclComm_t* out) {
+    if (comm == nullptr || out == nullptr) return Fail();
+    *out = nullptr;
+    bcclComm_t child = new bcclComm();
+    if (!comm->comm.Split(color, key, &child->comm)) {
+        delete child;
+        return Fail();
+    }
+    if (color < 0) {
+        delete child;
+        return 0;
+    }
+    *out = child;
+    return 0;
+}
+
 const char* bcclGetLastError(void) { return bccl::LastErrorMessage(); }
 
 const char* bcclVersion(void) { return "bccl 0.1.0 (sm_100a)"; }

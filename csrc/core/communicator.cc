@@ -86,7 +86,9 @@ Communicator::Communicator() : planner_(new Planner()) {}
 
 Communicator::~Communicator() { Finalize(); }
 
-bool Communicator::GetUniqueId(UniqueId& unique_id) {
+bool Communicator::GetUniqueId(UniqueId& unique_id) { return MakeUniqueId(unique_id, true); }
+
+bool Communicator::MakeUniqueId(UniqueId& unique_id, bool from_env) {
     if (have_unique_id_) {
         LOG_ERROR("GetUniqueId called twice on the same communicator");
         return false;
@@ -95,7 +97,8 @@ bool Communicator::GetUniqueId(UniqueId& unique_id) {
     // rank 0 listens on that port and announces that address; no id file is exchanged.
     uint16_t want = 0;
     std::string ip;
-    if (const char* m = std::getenv("BCCL_MASTER")) {
+    const char* m = from_env ? std::getenv("BCCL_MASTER") : nullptr;
+    if (m != nullptr) {
         const std::string ms(m);
         const size_t colon = ms.rfind(':');
         const long p = colon == std::string::npos ? -1 : std::atol(ms.c_str() + colon + 1);
@@ -115,6 +118,63 @@ bool Communicator::GetUniqueId(UniqueId& unique_id) {
     unique_id.port = port;
     have_unique_id_ = true;
     return true;
+}
+
+bool Communicator::Split(int color, int key, Communicator* out) {
+    if (!inited_ || out == nullptr) {
+        LOG_ERROR("Split needs an initialised communicator and an output");
+        return false;
+    }
+    struct Entry {
+        int32_t color, key, rank;
+    };
+    Entry me{color, key, config_.rank};
+    std::vector<uint8_t> blob(sizeof(me));
+    std::memcpy(blob.data(), &me, sizeof(me));
+    std::vector<std::vector<uint8_t>> all;
+    if (!bootstrap_->AllGather(blob, &all)) return false;
+    std::vector<Entry> members;
+    for (const auto& b : all) {
+        if (b.size() != sizeof(Entry)) return false;
+        Entry e;
+        std::memcpy(&e, b.data(), sizeof(e));
+        if (color >= 0 && e.color == color) members.push_back(e);
+    }
+    std::stable_sort(members.begin(), members.end(),
+                     [](const Entry& a, const Entry& b) { return a.key != b.key ? a.key < b.key : a.rank < b.rank; });
+    int new_rank = -1;
+    for (size_t i = 0; i < members.size(); ++i)
+        if (members[i].rank == config_.rank) new_rank = static_cast<int>(i);
+    // Each color's first member creates the new unique id; everyone learns every color's id.
+    UniqueId id;
+    bool ok = true;
+    std::vector<uint8_t> mine;
+    if (color >= 0 && new_rank == 0) {
+        ok = out->MakeUniqueId(id, false);
+        const int32_t c = color;
+        mine.resize(sizeof(c) + sizeof(id));
+        std::memcpy(mine.data(), &c, sizeof(c));
+        std::memcpy(mine.data() + sizeof(c), &id, sizeof(id));
+    }
+    std::vector<std::vector<uint8_t>> ids;
+    if (!bootstrap_->AllGather(mine, &ids) || !ok) return false;
+    if (color < 0) return true;
+    bool found = false;
+    for (const auto& b : ids) {
+        int32_t c = -1;
+        if (b.size() != sizeof(c) + sizeof(id)) continue;
+        std::memcpy(&c, b.data(), sizeof(c));
+        if (c == color) {
+            std::memcpy(&id, b.data() + sizeof(c), sizeof(id));
+            found = true;
+        }
+    }
+    if (!found) return false;
+    CommConfig cfg = config_;
+    cfg.rank = new_rank;
+    cfg.world_size = static_cast<int>(members.size());
+    cfg.unique_id = id;
+    return out->Init(cfg);
 }
 
 bool Communicator::Init(const CommConfig& cfg) {

@@ -39,6 +39,9 @@ int bcclGetUniqueId(bcclComm_t comm, char ip_addr[64], uint16_t* port);
 int bcclCommInit(bcclComm_t comm, const bcclConfig* cfg);
 int bcclCommFinalize(bcclComm_t comm);
 int bcclCommDestroy(bcclComm_t comm);
+/* Collective (MPI_Comm_split): ranks with the same color >= 0 get a new communicator in *out,
+ * ranked by (key, rank); a negative color gets *out = NULL. */
+int bcclCommSplit(bcclComm_t comm, int color, int key, bcclComm_t* out);
 const char* bcclGetLastError(void);
 const char* bcclVersion(void);
 

@@ -46,6 +46,11 @@ public:
     bool GetUniqueId(UniqueId& unique_id);
     bool Init(const CommConfig& cfg);
     void Finalize();
+    // Collective over this communicator (like MPI_Comm_split / ncclCommSplit): the ranks that
+    // pass the same color >= 0 form a new communicator in *out, ranked by (key, rank); it has the
+    // same kind (host or device), channels and timeouts. A negative color joins none (*out is
+    // left untouched). This communicator stays usable.
+    bool Split(int color, int key, Communicator* out);
 
     int GetRank() const { return config_.rank; }
     int GetWorldSize() const { return config_.world_size; }
@@ -116,6 +121,7 @@ public:
     long DumpTrace(const char* path);
 
 private:
+    bool MakeUniqueId(UniqueId& unique_id, bool from_env);
     bool Flush();
 
     CommConfig config_;

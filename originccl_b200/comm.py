@@ -190,6 +190,23 @@ class Communicator:
         self.blocking = blocking
         return self
 
+    def split(self, color: int, key: Optional[int] = None) -> Optional["Communicator"]:
+        """Collective: the ranks passing the same ``color`` >= 0 form a new communicator, ranked
+        by (``key``, rank) (``key`` defaults to this rank); ``color`` < 0 returns None. The new
+        communicator has the same kind (device or host), channels and timeouts."""
+        out = ctypes.c_void_p()
+        self._check(self._lib.bcclCommSplit(self._h, int(color), int(self.rank if key is None else key),
+                                            ctypes.byref(out)))
+        if not out.value:
+            return None
+        child = Communicator.__new__(Communicator)
+        child._lib = self._lib
+        child._h = out
+        child._inited = True
+        child.device = self.device
+        child.blocking = self.blocking
+        return child
+
     def finalize(self) -> None:
         if self._h is not None:
             self._lib.bcclCommFinalize(self._h)

@@ -603,3 +603,30 @@ def run_fuzz(rank: int, world: int, seed: int, n_ops: int) -> Dict:
         keep.clear()
     comm.destroy()
     return {"checked": done, "algorithms": sorted(used)}
+
+
+def run_split_device(rank: int, world: int) -> Dict:
+    """Device communicators split like MPI_Comm_split: all ranks in one color (reversed), then
+    every rank alone; AllReduce runs in each child against the oracle."""
+    import torch
+
+    import originccl_b200 as occl
+    from originccl_b200 import ReduceOp
+
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    both = comm.split(0, key=-rank)
+    alone = comm.split(rank)
+    ins = [rank_input(r, 5000, "float32", seed=9) for r in range(world)]
+    x = ins[rank].cuda()
+    y = torch.empty_like(x)
+    both.all_reduce(x, ReduceOp.SUM, out=y)
+    _close(y, oracle("sum", ins, world), "float32", "split: all ranks")
+    alone.all_reduce(x, ReduceOp.SUM, out=y)
+    _close(y, ins[rank], "float32", "split: one rank")
+    res = {"both_rank": both.rank, "alone_size": alone.world_size}
+    alone.destroy()
+    both.destroy()
+    comm.destroy()
+    return res

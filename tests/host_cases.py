@@ -494,3 +494,33 @@ def run_bf16_fp16_torch(rank: int, world: int) -> Dict:
                 checked += 1
     comm.destroy()
     return {"checked": checked}
+
+
+def run_split(rank: int, world: int) -> Dict:
+    """Communicator.split: even and odd ranks form two communicators ranked in reverse order
+    (key = -rank); the last rank also tries a negative color in a second split and gets None;
+    collectives run in the children and the parent is still usable afterwards."""
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    child = comm.split(rank % 2, key=-rank)
+    members = sorted((r for r in range(world) if r % 2 == rank % 2), reverse=True)
+    assert child.world_size == len(members) and child.rank == members.index(rank)
+    x = np.full(1000, rank + 1.0, np.float32)
+    child.all_reduce(x)
+    assert np.all(x == sum(m + 1 for m in members))
+    g = np.empty(len(members) * 3, np.int32)
+    child.all_gather(g, np.full(3, rank, np.int32))
+    assert list(g[::3]) == members  # child rank order follows the key
+    solo = comm.split(-1 if rank == world - 1 else 0)
+    assert (solo is None) == (rank == world - 1)
+    if solo is not None:
+        y = np.ones(5, np.float64)
+        solo.all_reduce(y)
+        assert np.all(y == world - 1)
+        solo.destroy()
+    z = np.full(7, 1, np.int64)
+    comm.all_reduce(z)  # the parent still works
+    assert np.all(z == world)
+    child.destroy()
+    comm.destroy()
+    return {"child_rank": members.index(rank), "child_size": len(members)}

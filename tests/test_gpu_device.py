@@ -161,3 +161,12 @@ def test_random_device_operation_sequences(world):
     _need(world)
     res = _mp.run(world, gpu_cases.run_fuzz, 5 + world, 60, timeout=600)
     assert all(r["checked"] >= 30 for r in res)
+
+
+@pytest.mark.multigpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="device communicator split not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_split_device_communicators():
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_split_device, timeout=300)
+    assert [r["both_rank"] for r in res] == [1, 0] and all(r["alone_size"] == 1 for r in res)

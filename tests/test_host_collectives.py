@@ -103,3 +103,8 @@ def test_random_operation_sequences(world, machine, seed):
 def test_bf16_fp16_on_host_tensors():
     res = _mp.run(3, host_cases.run_bf16_fp16_torch, timeout=180)
     assert all(r["checked"] == 36 for r in res)
+
+
+def test_communicator_split():
+    res = _mp.run(5, host_cases.run_split, timeout=180)
+    assert [r["child_rank"] for r in res] == [2, 1, 1, 0, 0] and [r["child_size"] for r in res] == [3, 2, 3, 2, 3]
