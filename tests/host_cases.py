@@ -524,3 +524,23 @@ def run_split(rank: int, world: int) -> Dict:
     child.destroy()
     comm.destroy()
     return {"child_rank": members.index(rank), "child_size": len(members)}
+
+
+def run_mesh(rank: int, world: int, tp: int) -> Dict:
+    """parallel.Mesh: TP groups of consecutive ranks, DP groups of equal TP position; an
+    AllReduce in each sums exactly its members."""
+    from originccl_b200 import init_from_env
+    from originccl_b200.parallel import Mesh
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    mesh = Mesh(comm, tp=tp)
+    x = np.full(16, rank + 1.0, np.float64)
+    mesh.tp.all_reduce(x)
+    g0 = (rank // tp) * tp
+    assert np.all(x == sum(r + 1 for r in range(g0, g0 + tp)))
+    y = np.full(16, rank + 1.0, np.float64)
+    mesh.dp.all_reduce(y)
+    assert np.all(y == sum(r + 1 for r in range(rank % tp, world, tp)))
+    out = {"tp": (mesh.tp.rank, mesh.tp.world_size), "dp": (mesh.dp.rank, mesh.dp.world_size)}
+    mesh.destroy()
+    comm.destroy()
+    return out

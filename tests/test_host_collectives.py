@@ -108,3 +108,9 @@ def test_bf16_fp16_on_host_tensors():
 def test_communicator_split():
     res = _mp.run(5, host_cases.run_split, timeout=180)
     assert [r["child_rank"] for r in res] == [2, 1, 1, 0, 0] and [r["child_size"] for r in res] == [3, 2, 3, 2, 3]
+
+
+def test_tp_dp_mesh():
+    res = _mp.run(6, host_cases.run_mesh, 3, timeout=180)
+    assert [r["tp"] for r in res] == [(0, 3), (1, 3), (2, 3)] * 2
+    assert [r["dp"] for r in res] == [(0, 2)] * 3 + [(1, 2)] * 3
