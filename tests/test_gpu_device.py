@@ -128,8 +128,6 @@ def test_zero_copy_nvls_two_ranks():
     assert res[0].get("skipped") or res[0]["algorithms"] == ["nvls_zero_copy"]
 
 
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="CUDA-graph replay not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_cuda_graph_replay_single_rank():
     _need(1)
     res = _mp.run(1, gpu_cases.run_graph, timeout=300)
@@ -154,10 +152,10 @@ def test_registered_buffers_zero_copy_two_ranks():
     assert res[0]["algorithms"] == ["p2p_zero_copy"] and res[0]["small_algorithm"] == "oneshot"
 
 
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="random device sequences not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 @pytest.mark.parametrize("world", [1, 2])
 def test_random_device_operation_sequences(world):
+    if world > 1 and os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1":
+        pytest.skip("two-rank random device sequences not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
     _need(world)
     res = _mp.run(world, gpu_cases.run_fuzz, 5 + world, 60, timeout=600)
     assert all(r["checked"] >= 30 for r in res)

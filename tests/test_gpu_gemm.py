@@ -36,8 +36,6 @@ def test_gemm_matches_fp32_reference(m, n, k, act, kernel, monkeypatch):
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
 
 
-@pytest.mark.skipif(__import__("os").environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="224-wide 2-SM tiles not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 @pytest.mark.parametrize("m,n,k,act", [
     (256, 224, 64, None),        # one tile
     (300, 200, 136, "silu"),     # ragged in every dimension
