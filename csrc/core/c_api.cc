@@ -223,6 +223,11 @@ int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uint
     BCCL_SUBMIT(MakeTask(bccl::CollFunc::Recv, nullptr, buf, count, dtype, 0, 0, peer, 1.0f, 0));
 }
 
+int bcclCommGetAsyncError(bcclComm_t comm, int* code) {
+    if (comm == nullptr || code == nullptr) return Fail();
+    *code = comm->comm.AsyncError();
+    return 0;
+}
 int bcclSynchronize(bcclComm_t comm) { return comm && comm->comm.Synchronize() ? 0 : Fail(); }
 int bcclBarrier(bcclComm_t comm) { return comm && comm->comm.Barrier() ? 0 : Fail(); }
 int bcclCommAbort(bcclComm_t comm) {

@@ -469,6 +469,14 @@ void* Communicator::GetStream() const {
     return device_ ? static_cast<void*>(device_->internal_stream()) : nullptr;
 }
 
+int Communicator::AsyncError() const {
+    if (device_) {
+        const int code = device_->PeekDeviceError();
+        if (code != 0) return code;
+    }
+    return failed_ ? 1 : 0;
+}
+
 bool Communicator::Synchronize() {
     if (!device_) return true;
     cudaStream_t s = static_cast<cudaStream_t>(GetStream());

@@ -42,6 +42,9 @@ public:
     bool Execute(const std::vector<CollTask>& sorted, cudaStream_t stream);
     // Reads the host-mapped error record; false if any kernel reported a failure.
     bool CheckDeviceError();
+    // The host-mapped error record's code (kDevOk, kDevTimeout, kDevAborted, kDevBadArgs) as the
+    // kernels left it so far, without synchronising (ncclCommGetAsyncError's role).
+    int PeekDeviceError() const { return err_host_ ? static_cast<const volatile ErrorRecord*>(err_host_)->code : kDevOk; }
     bool Synchronize(cudaStream_t stream);
     void Abort();
     // Runs the bounded-wait self-test; returns the error code it recorded (kDevTimeout

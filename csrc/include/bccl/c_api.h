@@ -81,6 +81,9 @@ int bcclReduceScatter(bcclComm_t comm, const void* send, void* recv, size_t coun
 int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
 int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
 int bcclSynchronize(bcclComm_t comm);
+/* Without synchronising (like ncclCommGetAsyncError): *code = 0, or the failure a device kernel
+ * recorded so far (1 timeout, 2 aborted, 3 bad arguments; 1 after a failed host operation). */
+int bcclCommGetAsyncError(bcclComm_t comm, int* code);
 int bcclBarrier(bcclComm_t comm);
 /* Aborts the communicator's operations in flight; callable from any thread (like ncclCommAbort).
  * Host waits return at once, device waits within about a millisecond; afterwards only

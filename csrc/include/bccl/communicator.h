@@ -88,6 +88,9 @@ public:
     void ClearStream();
     void* GetStream() const;
     bool Synchronize();
+    // Without synchronising: 0, or the code a device kernel recorded (1 timeout, 2 aborted,
+    // 3 bad arguments); host communicators report 1 once a host operation has failed.
+    int AsyncError() const;
     // Device communicators: collective allocation of peer-addressable memory.
     void* SymmetricAlloc(size_t bytes);
     bool SymmetricFree(void* ptr);

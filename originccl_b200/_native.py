@@ -55,6 +55,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclCommInit": (c_int, [vp, ctypes.POINTER(BcclConfig)]),
         "bcclCommFinalize": (c_int, [vp]),
         "bcclCommDestroy": (c_int, [vp]),
+        "bcclCommGetAsyncError": (c_int, [vp, ctypes.POINTER(c_int)]),
         "bcclCommSplit": (c_int, [vp, c_int, c_int, ctypes.POINTER(vp)]),
         "bcclGetLastError": (ctypes.c_char_p, []),
         "bcclVersion": (ctypes.c_char_p, []),

@@ -416,6 +416,14 @@ class Communicator:
                     pass
 
     # ---------------------------------------------------------------- misc
+    def async_error(self) -> int:
+        """Without synchronising: 0, or the failure a device kernel has recorded so far (1 timeout,
+        2 aborted, 3 bad arguments); 1 after a failed host operation. For CUDA-graph replays and
+        other stream-ordered use, where no library call returns the error."""
+        code = ctypes.c_int(0)
+        self._check(self._lib.bcclCommGetAsyncError(self._h, ctypes.byref(code)))
+        return code.value
+
     def synchronize(self) -> None:
         self._check(self._lib.bcclSynchronize(self._h))
 

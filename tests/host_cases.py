@@ -283,6 +283,7 @@ def run_abort(rank: int, world: int) -> Dict:
     from originccl_b200 import BcclError, init_from_env
     comm = init_from_env(n_channels=2, timeout_ms=30000)
     elapsed = None
+    assert comm.async_error() == 0
     if rank == 0:
         x = np.ones(1 << 16, np.float32)
         timer = threading.Timer(0.3, comm.abort)
@@ -296,6 +297,7 @@ def run_abort(rank: int, world: int) -> Dict:
         elapsed = time.time() - t0
         timer.join()
         assert failed, "aborted AllReduce returned success"
+        assert comm.async_error() != 0  # the failure stays visible without another call
     comm.destroy()
     return {"elapsed": elapsed}
 
