@@ -32,3 +32,8 @@ def test_ddp_cuda_on_bccl_backend():
     for hook in (False, True):
         res = _mp.run(2, torch_backend_cases.run_ddp_cuda, hook, timeout=300)
         assert all(r["worst"] < 1e-4 for r in res)
+
+
+def test_subgroups_on_bccl_backend():
+    res = _mp.run(4, torch_backend_cases.run_subgroups, timeout=240)
+    assert [r["members"] for r in res] == [[0, 1], [0, 1], [2, 3], [2, 3]]

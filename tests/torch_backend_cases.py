@@ -127,3 +127,23 @@ def run_ddp_cuda(rank: int, world: int, hook: bool = False) -> Dict:
         h.close()
     dist.destroy_process_group()
     return {"worst": worst}
+
+
+def run_subgroups(rank: int, world: int) -> Dict:
+    """dist.new_group on the "bccl" backend: each subgroup gets its own communicators (the
+    group's prefixed store carries their unique ids) and collectives stay inside it."""
+    import torch
+    dist = _init(rank, world)
+    lo, hi = list(range(world // 2)), list(range(world // 2, world))
+    g_lo = dist.new_group(lo, backend="bccl")
+    g_hi = dist.new_group(hi, backend="bccl")
+    mine = g_lo if rank in lo else g_hi
+    members = lo if rank in lo else hi
+    x = torch.full((11,), float(rank + 1))
+    dist.all_reduce(x, group=mine)
+    assert torch.all(x == sum(r + 1 for r in members)), x[:3]
+    y = torch.full((3,), float(rank))
+    dist.all_reduce(y)  # the default group still spans everyone
+    assert torch.all(y == sum(range(world)))
+    dist.destroy_process_group()
+    return {"members": members}
