@@ -322,6 +322,24 @@ struct Checker {
         mem.Free(d);
     }
 
+    // Split: ranks of equal parity form a child communicator ranked in reverse (key = -rank);
+    // an AllReduce in the child sums exactly its members. Host buffers only.
+    void Split() {
+        if (mem.device) return;
+        Communicator child;
+        bool ok = comm->Split(rank % 2, -rank, &child);
+        int members = 0, expect = 0;
+        for (int r = rank % 2; r < world; r += 2) {
+            ++members;
+            expect += r + 1;
+        }
+        ok = ok && child.GetWorldSize() == members && child.GetRank() == (members - 1 - rank / 2);
+        int v = rank + 1;
+        ok = ok && child.AllReduce(&v, &v, 1, DataType::INT32, ReduceOp::SUM) && v == expect;
+        child.Finalize();
+        Record(ok, "split by parity");
+    }
+
     void Contract() {
         Record(comm->AllReduce(nullptr, nullptr, 0, DataType::FLOAT32, ReduceOp::SUM), "count 0 with null buffers");
         void* b = mem.Alloc(64);
@@ -548,6 +566,7 @@ int main(int argc, char** argv) {
             c.SendRecvRing(n);
         }
         c.SendRecvRing(300001);  // above the host path's single-copy threshold (256 KiB)
+        c.Split();
         c.Contract();
         int fails = c.failed, total_fail = 0;
         void* fb = mem.Alloc(sizeof(int));
