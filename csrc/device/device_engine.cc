@@ -98,6 +98,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_min_chunk_ = EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20);
     knob_pipe_debug_ = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
+    knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     dc_.data_bytes = data_bytes_;
     const long trace_cap = EnvInt("BCCL_TRACE", 0);
     if (trace_cap > 0) {
@@ -765,6 +766,24 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
             if (max_ctas_ > 0) c.ctas = std::min(c.ctas, max_ctas_);
             const long env_max = knob_max_ctas_;
             if (env_max > 0) c.ctas = std::min<int>(c.ctas, static_cast<int>(env_max));
+        }
+        // One rank, 1 MiB or more: every collective is a copy (times the AllReduce scale); a
+        // streaming copy kernel instead of the N-source push kernel.
+        if (nranks_ == 1 && knob_local_copy_ && bytes >= (1u << 20) && aligned16) {
+            if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+            const void* src = t.send_buf != nullptr ? t.send_buf : t.recv_buf;
+            const bool reducing = t.func == CollFunc::AllReduce || t.func == CollFunc::Reduce ||
+                                  t.func == CollFunc::ReduceScatter;
+            const float scale = reducing ? t.scale : 1.0f;
+            last_algo_ = "local_copy";
+            if (src == t.recv_buf && scale == 1.0f) continue;  // in place: nothing moves
+            cudaError_t e = LaunchLocalCopy(src, t.recv_buf, bytes, static_cast<int>(t.dtype), scale, num_sms_, stream);
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: local copy launch failed: %s", rank_, cudaGetErrorString(e));
+                return false;
+            }
+            launches_++;
+            continue;
         }
         if (nranks_ == 1 || c.algo == Algo::kOneShot || (c.algo == Algo::kRing && !ring)) {
             WorkItem w;

@@ -108,6 +108,7 @@ private:
     long knob_pipe_min_chunk_ = 4 << 20;
     int knob_pipe_debug_ = 0;
     long knob_pipe_kind_ = -1;
+    bool knob_local_copy_ = true;  // BCCL_LOCAL_COPY=0: one-rank collectives back on the push kernel
     const Planner* planner_ = nullptr;
     Bootstrap* bs_ = nullptr;
     SymmetricMemory sm_;

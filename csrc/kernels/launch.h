@@ -58,6 +58,11 @@ cudaError_t LaunchNvlsZeroCopy(const DevComm& c, int func, const void* send, voi
 cudaError_t LaunchP2pZeroCopy(const DevComm& c, int func, const char* const* in, char* const* out,
                               unsigned long long count, int dtype, int op, float scale, int nctas, cudaStream_t stream);
 
+// One-rank collective: dst = src, times `scale` for floating-point dtypes (1 = plain copy);
+// bytes and both pointers 16-byte aligned; grid sized for `sms` SMs.
+cudaError_t LaunchLocalCopy(const void* src, void* dst, unsigned long long bytes, int dtype, float scale, int sms,
+                            cudaStream_t stream);
+
 // Whether multimem.ld_reduce exists for (dtype, op) on this build.
 bool NvlsSupports(int dtype, int op);
 
