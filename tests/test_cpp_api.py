@@ -194,3 +194,12 @@ def test_perf_tool_device_one_gpu(op):
     assert r.returncode == 0, r.stdout + r.stderr
     recs = _json_lines(r.stdout)
     assert len(recs) >= 6 and all(x["check"] and x["path"] == "device" for x in recs)
+
+
+def test_launcher_tag_output():
+    r = _run(["-np", "3", "--tag-output", "--", "sh", "-c",
+              'echo out $BCCL_RANK; echo err $BCCL_RANK >&2; printf "tail $BCCL_RANK"'])
+    assert r.returncode == 0
+    out = sorted(r.stdout.splitlines())
+    assert out == sorted([f"[rank {q}] out {q}" for q in range(3)] + [f"[rank {q}] tail {q}" for q in range(3)])
+    assert sorted(r.stderr.splitlines()) == [f"[rank {q}] err {q}" for q in range(3)]
