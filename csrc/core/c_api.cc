@@ -9,6 +9,7 @@
 #include "core/planner.h"
 #include "device/device_engine.h"
 #include "kernels/gemm.h"
+#include "kernels/p2p_sched.h"
 
 #include <mutex>
 
@@ -325,6 +326,25 @@ int bcclGemmCheckError(void) {
     cudaMemcpy(&v, err, sizeof(int), cudaMemcpyDeviceToHost);
     cudaMemset(err, 0, sizeof(int));
     return v;
+}
+
+int bcclP2pChannels(unsigned long long pair_bytes) { return bccl::P2pChannels(pair_bytes); }
+
+int bcclP2pPlan(const unsigned long long* bytes, int nops, int nch, int ch, int max_out, int* op_out,
+                unsigned long long* off_out, unsigned long long* len_out) {
+    if (nops < 0 || nch < 1 || nch > bccl::kP2pMaxChannels || ch < 0 || ch >= nch || max_out < 0) return -1;
+    std::vector<bccl::P2pNativeOp> ops(static_cast<size_t>(nops));
+    for (int i = 0; i < nops; ++i) ops[i] = bccl::P2pNativeOp{nullptr, bytes[i]};
+    bccl::P2pCursor cur(0, nch, ch);
+    int n = 0, i = 0;
+    unsigned long long off = 0, len = 0;
+    while (n < max_out && cur.next(ops.data(), nops, &i, &off, &len)) {
+        op_out[n] = i;
+        off_out[n] = off;
+        len_out[n] = len;
+        ++n;
+    }
+    return n;
 }
 
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,

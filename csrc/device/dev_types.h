@@ -30,6 +30,19 @@ constexpr size_t kTpFlagsOff = 64u << 10;         // u64 flags of the fused tens
 constexpr size_t kTpFlagsBytes = 256u << 10;
 constexpr size_t kAlign = 256;
 
+// Native device Send/Recv (p2p_native.cu). Every directed pair (src -> dst) has kP2pMaxChannels
+// channels; a channel is one CTA on each side with kP2pSlots inbox slots of kP2pChunkBytes in
+// the receiver's P2P region, which follows the data region of the UC buffer.
+constexpr int kP2pMaxChannels = 8;
+constexpr int kP2pSlots = 4;
+constexpr size_t kP2pChunkBytes = 64u << 10;
+constexpr size_t kP2pBytesPerChannel = 256u << 10;  // one more channel per this many bytes of a pair
+constexpr size_t kP2pRegionBytes = static_cast<size_t>(kMaxRanks) * kP2pMaxChannels * kP2pSlots * kP2pChunkBytes;
+constexpr size_t kP2pPostedOff = 512u << 10;    // u64 [src][channel]: messages src posted into this rank's inbox
+constexpr size_t kP2pConsumedOff = 520u << 10;  // u64 [dst][channel]: messages dst consumed from this rank
+static_assert(kTpFlagsOff + kTpFlagsBytes <= kP2pPostedOff, "control region overlap");
+static_assert(kP2pConsumedOff + sizeof(uint64_t) * kMaxRanks * kP2pMaxChannels <= kCtrlBytes, "control region size");
+
 // Error codes written by kernels (host-mapped, read after the stream synchronises).
 enum DevError : int {
     kDevOk = 0,
@@ -59,6 +72,9 @@ struct DevState {
     unsigned int tp_done;
     unsigned int pad2;
     unsigned long long ring_seq;     // ring kernel: message numbers used so far (per CTA slot)
+    // Native Send/Recv: messages this rank sent to / received from each peer, per channel.
+    unsigned long long p2p_sent[kMaxRanks][kP2pMaxChannels];
+    unsigned long long p2p_recvd[kMaxRanks][kP2pMaxChannels];
 };
 
 // One device trace record (written when tracing is on): who did what, when.

@@ -58,7 +58,10 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
 
     data_bytes_ = cfg.buffer_bytes ? cfg.buffer_bytes : static_cast<size_t>(EnvInt("BCCL_BUFFSIZE", 512l << 20));
     data_bytes_ = std::max<size_t>(RoundUp(data_bytes_, 1u << 20), 4u << 20);
-    if (!sm_.Alloc(kCtrlBytes + data_bytes_, false, &uc_)) return false;
+    // Control region, data region, then the inboxes of the native Send/Recv.
+    if (!sm_.Alloc(kCtrlBytes + data_bytes_ + (nranks_ > 1 ? kP2pRegionBytes : 0), false, &uc_)) return false;
+    // Every flag starts at zero; no peer writes here before the barrier at the end of Init.
+    CUDA_OK(cudaMemset(uc_.ptr[rank_], 0, kCtrlBytes), "cudaMemset(control region)");
     if (sm_.multicast_supported()) {
         size_t nb = static_cast<size_t>(EnvInt("BCCL_NVLS_BUFFSIZE", 256l << 20));
         if (!sm_.Alloc(nb, true, &nvls_)) return false;
@@ -99,6 +102,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_debug_ = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
+    knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
     const long trace_cap = EnvInt("BCCL_TRACE", 0);
     if (trace_cap > 0) {
@@ -110,7 +114,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
         dc_.trace_cap = static_cast<unsigned int>(trace_cap);
     }
     CUDA_OK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
-    if (nranks_ > 1 && cfg.enable_nccl_p2p && !EnvFlag("BCCL_DISABLE_NCCL_P2P")) {
+    if (nranks_ > 1 && cfg.enable_nccl_p2p && !knob_p2p_native_ && !EnvFlag("BCCL_DISABLE_NCCL_P2P")) {
         if (!p2p_.Init(rank_, nranks_, bs)) LOG_WARN("rank %d: Send/Recv unavailable (NCCL init failed)", rank_);
     }
     if (!bs->Barrier()) return false;
@@ -806,9 +810,60 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
     }
     if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
     if (!p2p.empty()) {
+        if (knob_p2p_native_) return RunNativeP2p(p2p, stream);
         if (!p2p_.Run(p2p, stream)) return false;
         last_algo_ = "nccl_p2p";
     }
+    return true;
+}
+
+bool DeviceEngine::RunNativeP2p(const std::vector<CollTask>& tasks, cudaStream_t stream) {
+    // Operations grouped by (direction, peer), each pair's in the order the group issued them.
+    std::vector<P2pNativeOp> ops;
+    std::vector<P2pNativeRole> roles;
+    for (int dir = 0; dir < 2; ++dir) {
+        for (int q = 0; q < nranks_; ++q) {
+            if (q == rank_) continue;
+            const int begin = static_cast<int>(ops.size());
+            unsigned long long total = 0;
+            for (const CollTask& t : tasks) {
+                if (t.peer != q || t.count == 0 || (t.func == CollFunc::Send) != (dir == 0)) continue;
+                const unsigned long long b = static_cast<unsigned long long>(t.count) * DataTypeSize(t.dtype);
+                P2pNativeOp op;
+                op.buf = dir == 0 ? const_cast<char*>(static_cast<const char*>(t.send_buf)) : static_cast<char*>(t.recv_buf);
+                op.bytes = b;
+                ops.push_back(op);
+                total += b;
+            }
+            if (total == 0) continue;
+            const int nch = P2pChannels(total);
+            for (int ch = 0; ch < nch; ++ch) {
+                P2pNativeRole r;
+                r.peer = static_cast<short>(q);
+                r.dir = static_cast<short>(dir);
+                r.channel = static_cast<short>(ch);
+                r.nch = static_cast<short>(nch);
+                r.op_begin = begin;
+                r.op_end = static_cast<int>(ops.size());
+                roles.push_back(r);
+            }
+        }
+    }
+    if (roles.empty()) return true;
+    if (static_cast<int>(ops.size()) > kP2pMaxOps) {
+        LOG_ERROR("rank %d: native Send/Recv takes at most %d operations per group (got %zu)", rank_, kP2pMaxOps,
+                  ops.size());
+        return false;
+    }
+    dc_.kernel_serial = ++kernel_serial_;
+    cudaError_t e = LaunchP2pNative(dc_, ops.data(), static_cast<int>(ops.size()), roles.data(),
+                                    static_cast<int>(roles.size()), stream);
+    if (e != cudaSuccess) {
+        LOG_ERROR("rank %d: native Send/Recv launch failed: %s", rank_, cudaGetErrorString(e));
+        return false;
+    }
+    launches_++;
+    last_algo_ = "native_p2p";
     return true;
 }
 

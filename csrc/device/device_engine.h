@@ -91,6 +91,8 @@ public:
 
 private:
     bool FlushBatch(std::vector<WorkItem>* batch, unsigned long long* stream_bytes, cudaStream_t stream);
+    // Send/Recv of one group with the native kernel (p2p_native.cu).
+    bool RunNativeP2p(const std::vector<CollTask>& tasks, cudaStream_t stream);
     bool LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream);
 
     int rank_ = 0;
@@ -109,6 +111,7 @@ private:
     int knob_pipe_debug_ = 0;
     long knob_pipe_kind_ = -1;
     bool knob_local_copy_ = true;  // BCCL_LOCAL_COPY=0: one-rank collectives back on the push kernel
+    bool knob_p2p_native_ = false; // BCCL_P2P_NATIVE=1: Send/Recv on the native kernel instead of NCCL
     const Planner* planner_ = nullptr;
     Bootstrap* bs_ = nullptr;
     SymmetricMemory sm_;

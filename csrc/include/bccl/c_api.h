@@ -132,6 +132,13 @@ int bcclTpGemmReduceScatter(bcclComm_t comm, const void* h, const void* w, void*
 int bcclPlannerSort(int rank, int world, int n, const int* func, const size_t* count, const int* dtype, const int* op,
                     const int* root, const int* peer, int* order);
 int bcclPlannerP2pRound(int func, int rank, int peer, int world);
+/* Native device Send/Recv schedule hooks (used by tests). bcclP2pChannels: channels of a
+ * directed pair moving `pair_bytes` in one group. bcclP2pPlan: the chunks channel `ch` of `nch`
+ * carries for operations of sizes bytes[0..nops), in message order: operation index, byte offset
+ * and length of each (at most max_out); returns how many, or -1 on bad arguments. */
+int bcclP2pChannels(unsigned long long pair_bytes);
+int bcclP2pPlan(const unsigned long long* bytes, int nops, int nch, int ch, int max_out, int* op_out,
+                unsigned long long* off_out, unsigned long long* len_out);
 int bcclPlannerValidate(int rank, int world, int func, size_t count, int dtype, int op, int root, int peer,
                         int has_send, int has_recv);
 int bcclPlannerChoose(int func, int dtype, int op, size_t bytes, int world, int nvls_ok, int max_ctas, int* algo,

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "device/dev_types.h"
+#include "kernels/p2p_sched.h"
 
 namespace bccl {
 
@@ -57,6 +58,11 @@ cudaError_t LaunchNvlsZeroCopy(const DevComm& c, int func, const void* send, voi
 // every pointer 16-byte aligned.
 cudaError_t LaunchP2pZeroCopy(const DevComm& c, int func, const char* const* in, char* const* out,
                               unsigned long long count, int dtype, int op, float scale, int nctas, cudaStream_t stream);
+
+// Native Send/Recv of one group: one CTA per role (a channel of a directed pair), the pairs'
+// operations in ops (p2p_sched.h); at most kP2pMaxRoles roles and kP2pMaxOps operations.
+cudaError_t LaunchP2pNative(const DevComm& c, const P2pNativeOp* ops, int nops, const P2pNativeRole* roles,
+                            int nroles, cudaStream_t stream);
 
 // One-rank collective: dst = src, times `scale` for floating-point dtypes (1 = plain copy);
 // bytes and both pointers 16-byte aligned; grid sized for `sms` SMs.

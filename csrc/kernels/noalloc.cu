@@ -17,7 +17,7 @@ namespace {
 
 // Scratch layout: [DevState | ErrorRecord | abort word] in the first 256 bytes, then the
 // work list (BCCL_NOALLOC_MAX_ITEMS WorkItems).
-constexpr size_t kHeaderBytes = 256;
+constexpr size_t kHeaderBytes = 2048;
 static_assert(sizeof(DevState) + sizeof(ErrorRecord) + sizeof(int) <= kHeaderBytes, "scratch header too small");
 static_assert(kHeaderBytes + sizeof(WorkItem) * BCCL_NOALLOC_MAX_ITEMS <= BCCL_NOALLOC_SCRATCH_BYTES,
               "scratch array too small for the work list");

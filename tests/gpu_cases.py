@@ -154,6 +154,50 @@ def run_p2p(rank: int, world: int) -> Dict:
     return {"ok": True}
 
 
+def run_p2p_native(rank: int, world: int) -> Dict:
+    """Send/Recv on the native kernel (BCCL_P2P_NATIVE=1 in the environment): a ring exchange
+    and a both-ways exchange with every peer, several operations per pair (FIFO), odd and
+    unaligned sizes, sizes of many chunks, repeated so the per-channel counters carry over."""
+    import torch
+
+    import originccl_b200 as occl
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
+    nxt, prv = (rank + 1) % world, (rank - 1) % world
+    algos = set()
+    for it in range(3):
+        sizes = [1, 4097, (3 << 20) // 4 + 3, 65536 // 4]
+        outs = []
+        with comm.group():
+            for j, n in enumerate(sizes):
+                s = torch.arange(n, device="cuda", dtype=torch.float32) + 1000.0 * (rank * 10 + j) + it
+                r = torch.full((n,), -1.0, device="cuda")
+                comm.send(s, nxt)
+                comm.recv(r, prv)
+                outs.append((r, n, j))
+        algos.add(comm.last_algorithm)
+        for r, n, j in outs:
+            want = torch.arange(n, device="cuda", dtype=torch.float32) + 1000.0 * (prv * 10 + j) + it
+            assert torch.equal(r, want), (it, j)
+        # every peer both ways, bf16 at an odd element offset (2-byte aligned buffers)
+        base = torch.zeros(world * 70001 + 1, device="cuda", dtype=torch.bfloat16)
+        got = torch.full((world * 70001 + 1,), -1.0, device="cuda", dtype=torch.bfloat16)
+        for q in range(world):
+            base[1 + q * 70001:1 + (q + 1) * 70001] = float(rank * 8 + q)
+        with comm.group():
+            for q in range(world):
+                if q == rank:
+                    continue
+                comm.send(base[1 + q * 70001:1 + (q + 1) * 70001], q)
+                comm.recv(got[1 + q * 70001:1 + (q + 1) * 70001], q)
+        for q in range(world):
+            if q != rank:
+                assert torch.all(got[1 + q * 70001:1 + (q + 1) * 70001] == float(q * 8 + rank)).item(), (it, q)
+    comm.destroy()
+    return {"algorithms": sorted(algos)}
+
+
 def run_timeout_probe(rank: int, world: int) -> Dict:
     """Rank 1 never launches its collective; rank 0's bounded wait must expire and report an
     error status while the GPU context stays usable."""

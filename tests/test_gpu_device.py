@@ -63,6 +63,17 @@ def test_p2p_ring_over_nccl():
 
 
 @pytest.mark.multigpu
+@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
+                    reason="native Send/Recv kernel not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
+def test_p2p_native_kernel():
+    n = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _mp.run(n, gpu_cases.run_p2p_native, timeout=300, env={"BCCL_P2P_NATIVE": "1"})
+    assert res[0]["algorithms"] == ["native_p2p"]
+
+
+@pytest.mark.multigpu
 def test_bounded_wait_reports_timeout():
     _need(2)
     res = _mp.run(2, gpu_cases.run_timeout_probe, timeout=300, env={"NCCL_NVLS_ENABLE": "0"})
