@@ -6,6 +6,7 @@
  * writes "ip:port" to BCCL_ID_FILE (or every rank uses BCCL_MASTER when it is set), then every
  * rank runs an int32 AllReduce (SUM), a grouped AllGather + ReduceScatter (AVG) and a
  * Send/Recv around the ring on host memory, checks the results and prints one line. */
+#define _POSIX_C_SOURCE 200809L /* nanosleep under -std=c11 */
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
