@@ -50,24 +50,6 @@ struct PipeParams {
                 // 4 flip the warp-group split, 8 one-shot pulls instead of pushing
 };
 
-__device__ __forceinline__ void named_bar(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-// bar_id 0 = the whole CTA.
-__device__ __forceinline__ void sync_group(int bar_id, int nthreads) {
-    if (bar_id == 0) __syncthreads();
-    else named_bar(bar_id, nthreads);
-}
-__device__ __forceinline__ uint64_t ld_relaxed_gpu(const uint64_t* p) {
-    uint64_t v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_gpu(uint64_t* p, uint64_t v) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-
 
 // Group copy, `kUnroll` 16-byte vectors in flight per thread.
 __device__ __forceinline__ void grp_copy(char* d, const char* s, size_t bytes, int tid, int nt, bool cg) {
