@@ -15,7 +15,7 @@
 namespace bccl {
 namespace {
 
-// Scratch layout: [DevState | ErrorRecord | abort word] in the first 256 bytes, then the
+// Scratch layout: [DevState | ErrorRecord | abort word] in the first 2 KiB, then the
 // work list (BCCL_NOALLOC_MAX_ITEMS WorkItems).
 constexpr size_t kHeaderBytes = 2048;
 static_assert(sizeof(DevState) + sizeof(ErrorRecord) + sizeof(int) <= kHeaderBytes, "scratch header too small");
