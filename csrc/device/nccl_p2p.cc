@@ -101,7 +101,8 @@ void NcclP2p::Destroy() {
 bool NcclP2p::Run(const std::vector<CollTask>& tasks, cudaStream_t stream) {
     if (tasks.empty()) return true;
     if (comm_ == nullptr) {
-        LOG_ERROR("Send/Recv needs NCCL point-to-point, which is not initialised");
+        LOG_ERROR("Send/Recv needs NCCL point-to-point, which is not initialised "
+                  "(BCCL_P2P_NATIVE=1 runs it without NCCL)");
         return false;
     }
     ncclComm_t comm = static_cast<ncclComm_t>(comm_);
