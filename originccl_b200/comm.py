@@ -366,6 +366,28 @@ class Communicator:
         self._check(self._lib.bcclRecv(self._h, _ptr(tensor), _numel(tensor), int(_dtype_of(tensor)), int(peer), s, has))
         return tensor
 
+    def all_to_all(self, out: Any, tensor: Any, *, stream: Any = None) -> Any:
+        """out block q = block `rank` of rank q's tensor, where tensor and out (both contiguous,
+        world_size * n elements) are cut into world_size blocks of n: the exchange behind
+        expert-parallel dispatch and combine. One group of Send/Recv with every peer (on a device
+        communicator with BCCL_P2P_NATIVE=1 that is one kernel launch); the own block is copied
+        locally. The reference has no AllToAll (its collectives are the five of
+        OriginCCL include/types.h:30-38); this composes its Send/Recv semantics."""
+        w, r = self.world_size, self.rank
+        total = _numel(tensor)
+        if total % w != 0 or _numel(out) != total:
+            raise ValueError(f"all_to_all: tensor and out need world_size * n elements (got {total}, {_numel(out)})")
+        n = total // w
+        t, o = tensor.reshape(-1), out.reshape(-1)
+        o[r * n:(r + 1) * n] = t[r * n:(r + 1) * n]
+        if w > 1 and n > 0:
+            with self.group(stream):
+                for q in range(w):
+                    if q != r:
+                        self.send(t[q * n:(q + 1) * n], q, stream=stream)
+                        self.recv(o[q * n:(q + 1) * n], q, stream=stream)
+        return out
+
     def batch(self, tensors: Sequence[Any], outs: Optional[Sequence[Any]] = None) -> "TensorBatch":
         """Pointer arrays for :meth:`all_reduce_many`, built once for tensors that are synced often."""
         return TensorBatch(tensors, outs)

@@ -194,6 +194,13 @@ def run_p2p_native(rank: int, world: int) -> Dict:
         for q in range(world):
             if q != rank:
                 assert torch.all(got[1 + q * 70001:1 + (q + 1) * 70001] == float(q * 8 + rank)).item(), (it, q)
+    # all_to_all: one Send/Recv group with every peer
+    n = 3 * 65536 + 5
+    x = torch.cat([torch.full((n,), float(rank * 10 + q), device="cuda") for q in range(world)])
+    out = torch.empty_like(x)
+    comm.all_to_all(out, x)
+    want = torch.cat([torch.full((n,), float(q * 10 + rank), device="cuda") for q in range(world)])
+    assert torch.equal(out, want)
     comm.destroy()
     return {"algorithms": sorted(algos)}
 

@@ -498,6 +498,31 @@ def run_bf16_fp16_torch(rank: int, world: int) -> Dict:
     return {"checked": checked}
 
 
+def run_all_to_all(rank: int, world: int) -> Dict:
+    """Communicator.all_to_all: block q of every rank's input lands in block `rank` of rank q's
+    output, for empty, odd and multi-MiB blocks, float32 and int64, and a 2-D tensor."""
+    from originccl_b200 import init_from_env
+    comm = init_from_env(n_channels=2, timeout_ms=30000)
+    for n, dt in [(0, np.float32), (1, np.float32), (777, np.int64), ((1 << 20) + 3, np.float32)]:
+        x = np.concatenate([np.full(n, 1000 * rank + q, dt) for q in range(world)])
+        out = np.full(world * n, -1, dt)
+        comm.all_to_all(out, x)
+        want = np.concatenate([np.full(n, 1000 * q + rank, dt) for q in range(world)])
+        assert np.array_equal(out, want), n
+    x2 = np.arange(world * 6, dtype=np.int32).reshape(world * 2, 3) + 100 * rank
+    o2 = np.zeros_like(x2)
+    comm.all_to_all(o2, x2)
+    for q in range(world):
+        assert np.array_equal(o2.reshape(-1)[q * 6:(q + 1) * 6], np.arange(rank * 6, rank * 6 + 6) + 100 * q)
+    try:
+        comm.all_to_all(np.zeros(world * 2 + 1, np.float32), np.zeros(world * 2, np.float32))
+        raise AssertionError("mismatched output size accepted")
+    except ValueError:
+        pass
+    comm.destroy()
+    return {"ok": True}
+
+
 def run_split(rank: int, world: int) -> Dict:
     """Communicator.split: even and odd ranks form two communicators ranked in reverse order
     (key = -rank); the last rank also tries a negative color in a second split and gets None;

@@ -105,6 +105,11 @@ def test_bf16_fp16_on_host_tensors():
     assert all(r["checked"] == 36 for r in res)
 
 
+@pytest.mark.parametrize("world", [1, 3, 4])
+def test_all_to_all(world):
+    _mp.run(world, host_cases.run_all_to_all, timeout=180)
+
+
 def test_communicator_split():
     res = _mp.run(5, host_cases.run_split, timeout=180)
     assert [r["child_rank"] for r in res] == [2, 1, 1, 0, 0] and [r["child_size"] for r in res] == [3, 2, 3, 2, 3]
