@@ -164,11 +164,26 @@ class BcclProcessGroup(dist.ProcessGroup):
         return _done([])
 
     # ------------------------------------------------------------------ not in the reference
-    def alltoall_base(self, *args, **kwargs):
-        raise NotImplementedError("bccl: AllToAll is not provided (the reference has no AllToAll)")
+    def alltoall_base(self, output: torch.Tensor, input: torch.Tensor, output_split_sizes: List[int],
+                      input_split_sizes: List[int], opts=None):
+        """dist.all_to_all_single with equal splits (Communicator.all_to_all); uneven splits are
+        not provided."""
+        if output_split_sizes or input_split_sizes:
+            raise NotImplementedError("bccl: all_to_all_single takes equal splits only")
+        self._comm(input).all_to_all(output, input)
+        return _done([output])
 
-    def alltoall(self, *args, **kwargs):
-        raise NotImplementedError("bccl: AllToAll is not provided (the reference has no AllToAll)")
+    def alltoall(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor], opts=None):
+        """dist.all_to_all: inputs[q] to rank q, outputs[q] from rank q, as one Send/Recv group."""
+        comm = self._comm(inputs[0])
+        r = comm.rank
+        outputs[r].copy_(inputs[r])
+        with comm.group():
+            for q in range(comm.world_size):
+                if q != r:
+                    comm.send(inputs[q], q)
+                    comm.recv(outputs[q], q)
+        return _done(outputs)
 
     def gather(self, *args, **kwargs):
         raise NotImplementedError("bccl: gather is not provided")

@@ -12,7 +12,7 @@ pytest.importorskip("torch")
 @pytest.mark.parametrize("world", [2, 3])
 def test_torch_collectives_on_bccl_backend(world):
     res = _mp.run(world, torch_backend_cases.run_collectives, timeout=240)
-    assert all(r["alltoall_rejected"] for r in res)
+    assert all(r["uneven_alltoall_rejected"] for r in res)
 
 
 @pytest.mark.parametrize("hook", [False, True])

@@ -51,13 +51,20 @@ def run_collectives(rank: int, world: int) -> Dict:
             w.wait()
         assert torch.all(r == prv)
     dist.barrier()
+    a2a = torch.empty(world * 5)
+    dist.all_to_all_single(a2a, torch.arange(world * 5, dtype=torch.float32) + 100 * rank)
+    assert torch.equal(a2a, torch.cat([torch.arange(rank * 5, rank * 5 + 5, dtype=torch.float32) + 100 * q
+                                       for q in range(world)]))
+    outs = [torch.empty(2, dtype=torch.int64) for _ in range(world)]
+    dist.all_to_all(outs, [torch.full((2,), 10 * rank + q, dtype=torch.int64) for q in range(world)])
+    assert all(torch.all(o == 10 * q + rank) for q, o in enumerate(outs))
     try:
-        dist.all_to_all_single(torch.empty(world), torch.empty(world))
+        dist.all_to_all_single(torch.empty(world), torch.empty(world), [1] * world, [1] * world)
         raised = False
     except (NotImplementedError, RuntimeError):
         raised = True
     dist.destroy_process_group()
-    return {"alltoall_rejected": raised}
+    return {"uneven_alltoall_rejected": raised}
 
 
 def run_ddp(rank: int, world: int, hook: bool = False) -> Dict:
