@@ -4,13 +4,15 @@ One step = one out-of-place fp32 SUM AllReduce of ``--bytes`` per rank through t
 device communicator. Launch with N=1 as ``python bench.py``; for N>1 under torchrun (one rank per
 GPU). Rank 0 prints one JSON line:
 
-* ``value``: whole-job bus bandwidth, i.e. the NCCL bus bandwidth (algbw * 2(N-1)/N) summed over
-  the N ranks. For N=1 there is no bus (2(N-1)/N = 0): the single-rank AllReduce is a device
-  copy and ``value`` is its algbw, flagged in ``config.n1_semantics``.
+* ``value``: NCCL bus bandwidth per rank (algbw * 2(N-1)/N, time = max over ranks), the
+  convention the metric names; ``config.busbw_gbs_summed_over_ranks`` gives N times it. For N=1
+  there is no bus (2(N-1)/N = 0): the single-rank AllReduce is a device copy and ``value`` is its
+  algbw, flagged in ``config.n1_semantics``.
 * ``ms_per_step``: device time per AllReduce (CUDA events, max over ranks).
 * ``e2e``: the same metric through the public Python API with the step's input copied from
   pinned host memory and a sample of the result read back every step.
-* ``nccl``: the same op through torch.distributed (NCCL) on the same box, for comparison.
+* ``nccl``: the same op (out of place on the same rotating inputs, or in place with
+  ``--inplace``) through NCCL called directly on the same box, for comparison.
 
 ``--impl reference`` runs the reference's own code path; the reference is a CMake C++ project
 without a Python package and cannot be built on this image, so that arm prints an
@@ -28,8 +30,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 # Published busbw of the reference at 128 MiB, fp32 SUM, OCCL auto, 1 host x 4 ranks over shared
-# memory (README.md:223): 7.52 GB/s per rank, 30.08 GB/s summed over its 4 ranks.
-REFERENCE_WHOLE_JOB_GBS = 4 * 7.52
+# memory (README.md:223): 7.52 GB/s per rank.
+REFERENCE_BUSBW_GBS = 7.52
 
 REFERENCE_UNAVAILABLE = (
     "reference (qichen1336/OriginCCL) is a CPU-only CMake C++17 library with no setup.py/pyproject "
@@ -46,6 +48,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
+    p.add_argument("--inplace", action="store_true", help="in-place AllReduce (default: out of place)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-clocks", action="store_true", help="diagnostic: do not sample clocks (no clocks key)")
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
@@ -102,16 +105,34 @@ def main() -> None:
             comm.register(t_)
 
     def step(i: int) -> None:
-        comm.all_reduce(xs[i & 1], out=y)
+        if args.inplace:
+            comm.all_reduce(xs[i & 1])
+        else:
+            comm.all_reduce(xs[i & 1], out=y)
 
+    def reference_of(i: int):
+        """NCCL's fp32 AllReduce of step i's input (in-place steps change their input: only the
+        first step of each buffer is checked then)."""
+        ref = xs[i & 1].clone().float()
+        if world > 1:
+            dist.all_reduce(ref)
+        return ref
+
+    inputs0 = [x.clone() for x in xs] if args.inplace else None
+    check = reference_of(0) if args.warmup > 0 else None
     for i in range(args.warmup):
         step(i)
+        if i == 0 and check is not None:
+            torch.cuda.synchronize()
+            got = xs[0] if args.inplace else y
+            max_err = float((got.float() - check).abs().max().item())
     torch.cuda.synchronize()
-    # correctness of the last warm-up step against NCCL (fp32 accumulation of fp32 inputs)
-    check = xs[(args.warmup - 1) & 1].clone().float()
-    if world > 1:
-        dist.all_reduce(check)
-    max_err = float((y.float() - check).abs().max().item()) if args.warmup > 0 else 0.0
+    if args.inplace:  # restore the inputs the warm-up reduced in place
+        for x, x0 in zip(xs, inputs0):
+            x.copy_(x0)
+        del inputs0
+    if args.warmup == 0:
+        max_err = 0.0
 
     # Clocks of rank 0's GPU (NVML index = its position in CUDA_VISIBLE_DEVICES, if set).
     visible = [int(d) for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip().isdigit()]
@@ -134,30 +155,52 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
 
+    # The last timed step's output against NCCL's reduction of its input (out of place only:
+    # in-place steps feed each output into a later step).
+    last_err = None
+    if not args.inplace:
+        last_err = float((y.float() - reference_of(args.steps - 1)).abs().max().item())
+
     algbw = nbytes / (ms * 1e-3) / 1e9
     factor = busbw_factor("allreduce", world)
     busbw = algbw * factor
-    value = busbw * world if world > 1 else algbw
+    value = busbw if world > 1 else algbw
 
-    # NCCL (torch.distributed) on the same buffers, same timing rules.
+    # NCCL on the same buffers and the same op (out of place on the rotating inputs, or in
+    # place), called directly, with the same timing rules.
     nccl = None
     if world > 1 and not args.no_nccl:
-        yy = y.clone()
+        from originccl_b200.utils.nccl_direct import NcclDirect
+        ncomm = NcclDirect(dist.distributed_c10d._get_default_store(), rank, world, local, tag="bench")
+        saved = [x.clone() for x in xs] if args.inplace else None
+
+        def nstep(i: int) -> None:
+            if args.inplace:
+                ncomm.all_reduce(xs[i & 1], xs[i & 1])
+            else:
+                ncomm.all_reduce(xs[i & 1], y)
+
         for i in range(args.warmup):
-            yy.copy_(xs[i & 1]); dist.all_reduce(yy)
+            nstep(i)
         torch.cuda.synchronize()
-        # time only the all_reduce, in place on one buffer (the values do not affect the time)
         barrier(); torch.cuda.synchronize()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for i in range(args.steps):
-            dist.all_reduce(yy)
+            nstep(i)
         e2.record(); torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
         tn = torch.tensor([s2.elapsed_time(e2) / args.steps], dtype=torch.float64, device="cuda")
         dist.all_reduce(tn, op=dist.ReduceOp.MAX)
         nms = float(tn.item())
         nbus = nbytes / (nms * 1e-3) / 1e9 * factor
-        nccl = {"ms_per_step": round(nms, 4), "busbw_gbs_per_rank": round(nbus, 2), "value": round(nbus * world, 2)}
+        nccl = {"ms_per_step": round(nms, 4), "busbw_gbs_per_rank": round(nbus, 2),
+                "api": "ncclAllReduce (direct)", "inplace": args.inplace}
+        if saved is not None:
+            for x, x0 in zip(xs, saved):
+                x.copy_(x0)
+            del saved
+        torch.cuda.synchronize()
+        ncomm.destroy()
 
     # End to end through the public API: pinned H2D of this step's input, the collective, and a
     # device->host read of a 64 KiB sample of the result, every step (wall clock, max over ranks).
@@ -181,7 +224,7 @@ def main() -> None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
     e2e_algbw = nbytes / (e2e_ms * 1e-3) / 1e9
-    e2e_value = e2e_algbw * factor * world if world > 1 else e2e_algbw
+    e2e_value = e2e_algbw * factor if world > 1 else e2e_algbw
 
     # Clocks and throttle reasons under the same load: the same AllReduce loop for ~200 ms after
     # the measurements, sampled through NVML on rank 0's GPU. NVML queries during the timed loop
@@ -201,24 +244,26 @@ def main() -> None:
         out = {
             "metric": "AllReduce bus GB/s vs size at 2/4/8 B200 (max over ranks) vs reference & NCCL",
             "value": round(value, 2),
-            "unit": "GB/s (bus bandwidth summed over ranks)",
+            "unit": "GB/s (bus bandwidth per rank)" if world > 1 else "GB/s (algbw of a one-rank copy)",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(ms, 4),
             "higher_is_better": True,
             "scaling": "weak",
-            "vs_baseline": round(value / REFERENCE_WHOLE_JOB_GBS, 2),
+            "vs_baseline": round(value / REFERENCE_BUSBW_GBS, 2),
             "dtype": {"float32": "fp32", "bfloat16": "bf16"}[args.dtype],
             "buffers": args.buffers,
             "data": "synthetic (uniform [-1,1), seed 1234+rank)",
             "config": {
-                "model": f"AllReduce SUM out-of-place, {args.dtype}",
+                "model": f"AllReduce SUM {'in-place' if args.inplace else 'out-of-place'}, {args.dtype}",
                 "global_batch": world,
                 "seq_len": count,
                 "parallelism": f"dp{world}",
                 "bytes_per_rank": nbytes,
                 "busbw_gbs_per_rank": round(busbw, 2),
+                "busbw_gbs_summed_over_ranks": round(busbw * world, 2),
+                "inplace": args.inplace,
                 "algbw_gbs": round(algbw, 2),
                 "algorithm": comm.last_algorithm,
                 "buffers": args.buffers,
@@ -226,11 +271,12 @@ def main() -> None:
                 "l2": "inputs larger than L2: two rotating 128 MiB inputs + a 128 MiB output per rank",
                 "n1_semantics": ("N=1 has no bus (factor 2(N-1)/N = 0); value is the algbw of the single-rank "
                                  "AllReduce (a device copy)") if world == 1 else None,
-                "max_abs_err_vs_nccl": max_err,
-                "baseline_number": "reference 7.52 GB/s/rank x 4 ranks at 128 MiB fp32 (README.md:223)",
+                "max_abs_err_vs_nccl": {"first_warmup_step": max_err, "last_timed_step": last_err},
+                "baseline_number": "reference 7.52 GB/s busbw per rank, 4 ranks, 128 MiB fp32 (README.md:223)",
             },
             "nccl": nccl,
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s (bus bandwidth summed over ranks)",
+            "e2e": {"value": round(e2e_value, 2),
+                    "unit": "GB/s (bus bandwidth per rank)" if world > 1 else "GB/s (algbw of a one-rank copy)",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": nbytes,
                     "d2h_bytes_per_step": sample.numel() * esize, "steps": args.e2e_steps,
                     "api": "originccl_b200.Communicator.all_reduce"},

@@ -48,6 +48,7 @@ const DriverApi* Driver() {
         Load("cuMulticastGetGranularity", &api.cuMulticastGetGranularity);
         Load("cuTensorMapEncodeTiled", &api.cuTensorMapEncodeTiled);
         Load("cuMemGetAddressRange", &api.cuMemGetAddressRange);
+        Load("cuCtxGetCurrent", &api.cuCtxGetCurrent);
         api.loaded = ok;
         if (!ok) LOG_WARN("CUDA driver entry points unavailable (no driver?)");
     });

@@ -77,7 +77,10 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     int* abort_dev = nullptr;
     CUDA_OK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&err_dev), err_host_, 0), "cudaHostGetDevicePointer");
     CUDA_OK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&abort_dev), abort_host_, 0), "cudaHostGetDevicePointer");
-    CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    // A blocking stream: the synchronous API runs here, and a blocking stream starts its work
+    // only after what the caller queued on the legacy default stream, e.g. a pageable
+    // cudaMemcpy whose DMA may still be in flight when that call returns.
+    CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamDefault), "cudaStreamCreate");
 
     memset(&dc_, 0, sizeof(dc_));
     dc_.rank = rank_;
@@ -99,7 +102,6 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_slots_ = static_cast<int>(std::max<long>(3, std::min<long>(16, EnvInt("BCCL_PIPE_SLOTS", 3))));
     knob_pipe_rounds_ = EnvInt("BCCL_PIPE_ROUNDS", 0);
     knob_pipe_min_chunk_ = EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20);
-    knob_pipe_debug_ = static_cast<int>(EnvInt("BCCL_PIPE_DEBUG", 0));
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
@@ -305,7 +307,8 @@ int DeviceEngine::WaitProbe(int timeout_ms) {
 }
 
 double DeviceEngine::BandwidthProbe(int mode, int peer, size_t bytes, int ctas, int iters) {
-    if (!inited_ || peer < 0 || peer >= nranks_ || ctas <= 0 || ctas > 1024 || iters <= 0) return -1.0;
+    if (!inited_ || mode < 0 || mode > 3 || peer < 0 || peer >= nranks_ || ctas <= 0 || ctas > 1024 || iters <= 0)
+        return -1.0;
     cudaSetDevice(device_);
     // Both halves of the own data region serve as source/destination; the peer's data region
     // is the remote end. Probes must not overlap a collective on the peer.
@@ -322,20 +325,7 @@ double DeviceEngine::BandwidthProbe(int mode, int peer, size_t bytes, int ctas, 
         dst = nvls_.mc;
         mc = true;
     }
-    // Modes 4..9: fence-cost probe over a peer write (4-6) or a local copy (7-9) with a fence
-    // every `seg` bytes per CTA; seg is taken from BCCL_PROBE_SEG (default 256 KiB).
-    const bool fence_probe = mode >= 4;
-    const int fmode = fence_probe ? (mode - 4) % 3 : 0;
-    const size_t seg = static_cast<size_t>(EnvInt("BCCL_PROBE_SEG", 256 << 10));
-    if (fence_probe) {
-        src = mine;
-        dst = mode <= 6 ? theirs : mine + data_bytes_ / 2;
-        bytes = RoundDown(bytes, seg);
-    }
-    auto launch = [&]() {
-        if (fence_probe) LaunchFenceProbe(dst, src, bytes, seg, fmode, ctas, stream_);
-        else LaunchBandwidthProbe(dst, src, bytes, mc, ctas, stream_);
-    };
+    auto launch = [&]() { LaunchBandwidthProbe(dst, src, bytes, mc, ctas, stream_); };
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
@@ -606,7 +596,6 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         want = std::max<unsigned long long>(want, RoundUp(min_chunk, q));
         return std::max<unsigned long long>(q, std::min<unsigned long long>(want, RoundDown(cap, q)));
     };
-    const int debug = knob_pipe_debug_;
     int ctas = c.ctas;
     dc_.kernel_serial = ++kernel_serial_;
     if (c.algo == Algo::kRing) {
@@ -621,7 +610,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         const unsigned long long chunk = pick_chunk(slot);
         if (t.func == CollFunc::AllReduce) {
             e = LaunchAllReducePipe(dc_, kPipeNvls, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots,
-                                    ctas, stream, debug);
+                                    ctas, stream);
         } else {
             e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale,
                            chunk, slot, slots, ctas, stream);
@@ -643,7 +632,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
             chunk = pick_chunk(slot * nranks_);
         }
         e = LaunchAllReducePipe(dc_, kind, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots, ctas,
-                                stream, debug);
+                                stream);
         last_algo_ = kind == kPipeOneShot ? "oneshot_pipe" : "twoshot";
     }
     if (e != cudaSuccess) {

@@ -108,7 +108,6 @@ private:
     int knob_pipe_slots_ = 3;
     long knob_pipe_rounds_ = 0;  // 0: by size
     long knob_pipe_min_chunk_ = 4 << 20;
-    int knob_pipe_debug_ = 0;
     long knob_pipe_kind_ = -1;
     bool knob_local_copy_ = true;  // BCCL_LOCAL_COPY=0: one-rank collectives back on the push kernel
     bool knob_p2p_native_ = false; // BCCL_P2P_NATIVE=1: Send/Recv on the native kernel instead of NCCL

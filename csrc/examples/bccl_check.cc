@@ -265,6 +265,31 @@ struct Checker {
         mem.Free(d);
     }
 
+    // Inputs staged with a plain (pageable) copy right before each call, new values every
+    // iteration: a pageable host-to-device cudaMemcpy may return before its DMA lands, so a
+    // collective that is not ordered after the caller's default-stream work reads stale input.
+    void StagedLoop(size_t n, int iters) {
+        std::vector<float> in(n), out(n);
+        void* s = mem.Alloc(n * sizeof(float));
+        void* d = mem.Alloc(n * sizeof(float));
+        bool ok = s != nullptr && d != nullptr;
+        for (int it = 0; ok && it < iters; ++it) {
+            for (size_t i = 0; i < n; ++i) in[i] = Value<float>(rank + 3 * it, i);
+            mem.Put(s, in.data(), n * sizeof(float));
+            ok = comm->AllReduce(s, d, n, DataType::FLOAT32, ReduceOp::SUM);
+            ok = ok && comm->AllReduce(d, d, n, DataType::FLOAT32, ReduceOp::MAX);  // in place as well
+            mem.Get(out.data(), d, n * sizeof(float));
+            for (size_t i = 0; ok && i < n; ++i) {
+                std::vector<float> xs(world);
+                for (int r = 0; r < world; ++r) xs[r] = Value<float>(r + 3 * it, i);
+                ok = out[i] == Reduce<float>(ReduceOp::SUM, xs, world);
+            }
+        }
+        Record(ok, "staged inputs n=" + std::to_string(n) + " x" + std::to_string(iters));
+        mem.Free(s);
+        mem.Free(d);
+    }
+
     // A nested group of four independent collectives; only the outer GroupEnd runs them.
     void Group(size_t n) {
         std::vector<void*> bufs;
@@ -566,6 +591,8 @@ int main(int argc, char** argv) {
             c.SendRecvRing(n);
         }
         c.SendRecvRing(300001);  // above the host path's single-copy threshold (256 KiB)
+        c.StagedLoop(32768 + 3, 8);
+        c.StagedLoop((1u << 18) + 3, 8);  // 1 MiB + 12 bytes
         c.Split();
         c.Contract();
         int fails = c.failed, total_fail = 0;

@@ -23,7 +23,8 @@
  *   - the array exists once per device and every GPU that loads the library holds it until
  *     the process exits;
  *   - the first call on a device looks up the array's device address for that device (with
- *     the device current) and caches it;
+ *     the device current) and caches it; make that first call before any stream capture
+ *     begins on the device. After a cudaDeviceReset the next call looks the address up again;
  *   - all calls on a device share the one array, which keeps the previous call's contents
  *     (the call clears what must start at zero): calls that overlap on the GPU -- on
  *     different streams without ordering between them -- race on the array and must not be

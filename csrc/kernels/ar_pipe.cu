@@ -46,8 +46,6 @@ struct PipeParams {
     int op;
     float scale;
     int nvls;   // PipeKind
-    int debug;  // BCCL_PIPE_DEBUG bits (experiments): 1 no system fence before the barrier flags,
-                // 4 flip the warp-group split, 8 one-shot pulls instead of pushing
 };
 
 
@@ -318,13 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
     const int kind = p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
-    const bool sysf = (p.debug & 1) == 0;
-    // One-shot data flow: push (A stores into every peer's inbox) or, with debug bit 8, pull
-    // (A copies into this rank's own slot, B loads the peers' slots over NVLink).
-    const bool pull = (p.debug & 8) != 0;
     // Warp groups run their phases concurrently for NVLS (two local copies against one switch
-    // phase); for the push kinds a single group measured faster (BCCL_PIPE_DEBUG bit 4 flips it).
-    const bool split = (kind == kPipeNvls) != ((p.debug & 4) != 0);
+    // phase); for the push kinds a single group measured faster.
+    const bool split = kind == kPipeNvls;
     const uint64_t bar0 = load_state_u64(&c.state->barrier_seq);
     const uint64_t round0 = kind == kPipeNvls ? load_state_u64(&c.state->nvls_round_seq)
                                               : load_state_u64(&c.state->round_seq);
@@ -358,16 +352,11 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         const int slot = (int)((round0 + (uint64_t)j) % (uint64_t)S);
         if (kind == kPipeOneShot) {
             if (s0 < s1) {
-                if (pull) {  // stage into this rank's own slot; the peers read it over NVLink
-                    grp_copy(ts_region(c, r) + ((size_t)slot * n + r) * sb + s0, src + cbeg + s0, s1 - s0, tid, nt,
-                             false);
-                } else {
-                    char* outs[kMaxRanks];
-                    int no = 0;
-                    for (int q = 0; q < n; ++q)
-                        if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
-                    if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
-                }
+                char* outs[kMaxRanks];
+                int no = 0;
+                for (int q = 0; q < n; ++q)
+                    if (q != r) outs[no++] = ts_region(c, q) + ((size_t)slot * n + r) * sb + s0;
+                if (no > 0) grp_push_multi(outs, no, src + cbeg + s0, s1 - s0, tid, nt);
             }
         } else if (kind == kPipeTwoShot) {
             for (int q = 0; q < n; ++q) {
@@ -393,8 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
                 const char* srcs[kMaxRanks];
                 char* mine = ts_region(c, r);
                 for (int q = 0; q < n; ++q) {
-                    srcs[q] = (q == r) ? src + cbeg + s0
-                                       : (pull ? ts_region(c, q) : mine) + ((size_t)slot * n + q) * sb + s0;
+                    srcs[q] = (q == r) ? src + cbeg + s0 : mine + ((size_t)slot * n + q) * sb + s0;
                 }
                 char* outs[1] = {dst + cbeg + s0};
                 grp_reduce_multi<D, O>(outs, 1, srcs, n, r, s1 - s0, tid, nt, n, p.scale);
@@ -463,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         if (threadIdx.x == 0) trace(c, 0, kTrStaged, t);  // this CTA's phases of iteration t are issued
         const int tid = threadIdx.x;
         if (tid < n && tid != r) {
-            if (sysf) fence_acq_rel_sys();
+            fence_acq_rel_sys();
             st_relaxed_sys_flag(barrier_flag(c.uc[tid], blockIdx.x, r), bar0 + (uint64_t)t + 1);
             ok = wait_flag_geq(c, barrier_flag(c.uc[r], blockIdx.x, tid), bar0 + (uint64_t)t + 1, tid, t);
         }
@@ -497,7 +485,7 @@ cudaError_t launch_op(const PipeParams& p, int nctas, cudaStream_t s) {
 
 cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
                                 int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
-                                int nslots, int nctas, cudaStream_t stream, int debug) {
+                                int nslots, int nctas, cudaStream_t stream) {
     using namespace dev;
     const bool nvls = kind == kPipeNvls;
     if (nctas < 1 || nctas > kMaxCtas || nslots < 3 || chunk == 0 || (chunk % (16ull * c.nranks)) != 0) {
@@ -527,7 +515,6 @@ cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, voi
     p.op = op;
     p.scale = scale;
     p.nvls = kind == kPipeNvls ? 1 : (kind == kPipeOneShot ? 2 : 0);
-    p.debug = debug;
     // f32 MAX/MIN and f64 MAX/MIN have no multimem form; they only reach here for TWOSHOT.
     switch (dtype) {
     case kF32: return launch_op<kF32>(p, nctas, stream);

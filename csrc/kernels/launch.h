@@ -21,7 +21,7 @@ cudaError_t LaunchPushEngine(const DevComm& c, const WorkItem* items, int nitems
 enum PipeKind : int { kPipeTwoShot = 0, kPipeNvls = 1, kPipeOneShot = 2 };
 cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
                                 int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
-                                int nslots, int nctas, cudaStream_t stream, int debug = 0);
+                                int nslots, int nctas, cudaStream_t stream);
 
 // NVSwitch multicast Broadcast (func 1) and Reduce (func 2) over the NVLS slot ring.
 cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, unsigned long long count, int dtype,
@@ -34,11 +34,6 @@ cudaError_t LaunchWaitProbe(const DevComm& c, unsigned long long timeout_ns, cud
 // Copy-bandwidth probe over local, peer or multicast addresses.
 cudaError_t LaunchBandwidthProbe(void* dst, const void* src, unsigned long long bytes, bool multicast, int nctas,
                                  cudaStream_t stream);
-
-// Fence-cost probe: copy in `seg`-byte segments per CTA with a fence after each (mode 0 none,
-// 1 fence.acq_rel.sys, 2 fence.acq_rel.gpu).
-cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long bytes, unsigned long long seg, int mode,
-                             int nctas, cudaStream_t stream);
 
 // Ring AllReduce between neighbours (reduce-scatter then all-gather), `block` bytes per message
 // (multiple of 256), at most max_ctas channels.

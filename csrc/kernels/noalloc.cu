@@ -10,6 +10,7 @@
 #include "bccl/noalloc.h"
 #include "bccl/types.h"
 #include "core/logger.h"
+#include "device/cuda_driver.h"
 #include "kernels/push_engine.cuh"
 
 namespace bccl {
@@ -26,20 +27,31 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[BCCL_NOALLOC_SC
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_scratch_addr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch per device, and the context it was looked up in: a
+// cudaDeviceReset destroys the primary context and reloads the module at another address, so a
+// different current context means the cached address is stale.
+void* g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Once per device, with that device current: the array's name in host code is only a
-// host-side stand-in, so the device address comes from cudaGetSymbolAddress.
+// Once per device (and again after a context change), with that device current: the array's
+// name in host code is only a host-side stand-in, so the device address comes from
+// cudaGetSymbolAddress.
 void* ScratchFor(int device) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (g_scratch_addr[device] == nullptr) {
+    CUcontext ctx = nullptr;
+    const DriverApi* drv = Driver();
+    if (drv != nullptr && drv->cuCtxGetCurrent != nullptr) drv->cuCtxGetCurrent(&ctx);
+    if (g_scratch_addr[device] == nullptr || ctx != g_scratch_ctx[device]) {
         void* ptr = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess || ptr == nullptr) {
             LOG_ERROR("noalloc: cudaGetSymbolAddress failed on device %d: %s", device, cudaGetErrorString(e));
             return nullptr;
         }
+        // The runtime makes the primary context current in that call; record that one.
+        if (drv != nullptr && drv->cuCtxGetCurrent != nullptr) drv->cuCtxGetCurrent(&ctx);
         g_scratch_addr[device] = ptr;
+        g_scratch_ctx[device] = ctx;
     }
     return g_scratch_addr[device];
 }
@@ -107,7 +119,9 @@ extern "C" int bcclLocalAllReduceNoAlloc(const void* const* srcs, void* const* d
     if (m == 0) return 0;
 
     // The counters, the error record and the abort word must start at zero on every call
-    // (the array keeps the previous call's contents); the work list is copied behind them.
+    // (the array keeps the previous call's contents); the work list is copied behind them. The
+    // list is built in host memory on this stack frame; an asynchronous copy from pageable
+    // memory takes its bytes into the driver's staging memory before it returns.
     cudaError_t e = cudaMemsetAsync(scratch, 0, kHeaderBytes, stream);
     if (e == cudaSuccess) {
         e = cudaMemcpyAsync(scratch + kHeaderBytes, items, sizeof(WorkItem) * static_cast<size_t>(m),

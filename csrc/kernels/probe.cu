@@ -42,43 +42,8 @@ __global__ void __launch_bounds__(512, 1) bw_probe_kernel(char* dst, const char*
     for (; i < nv; i += stride) st_cg(dst + (i << 4), ld_cg(src + (i << 4)));
 }
 
-// Fence-cost probe: each CTA copies contiguous segments of `seg` bytes and, after each
-// segment, one thread issues fence.acq_rel.sys (mode 1), fence.acq_rel.gpu (mode 2) or
-// nothing (mode 0) before the CTA continues.
-__global__ void __launch_bounds__(512, 1) fence_probe_kernel(char* dst, const char* src, size_t bytes, size_t seg,
-                                                              int mode) {
-    const size_t nseg = bytes / seg;
-    for (size_t sgi = blockIdx.x; sgi < nseg; sgi += gridDim.x) {
-        const char* s = src + sgi * seg;
-        char* d = dst + sgi * seg;
-        const size_t nv = seg >> 4;
-        size_t i = threadIdx.x;
-        for (; i + 3 * blockDim.x < nv; i += 4 * blockDim.x) {
-            uint4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = ld_cg(s + ((i + u * blockDim.x) << 4));
-#pragma unroll
-            for (int u = 0; u < 4; ++u) st_cg(d + ((i + u * blockDim.x) << 4), v[u]);
-        }
-        for (; i < nv; i += blockDim.x) st_cg(d + (i << 4), ld_cg(s + (i << 4)));
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            if (mode == 1) fence_acq_rel_sys();
-            if (mode == 2) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        }
-        __syncthreads();
-    }
-}
-
 }  // namespace
 }  // namespace dev
-
-cudaError_t LaunchFenceProbe(void* dst, const void* src, unsigned long long bytes, unsigned long long seg, int mode,
-                             int nctas, cudaStream_t stream) {
-    dev::fence_probe_kernel<<<nctas, 512, 0, stream>>>(static_cast<char*>(dst), static_cast<const char*>(src), bytes,
-                                                       seg, mode);
-    return cudaGetLastError();
-}
 
 cudaError_t LaunchBandwidthProbe(void* dst, const void* src, unsigned long long bytes, bool multicast, int nctas,
                                  cudaStream_t stream) {

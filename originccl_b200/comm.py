@@ -311,6 +311,11 @@ class Communicator:
             if torch.cuda.is_current_stream_capturing():
                 raise BcclError("a blocking communicator runs on its own stream and waits on the host, so it "
                                 "cannot be captured into a CUDA graph; use a stream-ordered one (blocking=False)")
+            # The library's stream is ordered after the legacy default stream only; torch may have
+            # written the inputs on another stream of this device.
+            cur = torch.cuda.current_stream(self.device)
+            if cur.cuda_stream != 0:
+                cur.synchronize()
             return 0, 0
         if stream is None:
             return _current_raw_stream(self.device), 1

@@ -35,7 +35,7 @@ def parse_size(s: str) -> int:
 
 def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, factor: int = 2, warmup: int = 20,
               iters: int = 100, algo: str = "auto", inplace: bool = False, nccl: bool = True, redop: str = "sum",
-              seed: int = 1234, emit=print, graph: int = 0, buffers: str = "plain") -> list:
+              seed: int = 1234, emit=print, graph: int = 0, buffers: str = "plain", ref_comm=None) -> list:
     """Times ``op`` at every size from min_bytes to max_bytes (x factor) with this library and
     with NCCL on the same buffers; returns (and emits on rank 0) one record per size.
 
@@ -44,7 +44,9 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
     the host's launch path, as nccl-tests' ``-G`` does. ``buffers`` = ``"registered"`` registers
     this library's buffers with the communicator (zero-copy over peer memory) and
     ``"symmetric"`` allocates them in symmetric memory (zero-copy NVLS); NCCL uses plain copies
-    of them."""
+    of them. ``ref_comm`` (a ``utils.nccl_direct.NcclDirect``) times NCCL on exactly the same
+    operation, out of place or in place like this library's; without it the NCCL arm goes through
+    torch.distributed, whose collectives are in place."""
     import torch
     import torch.distributed as dist
     from originccl_b200 import Algo, ReduceOp
@@ -115,25 +117,31 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
             for t_ in ({id(x): x, id(y): y}).values():
                 comm.register(t_)
                 registered.append(t_)
+        rc = ref_comm
         if op == "allreduce":
             ours = lambda: comm.all_reduce(x, rop, out=y, algo=algo_v)  # noqa: E731
-            ref = lambda: dist.all_reduce(y, op=nccl_op)  # noqa: E731
+            ref = ((lambda: rc.all_reduce(x, y, redop)) if rc is not None  # noqa: E731
+                   else (lambda: dist.all_reduce(y, op=nccl_op)))
             nbytes = n * es
         elif op == "allgather":
             ours = lambda: comm.all_gather(y, x)  # noqa: E731
-            ref = lambda: dist.all_gather_into_tensor(y, x)  # noqa: E731
+            ref = ((lambda: rc.all_gather(x, y)) if rc is not None  # noqa: E731
+                   else (lambda: dist.all_gather_into_tensor(y, x)))
             nbytes = n * es * world
         elif op == "reducescatter":
             ours = lambda: comm.reduce_scatter(y, x, rop)  # noqa: E731
-            ref = lambda: dist.reduce_scatter_tensor(y, x, op=nccl_op)  # noqa: E731
+            ref = ((lambda: rc.reduce_scatter(x, y, redop)) if rc is not None  # noqa: E731
+                   else (lambda: dist.reduce_scatter_tensor(y, x, op=nccl_op)))
             nbytes = n * es * world
         elif op == "broadcast":
             ours = lambda: comm.broadcast(y, 0, src=x if rank == 0 else None, algo=algo_v)  # noqa: E731
-            ref = lambda: dist.broadcast(y, 0)  # noqa: E731
+            ref = ((lambda: rc.broadcast(x, y, 0)) if rc is not None  # noqa: E731
+                   else (lambda: dist.broadcast(y, 0)))
             nbytes = n * es
         else:
             ours = lambda: comm.reduce(x, 0, rop, out=y, algo=algo_v)  # noqa: E731
-            ref = lambda: dist.reduce(y, 0, op=nccl_op)  # noqa: E731
+            ref = ((lambda: rc.reduce(x, y, 0, redop)) if rc is not None  # noqa: E731
+                   else (lambda: dist.reduce(y, 0, op=nccl_op)))
             nbytes = n * es
         ok = _check(comm, op, x, rop, nccl_op, dtype)
         t_ours = timed(ours)
@@ -143,7 +151,7 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
         rec = {"op": op, "dtype": dtype, "redop": redop, "bytes": n * es, "ranks": world, "algo": used,
                "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
                "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok,
-               "graph": graph, "buffers": buffers}
+               "graph": graph, "buffers": buffers, "nccl_api": "direct" if rc is not None else "torch.distributed"}
         if t_nccl is not None:
             rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
                         "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
@@ -209,7 +217,8 @@ def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--op", default="allreduce",
                    choices=["allreduce", "allgather", "reducescatter", "broadcast", "reduce"])
-    p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16", "float16", "int32"])
+    p.add_argument("--dtype", default="float32",
+                   help="comma list of float32, bfloat16, float16, int32 (each swept in turn)")
     p.add_argument("--redop", default="sum", choices=["sum", "max", "min", "avg"])
     p.add_argument("--min-bytes", default="8")
     p.add_argument("--max-bytes", default="1G")
@@ -218,10 +227,14 @@ def main(argv=None) -> None:
     p.add_argument("--iters", type=int, default=100)
     p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring"])
     p.add_argument("--inplace", action="store_true")
+    p.add_argument("--both-places", action="store_true", help="sweep out of place, then in place")
     p.add_argument("--no-nccl", action="store_true")
     p.add_argument("--out", default="", help="also append the records to this JSON-lines file")
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
                    help="this library's buffers: plain tensors, registered tensors or symmetric memory")
+    p.add_argument("--nccl-api", default="direct", choices=["direct", "torch"],
+                   help="NCCL arm: ncclAllReduce & co. called directly on the same op (default) or "
+                        "torch.distributed (in place)")
     p.add_argument("--graph", type=int, default=0,
                    help="capture this many calls per CUDA graph and time replays (0: eager calls)")
     args = p.parse_args(argv)
@@ -240,10 +253,25 @@ def main(argv=None) -> None:
     from originccl_b200.utils.results import ResultLog
     log = ResultLog("sweep", args.out, enabled=rank == 0)
 
-    run_sweep(comm, op=args.op, dtype=args.dtype, min_bytes=parse_size(args.min_bytes),
-              max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup, iters=args.iters,
-              algo=args.algo, inplace=args.inplace, nccl=not args.no_nccl, redop=args.redop, emit=log, graph=args.graph, buffers=args.buffers)
+    ref_comm = None
+    if not args.no_nccl and args.nccl_api == "direct":
+        from originccl_b200.utils.nccl_direct import NcclDirect
+        ref_comm = NcclDirect(dist.distributed_c10d._get_default_store(), rank, world, local, tag="sweep")
+    dtypes = [d.strip() for d in args.dtype.split(",") if d.strip()]
+    for d in dtypes:
+        if d not in ("float32", "bfloat16", "float16", "int32"):
+            raise SystemExit(f"unsupported dtype {d}")
+    places = [False, True] if args.both_places else [args.inplace]
+    for d in dtypes:
+        for inplace in places:
+            run_sweep(comm, op=args.op, dtype=d, min_bytes=parse_size(args.min_bytes),
+                      max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup,
+                      iters=args.iters, algo=args.algo, inplace=inplace, nccl=not args.no_nccl, redop=args.redop,
+                      emit=log, graph=args.graph, buffers=args.buffers, ref_comm=ref_comm)
     log.close()
+    if ref_comm is not None:
+        torch.cuda.synchronize()
+        ref_comm.destroy()
     comm.destroy()
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()

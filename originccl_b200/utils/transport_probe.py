@@ -24,8 +24,6 @@ def main(argv=None) -> None:
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--all-ranks", action="store_true",
                    help="every rank probes at the same time (rank r targets rank r+1): bidirectional traffic")
-    p.add_argument("--fences", action="store_true",
-                   help="measure the cost of a fence every BCCL_PROBE_SEG bytes per CTA instead")
     args = p.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -45,9 +43,6 @@ def main(argv=None) -> None:
     nbytes = parse_size(args.bytes)
     peer = (rank + 1) % world if args.all_ranks else (1 if world > 1 else 0)
     modes = {0: "local_copy", 1: "peer_write", 2: "peer_read", 3: "multimem_st"}
-    if args.fences:
-        modes = {4: "peer_write_nofence", 5: "peer_write_fence_sys", 6: "peer_write_fence_gpu",
-                 7: "local_copy_nofence", 8: "local_copy_fence_sys", 9: "local_copy_fence_gpu"}
     for mode, name in modes.items():
         if mode == 3 and not comm.nvls_enabled:
             continue
@@ -57,8 +52,7 @@ def main(argv=None) -> None:
                 gbs = lib.bcclDebugBandwidth(comm._h, mode, peer, nbytes, ctas, args.iters)
                 if rank == 0:
                     print(json.dumps({"probe": name, "bytes": nbytes, "ctas": ctas, "gbs": round(gbs, 1), "peer": peer,
-                                      "ranks": world, "seg": os.environ.get("BCCL_PROBE_SEG"),
-                                      "all_ranks": args.all_ranks}), flush=True)
+                                      "ranks": world, "all_ranks": args.all_ranks}), flush=True)
             dist.barrier()
     comm.destroy()
     dist.destroy_process_group()
