@@ -208,12 +208,22 @@ int bcclReduce(bcclComm_t comm, const void* send, void* recv, size_t count, int 
 
 int bcclAllGather(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, uintptr_t stream,
                   int has_stream) {
-    BCCL_SUBMIT(MakeTask(bccl::CollFunc::AllGather, send, recv, count, dtype, 0, 0, -1, 1.0f, 0));
+    return bcclAllGatherAlgo(comm, send, recv, count, dtype, 0, stream, has_stream);
+}
+
+int bcclAllGatherAlgo(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int algo,
+                      uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::AllGather, send, recv, count, dtype, 0, 0, -1, 1.0f, algo));
 }
 
 int bcclReduceScatter(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op,
                       uintptr_t stream, int has_stream) {
-    BCCL_SUBMIT(MakeTask(bccl::CollFunc::ReduceScatter, send, recv, count, dtype, op, 0, -1, 1.0f, 0));
+    return bcclReduceScatterAlgo(comm, send, recv, count, dtype, op, 0, stream, has_stream);
+}
+
+int bcclReduceScatterAlgo(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, int algo,
+                          uintptr_t stream, int has_stream) {
+    BCCL_SUBMIT(MakeTask(bccl::CollFunc::ReduceScatter, send, recv, count, dtype, op, 0, -1, 1.0f, algo));
 }
 
 int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream) {

@@ -58,8 +58,15 @@ std::vector<TuningRow> DefaultTable() {
         {CollFunc::Reduce, 2, ~size_t(0), Algo::kOneShot, 0},
         {CollFunc::Reduce, 0, 512 << 10, Algo::kOneShot, 0},
         {CollFunc::Reduce, 0, ~size_t(0), Algo::kNvls, 0},
-        {CollFunc::AllGather, 0, ~size_t(0), Algo::kOneShot, 0},
-        {CollFunc::ReduceScatter, 0, ~size_t(0), Algo::kOneShot, 0},
+        // AllGather through the switch: a rank's block leaves its GPU once (multimem.st) instead
+        // of once per peer; ReduceScatter: the switch reduces, the SMs only stage and store.
+        // Two ranks gain nothing (one peer either way).
+        {CollFunc::AllGather, 2, ~size_t(0), Algo::kOneShot, 0},
+        {CollFunc::AllGather, 0, 256 << 10, Algo::kOneShot, 0},
+        {CollFunc::AllGather, 0, ~size_t(0), Algo::kNvls, 0},
+        {CollFunc::ReduceScatter, 2, ~size_t(0), Algo::kOneShot, 0},
+        {CollFunc::ReduceScatter, 0, 1 << 20, Algo::kOneShot, 0},
+        {CollFunc::ReduceScatter, 0, ~size_t(0), Algo::kNvls, 0},
     };
 }
 
@@ -236,9 +243,6 @@ AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_
     if ((algo == Algo::kTwoShot || algo == Algo::kRing) && func != CollFunc::AllReduce) algo = Algo::kOneShot;
     if (algo == Algo::kNvls && !nvls_ok) algo = (func == CollFunc::AllReduce && bytes > (256u << 10))
                                                     ? Algo::kTwoShot : Algo::kOneShot;
-    if (algo == Algo::kNvls && (func == CollFunc::AllGather || func == CollFunc::ReduceScatter)) {
-        algo = Algo::kOneShot;
-    }
     if (ctas <= 0) ctas = DefaultCtas(algo, bytes);
     if (env_max_ctas_ > 0) ctas = std::min<int>(ctas, static_cast<int>(env_max_ctas_));
     if (max_ctas > 0) ctas = std::min(ctas, max_ctas);

@@ -132,6 +132,11 @@ void DeviceEngine::Finalize() {
     cudaSetDevice(device_);
     cudaDeviceSynchronize();
     p2p_.Destroy();
+    if (p2p_stream_ != nullptr) cudaStreamDestroy(p2p_stream_);
+    if (p2p_fork_ != nullptr) cudaEventDestroy(p2p_fork_);
+    if (p2p_join_ != nullptr) cudaEventDestroy(p2p_join_);
+    p2p_stream_ = nullptr;
+    p2p_fork_ = p2p_join_ = nullptr;
     // Nobody may unmap while a peer could still touch our memory.
     if (bs_ != nullptr && bs_->ready()) bs_->Barrier();
     for (SymBuffer& b : user_bufs_) sm_.Free(&b);
@@ -611,6 +616,14 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         if (t.func == CollFunc::AllReduce) {
             e = LaunchAllReducePipe(dc_, kPipeNvls, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots,
                                     ctas, stream);
+        } else if (t.func == CollFunc::AllGather || t.func == CollFunc::ReduceScatter) {
+            // A slot holds one chunk of every rank's block.
+            const unsigned long long cap = RoundDown(slot / static_cast<unsigned long long>(nranks_), 16);
+            unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, 16);
+            want = std::max<unsigned long long>(want, RoundUp(min_chunk / static_cast<unsigned long long>(nranks_), 16));
+            const unsigned long long pc = std::max<unsigned long long>(16, std::min<unsigned long long>(want, cap));
+            e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale,
+                           pc, slot, slots, ctas, stream);
         } else {
             e = LaunchNvls(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count, dt, op, t.root, t.scale,
                            chunk, slot, slots, ctas, stream);
@@ -643,24 +656,71 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     return true;
 }
 
+bool DeviceEngine::EnsureP2pStream() {
+    if (p2p_stream_ != nullptr) return true;
+    CUDA_OK(cudaStreamCreateWithFlags(&p2p_stream_, cudaStreamNonBlocking), "cudaStreamCreate(p2p)");
+    CUDA_OK(cudaEventCreateWithFlags(&p2p_fork_, cudaEventDisableTiming), "cudaEventCreate(p2p fork)");
+    CUDA_OK(cudaEventCreateWithFlags(&p2p_join_, cudaEventDisableTiming), "cudaEventCreate(p2p join)");
+    return true;
+}
+
 bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t stream) {
     if (!inited_) {
         LOG_ERROR("device engine not initialised");
         return false;
     }
     if (err_host_->code != kDevOk) return CheckDeviceError();
-    std::vector<WorkItem> batch;
-    unsigned long long stream_bytes = 0;
     std::vector<CollTask> p2p;
+    bool has_coll = false;
     for (const CollTask& t : sorted) {
         if (IsP2p(t.func)) {
-            p2p.push_back(t);
-            continue;
+            if (t.count > 0) p2p.push_back(t);
+        } else if (t.count > 0) {
+            has_coll = true;
         }
+    }
+    // A group with both kinds: NCCL's Send/Recv go first, on the side stream forked here, and
+    // the collectives use at most num_sms - kP2pReservedSms CTAs, so NCCL's kernels find SMs
+    // while ours (whose CTAs wait on their peers' CTAs) are resident. The join follows below.
+    const int sms_all = num_sms_;
+    bool forked = false;
+    if (!p2p.empty() && has_coll && !knob_p2p_native_ && p2p_.ready()) {
+        if (!EnsureP2pStream()) return false;
+        CUDA_OK(cudaEventRecord(p2p_fork_, stream), "cudaEventRecord(p2p fork)");
+        CUDA_OK(cudaStreamWaitEvent(p2p_stream_, p2p_fork_, 0), "cudaStreamWaitEvent(p2p fork)");
+        if (!p2p_.Run(p2p, p2p_stream_)) return false;
+        CUDA_OK(cudaEventRecord(p2p_join_, p2p_stream_), "cudaEventRecord(p2p join)");
+        p2p.clear();
+        forked = true;
+        num_sms_ = std::max(16, sms_all - kP2pReservedSms);
+    }
+    const bool ok = ExecuteCollectives(sorted, stream) && (p2p.empty() || RunP2p(p2p, stream));
+    num_sms_ = sms_all;
+    if (forked) {
+        // Joined even after a failure, so the caller's stream never outruns the side stream.
+        CUDA_OK(cudaStreamWaitEvent(stream, p2p_join_, 0), "cudaStreamWaitEvent(p2p join)");
+        if (ok && has_coll) last_algo_ = "mixed+nccl_p2p";
+    }
+    return ok;
+}
+
+bool DeviceEngine::RunP2p(const std::vector<CollTask>& p2p, cudaStream_t stream) {
+    if (knob_p2p_native_) return RunNativeP2p(p2p, stream);
+    if (!p2p_.Run(p2p, stream)) return false;
+    last_algo_ = "nccl_p2p";
+    return true;
+}
+
+bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaStream_t stream) {
+    std::vector<WorkItem> batch;
+    unsigned long long stream_bytes = 0;
+    for (const CollTask& t : sorted) {
+        if (IsP2p(t.func)) continue;
         if (t.count == 0) continue;
         const size_t bytes = t.count * DataTypeSize(t.dtype);
         const bool nvls_ok = nvls_.mc != nullptr &&
-                             (t.func == CollFunc::Broadcast || NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
+                             (t.func == CollFunc::Broadcast || t.func == CollFunc::AllGather ||
+                              NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
         AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
                                             t.algo != Algo::kAuto ? t.algo : forced_);
         const bool ring = c.algo == Algo::kRing && t.func == CollFunc::AllReduce && nranks_ > 1;
@@ -753,7 +813,8 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls) {
             // Large-payload kernels: per-CTA barriers with the same CTA index on every rank, so
             // every CTA must be resident: at most one per SM.
-            int want = static_cast<int>(std::min<size_t>(std::max<size_t>(bytes / (32u << 10), 8),
+            const size_t moved = (t.func == CollFunc::AllGather || t.func == CollFunc::ReduceScatter) ? all_bytes : bytes;
+            int want = static_cast<int>(std::min<size_t>(std::max<size_t>(moved / (32u << 10), 8),
                                                          static_cast<size_t>(num_sms_)));
             c.ctas = std::min(want, kMaxCtas);
             if (max_ctas_ > 0) c.ctas = std::min(c.ctas, max_ctas_);
@@ -797,13 +858,7 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
         if (!LaunchLarge(t, c, stream)) return false;
     }
-    if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
-    if (!p2p.empty()) {
-        if (knob_p2p_native_) return RunNativeP2p(p2p, stream);
-        if (!p2p_.Run(p2p, stream)) return false;
-        last_algo_ = "nccl_p2p";
-    }
-    return true;
+    return FlushBatch(&batch, &stream_bytes, stream);
 }
 
 bool DeviceEngine::RunNativeP2p(const std::vector<CollTask>& tasks, cudaStream_t stream) {

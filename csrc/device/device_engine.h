@@ -7,7 +7,9 @@
 //     reference's dynamic executor and its per-slice control broadcast become the kernel's
 //     CTA-owns-piece rule);
 //   * each large collective -> one NVLS or two-shot launch, in sorted order;
-//   * all Send/Recv -> one NCCL group, after the collectives.
+//   * all Send/Recv -> one NCCL group on a side stream forked from the caller's stream before
+//     the collectives launch and joined back after them, so a group's point-to-point traffic
+//     overlaps its collective kernels (the collectives then leave SMs free for NCCL's kernels).
 // Every rank derives the same launches from the same sorted batch, so no control message
 // is needed at run time.
 #pragma once
@@ -94,6 +96,10 @@ private:
     // Send/Recv of one group with the native kernel (p2p_native.cu).
     bool RunNativeP2p(const std::vector<CollTask>& tasks, cudaStream_t stream);
     bool LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStream_t stream);
+    bool ExecuteCollectives(const std::vector<CollTask>& sorted, cudaStream_t stream);
+    bool RunP2p(const std::vector<CollTask>& p2p, cudaStream_t stream);
+    // SMs left to NCCL's point-to-point kernels while a mixed group's collectives run.
+    static constexpr int kP2pReservedSms = 32;
 
     int rank_ = 0;
     int nranks_ = 1;
@@ -136,6 +142,10 @@ private:
     unsigned long long data_bytes_ = 0;
     cudaStream_t stream_ = nullptr;
     NcclP2p p2p_;
+    // Side stream and fork/join events of the NCCL Send/Recv of a mixed group.
+    cudaStream_t p2p_stream_ = nullptr;
+    cudaEvent_t p2p_fork_ = nullptr, p2p_join_ = nullptr;
+    bool EnsureP2pStream();
     std::atomic<unsigned long long> launches_{0};
     const char* last_algo_ = "none";
     // Tensor-parallel workspaces (symmetric, double-buffered by call parity) and call counters.

@@ -78,6 +78,11 @@ int bcclAllGather(bcclComm_t comm, const void* send, void* recv, size_t count, i
                   int has_stream);
 int bcclReduceScatter(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op,
                       uintptr_t stream, int has_stream);
+/* The same with an algorithm override (0 auto, 1 one-shot push, 3 NVLS; others mean auto). */
+int bcclAllGatherAlgo(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int algo,
+                      uintptr_t stream, int has_stream);
+int bcclReduceScatterAlgo(bcclComm_t comm, const void* send, void* recv, size_t count, int dtype, int op, int algo,
+                          uintptr_t stream, int has_stream);
 int bcclSend(bcclComm_t comm, const void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
 int bcclRecv(bcclComm_t comm, void* buf, size_t count, int dtype, int peer, uintptr_t stream, int has_stream);
 int bcclSynchronize(bcclComm_t comm);

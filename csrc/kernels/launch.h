@@ -23,7 +23,10 @@ cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, voi
                                 int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
                                 int nslots, int nctas, cudaStream_t stream);
 
-// NVSwitch multicast Broadcast (func 1) and Reduce (func 2) over the NVLS slot ring.
+// NVSwitch multicast Broadcast (func 1), Reduce (2), AllGather (3) and ReduceScatter (4) over
+// the NVLS slot ring. count is the payload (Broadcast, Reduce) or the per-rank block
+// (AllGather, ReduceScatter) in elements; for the latter `chunk` is bytes of each rank's block
+// per round (a multiple of 16, nranks * chunk <= slot_bytes) and ReduceScatter needs 3+ slots.
 cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, unsigned long long count, int dtype,
                        int op, int root, float scale, unsigned long long chunk, unsigned long long slot_bytes,
                        int nslots, int nctas, cudaStream_t stream);

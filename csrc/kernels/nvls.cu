@@ -1,12 +1,22 @@
-// NVSwitch multicast Broadcast and Reduce.
+// NVSwitch multicast Broadcast, Reduce, AllGather and ReduceScatter on staged (unregistered)
+// buffers.
 //
 // The reference moves every byte through per-edge transports and reduces on the CPU
-// (OriginCCL src/topology/topology_ring.cpp:178-229). With NVLS:
-//   Broadcast: the root multimem.st's each chunk once (one egress copy; the switch fans it
-//              out to every GPU) -> barrier -> every rank copies the slot to its output.
-//   Reduce:    every rank copies its chunk into its slot -> barrier -> the root
-//              multimem.ld_reduce's the slot (the switch reads and reduces all copies) into
-//              its output -> barrier.
+// (OriginCCL src/topology/topology_ring.cpp:178-253). With NVLS:
+//   Broadcast:     the root multimem.st's each chunk once (one egress copy; the switch fans it
+//                  out to every GPU) -> barrier -> every rank copies the slot to its output.
+//   Reduce:        every rank copies its chunk into its slot -> barrier -> the root
+//                  multimem.ld_reduce's the slot (the switch reads and reduces all copies) into
+//                  its output -> barrier.
+//   AllGather:     every rank multimem.st's its block's chunk into sub-slot `rank` of every
+//                  GPU's slot (one egress copy of the block instead of N-1) -> barrier -> every
+//                  rank copies the N sub-slots to its output.
+//   ReduceScatter: every rank copies the chunk of each of its N input blocks into sub-slot q of
+//                  its slot -> barrier -> rank r multimem.ld_reduce's sub-slot r (the switch
+//                  reduces the N copies) into its output. One barrier per round: with three or
+//                  more slots, round j+1's copy-in lands in a slot no rank still reads.
+// AllGather and ReduceScatter take `chunk` bytes of every rank's block per round, so a slot
+// holds N chunks.
 // Slots form the same ring (indexed by DevState::nvls_round_seq) as the pipelined AllReduce,
 // so the two kinds of launch can follow each other.
 // No fence.proxy.alias between the multicast and unicast views of a slot: the system-scope
@@ -85,11 +95,70 @@ struct NvlsParams {
     unsigned long long slot_bytes;  // >= chunk, multiple of 16
     int nslots;
     int nrounds;
-    int func;  // 1 Broadcast, 2 Reduce
+    int func;  // 1 Broadcast, 2 Reduce, 3 AllGather, 4 ReduceScatter (CollFunc values)
     int op;
     int root;
     float scale;
 };
+
+// Multicast stores of [lo, hi) of `src` to `mc` (four 16-byte loads in flight per thread).
+__device__ __forceinline__ void mcast_range(char* mc, const char* src, size_t lo, size_t hi) {
+    const size_t t = threadIdx.x, nt = blockDim.x;
+    size_t off = lo + t * 16;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(src + off + u * nt * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) mm_st(mc + off + u * nt * 16, v[u]);
+        }
+    }
+    for (; off < hi; off += nt * 16) mm_st(mc + off, load_partial(src + off, hi - off));
+}
+
+// dst[lo, hi) = epilogue(multimem.ld_reduce of mc[lo, hi)); four switch reductions in flight
+// per thread (each is a round trip through the switch to every GPU), then their stores.
+template <int D, int O>
+__device__ __forceinline__ void reduce_range(char* dst, const char* mc, size_t lo, size_t hi, int op, int n,
+                                             float scale) {
+    constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
+    const bool post = op == kAvg || scale != 1.0f;
+    const size_t t = threadIdx.x, nt = blockDim.x;
+    size_t off = lo + t * 16;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
+            V16<D> v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(mc + off + u * nt * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (post) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        v[u].b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(op, Ty<D>::load(v[u].b[e]), n, scale));
+                }
+                *reinterpret_cast<uint4*>(dst + off + u * nt * 16) = v[u].u;
+            }
+        }
+    }
+    for (; off < hi; off += nt * 16) {
+        V16<D> v;
+        v.u = red16<D, O>(mc + off);
+        if (post) {
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+                v.b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(op, Ty<D>::load(v.b[e]), n, scale));
+        }
+        const size_t valid = min((size_t)16, hi - off);
+        char* d = dst + off;
+        if (valid == 16 && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            *reinterpret_cast<uint4*>(d) = v.u;
+        } else {
+            for (size_t i = 0; i < valid; ++i) d[i] = reinterpret_cast<const char*>(&v.u)[i];
+        }
+    }
+}
 
 template <int D, int O>
 __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ NvlsParams p) {
@@ -97,8 +166,10 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
     const int r = c.rank, n = c.nranks;
     const uint64_t round0 = load_state_u64(&c.state->nvls_round_seq);
     uint64_t bar = load_state_u64(&c.state->barrier_seq);
-    const int per_round = (p.func == 1) ? 1 : 2;
-    const size_t t = threadIdx.x, nt = blockDim.x;
+    if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar & 0x7fffffffull));
+    const int per_round = (p.func == 2) ? 2 : 1;
+    const char* sbase = static_cast<const char*>(p.src);
+    char* dbase = static_cast<char*>(p.dst);
     for (int j = 0; j < p.nrounds; ++j) {
         const size_t cbeg = (size_t)j * p.chunk;
         const size_t clen = min((size_t)p.bytes - cbeg, (size_t)p.chunk);
@@ -107,72 +178,42 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
         const size_t slot = (size_t)((round0 + (uint64_t)j) % (uint64_t)p.nslots);
         char* uc = c.nvls_uc + slot * p.slot_bytes;
         char* mc = c.nvls_mc + slot * p.slot_bytes;
-        const char* src = static_cast<const char*>(p.src) + cbeg;
-        char* dst = static_cast<char*>(p.dst) + cbeg;
         if (p.func == 1) {  // Broadcast
-            if (r == p.root) {
-                size_t off = lo + t * 16;
-                // Four 16-byte loads in flight per thread, then their multicast stores.
-                if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-                    for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
-                        uint4 v[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(src + off + u * nt * 16);
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) mm_st(mc + off + u * nt * 16, v[u]);
-                    }
-                }
-                for (; off < hi; off += nt * 16) mm_st(mc + off, load_partial(src + off, hi - off));
-            }
+            const char* src = sbase + cbeg;
+            char* dst = dbase + cbeg;
+            if (r == p.root) mcast_range(mc, src, lo, hi);
             if (!cta_barrier(c, ++bar, j)) break;
             if (lo < hi && r != p.root) cta_copy(dst + lo, uc + lo, hi - lo, true);
             if (lo < hi && r == p.root && dst != src) cta_copy(dst + lo, src + lo, hi - lo, false);
-        } else {  // Reduce
+        } else if (p.func == 2) {  // Reduce
+            const char* src = sbase + cbeg;
             if (lo < hi) cta_copy(uc + lo, src + lo, hi - lo, false);
             if (!cta_barrier(c, ++bar, 2 * j)) break;
-            if (r == p.root) {
-                constexpr int E = 16 / sizeof(typename Ty<D>::Bits);
-                const bool post = p.op == kAvg || p.scale != 1.0f;
-                size_t off = lo + t * 16;
-                // Four switch reductions in flight per thread (each is a round trip through the
-                // switch to every GPU), then their stores.
-                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                    for (; off + 3 * nt * 16 + 16 <= hi; off += 4 * nt * 16) {
-                        V16<D> v[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) v[u].u = red16<D, O>(mc + off + u * nt * 16);
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            if (post) {
-#pragma unroll
-                                for (int e = 0; e < E; ++e)
-                                    v[u].b[e] = Ty<D>::store(
-                                        epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v[u].b[e]), n, p.scale));
-                            }
-                            *reinterpret_cast<uint4*>(dst + off + u * nt * 16) = v[u].u;
-                        }
-                    }
-                }
-                for (; off < hi; off += nt * 16) {
-                    V16<D> v;
-                    v.u = red16<D, O>(mc + off);
-                    if (post) {
-#pragma unroll
-                        for (int e = 0; e < E; ++e)
-                            v.b[e] = Ty<D>::store(epilogue<typename Ty<D>::Acc>(p.op, Ty<D>::load(v.b[e]), n, p.scale));
-                    }
-                    const size_t valid = min((size_t)16, hi - off);
-                    char* d = dst + off;
-                    if (valid == 16 && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
-                        *reinterpret_cast<uint4*>(d) = v.u;
+            if (r == p.root) reduce_range<D, O>(dbase + cbeg, mc, lo, hi, p.op, n, p.scale);
+            if (!cta_barrier(c, ++bar, 2 * j + 1)) break;
+        } else if (p.func == 3) {  // AllGather: src = this rank's block, dst = [n][bytes]
+            mcast_range(mc + (size_t)r * p.chunk, sbase + cbeg, lo, hi);
+            if (!cta_barrier(c, ++bar, j)) break;
+            if (lo < hi) {
+                for (int q = 0; q < n; ++q) {
+                    char* out = dbase + (size_t)q * p.bytes + cbeg;
+                    if (q == r) {
+                        if (out != sbase + cbeg) cta_copy(out + lo, sbase + cbeg + lo, hi - lo, false);
                     } else {
-                        for (size_t i = 0; i < valid; ++i) d[i] = reinterpret_cast<const char*>(&v.u)[i];
+                        cta_copy(out + lo, uc + (size_t)q * p.chunk + lo, hi - lo, true);
                     }
                 }
             }
-            if (!cta_barrier(c, ++bar, 2 * j + 1)) break;
+        } else {  // ReduceScatter: src = [n][bytes], dst = this rank's block
+            if (lo < hi) {
+                for (int q = 0; q < n; ++q)
+                    cta_copy(uc + (size_t)q * p.chunk + lo, sbase + (size_t)q * p.bytes + cbeg + lo, hi - lo, false);
+            }
+            if (!cta_barrier(c, ++bar, j)) break;
+            reduce_range<D, O>(dbase + cbeg, mc + (size_t)r * p.chunk, lo, hi, p.op, n, p.scale);
         }
     }
+    if (threadIdx.x == 0) trace(c, 0, kTrEnd, p.nrounds);
     finish_launch(c, 0, (uint64_t)per_round * (uint64_t)p.nrounds, (uint64_t)p.nrounds);
 }
 
@@ -339,11 +380,13 @@ cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, u
                        int op, int root, float scale, unsigned long long chunk, unsigned long long slot_bytes,
                        int nslots, int nctas, cudaStream_t stream) {
     using namespace dev;
-    if (c.nvls_mc == nullptr || nctas <= 0 || nctas > kMaxCtas || nslots < 2 || chunk == 0 || slot_bytes < chunk ||
-        (slot_bytes & 15) != 0 || (size_t)nslots * slot_bytes > c.nvls_bytes || (func != 1 && func != 2)) {
+    const bool per_rank = func == 3 || func == 4;  // a slot holds one chunk of every rank's block
+    if (c.nvls_mc == nullptr || nctas <= 0 || nctas > kMaxCtas || nslots < (func == 4 ? 3 : 2) || chunk == 0 ||
+        (chunk & 15) != 0 || (per_rank ? chunk * (unsigned long long)c.nranks : chunk) > slot_bytes ||
+        (slot_bytes & 15) != 0 || (size_t)nslots * slot_bytes > c.nvls_bytes || func < 1 || func > 4) {
         return cudaErrorInvalidValue;
     }
-    if (func == 2 && !NvlsSupports(dtype, op)) return cudaErrorNotSupported;
+    if ((func == 2 || func == 4) && !NvlsSupports(dtype, op)) return cudaErrorNotSupported;
     NvlsParams p;
     p.comm = c;
     p.src = src;
@@ -358,7 +401,7 @@ cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, u
     p.op = op;
     p.root = root;
     p.scale = scale;
-    if (func == 1) return launch_t<kF32, kSum>(p, nctas, stream);
+    if (func == 1 || func == 3) return launch_t<kF32, kSum>(p, nctas, stream);  // data movement only
     const int o = (op == kAvg) ? kSum : op;
 #define NV_CASE(D, O) \
     if (dtype == D && o == O) return launch_t<D, O>(p, nctas, stream);

@@ -76,6 +76,8 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclReduce": (c_int, [vp, vp, vp, c_size, c_int, c_int, c_int, c_int, up, c_int]),
         "bcclAllGather": (c_int, [vp, vp, vp, c_size, c_int, up, c_int]),
         "bcclReduceScatter": (c_int, [vp, vp, vp, c_size, c_int, c_int, up, c_int]),
+        "bcclAllGatherAlgo": (c_int, [vp, vp, vp, c_size, c_int, c_int, up, c_int]),
+        "bcclReduceScatterAlgo": (c_int, [vp, vp, vp, c_size, c_int, c_int, c_int, up, c_int]),
         "bcclSend": (c_int, [vp, vp, c_size, c_int, c_int, up, c_int]),
         "bcclRecv": (c_int, [vp, vp, c_size, c_int, c_int, up, c_int]),
         "bcclSynchronize": (c_int, [vp]),

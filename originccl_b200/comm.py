@@ -348,18 +348,19 @@ class Communicator:
                                          int(op), int(root), int(algo), s, has))
         return dst
 
-    def all_gather(self, out: Any, tensor: Any, *, stream: Any = None) -> Any:
+    def all_gather(self, out: Any, tensor: Any, *, algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
         """out (world_size * numel) = concatenation of every rank's tensor in rank order."""
         s, has = self._stream(stream)
-        self._check(self._lib.bcclAllGather(self._h, _ptr(tensor), _ptr(out), _numel(tensor), int(_dtype_of(tensor)),
-                                            s, has))
+        self._check(self._lib.bcclAllGatherAlgo(self._h, _ptr(tensor), _ptr(out), _numel(tensor),
+                                                int(_dtype_of(tensor)), int(algo), s, has))
         return out
 
-    def reduce_scatter(self, out: Any, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, stream: Any = None) -> Any:
+    def reduce_scatter(self, out: Any, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, algo: Algo = Algo.AUTO,
+                       stream: Any = None) -> Any:
         """out (numel) = this rank's block of reduce(tensor (world_size * numel))."""
         s, has = self._stream(stream)
-        self._check(self._lib.bcclReduceScatter(self._h, _ptr(tensor), _ptr(out), _numel(out), int(_dtype_of(out)),
-                                                int(op), s, has))
+        self._check(self._lib.bcclReduceScatterAlgo(self._h, _ptr(tensor), _ptr(out), _numel(out),
+                                                    int(_dtype_of(out)), int(op), int(algo), s, has))
         return out
 
     def send(self, tensor: Any, peer: int, *, stream: Any = None) -> None:

@@ -101,15 +101,23 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
                 comm.all_reduce(xi, ReduceOp(OPS[op]))
                 _close(xi, exp.to(td), dtype, f"allreduce in-place {dtype} {op} n={n}")
                 _close(x, inputs[rank].cuda(), dtype, "input changed")
-            # ReduceScatter: input world*n
+            # ReduceScatter: input world*n; AllGather (each algorithm that applies: one-shot push or
+            # NVLS; the others fall back to auto)
             rs_in = [rank_input(r, n * world, dtype, seed=n + 1) for r in range(world)]
-            out = torch.empty(n, dtype=td, device="cuda")
-            comm.reduce_scatter(out, rs_in[rank].cuda())
-            _close(out, oracle("sum", rs_in, world)[rank * n:(rank + 1) * n].to(td), dtype, f"reducescatter {dtype} n={n}")
-            # AllGather
-            ag = torch.empty(n * world, dtype=td, device="cuda")
-            comm.all_gather(ag, x)
-            _close(ag, torch.cat(inputs).to(td), dtype, f"allgather {dtype} n={n}")
+            rs_x = rs_in[rank].cuda()
+            for algo in algos:
+                out = torch.full((n + 1,), 7, dtype=td, device="cuda")
+                comm.reduce_scatter(out[:n], rs_x, algo=algo_map[algo])
+                used.add("rs:" + comm.last_algorithm)
+                _close(out[:n], oracle("sum", rs_in, world)[rank * n:(rank + 1) * n].to(td), dtype,
+                       f"reducescatter {dtype} n={n} algo={algo}")
+                assert out[n].item() == 7, "reducescatter wrote past the end"
+                ag = torch.full((n * world + 1,), 7, dtype=td, device="cuda")
+                comm.all_gather(ag[:n * world], x, algo=algo_map[algo])
+                used.add("ag:" + comm.last_algorithm)
+                _close(ag[:n * world], torch.cat(inputs).to(td), dtype, f"allgather {dtype} n={n} algo={algo}")
+                assert ag[n * world].item() == 7, "allgather wrote past the end"
+            _close(rs_x, rs_in[rank].cuda(), dtype, "reducescatter input changed")
             # Broadcast from the last rank, Reduce MAX to rank 0
             root = world - 1
             b = x.clone()

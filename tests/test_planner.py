@@ -93,7 +93,12 @@ def test_algorithm_table():
     assert choose(AR, 256 << 20, 2, True)[0] == TWOSHOT       # two ranks, large: two-shot
     assert choose(BC, 256 << 20, 2, True)[0] == ONESHOT       # two ranks: no NVLS for Broadcast
     assert choose(BC, 256 << 20, 8, True)[0] == NVLS
-    assert choose(AG, 64 << 20, 8, True)[0] == ONESHOT
+    assert choose(AG, 64 << 20, 8, True)[0] == NVLS           # block leaves the GPU once
+    assert choose(AG, 64 << 10, 8, True)[0] == ONESHOT
+    assert choose(AG, 64 << 20, 8, False)[0] == ONESHOT      # no multicast
+    assert choose(AG, 64 << 20, 2, True)[0] == ONESHOT       # two ranks: nothing to save
+    assert choose(RS, 64 << 20, 8, True)[0] == NVLS
+    assert choose(RS, 256 << 10, 8, True)[0] == ONESHOT
     assert choose(AR, 8, 8, True)[1] == 1
 
 
