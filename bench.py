@@ -49,6 +49,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
     p.add_argument("--inplace", action="store_true", help="in-place AllReduce (default: out of place)")
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"],
+                   help="force one algorithm (default: the planner's choice)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-clocks", action="store_true", help="diagnostic: do not sample clocks (no clocks key)")
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
@@ -104,11 +106,13 @@ def main() -> None:
         for t_ in (*xs, y):
             comm.register(t_)
 
+    algo = getattr(occl.Algo, args.algo.upper())
+
     def step(i: int) -> None:
         if args.inplace:
-            comm.all_reduce(xs[i & 1])
+            comm.all_reduce(xs[i & 1], algo=algo)
         else:
-            comm.all_reduce(xs[i & 1], out=y)
+            comm.all_reduce(xs[i & 1], out=y, algo=algo)
 
     def reference_of(i: int):
         """NCCL's fp32 AllReduce of step i's input (in-place steps change their input: only the

@@ -78,6 +78,7 @@ const char* AlgoName(Algo a) {
     case Algo::kTwoShot: return "twoshot";
     case Algo::kNvls: return "nvls";
     case Algo::kRing: return "ring";
+    case Algo::kHybrid: return "hybrid";
     }
     return "unknown";
 }

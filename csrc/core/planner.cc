@@ -100,6 +100,7 @@ Algo Planner::ParseAlgo(const std::string& s) {
     if (s == "twoshot") return Algo::kTwoShot;
     if (s == "nvls") return Algo::kNvls;
     if (s == "ring") return Algo::kRing;
+    if (s == "hybrid") return Algo::kHybrid;
     return Algo::kAuto;
 }
 
@@ -241,6 +242,8 @@ AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_
     // Two-shot and ring exist for AllReduce only; the other collectives are already
     // bandwidth-optimal as one-shot pushes.
     if ((algo == Algo::kTwoShot || algo == Algo::kRing) && func != CollFunc::AllReduce) algo = Algo::kOneShot;
+    if (algo == Algo::kHybrid && func != CollFunc::AllReduce) algo = Algo::kNvls;
+    if (algo == Algo::kHybrid && !nvls_ok) algo = Algo::kTwoShot;
     if (algo == Algo::kNvls && !nvls_ok) algo = (func == CollFunc::AllReduce && bytes > (256u << 10))
                                                     ? Algo::kTwoShot : Algo::kOneShot;
     if (ctas <= 0) ctas = DefaultCtas(algo, bytes);

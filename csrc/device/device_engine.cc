@@ -103,6 +103,8 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_rounds_ = EnvInt("BCCL_PIPE_ROUNDS", 0);
     knob_pipe_min_chunk_ = EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20);
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
+    knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
+    knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
@@ -596,13 +598,38 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const unsigned long long rounds = static_cast<unsigned long long>(
         std::max<long>(1, knob_pipe_rounds_ > 0 ? knob_pipe_rounds_ : (bytes <= (64u << 20) ? 2 : 4)));
     const unsigned long long min_chunk = static_cast<unsigned long long>(knob_pipe_min_chunk_);
-    auto pick_chunk = [&](unsigned long long cap) {
-        unsigned long long want = RoundUp((bytes + rounds - 1) / rounds, q);
+    auto pick_chunk_for = [&](unsigned long long part, unsigned long long cap) {
+        unsigned long long want = RoundUp((part + rounds - 1) / rounds, q);
         want = std::max<unsigned long long>(want, RoundUp(min_chunk, q));
         return std::max<unsigned long long>(q, std::min<unsigned long long>(want, RoundDown(cap, q)));
     };
+    auto pick_chunk = [&](unsigned long long cap) { return pick_chunk_for(bytes, cap); };
     int ctas = c.ctas;
     dc_.kernel_serial = ++kernel_serial_;
+    if (c.algo == Algo::kHybrid) {
+        // The switch's reduction rate, not NVLink, bounds NVLS; the two-shot part uses the link
+        // bandwidth NVLS leaves idle. Split by BCCL_HYBRID_NVLS_PERMILLE (bytes through NVLS).
+        const unsigned long long nb = RoundDown(static_cast<unsigned long long>(bytes * knob_hybrid_frac_), q);
+        if (nb > 0 && nb < bytes && ctas >= 2 && nvls_.mc != nullptr && nranks_ > 1) {
+            int nv_ctas = knob_hybrid_ctas_ > 0 ? static_cast<int>(knob_hybrid_ctas_)
+                                                : static_cast<int>(ctas * knob_hybrid_frac_ + 0.5);
+            nv_ctas = std::max(1, std::min(ctas - 1, nv_ctas));
+            const unsigned long long nslot = RoundDown(nvls_.bytes / slots, 256);
+            const unsigned long long tslot =
+                RoundDown(data_bytes_ / 2 / (static_cast<unsigned long long>(slots) * 2ull * nranks_), 256);
+            e = LaunchAllReduceHybrid(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, nb,
+                                      pick_chunk_for(nb, nslot), nslot, nv_ctas,
+                                      pick_chunk_for(bytes - nb, tslot * nranks_), tslot, ctas - nv_ctas, slots,
+                                      stream);
+            last_algo_ = "hybrid";
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: hybrid launch failed: %s", rank_, cudaGetErrorString(e));
+                return false;
+            }
+            launches_++;
+            return true;
+        }
+    }
     if (c.algo == Algo::kRing) {
         // Messages of up to 128 KiB, small enough that every SM gets a channel.
         const unsigned long long per = (bytes + static_cast<unsigned long long>(nranks_) * num_sms_ - 1) /
@@ -610,7 +637,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         const unsigned long long block = std::min<unsigned long long>(128u << 10, std::max<unsigned long long>(256, RoundUp(per, 256)));
         e = LaunchRingAllReduce(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, block, ctas, stream);
         last_algo_ = "ring";
-    } else if (c.algo == Algo::kNvls) {
+    } else if (c.algo == Algo::kNvls || (c.algo == Algo::kHybrid && nvls_.mc != nullptr)) {
         const unsigned long long slot = RoundDown(nvls_.bytes / slots, 256);
         const unsigned long long chunk = pick_chunk(slot);
         if (t.func == CollFunc::AllReduce) {
@@ -810,7 +837,7 @@ bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaS
             last_algo_ = "nvls_zero_copy";
             continue;
         }
-        if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls) {
+        if (c.algo == Algo::kTwoShot || c.algo == Algo::kNvls || c.algo == Algo::kHybrid) {
             // Large-payload kernels: per-CTA barriers with the same CTA index on every rank, so
             // every CTA must be resident: at most one per SM.
             const size_t moved = (t.func == CollFunc::AllGather || t.func == CollFunc::ReduceScatter) ? all_bytes : bytes;

@@ -52,6 +52,7 @@ enum class Algo : int {
     kTwoShot = 2,  // reduce-scatter by push, all-gather by pull
     kNvls = 3,     // NVSwitch multicast: multimem.ld_reduce / multimem.st
     kRing = 4,     // neighbour-only pipeline (parity with the reference's ring)
+    kHybrid = 5,   // AllReduce: part of the payload through the switch (NVLS), the rest two-shot
 };
 
 struct UniqueId {

@@ -46,6 +46,16 @@ struct PipeParams {
     int op;
     float scale;
     int nvls;   // PipeKind
+    // Hybrid launch (hyb_ctas > 0): CTAs [0, hyb_ctas) run NVLS on bytes [0, hyb_bytes) in
+    // hyb_rounds rounds of hyb_chunk (NVLS slots of hyb_slot bytes), the remaining CTAs run
+    // `nvls` (two-shot) on [hyb_bytes, bytes) with chunk / slot_bytes / nrounds above. The two
+    // parts share nothing but the launch: their staging buffers, round counters and per-CTA
+    // barriers are disjoint.
+    int hyb_ctas;
+    int hyb_rounds;
+    unsigned long long hyb_bytes;
+    unsigned long long hyb_chunk;
+    unsigned long long hyb_slot;
 };
 
 
@@ -315,7 +325,15 @@ template <int D, int O>
 __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_constant__ PipeParams p) {
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
-    const int kind = p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
+    // This CTA's part of the launch (the whole payload unless the launch is a hybrid).
+    const bool hyb_nvls = p.hyb_ctas > 0 && (int)blockIdx.x < p.hyb_ctas;
+    const int kind = hyb_nvls ? kPipeNvls : p.nvls;  // kPipeTwoShot / kPipeNvls / kPipeOneShot
+    const size_t part_off = (p.hyb_ctas > 0 && !hyb_nvls) ? (size_t)p.hyb_bytes : 0;
+    const size_t part_bytes = hyb_nvls ? (size_t)p.hyb_bytes : (size_t)p.bytes - part_off;
+    const size_t part_chunk = hyb_nvls ? (size_t)p.hyb_chunk : (size_t)p.chunk;
+    const int nrounds = hyb_nvls ? p.hyb_rounds : p.nrounds;
+    const int cta = (p.hyb_ctas > 0 && !hyb_nvls) ? (int)blockIdx.x - p.hyb_ctas : (int)blockIdx.x;
+    const int nct = p.hyb_ctas > 0 ? (hyb_nvls ? p.hyb_ctas : (int)gridDim.x - p.hyb_ctas) : (int)gridDim.x;
     // Warp groups run their phases concurrently for NVLS (two local copies against one switch
     // phase); for the push kinds a single group measured faster.
     const bool split = kind == kPipeNvls;
@@ -323,11 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const uint64_t round0 = kind == kPipeNvls ? load_state_u64(&c.state->nvls_round_seq)
                                               : load_state_u64(&c.state->round_seq);
     const int S = p.nslots;
-    const size_t sb = p.slot_bytes;
-    const char* src = static_cast<const char*>(p.src);
-    char* dst = static_cast<char*>(p.dst);
+    const size_t sb = hyb_nvls ? (size_t)p.hyb_slot : (size_t)p.slot_bytes;
+    const char* src = static_cast<const char*>(p.src) + part_off;
+    char* dst = static_cast<char*>(p.dst) + part_off;
     const int depth = (kind == kPipeOneShot) ? 1 : 2;
-    const int iters = p.nrounds + depth;
+    const int iters = nrounds + depth;
     // Two warp groups: "net" (warps 0-7) runs the phase that crosses NVLink, "local" (warps
     // 8-15) the phases that stay in this GPU's memory; without the split both do everything.
     const int half = blockDim.x / 2;
@@ -338,11 +356,11 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar0 & 0x7fffffffull));  // round field: barrier base
 
     auto geom = [&](int j, size_t* cbeg, size_t* clen, size_t* shard, size_t* s0, size_t* s1) {
-        *cbeg = (size_t)j * p.chunk;
-        *clen = min((size_t)p.bytes - *cbeg, (size_t)p.chunk);
+        *cbeg = (size_t)j * part_chunk;
+        *clen = min(part_bytes - *cbeg, part_chunk);
         *shard = (kind == kPipeOneShot) ? *clen : round_up((*clen + n - 1) / n, 16);
-        const size_t piece = round_up((*shard + gridDim.x - 1) / gridDim.x, 16);
-        *s0 = min(*shard, (size_t)blockIdx.x * piece);
+        const size_t piece = round_up((*shard + nct - 1) / nct, 16);
+        *s0 = min(*shard, (size_t)cta * piece);
         *s1 = min(*shard, *s0 + piece);
     };
     // ---- phase bodies (tid/nt are group-relative)
@@ -433,8 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     };
     bool ok = true;
     for (int t = 0; t < iters && ok; ++t) {
-        const bool has_a = t < p.nrounds, has_b = t >= 1 && t - 1 < p.nrounds;
-        const bool has_c = depth == 2 && t >= 2 && t - 2 < p.nrounds;
+        const bool has_a = t < nrounds, has_b = t >= 1 && t - 1 < nrounds;
+        const bool has_c = depth == 2 && t >= 2 && t - 2 < nrounds;
         // Which group runs what: NVLS crosses NVLink in B (multimem); two-shot and one-shot
         // cross it in A (pushes). The other phases run on the local group.
         if (kind == kPipeNvls) {
@@ -459,8 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
         if (tid == 0) trace(c, 0, kTrBarrier, t);
     }
     if (threadIdx.x == 0) trace(c, 0, kTrEnd, iters);
-    if (kind == kPipeNvls) finish_launch(c, 0, (uint64_t)iters, (uint64_t)p.nrounds);
-    else finish_launch(c, (uint64_t)p.nrounds, (uint64_t)iters, 0);
+    // Every CTA passes the launch-wide totals (the last one to finish applies them).
+    if (p.hyb_ctas > 0) {
+        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)max(p.nrounds, p.hyb_rounds) + 2, (uint64_t)p.hyb_rounds);
+    } else if (p.nvls == kPipeNvls) {
+        finish_launch(c, 0, (uint64_t)p.nrounds + 2, (uint64_t)p.nrounds);
+    } else {
+        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)p.nrounds + (p.nvls == kPipeOneShot ? 1 : 2), 0);
+    }
 }
 
 template <int D, int O>
@@ -515,7 +539,54 @@ cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, voi
     p.op = op;
     p.scale = scale;
     p.nvls = kind == kPipeNvls ? 1 : (kind == kPipeOneShot ? 2 : 0);
+    p.hyb_ctas = 0;
+    p.hyb_rounds = 0;
+    p.hyb_bytes = p.hyb_chunk = p.hyb_slot = 0;
     // f32 MAX/MIN and f64 MAX/MIN have no multimem form; they only reach here for TWOSHOT.
+    switch (dtype) {
+    case kF32: return launch_op<kF32>(p, nctas, stream);
+    case kF64: return launch_op<kF64>(p, nctas, stream);
+    case kI32: return launch_op<kI32>(p, nctas, stream);
+    case kI64: return launch_op<kI64>(p, nctas, stream);
+    case kBF16: return launch_op<kBF16>(p, nctas, stream);
+    case kF16: return launch_op<kF16>(p, nctas, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t LaunchAllReduceHybrid(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
+                                  int op, float scale, unsigned long long nvls_bytes, unsigned long long nvls_chunk,
+                                  unsigned long long nvls_slot, int nvls_ctas, unsigned long long ts_chunk,
+                                  unsigned long long ts_slot, int ts_ctas, int nslots, cudaStream_t stream) {
+    using namespace dev;
+    const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
+    const unsigned long long q = 16ull * c.nranks;
+    if (nvls_ctas < 1 || ts_ctas < 1 || nvls_ctas + ts_ctas > kMaxCtas || nslots < 3 || nvls_bytes == 0 ||
+        nvls_bytes >= bytes || (nvls_bytes % q) != 0 || nvls_chunk == 0 || (nvls_chunk % q) != 0 || ts_chunk == 0 ||
+        (ts_chunk % q) != 0 || c.nvls_mc == nullptr || !NvlsSupports(dtype, op) ||
+        (size_t)nslots * nvls_slot > c.nvls_bytes || nvls_slot < nvls_chunk ||
+        (size_t)nslots * 2 * c.nranks * ts_slot > c.data_bytes / 2 || ts_slot * c.nranks < ts_chunk) {
+        return cudaErrorInvalidValue;
+    }
+    PipeParams p;
+    p.comm = c;
+    p.src = src;
+    p.dst = dst;
+    p.bytes = bytes;
+    p.chunk = ts_chunk;
+    p.slot_bytes = ts_slot;
+    p.nrounds = (int)((bytes - nvls_bytes + ts_chunk - 1) / ts_chunk);
+    p.nslots = nslots;
+    p.dtype = dtype;
+    p.op = op;
+    p.scale = scale;
+    p.nvls = kPipeTwoShot;
+    p.hyb_ctas = nvls_ctas;
+    p.hyb_bytes = nvls_bytes;
+    p.hyb_chunk = nvls_chunk;
+    p.hyb_slot = nvls_slot;
+    p.hyb_rounds = (int)((nvls_bytes + nvls_chunk - 1) / nvls_chunk);
+    const int nctas = nvls_ctas + ts_ctas;
     switch (dtype) {
     case kF32: return launch_op<kF32>(p, nctas, stream);
     case kF64: return launch_op<kF64>(p, nctas, stream);

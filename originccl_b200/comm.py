@@ -45,6 +45,7 @@ class Algo(enum.IntEnum):
     TWOSHOT = 2
     NVLS = 3
     RING = 4
+    HYBRID = 5  # AllReduce: part through the switch (NVLS), the rest two-shot, in one launch
 
 
 class CollFunc(enum.IntEnum):

@@ -56,7 +56,7 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
     dt = getattr(torch, dtype)
     es = torch.empty((), dtype=dt).element_size()
     algo_v = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS,
-              "ring": Algo.RING}[algo]
+              "ring": Algo.RING, "hybrid": Algo.HYBRID}[algo]
     rop = {"sum": ReduceOp.SUM, "max": ReduceOp.MAX, "min": ReduceOp.MIN, "avg": ReduceOp.AVG}[redop]
     nccl_op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
                "avg": dist.ReduceOp.AVG}[redop]
@@ -225,7 +225,7 @@ def main(argv=None) -> None:
     p.add_argument("--factor", type=int, default=2)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--iters", type=int, default=100)
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring"])
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"])
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--both-places", action="store_true", help="sweep out of place, then in place")
     p.add_argument("--no-nccl", action="store_true")

@@ -60,7 +60,7 @@ def main(argv=None) -> None:
                                                          "reducescatter"])
     p.add_argument("--bytes", default="128M", help="payload per rank (AllGather/ReduceScatter: per-rank block)")
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring"])
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"])
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"])
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--traced", type=int, default=3)
@@ -87,7 +87,7 @@ def main(argv=None) -> None:
     es = torch.empty((), dtype=dt).element_size()
     n = max(1, parse_size(args.bytes) // es)
     algo = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS,
-            "ring": Algo.RING}[args.algo]
+            "ring": Algo.RING, "hybrid": Algo.HYBRID}[args.algo]
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     nin = n * world if args.op == "reducescatter" else n
     nout = n * world if args.op == "allgather" else n
@@ -107,9 +107,9 @@ def main(argv=None) -> None:
         elif args.op == "reduce":
             comm.reduce(x, 0, out=y, algo=algo)
         elif args.op == "allgather":
-            comm.all_gather(y, x)
+            comm.all_gather(y, x, algo=algo)
         else:
-            comm.reduce_scatter(y, x)
+            comm.reduce_scatter(y, x, algo=algo)
 
     barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
     for _ in range(args.warmup):

@@ -78,7 +78,8 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
     dev = rank % torch.cuda.device_count()
     torch.cuda.set_device(dev)
     comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
-    algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS, "ring": Algo.RING}
+    algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS, "ring": Algo.RING,
+                "hybrid": Algo.HYBRID}
     ran = 0
     used = set()
     dtypes = ["float32", "bfloat16", "int32"] if quick else DTYPES
@@ -140,8 +141,9 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
     for i, o in enumerate(outs):
         exp = oracle("sum", [rank_input(r, 1024 + 3 * i, "float32", seed=i) for r in range(world)], world) * 0.5
         _close(o, exp.float(), "float32", f"group item {i}")
+    nvls = comm.nvls_enabled
     comm.destroy()
-    return {"ran": ran, "algorithms": sorted(used), "group_launches": launches}
+    return {"ran": ran, "algorithms": sorted(used), "group_launches": launches, "nvls": nvls}
 
 
 def run_p2p(rank: int, world: int) -> Dict:
