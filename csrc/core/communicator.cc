@@ -5,6 +5,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -197,7 +198,13 @@ bool Communicator::Init(const CommConfig& cfg) {
     }
     // Every listener exists before the bootstrap announces it (no port races).
     fdpass_.reset(new FdPasser());
-    const std::string ns = std::string(cfg.unique_id.ip_addr) + ":" + std::to_string(cfg.unique_id.port);
+    // A one-rank communicator has no unique id to share; its socket name must still be unique
+    // among the communicators of this host (several may live in one process).
+    static std::atomic<unsigned> solo_serial{0};
+    const std::string ns = cfg.world_size > 1
+                               ? std::string(cfg.unique_id.ip_addr) + ":" + std::to_string(cfg.unique_id.port)
+                               : "solo." + std::to_string(static_cast<long>(getpid())) + "." +
+                                     std::to_string(solo_serial.fetch_add(1));
     if (!fdpass_->Listen(ns, cfg.rank)) return false;
     uint16_t data_port = 0;
     if (cfg.device < 0) {

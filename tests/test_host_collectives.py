@@ -119,3 +119,17 @@ def test_tp_dp_mesh():
     res = _mp.run(6, host_cases.run_mesh, 3, timeout=180)
     assert [r["tp"] for r in res] == [(0, 3), (1, 3), (2, 3)] * 2
     assert [r["dp"] for r in res] == [(0, 2)] * 3 + [(1, 2)] * 3
+
+
+def test_several_single_rank_communicators_in_one_process():
+    # One-rank communicators share no unique id; each still needs its own local socket name.
+    import numpy as np
+
+    import originccl_b200 as occl
+    comms = [occl.Communicator().init(0, 1, None) for _ in range(3)]
+    x = np.arange(8, dtype=np.float32)
+    for c in comms:
+        c.all_reduce(x)
+    assert (x == np.arange(8, dtype=np.float32)).all()
+    for c in comms:
+        c.destroy()
