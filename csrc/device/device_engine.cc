@@ -105,6 +105,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
     knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
+    knob_tp_multicast_ = EnvInt("BCCL_TP_MULTICAST", 1) != 0;
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
@@ -195,14 +196,14 @@ bool DeviceEngine::Synchronize(cudaStream_t stream) {
     return CheckDeviceError();
 }
 
-bool DeviceEngine::EnsureTpBuffer(SymBuffer (&bufs)[2], size_t* have, size_t need) {
+bool DeviceEngine::EnsureTpBuffer(SymBuffer (&bufs)[2], size_t* have, size_t need, bool multicast) {
     if (*have >= need) return true;
     cudaDeviceSynchronize();
     if (!bs_->Barrier()) return false;  // no peer may still use the old buffers
     for (SymBuffer& b : bufs) sm_.Free(&b);
     *have = 0;
     for (SymBuffer& b : bufs) {
-        if (!sm_.Alloc(need, false, &b)) return false;
+        if (!sm_.Alloc(need, multicast && sm_.multicast_supported(), &b)) return false;
     }
     *have = need;
     return true;
@@ -239,7 +240,7 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
     if (nranks_ == 1) {
         e = LaunchGemmBf16(x_local, w, y, m, n, k, n, act, tp_err_, 0, stream);
     } else {
-        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2)) return false;
+        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2, knob_tp_multicast_)) return false;
         const unsigned long long seq = ++tp_ag_calls_;
         const int par = static_cast<int>(seq & 1ull);
         TpArgs t;
@@ -250,6 +251,7 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
             t.ag_counters_peer[p] = TpFlags(uc_.ptr[p], kAgCountersOff);
         }
         t.ag_counters = TpFlags(uc_.ptr[rank_], kAgCountersOff);
+        t.xg_mc = knob_tp_multicast_ ? tp_xg_[par].mc : nullptr;
         e = LaunchTpGemm(kModeAllGather, x_local, tp_xg_[par].ptr[rank_], w, y, m, n, k, act, tp_err_, t, stream);
     }
     if (e != cudaSuccess) {
@@ -279,7 +281,7 @@ bool DeviceEngine::TpGemmReduceScatter(const void* h, const void* w, void* out, 
             LOG_ERROR("GEMM-ReduceScatter: too many output tiles per rank");
             return false;
         }
-        if (!EnsureTpBuffer(tp_rs_, &tp_rs_bytes_, static_cast<size_t>(m) * n * 2)) return false;
+        if (!EnsureTpBuffer(tp_rs_, &tp_rs_bytes_, static_cast<size_t>(m) * n * 2, false)) return false;
         const unsigned long long seq = ++tp_rs_calls_;
         const int par = static_cast<int>(seq & 1ull);
         TpArgs t;

@@ -23,6 +23,7 @@ struct TpArgs {
     // AllGather -> GEMM
     const void* x_local;                      // this rank's shard [ms, K]
     void* xg[kMaxRanks];                      // every rank's gathered-X buffer (this call's half)
+    void* xg_mc;                              // its NVLS multicast address (null: one store per peer)
     const unsigned long long* ag_counters;    // here: [src][kTpMaxChunks]
     unsigned long long* ag_counters_peer[kMaxRanks];  // the same array on every rank
     // GEMM -> ReduceScatter

@@ -64,6 +64,12 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 __device__ __forceinline__ void red_add_sys(unsigned long long* p, unsigned long long v) {
     asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// One 16-byte store that the switch writes into every GPU's copy of a multicast-bound buffer.
+__device__ __forceinline__ void multimem_st16(void* p, const uint4& v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -116,6 +122,8 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
         if (MODE == kModeAllGather) {
             // Push this rank's shard, chunk by chunk, into every peer's gathered-X buffer;
             // CTA b owns slice b of every chunk. One counter bump per (peer, chunk) per CTA.
+            // With a multicast-bound buffer each vector leaves this GPU once (multimem.st; the
+            // switch writes every copy) instead of once per peer.
             const int per = g.tp.ms / BM;
             const size_t chunk_bytes = (size_t)BM * g.K * 2;
             const size_t slice = ((chunk_bytes + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
@@ -127,11 +135,25 @@ __device__ __forceinline__ void comm_warps(const Args& g, int num_n, volatile in
             for (int c = 0; c < per; ++c) {
                 const char* srcp = reinterpret_cast<const char*>(g.tp.x_local) + (size_t)c * chunk_bytes;
                 const size_t dst_off = ((size_t)g.tp.rank * per + c) * chunk_bytes;
-                for (size_t o = lo + (size_t)ctid * 16; ctid < pushers && o < hi; o += (size_t)pushers * 16) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
-                    for (int q = 0; q < g.tp.nranks; ++q) {
-                        if (q == g.tp.rank) continue;
-                        __stcg(reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.tp.xg[q]) + dst_off + o), v);
+                if (g.tp.xg_mc != nullptr) {
+                    char* mc = reinterpret_cast<char*>(g.tp.xg_mc) + dst_off;
+                    size_t o = lo + (size_t)ctid * 16;
+                    const size_t step = (size_t)pushers * 16;
+                    for (; ctid < pushers && o + 3 * step < hi; o += 4 * step) {  // four loads in flight
+                        uint4 v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(srcp + o + u * step);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) multimem_st16(mc + o + u * step, v[u]);
+                    }
+                    for (; ctid < pushers && o < hi; o += step) multimem_st16(mc + o, *reinterpret_cast<const uint4*>(srcp + o));
+                } else {
+                    for (size_t o = lo + (size_t)ctid * 16; ctid < pushers && o < hi; o += (size_t)pushers * 16) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(srcp + o);
+                        for (int q = 0; q < g.tp.nranks; ++q) {
+                            if (q == g.tp.rank) continue;
+                            __stcg(reinterpret_cast<uint4*>(reinterpret_cast<char*>(g.tp.xg[q]) + dst_off + o), v);
+                        }
                     }
                 }
                 asm volatile("bar.sync 2, %0;" ::"r"(cnt_threads) : "memory");
