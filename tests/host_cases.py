@@ -571,3 +571,27 @@ def run_mesh(rank: int, world: int, tp: int) -> Dict:
     mesh.destroy()
     comm.destroy()
     return out
+
+
+def run_algo_overrides(rank: int, world: int) -> Dict:
+    """AllGather / ReduceScatter with an explicit algorithm (the host path has one algorithm, so
+    the override is accepted and the result stays exact)."""
+    import numpy as np
+
+    import originccl_b200 as occl
+    from originccl_b200 import Algo, ReduceOp
+    comm = occl.init_from_env()
+    n = 1000
+    x = (np.arange(n, dtype=np.float32) + rank * 0.5)
+    for algo in (Algo.AUTO, Algo.ONESHOT, Algo.NVLS):
+        out = np.zeros(n * world, np.float32)
+        comm.all_gather(out, x, algo=algo)
+        want = np.concatenate([np.arange(n, dtype=np.float32) + r * 0.5 for r in range(world)])
+        assert (out == want).all(), algo
+        big = np.tile(x, world)
+        rs = np.zeros(n, np.float32)
+        comm.reduce_scatter(rs, big, ReduceOp.SUM, algo=algo)
+        exp = sum(np.arange(n, dtype=np.float32) + r * 0.5 for r in range(world))
+        assert (rs == exp).all(), algo
+    comm.destroy()
+    return {"ok": True}

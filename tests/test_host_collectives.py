@@ -133,3 +133,8 @@ def test_several_single_rank_communicators_in_one_process():
     assert (x == np.arange(8, dtype=np.float32)).all()
     for c in comms:
         c.destroy()
+
+
+def test_allgather_reducescatter_algorithm_override():
+    res = _mp.run(3, host_cases.run_algo_overrides, timeout=120)
+    assert all(r["ok"] for r in res)
