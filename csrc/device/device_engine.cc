@@ -100,6 +100,7 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_zero_copy_ = EnvInt("BCCL_ZERO_COPY", 1) != 0;
     knob_p2p_zc_min_ = static_cast<size_t>(std::max<long>(16, EnvInt("BCCL_P2P_ZC_MIN_BYTES", 1 << 20)));
     knob_pipe_slots_ = static_cast<int>(std::max<long>(3, std::min<long>(16, EnvInt("BCCL_PIPE_SLOTS", 3))));
+    knob_pipe_lag_ = static_cast<int>(std::max<long>(1, std::min<long>(2, EnvInt("BCCL_PIPE_LAG", 1))));
     knob_pipe_rounds_ = EnvInt("BCCL_PIPE_ROUNDS", 0);
     knob_pipe_min_chunk_ = EnvInt("BCCL_PIPE_MIN_CHUNK", 4 << 20);
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
@@ -592,7 +593,10 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
     const int dt = static_cast<int>(t.dtype), op = static_cast<int>(t.op);
     const size_t bytes = t.count * DataTypeSize(t.dtype);
     const unsigned long long q = 16ull * nranks_;
-    const int slots = knob_pipe_slots_;
+    // The slot ring must be 2L+1 deep for a barrier lag of L (ar_pipe.cu); every NVLS launch kind
+    // uses the same slot count, so their rings line up.
+    const int lag = knob_pipe_lag_;
+    const int slots = std::max(knob_pipe_slots_, 2 * lag + 1);
     // Rounds of at least `min_chunk` bytes (each CTA then moves >= ~100 KB between fences),
     // about `rounds` of them so the software pipeline has something to overlap.
     // Two rounds up to 64 MiB, four above (measured on 2 and 8 x B200: fewer, larger rounds win
@@ -622,7 +626,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
             e = LaunchAllReduceHybrid(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, nb,
                                       pick_chunk_for(nb, nslot), nslot, nv_ctas,
                                       pick_chunk_for(bytes - nb, tslot * nranks_), tslot, ctas - nv_ctas, slots,
-                                      stream);
+                                      stream, lag);
             last_algo_ = "hybrid";
             if (e != cudaSuccess) {
                 LOG_ERROR("rank %d: hybrid launch failed: %s", rank_, cudaGetErrorString(e));
@@ -644,7 +648,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         const unsigned long long chunk = pick_chunk(slot);
         if (t.func == CollFunc::AllReduce) {
             e = LaunchAllReducePipe(dc_, kPipeNvls, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots,
-                                    ctas, stream);
+                                    ctas, stream, lag);
         } else if (t.func == CollFunc::AllGather || t.func == CollFunc::ReduceScatter) {
             // A slot holds one chunk of every rank's block.
             const unsigned long long cap = RoundDown(slot / static_cast<unsigned long long>(nranks_), 16);
@@ -674,7 +678,7 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
             chunk = pick_chunk(slot * nranks_);
         }
         e = LaunchAllReducePipe(dc_, kind, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, chunk, slot, slots, ctas,
-                                stream);
+                                stream, lag);
         last_algo_ = kind == kPipeOneShot ? "oneshot_pipe" : "twoshot";
     }
     if (e != cudaSuccess) {

@@ -112,6 +112,7 @@ private:
     bool knob_zero_copy_ = true;
     size_t knob_p2p_zc_min_ = 1u << 20;
     int knob_pipe_slots_ = 3;
+    int knob_pipe_lag_ = 1;           // BCCL_PIPE_LAG: barrier lag of the pipelined kernels (1 or 2)
     long knob_pipe_rounds_ = 0;  // 0: by size
     long knob_pipe_min_chunk_ = 4 << 20;
     long knob_pipe_kind_ = -1;

@@ -46,6 +46,7 @@ struct PipeParams {
     int op;
     float scale;
     int nvls;   // PipeKind
+    int lag;    // barrier lag L (1 or 2): iteration t waits for barrier t-L; needs nslots >= 2L+1
     // Hybrid launch (hyb_ctas > 0): CTAs [0, hyb_ctas) run NVLS on bytes [0, hyb_bytes) in
     // hyb_rounds rounds of hyb_chunk (NVLS slots of hyb_slot bytes), the remaining CTAs run
     // `nvls` (two-shot) on [hyb_bytes, bytes) with chunk / slot_bytes / nrounds above. The two
@@ -345,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const char* src = static_cast<const char*>(p.src) + part_off;
     char* dst = static_cast<char*>(p.dst) + part_off;
     const int depth = (kind == kPipeOneShot) ? 1 : 2;
-    const int iters = nrounds + depth;
+    const int L = p.lag;
+    const int iters = nrounds + depth * L;
     // Two warp groups: "net" (warps 0-7) runs the phase that crosses NVLink, "local" (warps
     // 8-15) the phases that stay in this GPU's memory; without the split both do everything.
     const int half = blockDim.x / 2;
@@ -449,41 +451,57 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
             }
         }
     };
+    // Barrier k closes iteration k on every rank. Iteration t starts only once barrier t-L has
+    // closed: L = 1 is the lock-step schedule; L = 2 lets a CTA run one iteration ahead of the
+    // slowest CTA with its index on the other GPUs, which hides the barrier's latency behind
+    // the next iteration's work (the slot ring is then 2L+1 deep, so no slot is rewritten
+    // while a rank may still read it).
+    auto wait_barrier = [&](int k) {
+        bool w = true;
+        if (threadIdx.x < n && threadIdx.x != r) {
+            w = wait_flag_geq(c, barrier_flag(c.uc[r], blockIdx.x, threadIdx.x), bar0 + (uint64_t)k + 1,
+                              threadIdx.x, k);
+        }
+        w = __syncthreads_and(w) != 0;
+        if (threadIdx.x == 0) trace(c, 0, kTrBarrier, k);
+        return w;
+    };
     bool ok = true;
     for (int t = 0; t < iters && ok; ++t) {
-        const bool has_a = t < nrounds, has_b = t >= 1 && t - 1 < nrounds;
-        const bool has_c = depth == 2 && t >= 2 && t - 2 < nrounds;
+        if (t >= L && !(ok = wait_barrier(t - L))) break;
+        const bool has_a = t < nrounds, has_b = t >= L && t - L < nrounds;
+        const bool has_c = depth == 2 && t >= 2 * L && t - 2 * L < nrounds;
         // Which group runs what: NVLS crosses NVLink in B (multimem); two-shot and one-shot
         // cross it in A (pushes). The other phases run on the local group.
         if (kind == kPipeNvls) {
-            if (do_net && has_b) phase_b(t - 1, gtid, gnt);
+            if (do_net && has_b) phase_b(t - L, gtid, gnt);
             if (do_local && has_a) phase_a(t, gtid, gnt);
-            if (do_local && has_c) phase_c(t - 2, gtid, gnt);
+            if (do_local && has_c) phase_c(t - 2 * L, gtid, gnt);
         } else {
             if (do_net && has_a) phase_a(t, gtid, gnt);
-            if (do_local && has_b) phase_b(t - 1, gtid, gnt);
-            if (do_local && has_c) phase_c(t - 2, gtid, gnt);
+            if (do_local && has_b) phase_b(t - L, gtid, gnt);
+            if (do_local && has_c) phase_c(t - 2 * L, gtid, gnt);
         }
-        // ---- barrier t: both groups' writes are issued; fence + signal + wait.
+        // ---- barrier t: both groups' writes are issued; fence + signal (the wait comes L
+        // iterations later).
         __syncthreads();
         if (threadIdx.x == 0) trace(c, 0, kTrStaged, t);  // this CTA's phases of iteration t are issued
-        const int tid = threadIdx.x;
-        if (tid < n && tid != r) {
+        if (threadIdx.x < n && threadIdx.x != r) {
             fence_acq_rel_sys();
-            st_relaxed_sys_flag(barrier_flag(c.uc[tid], blockIdx.x, r), bar0 + (uint64_t)t + 1);
-            ok = wait_flag_geq(c, barrier_flag(c.uc[r], blockIdx.x, tid), bar0 + (uint64_t)t + 1, tid, t);
+            st_relaxed_sys_flag(barrier_flag(c.uc[threadIdx.x], blockIdx.x, r), bar0 + (uint64_t)t + 1);
         }
-        ok = __syncthreads_and(ok) != 0;
-        if (tid == 0) trace(c, 0, kTrBarrier, t);
     }
+    // The launch ends with every rank's last iteration closed: a completed launch implies every
+    // rank finished all its phases, whatever kind of launch comes next.
+    if (ok) ok = wait_barrier(iters - 1);
     if (threadIdx.x == 0) trace(c, 0, kTrEnd, iters);
     // Every CTA passes the launch-wide totals (the last one to finish applies them).
     if (p.hyb_ctas > 0) {
-        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)max(p.nrounds, p.hyb_rounds) + 2, (uint64_t)p.hyb_rounds);
+        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)max(p.nrounds, p.hyb_rounds) + 2 * p.lag, (uint64_t)p.hyb_rounds);
     } else if (p.nvls == kPipeNvls) {
-        finish_launch(c, 0, (uint64_t)p.nrounds + 2, (uint64_t)p.nrounds);
+        finish_launch(c, 0, (uint64_t)p.nrounds + 2 * p.lag, (uint64_t)p.nrounds);
     } else {
-        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)p.nrounds + (p.nvls == kPipeOneShot ? 1 : 2), 0);
+        finish_launch(c, (uint64_t)p.nrounds, (uint64_t)p.nrounds + (p.nvls == kPipeOneShot ? 1 : 2) * p.lag, 0);
     }
 }
 
@@ -509,10 +527,11 @@ cudaError_t launch_op(const PipeParams& p, int nctas, cudaStream_t s) {
 
 cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
                                 int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
-                                int nslots, int nctas, cudaStream_t stream) {
+                                int nslots, int nctas, cudaStream_t stream, int lag) {
     using namespace dev;
     const bool nvls = kind == kPipeNvls;
-    if (nctas < 1 || nctas > kMaxCtas || nslots < 3 || chunk == 0 || (chunk % (16ull * c.nranks)) != 0) {
+    if (nctas < 1 || nctas > kMaxCtas || lag < 1 || lag > 2 || nslots < 2 * lag + 1 || chunk == 0 ||
+        (chunk % (16ull * c.nranks)) != 0) {
         return cudaErrorInvalidValue;
     }
     if (kind == kPipeOneShot && ((size_t)nslots * c.nranks * slot_bytes > c.data_bytes / 2 || slot_bytes < chunk)) {
@@ -539,6 +558,7 @@ cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, voi
     p.op = op;
     p.scale = scale;
     p.nvls = kind == kPipeNvls ? 1 : (kind == kPipeOneShot ? 2 : 0);
+    p.lag = lag;
     p.hyb_ctas = 0;
     p.hyb_rounds = 0;
     p.hyb_bytes = p.hyb_chunk = p.hyb_slot = 0;
@@ -557,11 +577,12 @@ cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, voi
 cudaError_t LaunchAllReduceHybrid(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
                                   int op, float scale, unsigned long long nvls_bytes, unsigned long long nvls_chunk,
                                   unsigned long long nvls_slot, int nvls_ctas, unsigned long long ts_chunk,
-                                  unsigned long long ts_slot, int ts_ctas, int nslots, cudaStream_t stream) {
+                                  unsigned long long ts_slot, int ts_ctas, int nslots, cudaStream_t stream, int lag) {
     using namespace dev;
     const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
     const unsigned long long q = 16ull * c.nranks;
-    if (nvls_ctas < 1 || ts_ctas < 1 || nvls_ctas + ts_ctas > kMaxCtas || nslots < 3 || nvls_bytes == 0 ||
+    if (nvls_ctas < 1 || ts_ctas < 1 || nvls_ctas + ts_ctas > kMaxCtas || lag < 1 || lag > 2 ||
+        nslots < 2 * lag + 1 || nvls_bytes == 0 ||
         nvls_bytes >= bytes || (nvls_bytes % q) != 0 || nvls_chunk == 0 || (nvls_chunk % q) != 0 || ts_chunk == 0 ||
         (ts_chunk % q) != 0 || c.nvls_mc == nullptr || !NvlsSupports(dtype, op) ||
         (size_t)nslots * nvls_slot > c.nvls_bytes || nvls_slot < nvls_chunk ||
@@ -581,6 +602,7 @@ cudaError_t LaunchAllReduceHybrid(const DevComm& c, const void* src, void* dst, 
     p.op = op;
     p.scale = scale;
     p.nvls = kPipeTwoShot;
+    p.lag = lag;
     p.hyb_ctas = nvls_ctas;
     p.hyb_bytes = nvls_bytes;
     p.hyb_chunk = nvls_chunk;

@@ -21,14 +21,15 @@ cudaError_t LaunchPushEngine(const DevComm& c, const WorkItem* items, int nitems
 enum PipeKind : int { kPipeTwoShot = 0, kPipeNvls = 1, kPipeOneShot = 2 };
 cudaError_t LaunchAllReducePipe(const DevComm& c, int kind, const void* src, void* dst, unsigned long long count,
                                 int dtype, int op, float scale, unsigned long long chunk, unsigned long long slot_bytes,
-                                int nslots, int nctas, cudaStream_t stream);
+                                int nslots, int nctas, cudaStream_t stream, int lag = 1);
 // One launch of the pipelined AllReduce split in two parts that run side by side: nvls_ctas
 // CTAs reduce bytes [0, nvls_bytes) through the switch (NVLS kind), ts_ctas CTAs the rest over
 // peer memory (two-shot kind). nvls_bytes and both chunks are multiples of 16 * nranks.
 cudaError_t LaunchAllReduceHybrid(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
                                   int op, float scale, unsigned long long nvls_bytes, unsigned long long nvls_chunk,
                                   unsigned long long nvls_slot, int nvls_ctas, unsigned long long ts_chunk,
-                                  unsigned long long ts_slot, int ts_ctas, int nslots, cudaStream_t stream);
+                                  unsigned long long ts_slot, int ts_ctas, int nslots, cudaStream_t stream,
+                                  int lag = 1);
 
 // NVSwitch multicast Broadcast (func 1), Reduce (2), AllGather (3) and ReduceScatter (4) over
 // the NVLS slot ring. count is the payload (Broadcast, Reduce) or the per-rank block

@@ -48,6 +48,15 @@ def test_two_rank_suite_all_algorithms():
 
 
 @pytest.mark.multigpu
+def test_two_rank_pipelines_with_barrier_lag():
+    # BCCL_PIPE_LAG=2: iteration t waits for barrier t-2 over a five-slot ring; several rounds.
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_suite, [(3 << 20) + 5, (40 << 20) + 3], ["twoshot", "nvls", "hybrid", "auto"],
+                  True, timeout=900, env={"BCCL_PIPE_LAG": "2", "BCCL_PIPE_MIN_CHUNK": str(1 << 20)})
+    assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
 def test_all_gpu_suite():
     n = torch.cuda.device_count() if torch.cuda.is_available() else 0
     if n < 3:
