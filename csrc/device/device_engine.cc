@@ -747,6 +747,8 @@ bool DeviceEngine::RunP2p(const std::vector<CollTask>& p2p, cudaStream_t stream)
 bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaStream_t stream) {
     std::vector<WorkItem> batch;
     unsigned long long stream_bytes = 0;
+    int ncoll = 0;
+    for (const CollTask& t : sorted) ncoll += (!IsP2p(t.func) && t.count > 0) ? 1 : 0;
     for (const CollTask& t : sorted) {
         if (IsP2p(t.func)) continue;
         if (t.count == 0) continue;
@@ -756,6 +758,13 @@ bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaS
                               NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
         AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
                                             t.algo != Algo::kAuto ? t.algo : forced_);
+        // Inside a group, a collective of up to kGroupPushMaxBytes per rank joins the batched push
+        // launch even where the planner would give it a launch of its own: the launch and its
+        // barriers cost more than the push moves extra at that size, and the group stays one
+        // kernel (the reference's dynamic executor keeps a batch on its channels for the same reason).
+        if (ncoll > 1 && t.algo == Algo::kAuto && forced_ == Algo::kAuto && bytes <= kGroupPushMaxBytes) {
+            c.algo = Algo::kOneShot;
+        }
         const bool ring = c.algo == Algo::kRing && t.func == CollFunc::AllReduce && nranks_ > 1;
         if (ring) c.ctas = max_ctas_ > 0 ? std::min(num_sms_, max_ctas_) : num_sms_;
         // Symmetric (multicast-bound) user buffers: NVLS without staging. AllReduce when the

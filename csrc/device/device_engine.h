@@ -100,6 +100,8 @@ private:
     bool RunP2p(const std::vector<CollTask>& p2p, cudaStream_t stream);
     // SMs left to NCCL's point-to-point kernels while a mixed group's collectives run.
     static constexpr int kP2pReservedSms = 32;
+    // Collectives of a group up to this many bytes per rank run in the group's push launch.
+    static constexpr size_t kGroupPushMaxBytes = 1u << 20;
 
     int rank_ = 0;
     int nranks_ = 1;
