@@ -56,7 +56,11 @@ def main(argv=None) -> int:
     lo, hi = parse_size(args.min_bytes), parse_size(args.max_bytes)
     from originccl_b200.utils.results import ResultLog
     emit = ResultLog("mixed_bench", args.out, enabled=rank == 0)
-    common = dict(factor=args.factor, warmup=args.warmup, iters=args.iters, seed=42, emit=emit)
+    # The NCCL arm of the size sweeps calls ncclReduceScatter & co. directly on the same out-of-place
+    # operation as this library (torch.distributed's broadcast / reduce work in place).
+    from originccl_b200.utils.nccl_direct import NcclDirect
+    ref_comm = NcclDirect(dist.distributed_c10d._get_default_store(), rank, world, local, tag="mixed")
+    common = dict(factor=args.factor, warmup=args.warmup, iters=args.iters, seed=42, emit=emit, ref_comm=ref_comm)
     all_ok = True
 
     def timed(fn) -> float:
@@ -182,6 +186,8 @@ def main(argv=None) -> int:
                                  "kernel_launches": launches, "nccl_time_us": round(t_n, 2),
                                  "speedup_vs_nccl": round(t_n / t_o, 3), "check": ok}))
             del xs, outs, ref_outs
+    torch.cuda.synchronize()
+    ref_comm.destroy()
     comm.destroy()
     barrier()
     dist.destroy_process_group()
