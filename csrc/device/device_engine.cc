@@ -106,7 +106,6 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
     knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
-    knob_tp_multicast_ = EnvInt("BCCL_TP_MULTICAST", 1) != 0;
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
@@ -241,7 +240,10 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
     if (nranks_ == 1) {
         e = LaunchGemmBf16(x_local, w, y, m, n, k, n, act, tp_err_, 0, stream);
     } else {
-        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2, knob_tp_multicast_)) return false;
+        // Read per call (a fused op costs far more than a getenv), so benchmarks can compare both
+        // pushes in one process; the buffer is multicast-bound from its first allocation on.
+        const bool multicast = EnvInt("BCCL_TP_MULTICAST", 1) != 0;
+        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2, true)) return false;
         const unsigned long long seq = ++tp_ag_calls_;
         const int par = static_cast<int>(seq & 1ull);
         TpArgs t;
@@ -252,7 +254,7 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
             t.ag_counters_peer[p] = TpFlags(uc_.ptr[p], kAgCountersOff);
         }
         t.ag_counters = TpFlags(uc_.ptr[rank_], kAgCountersOff);
-        t.xg_mc = knob_tp_multicast_ ? tp_xg_[par].mc : nullptr;
+        t.xg_mc = multicast ? tp_xg_[par].mc : nullptr;
         e = LaunchTpGemm(kModeAllGather, x_local, tp_xg_[par].ptr[rank_], w, y, m, n, k, act, tp_err_, t, stream);
     }
     if (e != cudaSuccess) {

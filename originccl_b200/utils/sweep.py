@@ -35,7 +35,8 @@ def parse_size(s: str) -> int:
 
 def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, factor: int = 2, warmup: int = 20,
               iters: int = 100, algo: str = "auto", inplace: bool = False, nccl: bool = True, redop: str = "sum",
-              seed: int = 1234, emit=print, graph: int = 0, buffers: str = "plain", ref_comm=None) -> list:
+              seed: int = 1234, emit=print, graph: int = 0, buffers: str = "plain", ref_comm=None,
+              variant: str = "") -> list:
     """Times ``op`` at every size from min_bytes to max_bytes (x factor) with this library and
     with NCCL on the same buffers; returns (and emits on rank 0) one record per size.
 
@@ -152,6 +153,8 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
                "time_us": round(t_ours, 3), "algbw_gbs": round(nbytes / t_ours / 1e3, 3),
                "busbw_gbs": round(nbytes / t_ours / 1e3 * f, 3), "inplace": inplace, "check": ok,
                "graph": graph, "buffers": buffers, "nccl_api": "direct" if rc is not None else "torch.distributed"}
+        if variant:
+            rec["variant"] = variant
         if t_nccl is not None:
             rec.update({"nccl_time_us": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e3 * f, 3),
                         "speedup_vs_nccl": round(t_nccl / t_ours, 3)})
@@ -225,7 +228,12 @@ def main(argv=None) -> None:
     p.add_argument("--factor", type=int, default=2)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--iters", type=int, default=100)
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"])
+    p.add_argument("--algo", default="auto",
+                   help="comma list of auto, oneshot, twoshot, nvls, ring, hybrid (each swept in turn)")
+    p.add_argument("--variants", default="",
+                   help="';'-separated environment variants, each a ','-separated list of NAME=VALUE set "
+                        "while a fresh communicator initialises (e.g. 'BCCL_PIPE_LAG=2;BCCL_PIPE_LAG=1'); "
+                        "every algorithm is swept under every variant")
     p.add_argument("--inplace", action="store_true")
     p.add_argument("--both-places", action="store_true", help="sweep out of place, then in place")
     p.add_argument("--no-nccl", action="store_true")
@@ -249,30 +257,53 @@ def main(argv=None) -> None:
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=300))
-    comm = occl.init_from_store(dist.distributed_c10d._get_default_store(), rank, world, device=local)
+    store = dist.distributed_c10d._get_default_store()
     from originccl_b200.utils.results import ResultLog
     log = ResultLog("sweep", args.out, enabled=rank == 0)
 
     ref_comm = None
     if not args.no_nccl and args.nccl_api == "direct":
         from originccl_b200.utils.nccl_direct import NcclDirect
-        ref_comm = NcclDirect(dist.distributed_c10d._get_default_store(), rank, world, local, tag="sweep")
+        ref_comm = NcclDirect(store, rank, world, local, tag="sweep")
     dtypes = [d.strip() for d in args.dtype.split(",") if d.strip()]
     for d in dtypes:
         if d not in ("float32", "bfloat16", "float16", "int32"):
             raise SystemExit(f"unsupported dtype {d}")
+    algos = [a.strip() for a in args.algo.split(",") if a.strip()]
+    for a in algos:
+        if a not in ("auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"):
+            raise SystemExit(f"unknown algorithm {a}")
     places = [False, True] if args.both_places else [args.inplace]
-    for d in dtypes:
-        for inplace in places:
-            run_sweep(comm, op=args.op, dtype=d, min_bytes=parse_size(args.min_bytes),
-                      max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup,
-                      iters=args.iters, algo=args.algo, inplace=inplace, nccl=not args.no_nccl, redop=args.redop,
-                      emit=log, graph=args.graph, buffers=args.buffers, ref_comm=ref_comm)
+    variants = [v.strip() for v in args.variants.split(";")] if args.variants else [""]
+    nccl_done = set()
+    for variant in variants:
+        saved = {}
+        for kv in filter(None, (x.strip() for x in variant.split(","))):
+            k, v = kv.split("=", 1)
+            saved[k] = os.environ.get(k)
+            os.environ[k] = v
+        comm = occl.init_from_store(store, rank, world, device=local)
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+        for d in dtypes:
+            for inplace in places:
+                for a in algos:
+                    # NCCL once per (dtype, place): it does not depend on this library's settings.
+                    want_nccl = not args.no_nccl and (d, inplace) not in nccl_done
+                    nccl_done.add((d, inplace))
+                    run_sweep(comm, op=args.op, dtype=d, min_bytes=parse_size(args.min_bytes),
+                              max_bytes=parse_size(args.max_bytes), factor=args.factor, warmup=args.warmup,
+                              iters=args.iters, algo=a, inplace=inplace, nccl=want_nccl, redop=args.redop,
+                              emit=log, graph=args.graph, buffers=args.buffers, ref_comm=ref_comm, variant=variant)
+        comm.destroy()
+        dist.barrier(device_ids=[local])
     log.close()
     if ref_comm is not None:
         torch.cuda.synchronize()
         ref_comm.destroy()
-    comm.destroy()
     dist.barrier(device_ids=[local])
     dist.destroy_process_group()
 
