@@ -263,6 +263,11 @@ double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int
     return comm->comm.device_engine()->BandwidthProbe(mode, peer, bytes, ctas, iters);
 }
 
+int bcclDebugDeviceState(bcclComm_t comm, unsigned long long* out) {
+    if (comm == nullptr || out == nullptr || comm->comm.device_engine() == nullptr) return -1;
+    return comm->comm.device_engine()->ReadState(out) ? 0 : -1;
+}
+
 long bcclTraceDump(bcclComm_t comm, const char* path) {
     if (comm == nullptr || path == nullptr) return -1;
     return comm->comm.DumpTrace(path);

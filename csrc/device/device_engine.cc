@@ -318,6 +318,22 @@ int DeviceEngine::WaitProbe(int timeout_ms) {
     return code;
 }
 
+bool DeviceEngine::ReadState(unsigned long long* out) {
+    if (!inited_) return false;
+    cudaSetDevice(device_);
+    DevState s;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&s, state_, sizeof(s), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        return false;
+    }
+    out[0] = s.round_seq;
+    out[1] = s.barrier_seq;
+    out[2] = s.nvls_round_seq;
+    out[3] = s.ring_seq;
+    out[4] = s.tp_seq;
+    out[5] = s.done_ctas;
+    return true;
+}
+
 double DeviceEngine::BandwidthProbe(int mode, int peer, size_t bytes, int ctas, int iters) {
     if (!inited_ || mode < 0 || mode > 3 || peer < 0 || peer >= nranks_ || ctas <= 0 || ctas > 1024 || iters <= 0)
         return -1.0;

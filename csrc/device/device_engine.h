@@ -56,6 +56,8 @@ public:
     // mode 0 local copy, 1 write to `peer`, 2 read from `peer`, 3 multimem.st. Returns GB/s
     // of the copied bytes, or a negative value on error.
     double BandwidthProbe(int mode, int peer, size_t bytes, int ctas, int iters);
+    // Copies the DevState counters (see bcclDebugDeviceState) after a device synchronize.
+    bool ReadState(unsigned long long* out);
     // Device trace (BCCL_TRACE=<records>): writes the records gathered so far as a Chrome
     // trace (chrome://tracing, Perfetto) and resets the buffer. Returns records written.
     long DumpTrace(const char* path);

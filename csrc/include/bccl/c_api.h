@@ -109,6 +109,12 @@ int bcclDebugWaitProbe(bcclComm_t comm, int timeout_ms);
  * 3 multimem.st (peers must be idle). */
 double bcclDebugBandwidth(bcclComm_t comm, int mode, int peer, size_t bytes, int ctas, int iters);
 
+/* The device-side sequence counters after the work queued so far (synchronises the device):
+ * out[0..6) = round, barrier, NVLS round, ring message, fused-TP launch counters and the
+ * finished-CTA count of the current launch (0 between launches). Every rank must hold the same
+ * values after the same calls; tests compare them across ranks. */
+int bcclDebugDeviceState(bcclComm_t comm, unsigned long long* out);
+
 /* Device trace (enabled with BCCL_TRACE=<records>): writes a Chrome trace JSON and resets the
  * buffer; returns the number of records or -1 when tracing is off. */
 long bcclTraceDump(bcclComm_t comm, const char* path);

@@ -90,6 +90,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
                                     ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int),
                                     ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
         "bcclDebugWaitProbe": (c_int, [vp, c_int]),
+        "bcclDebugDeviceState": (c_int, [vp, ctypes.POINTER(ctypes.c_ulonglong)]),
         "bcclGemmBf16": (c_int, [vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp]),
         "bcclGemmCheckError": (c_int, []),
         "bcclGemmUsesPair": (c_int, []),

@@ -456,6 +456,15 @@ class Communicator:
     def synchronize(self) -> None:
         self._check(self._lib.bcclSynchronize(self._h))
 
+    def device_state(self) -> tuple:
+        """Device communicators: the device-side sequence counters after the queued work (round,
+        barrier, NVLS round, ring message, fused-TP launch, finished CTAs of the current launch).
+        Every rank holds the same values after the same calls; synchronises the device."""
+        out = (ctypes.c_ulonglong * 6)()
+        if self._lib.bcclDebugDeviceState(self._h, out) != 0:
+            raise BcclError("device state unavailable (not a device communicator?)")
+        return tuple(int(v) for v in out)
+
     def dump_trace(self, path: str) -> int:
         """Writes the trace recorded since the last dump (BCCL_TRACE=<records> at init) as
         Chrome-trace JSON: per-CTA kernel events on device communicators, per-channel phases

@@ -46,7 +46,10 @@ class BcclProcessGroup(dist.ProcessGroup):
 
     # ------------------------------------------------------------------ communicators
     def _comm(self, t: torch.Tensor) -> Communicator:
-        key = f"cuda:{t.device.index}" if t.is_cuda else "cpu"
+        # One device communicator per process (each rank drives its own GPU, whose index differs
+        # from rank to rank), one host communicator for CPU tensors: the store key names the
+        # kind only, so every rank meets under the same key.
+        key = "cuda" if t.is_cuda else "cpu"
         comm = self._comms.get(key)
         if comm is None:
             device = t.device.index if t.is_cuda else -1

@@ -42,7 +42,8 @@ class NcclDirect:
         uid = _UniqueId()
         if rank == 0:
             self._ok(self.lib.ncclGetUniqueId(ctypes.byref(uid)), "ncclGetUniqueId")
-            store.set(key, bytes(uid.internal))
+            # All 128 bytes: reading the c_char array field would stop at its first zero byte.
+            store.set(key, ctypes.string_at(ctypes.addressof(uid), ctypes.sizeof(uid)))
         else:
             raw = store.get(key)
             ctypes.memmove(ctypes.byref(uid), raw, 128)

@@ -68,6 +68,20 @@ def _close(got, exp, dtype: str, what: str) -> None:
 OPS = {"sum": 0, "max": 1, "min": 2, "avg": 3}
 
 
+def agree_state(comm, what: str) -> None:
+    """Every rank's device-side sequence counters must be equal after the same calls (a rank whose
+    counters drift would pass a later cross-rank barrier early or use the wrong inbox half)."""
+    import torch
+    if comm.world_size < 2:
+        return
+    mine = torch.tensor(comm.device_state(), dtype=torch.int64, device="cuda")
+    allst = torch.empty(comm.world_size * mine.numel(), dtype=torch.int64, device="cuda")
+    comm.all_gather(allst, mine)
+    rows = allst.view(comm.world_size, -1).cpu().tolist()
+    assert all(r == rows[0] for r in rows), f"device counters diverged after {what}: {rows}"
+    assert rows[0][5] == 0, f"finished-CTA count left at {rows[0][5]} after {what}"
+
+
 def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: bool = False) -> Dict:
     """Runs every collective over dtypes x ops x sizes x algorithms; returns a summary."""
     import torch
@@ -95,6 +109,7 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
                     y = torch.full((n + 1,), 7, dtype=td, device="cuda")  # sentinel after the output
                     comm.all_reduce(x, ReduceOp(OPS[op]), out=y[:n], algo=algo_map[algo])
                     used.add(comm.last_algorithm)
+                    agree_state(comm, f"allreduce {dtype} {op} n={n} algo={algo}")
                     _close(y[:n], exp.to(td), dtype, f"allreduce {dtype} {op} n={n} algo={algo}")
                     assert y[n].item() == 7, "allreduce wrote past the end"
                     ran += 1
@@ -110,12 +125,14 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
                 out = torch.full((n + 1,), 7, dtype=td, device="cuda")
                 comm.reduce_scatter(out[:n], rs_x, algo=algo_map[algo])
                 used.add("rs:" + comm.last_algorithm)
+                agree_state(comm, f"reducescatter {dtype} n={n} algo={algo}")
                 _close(out[:n], oracle("sum", rs_in, world)[rank * n:(rank + 1) * n].to(td), dtype,
                        f"reducescatter {dtype} n={n} algo={algo}")
                 assert out[n].item() == 7, "reducescatter wrote past the end"
                 ag = torch.full((n * world + 1,), 7, dtype=td, device="cuda")
                 comm.all_gather(ag[:n * world], x, algo=algo_map[algo])
                 used.add("ag:" + comm.last_algorithm)
+                agree_state(comm, f"allgather {dtype} n={n} algo={algo}")
                 _close(ag[:n * world], torch.cat(inputs).to(td), dtype, f"allgather {dtype} n={n} algo={algo}")
                 assert ag[n * world].item() == 7, "allgather wrote past the end"
             _close(rs_x, rs_in[rank].cuda(), dtype, "reducescatter input changed")
@@ -123,6 +140,7 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
             root = world - 1
             b = x.clone()
             comm.broadcast(b, root)
+            agree_state(comm, f"broadcast {dtype} n={n}")
             _close(b, inputs[root].to(td), dtype, f"broadcast {dtype} n={n}")
             for algo in algos:
                 r_out = torch.empty(n, dtype=td, device="cuda") if rank == 0 else None

@@ -48,6 +48,16 @@ def test_two_rank_suite_all_algorithms():
 
 
 @pytest.mark.multigpu
+def test_two_rank_large_multi_round():
+    # Payloads of several push-engine / pipeline rounds on two ranks (160 MiB fp32), device counters
+    # compared across ranks after every call.
+    _need(2)
+    res = _mp.run(2, gpu_cases.run_suite, [(40 << 20) + 3], ["twoshot", "nvls", "hybrid", "auto"], True,
+                  timeout=900)
+    assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
 def test_two_rank_pipelines_with_barrier_lag():
     # BCCL_PIPE_LAG=2: iteration t waits for barrier t-2 over a five-slot ring; several rounds.
     _need(2)
