@@ -182,8 +182,6 @@ def test_perf_tool_host(args):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="bccl_perf --device not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 @pytest.mark.parametrize("op", ["allreduce", "allgather", "reducescatter", "broadcast", "reduce"])
 def test_perf_tool_device_one_gpu(op):
     import torch

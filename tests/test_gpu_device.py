@@ -84,8 +84,6 @@ def test_p2p_ring_over_nccl():
 
 
 @pytest.mark.multigpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="native Send/Recv kernel not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_p2p_native_kernel():
     n = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
     if n < 2:
@@ -163,8 +161,6 @@ def test_data_parallel_sync_two_ranks():
 
 
 @pytest.mark.multigpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="zero-copy NVLS kernel not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_zero_copy_nvls_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_zero_copy, timeout=300)
@@ -178,8 +174,6 @@ def test_cuda_graph_replay_single_rank():
 
 
 @pytest.mark.multigpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="CUDA-graph replay not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_cuda_graph_replay_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_graph, timeout=300)
@@ -187,8 +181,6 @@ def test_cuda_graph_replay_two_ranks():
 
 
 @pytest.mark.multigpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="registered-buffer zero-copy kernels not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_registered_buffers_zero_copy_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_registered, timeout=300)
@@ -197,16 +189,12 @@ def test_registered_buffers_zero_copy_two_ranks():
 
 @pytest.mark.parametrize("world", [1, 2])
 def test_random_device_operation_sequences(world):
-    if world > 1 and os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1":
-        pytest.skip("two-rank random device sequences not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
     _need(world)
     res = _mp.run(world, gpu_cases.run_fuzz, 5 + world, 60, timeout=600)
     assert all(r["checked"] >= 30 for r in res)
 
 
 @pytest.mark.multigpu
-@pytest.mark.skipif(os.environ.get("BCCL_TEST_EXPERIMENTAL") != "1",
-                    reason="device communicator split not yet run on a B200 (set BCCL_TEST_EXPERIMENTAL=1)")
 def test_split_device_communicators():
     _need(2)
     res = _mp.run(2, gpu_cases.run_split_device, timeout=300)
