@@ -1,5 +1,4 @@
 """Device communicator tests (need a B200). Numerics are checked against a float64 host oracle."""
-import os
 
 import pytest
 
