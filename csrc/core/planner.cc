@@ -41,11 +41,13 @@ CollFunc ParseFunc(const std::string& s) {
 std::vector<TuningRow> DefaultTable() {
     return {
         // Two ranks (2 x B200): the switch reads the issuing GPU's own copy too, so NVLS moves
-        // 1.5*S per direction against S for the peer-to-peer kernels. Pipelined push up to
-        // 8 MiB, the ring (fine-grained neighbour flags) up to 96 MiB, two-shot above.
-        {CollFunc::AllReduce, 2, 1 << 20, Algo::kOneShot, 0},
-        {CollFunc::AllReduce, 2, 8 << 20, Algo::kTwoShot, 0},
-        {CollFunc::AllReduce, 2, 96 << 20, Algo::kRing, 0},
+        // 1.5*S per direction against S for the peer-to-peer kernels (measured: NVLS and the
+        // hybrid lose at every size). One-shot push up to 2 MiB, the pipelined push up to 6 MiB,
+        // the ring (fine-grained neighbour flags) up to 48 MiB, two-shot above (64 MiB: two-shot
+        // 160.6 us, ring 167.0 us).
+        {CollFunc::AllReduce, 2, 2 << 20, Algo::kOneShot, 0},
+        {CollFunc::AllReduce, 2, 6 << 20, Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 2, 48 << 20, Algo::kRing, 0},
         {CollFunc::AllReduce, 2, ~size_t(0), Algo::kTwoShot, 0},
         // Three or more ranks (8 x B200): one-shot up to 1 MiB, pipelined two-shot up to 8 MiB,
         // NVLS above.

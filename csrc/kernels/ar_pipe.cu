@@ -357,13 +357,21 @@ __global__ void __launch_bounds__(kThreads, 1) ar_sched_kernel(const __grid_cons
     const bool do_net = !split || is_net, do_local = !split || !is_net;
     if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar0 & 0x7fffffffull));  // round field: barrier base
 
+    // Shards and CTA pieces follow the full chunk in every round, the last (shorter) one included,
+    // so CTA b owns the same bytes of a slot in every round: a slot is reused every S rounds, and
+    // the per-CTA barrier that frees it only covers CTA b on the other ranks.
+    const size_t full_chunk = min(part_bytes, part_chunk);
+    const size_t full_shard = (kind == kPipeOneShot) ? full_chunk : round_up((full_chunk + n - 1) / n, 16);
+    const size_t piece = round_up((full_shard + nct - 1) / nct, 16);
     auto geom = [&](int j, size_t* cbeg, size_t* clen, size_t* shard, size_t* s0, size_t* s1) {
         *cbeg = (size_t)j * part_chunk;
         *clen = min(part_bytes - *cbeg, part_chunk);
-        *shard = (kind == kPipeOneShot) ? *clen : round_up((*clen + n - 1) / n, 16);
-        const size_t piece = round_up((*shard + nct - 1) / nct, 16);
-        *s0 = min(*shard, (size_t)cta * piece);
-        *s1 = min(*shard, *s0 + piece);
+        *shard = full_shard;
+        // One-shot: the piece is a range of the chunk itself, cut at its end; the other kinds cut
+        // rank q's range q * shard + [s0, s1) at the chunk's end where they use it.
+        const size_t lim = (kind == kPipeOneShot) ? *clen : full_shard;
+        *s0 = min(lim, (size_t)cta * piece);
+        *s1 = min(lim, *s0 + piece);
     };
     // ---- phase bodies (tid/nt are group-relative)
     auto phase_a = [&](int j, int tid, int nt) {  // stage round j

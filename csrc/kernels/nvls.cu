@@ -170,10 +170,12 @@ __global__ void __launch_bounds__(512, 1) nvls_kernel(const __grid_constant__ Nv
     const int per_round = (p.func == 2) ? 2 : 1;
     const char* sbase = static_cast<const char*>(p.src);
     char* dbase = static_cast<char*>(p.dst);
+    // CTA b owns the same bytes of a slot in every round (the last, shorter one included): a slot
+    // is reused every nslots rounds and the per-CTA barrier only covers CTA b on the other ranks.
+    const size_t piece = round_up((min((size_t)p.bytes, (size_t)p.chunk) + gridDim.x - 1) / gridDim.x, 16);
     for (int j = 0; j < p.nrounds; ++j) {
         const size_t cbeg = (size_t)j * p.chunk;
         const size_t clen = min((size_t)p.bytes - cbeg, (size_t)p.chunk);
-        const size_t piece = round_up((clen + gridDim.x - 1) / gridDim.x, 16);
         const size_t lo = min(clen, (size_t)blockIdx.x * piece), hi = min(clen, lo + piece);
         const size_t slot = (size_t)((round0 + (uint64_t)j) % (uint64_t)p.nslots);
         char* uc = c.nvls_uc + slot * p.slot_bytes;

@@ -154,11 +154,15 @@ __device__ __forceinline__ void push_engine_body(const DevComm& c, const WorkIte
     if (threadIdx.x == 0) trace(c, 0, kTrBegin, (int)(bar0 & 0x7fffffffull));  // round field: barrier base
     bool ok = true;
     int first = 0;  // first item that can still overlap this CTA's pieces (items are sorted)
+    // CTA b owns the same bytes [b * piece, (b + 1) * piece) of every round's inbox slot, the last
+    // (shorter) round included: the per-CTA barrier that frees a half only covers CTA b on the
+    // peers, so a CTA must never write bytes of a half that another CTA may still be reading.
+    const size_t full = min(stream_bytes, slot);
+    const size_t piece = round_up((full + gridDim.x - 1) / gridDim.x, 16);
     for (int j = 0; j < nrounds && ok; ++j) {
         const int half = (int)((round0 + (uint64_t)j) & 1ull);
         const size_t rbeg = (size_t)j * slot;
         const size_t rend = min(stream_bytes, rbeg + slot);
-        const size_t piece = round_up((rend - rbeg + gridDim.x - 1) / gridDim.x, 16);
         const size_t a = min(rend, rbeg + (size_t)blockIdx.x * piece);
         const size_t b = min(rend, a + piece);
         while (first < nitems && items[first].stream_off + payload_bytes(items[first]) <= a) ++first;

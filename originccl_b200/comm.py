@@ -558,8 +558,19 @@ def _tensor_from_ptr(ptr: int, shape: Sequence[int], dtype: Any, device: int) ->
 
 # ---------------------------------------------------------------- bootstrapping helpers
 
+_STORE_KEY_USES: dict = {}
+
+
 def init_from_store(store: Any, rank: int, world_size: int, *, key: str = "bccl_uid", **kwargs) -> Communicator:
-    """Creates a communicator, distributing the unique id through a torch.distributed Store."""
+    """Creates a communicator, distributing the unique id through a torch.distributed Store.
+
+    Collective over the ranks. Each call with the same ``store`` and ``key`` in a process uses a
+    fresh store entry (``key``, ``key.1``, ``key.2``, ...), so ranks that create several
+    communicators on one store in the same order never read an earlier communicator's id."""
+    uses = (id(store), key)
+    n = _STORE_KEY_USES.get(uses, 0)
+    _STORE_KEY_USES[uses] = n + 1
+    key = key if n == 0 else f"{key}.{n}"
     comm = Communicator()
     if rank == 0:
         uid = comm.get_unique_id()
