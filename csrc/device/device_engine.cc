@@ -658,7 +658,10 @@ bool DeviceEngine::LaunchLarge(const CollTask& t, const AlgoChoice& c, cudaStrea
         // Messages of up to 128 KiB, small enough that every SM gets a channel.
         const unsigned long long per = (bytes + static_cast<unsigned long long>(nranks_) * num_sms_ - 1) /
                                        (static_cast<unsigned long long>(nranks_) * num_sms_);
-        const unsigned long long block = std::min<unsigned long long>(128u << 10, std::max<unsigned long long>(256, RoundUp(per, 256)));
+        // Every CTA's two inbox slots must fit the second half of the data region.
+        const unsigned long long fit = RoundDown(data_bytes_ / 2 / (2ull * static_cast<unsigned long long>(std::max(1, ctas))), 256);
+        const unsigned long long block = std::max<unsigned long long>(
+            256, std::min<unsigned long long>(fit, std::min<unsigned long long>(128u << 10, std::max<unsigned long long>(256, RoundUp(per, 256)))));
         e = LaunchRingAllReduce(dc_, t.send_buf, t.recv_buf, t.count, dt, op, t.scale, block, ctas, stream);
         last_algo_ = "ring";
     } else if (c.algo == Algo::kNvls || (c.algo == Algo::kHybrid && nvls_.mc != nullptr)) {

@@ -46,22 +46,27 @@ def test_two_rank_suite_all_algorithms():
     assert res[0]["ran"] > 0
 
 
+# Small staging buffers: every kernel runs many rounds and reuses its staging slots within one
+# launch, with a shorter last round (the case where CTA ranges must stay fixed across rounds).
+_SMALL_STAGING = {"BCCL_BUFFSIZE": str(16 << 20), "BCCL_NVLS_BUFFSIZE": str(16 << 20),
+                  "BCCL_PIPE_MIN_CHUNK": str(64 << 10)}
+
+
 @pytest.mark.multigpu
-def test_two_rank_large_multi_round():
-    # Payloads of several push-engine / pipeline rounds on two ranks (160 MiB fp32), device counters
-    # compared across ranks after every call.
+def test_two_rank_many_rounds_reusing_slots():
+    # Device counters are compared across ranks after every call.
     _need(2)
-    res = _mp.run(2, gpu_cases.run_suite, [(40 << 20) + 3], ["twoshot", "nvls", "hybrid", "auto"], True,
-                  timeout=900)
+    res = _mp.run(2, gpu_cases.run_suite, [(9 << 20) + 7], ["twoshot", "nvls", "hybrid", "ring", "auto"], True,
+                  timeout=900, env=_SMALL_STAGING)
     assert res[0]["ran"] > 0
 
 
 @pytest.mark.multigpu
 def test_two_rank_pipelines_with_barrier_lag():
-    # BCCL_PIPE_LAG=2: iteration t waits for barrier t-2 over a five-slot ring; several rounds.
+    # BCCL_PIPE_LAG=2: iteration t waits for barrier t-2 over a five-slot ring; many rounds.
     _need(2)
-    res = _mp.run(2, gpu_cases.run_suite, [(3 << 20) + 5, (40 << 20) + 3], ["twoshot", "nvls", "hybrid", "auto"],
-                  True, timeout=900, env={"BCCL_PIPE_LAG": "2", "BCCL_PIPE_MIN_CHUNK": str(1 << 20)})
+    res = _mp.run(2, gpu_cases.run_suite, [(3 << 20) + 5, (9 << 20) + 7], ["twoshot", "nvls", "hybrid", "auto"],
+                  True, timeout=900, env={**_SMALL_STAGING, "BCCL_PIPE_LAG": "2"})
     assert res[0]["ran"] > 0
 
 
@@ -74,6 +79,17 @@ def test_all_gpu_suite():
     res = _mp.run(n, gpu_cases.run_suite, [5, 70001, (9 << 20) + 7], ["oneshot", "twoshot", "nvls", "hybrid"], True,
                   timeout=900)
     assert res[0]["ran"] > 0
+
+
+@pytest.mark.multigpu
+def test_all_gpu_many_rounds_reusing_slots():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 3:
+        pytest.skip("needs 3+ GPUs")
+    for lag in ("1", "2"):
+        res = _mp.run(min(n, 8), gpu_cases.run_suite, [(9 << 20) + 7], ["twoshot", "nvls", "hybrid", "auto"], True,
+                      timeout=900, env={**_SMALL_STAGING, "BCCL_PIPE_LAG": lag})
+        assert res[0]["ran"] > 0
 
 
 @pytest.mark.multigpu
