@@ -34,6 +34,8 @@ def main(argv=None) -> int:
                    help="gradient buckets in the communicator's symmetric (multicast-bound) memory")
     p.add_argument("--register", action="store_true",
                    help="register the gradient storage with the communicator (zero-copy over peer memory)")
+    p.add_argument("--also-register", action="store_true",
+                   help="after the main measurement, time the same sync with the storage registered")
     args = p.parse_args(argv)
 
     import torch
@@ -121,6 +123,13 @@ def main(argv=None) -> int:
     from originccl_b200 import ReduceOp
     comm.all_reduce(grads.bucket(0), ReduceOp.SUM, scale=1.0 / world)  # untimed: which kernel a bucket uses
     bucket_algo = comm.last_algorithm
+    reg = None
+    if args.also_register and not args.register and world > 1:
+        dp_reg = DataParallelSync(comm, grads, register=True)
+        t_reg = timed(dp_reg.sync)
+        comm.all_reduce(grads.bucket(0), ReduceOp.SUM, scale=1.0 / world)
+        reg = {"registered_ms_per_sync": round(t_reg, 3), "registered_bucket_algorithm": comm.last_algorithm}
+        dp_reg.close()
     nbytes = grads.numel * 2
     f = 2.0 * (world - 1) / world if world > 1 else 1.0
     rec = {"workload": "dp_grad_sync", "model": f"llama3-8b-shaped ({args.layers} layers)", "ranks": world,
@@ -129,6 +138,10 @@ def main(argv=None) -> int:
            "ms_per_sync": round(t_ours, 3), "busbw_gbs": round(nbytes / t_ours / 1e6 * f, 1),
            "launches_per_sync": launches, "small_group_us": round(t_small * 1e3, 2), "check_rel_err": worst,
            "ok": ok, "steps": args.steps, "warmup": args.warmup}
+    if reg is not None:
+        rec.update(reg)
+        if t_nccl is not None:
+            rec["registered_speedup_vs_nccl"] = round(t_nccl / reg["registered_ms_per_sync"], 3)
     if t_nccl is not None:
         rec.update({"nccl_ms_per_sync": round(t_nccl, 3), "nccl_busbw_gbs": round(nbytes / t_nccl / 1e6 * f, 1),
                     "speedup_vs_nccl": round(t_nccl / t_ours, 3), "nccl_small_group_us": round(t_small_nccl * 1e3, 2)})

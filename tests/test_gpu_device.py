@@ -87,8 +87,8 @@ def test_all_gpu_many_rounds_reusing_slots():
     if n < 3:
         pytest.skip("needs 3+ GPUs")
     for lag in ("1", "2"):
-        res = _mp.run(min(n, 8), gpu_cases.run_suite, [(9 << 20) + 7], ["twoshot", "nvls", "hybrid", "auto"], True,
-                      timeout=900, env={**_SMALL_STAGING, "BCCL_PIPE_LAG": lag})
+        res = _mp.run(min(n, 8), gpu_cases.run_suite, [(3 << 20) + 7], ["twoshot", "nvls", "hybrid", "auto"], True,
+                      timeout=900, env={**_SMALL_STAGING, "BCCL_BUFFSIZE": str(8 << 20), "BCCL_PIPE_LAG": lag})
         assert res[0]["ran"] > 0
 
 
