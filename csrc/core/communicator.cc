@@ -359,12 +359,16 @@ bool Communicator::Flush() {
         LOG_ERROR("communicator is in an error state after an earlier failure");
         return false;
     }
-    if (!planner_->SortTasks(tasks, config_.rank, config_.world_size)) return false;
-    char range[48];
-    if (tasks.size() == 1) {
-        std::snprintf(range, sizeof(range), "bccl:%s", CollFuncName(tasks[0].func));
-    } else {
-        std::snprintf(range, sizeof(range), "bccl:group(%zu)", tasks.size());
+    // One task was validated by Submit and needs no ordering: the per-call path of every
+    // ungrouped collective skips the sort.
+    if (tasks.size() > 1 && !planner_->SortTasks(tasks, config_.rank, config_.world_size)) return false;
+    char range[48] = "bccl";
+    if (NvtxEnabled()) {
+        if (tasks.size() == 1) {
+            std::snprintf(range, sizeof(range), "bccl:%s", CollFuncName(tasks[0].func));
+        } else {
+            std::snprintf(range, sizeof(range), "bccl:group(%zu)", tasks.size());
+        }
     }
     NvtxRange nvtx(range);
     bool ok;
