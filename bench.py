@@ -49,7 +49,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison")
     p.add_argument("--inplace", action="store_true", help="in-place AllReduce (default: out of place)")
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"],
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid", "ll"],
                    help="force one algorithm (default: the planner's choice)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-clocks", action="store_true", help="diagnostic: do not sample clocks (no clocks key)")

@@ -80,6 +80,7 @@ const char* AlgoName(Algo a) {
     case Algo::kNvls: return "nvls";
     case Algo::kRing: return "ring";
     case Algo::kHybrid: return "hybrid";
+    case Algo::kLL: return "ll";
     }
     return "unknown";
 }

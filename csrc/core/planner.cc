@@ -103,6 +103,7 @@ Algo Planner::ParseAlgo(const std::string& s) {
     if (s == "nvls") return Algo::kNvls;
     if (s == "ring") return Algo::kRing;
     if (s == "hybrid") return Algo::kHybrid;
+    if (s == "ll") return Algo::kLL;
     return Algo::kAuto;
 }
 
@@ -245,6 +246,7 @@ AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_
     // bandwidth-optimal as one-shot pushes.
     if ((algo == Algo::kTwoShot || algo == Algo::kRing) && func != CollFunc::AllReduce) algo = Algo::kOneShot;
     if (algo == Algo::kHybrid && func != CollFunc::AllReduce) algo = Algo::kNvls;
+    if (algo == Algo::kLL && (func != CollFunc::AllReduce || bytes > (128u << 10))) algo = Algo::kOneShot;
     if (algo == Algo::kHybrid && !nvls_ok) algo = Algo::kTwoShot;
     if (algo == Algo::kNvls && !nvls_ok) algo = (func == CollFunc::AllReduce && bytes > (256u << 10))
                                                     ? Algo::kTwoShot : Algo::kOneShot;

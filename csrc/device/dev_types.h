@@ -41,6 +41,11 @@ constexpr size_t kP2pRegionBytes = static_cast<size_t>(kMaxRanks) * kP2pMaxChann
 constexpr size_t kP2pPostedOff = 512u << 10;    // u64 [src][channel]: messages src posted into this rank's inbox
 constexpr size_t kP2pConsumedOff = 520u << 10;  // u64 [dst][channel]: messages dst consumed from this rank
 static_assert(kTpFlagsOff + kTpFlagsBytes <= kP2pPostedOff, "control region overlap");
+
+// Low-latency AllReduce (ll.cu): 16-byte lines carrying 8 payload bytes and two epoch words,
+// [parity 2][source kMaxRanks][kLLMaxLines] per rank, after the native Send/Recv region.
+constexpr size_t kLLMaxLines = 16384;  // 128 KiB of payload per launch
+constexpr size_t kLLRegionBytes = 2ull * kMaxRanks * kLLMaxLines * 16;
 static_assert(kP2pConsumedOff + sizeof(uint64_t) * kMaxRanks * kP2pMaxChannels <= kCtrlBytes, "control region size");
 
 // Error codes written by kernels (host-mapped, read after the stream synchronises).
@@ -72,6 +77,7 @@ struct DevState {
     unsigned int tp_done;
     unsigned int pad2;
     unsigned long long ring_seq;     // ring kernel: message numbers used so far (per CTA slot)
+    unsigned long long ll_seq;       // low-latency AllReduce: launches so far (its line epoch)
     // Native Send/Recv: messages this rank sent to / received from each peer, per channel.
     unsigned long long p2p_sent[kMaxRanks][kP2pMaxChannels];
     unsigned long long p2p_recvd[kMaxRanks][kP2pMaxChannels];
@@ -116,6 +122,7 @@ struct DevComm {
     unsigned int trace_cap;
     unsigned int kernel_serial;     // host launch counter (trace labels only)
     int spin_wait;                  // 1: flag waits poll without __nanosleep (BCCL_SPIN_WAIT)
+    unsigned long long ll_off;      // byte offset of the low-latency line buffers in every UC buffer (0: none)
 };
 
 // One collective in a push-engine launch. All byte offsets refer to the per-peer stream:

@@ -59,9 +59,13 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     data_bytes_ = cfg.buffer_bytes ? cfg.buffer_bytes : static_cast<size_t>(EnvInt("BCCL_BUFFSIZE", 512l << 20));
     data_bytes_ = std::max<size_t>(RoundUp(data_bytes_, 1u << 20), 4u << 20);
     // Control region, data region, then the inboxes of the native Send/Recv.
-    if (!sm_.Alloc(kCtrlBytes + data_bytes_ + (nranks_ > 1 ? kP2pRegionBytes : 0), false, &uc_)) return false;
+    if (!sm_.Alloc(kCtrlBytes + data_bytes_ + (nranks_ > 1 ? kP2pRegionBytes + kLLRegionBytes : 0), false, &uc_)) {
+        return false;
+    }
     // Every flag starts at zero; no peer writes here before the barrier at the end of Init.
     CUDA_OK(cudaMemset(uc_.ptr[rank_], 0, kCtrlBytes), "cudaMemset(control region)");
+    const unsigned long long ll_off = nranks_ > 1 ? kCtrlBytes + data_bytes_ + kP2pRegionBytes : 0;
+    if (ll_off != 0) CUDA_OK(cudaMemset(uc_.ptr[rank_] + ll_off, 0, kLLRegionBytes), "cudaMemset(LL lines)");
     if (sm_.multicast_supported()) {
         size_t nb = static_cast<size_t>(EnvInt("BCCL_NVLS_BUFFSIZE", 256l << 20));
         if (!sm_.Alloc(nb, true, &nvls_)) return false;
@@ -106,9 +110,11 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
     knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
+    knob_ll_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_MAX_BYTES", 64 << 10)));
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
+    dc_.ll_off = ll_off;
     const long trace_cap = EnvInt("BCCL_TRACE", 0);
     if (trace_cap > 0) {
         CUDA_OK(cudaMalloc(&trace_, sizeof(TraceRecord) * static_cast<size_t>(trace_cap)), "cudaMalloc(trace)");
@@ -779,6 +785,24 @@ bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaS
                               NvlsSupports(static_cast<int>(t.dtype), static_cast<int>(t.op)));
         AlgoChoice c = planner_->ChooseAlgo(t.func, t.dtype, t.op, bytes, nranks_, nvls_ok, max_ctas_,
                                             t.algo != Algo::kAuto ? t.algo : forced_);
+        // An ungrouped small AllReduce runs the low-latency kernel: no barrier, one NVLink trip
+        // (what the push engine would pay a fenced flag barrier for).
+        const bool want_ll = t.algo == Algo::kLL || (t.algo == Algo::kAuto && forced_ == Algo::kAuto &&
+                                                       c.algo == Algo::kOneShot && bytes <= knob_ll_max_);
+        if (t.func == CollFunc::AllReduce && nranks_ > 1 && ncoll == 1 && dc_.ll_off != 0 && want_ll &&
+            bytes <= kLLMaxLines * 8) {
+            if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
+            dc_.kernel_serial = ++kernel_serial_;
+            cudaError_t e = LaunchAllReduceLL(dc_, t.send_buf, t.recv_buf, t.count, static_cast<int>(t.dtype),
+                                              static_cast<int>(t.op), t.scale, stream);
+            if (e != cudaSuccess) {
+                LOG_ERROR("rank %d: low-latency AllReduce launch failed: %s", rank_, cudaGetErrorString(e));
+                return false;
+            }
+            launches_++;
+            last_algo_ = "ll";
+            continue;
+        }
         // Inside a group, a collective of up to kGroupPushMaxBytes per rank joins the batched push
         // launch even where the planner would give it a launch of its own: the launch and its
         // barriers cost more than the push moves extra at that size, and the group stays one

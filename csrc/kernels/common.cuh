@@ -153,7 +153,7 @@ __device__ __forceinline__ bool cta_barrier(const DevComm& c, uint64_t seq, int 
 // Called by every CTA once at the end of a launch: the last CTA advances the device-side
 // counters so the next launch (possibly a CUDA-graph replay) starts from fresh values.
 __device__ __forceinline__ void finish_launch(const DevComm& c, uint64_t rounds, uint64_t barriers,
-                                              uint64_t nvls_rounds, uint64_t ring_msgs = 0) {
+                                              uint64_t nvls_rounds, uint64_t ring_msgs = 0, uint64_t ll = 0) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -163,6 +163,7 @@ __device__ __forceinline__ void finish_launch(const DevComm& c, uint64_t rounds,
             c.state->barrier_seq += barriers;
             c.state->nvls_round_seq += nvls_rounds;
             c.state->ring_seq += ring_msgs;
+            c.state->ll_seq += ll;
             c.state->done_ctas = 0;
             __threadfence();
         }

@@ -1,0 +1,233 @@
+// Low-latency AllReduce for small payloads: data and synchronisation travel in the same store.
+//
+// The push engine's small-message cost is its barrier: the NVLink data stores, a system-scope
+// fence that waits for them, a flag store, then the peer's poll. Here every 8 bytes of payload
+// travel in one 16-byte line {data.lo, epoch, data.hi, epoch} written with a single vector
+// store into every peer's line buffer; the receiver polls the lines themselves and takes a line
+// once both epoch words match the launch's epoch (a 16-byte store may reach the peer as two
+// 8-byte halves, hence two epoch words). No fence, no flag, no barrier: one NVLink trip.
+//
+//   rank r, launch epoch e (DevState::ll_seq + 1, the same on every rank), parity e & 1:
+//     for each of its lines i: store line(i, own payload, e) into buf[peer][parity][r][i]
+//                              poll buf[r][parity][p][i] for every peer p until epoch == e
+//                              out[i] = epilogue(reduce(own, peers in rank order))
+//
+// Buffers alternate by parity; a rank writes parity e & 1 again only in launch e + 2, which it
+// can reach only after every peer has sent its launch e + 1 lines, i.e. after every peer's
+// launch e (which read those buffers) has completed. Lines are owned by the same thread on
+// every rank, so a thread's sends and receives need no synchronisation with other threads.
+// The line buffers are zeroed at Init (epochs start at 1). Every wait is bounded.
+// The reference's small-message path is its Tree (OriginCCL src/topology/topology_tree.cpp),
+// whose role on one NVSwitch node is this one-hop exchange.
+#include <algorithm>
+
+#include "kernels/common.cuh"
+#include "kernels/launch.h"
+
+namespace bccl {
+namespace dev {
+namespace {
+
+struct LLParams {
+    DevComm comm;
+    const char* src;
+    char* dst;
+    unsigned long long bytes;
+    int op;
+    float scale;
+};
+
+__device__ __forceinline__ uint4* ll_line(const DevComm& c, int owner, int parity, int src, size_t i) {
+    char* base = c.uc[owner] + c.ll_off;
+    return reinterpret_cast<uint4*>(base) + ((size_t)parity * kMaxRanks + src) * kLLMaxLines + i;
+}
+
+__device__ __forceinline__ void st_line(uint4* p, uint4 v) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_line(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// 8 payload bytes <-> accumulators (per dtype), combined like cta_reduce does.
+template <int D> struct Pack8;
+template <> struct Pack8<kF32> {
+    static constexpr int E = 2;
+    using Acc = float;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) { a[0] = __uint_as_float(w.x); a[1] = __uint_as_float(w.y); }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) { return make_uint2(__float_as_uint(a[0]), __float_as_uint(a[1])); }
+};
+template <> struct Pack8<kI32> {
+    static constexpr int E = 2;
+    using Acc = int32_t;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) { a[0] = (int32_t)w.x; a[1] = (int32_t)w.y; }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) { return make_uint2((uint32_t)a[0], (uint32_t)a[1]); }
+};
+template <> struct Pack8<kF64> {
+    static constexpr int E = 1;
+    using Acc = double;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) {
+        a[0] = __longlong_as_double((long long)(((unsigned long long)w.y << 32) | w.x));
+    }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) {
+        const unsigned long long b = (unsigned long long)__double_as_longlong(a[0]);
+        return make_uint2((uint32_t)b, (uint32_t)(b >> 32));
+    }
+};
+template <> struct Pack8<kI64> {
+    static constexpr int E = 1;
+    using Acc = long long;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) { a[0] = (long long)(((unsigned long long)w.y << 32) | w.x); }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) {
+        return make_uint2((uint32_t)(unsigned long long)a[0], (uint32_t)((unsigned long long)a[0] >> 32));
+    }
+};
+template <> struct Pack8<kBF16> {
+    static constexpr int E = 4;
+    using Acc = float;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) {
+        a[0] = __uint_as_float(w.x << 16); a[1] = __uint_as_float(w.x & 0xffff0000u);
+        a[2] = __uint_as_float(w.y << 16); a[3] = __uint_as_float(w.y & 0xffff0000u);
+    }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) {
+        uint32_t b[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) b[e] = Ty<kBF16>::store(a[e]);
+        return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+    }
+};
+template <> struct Pack8<kF16> {
+    static constexpr int E = 4;
+    using Acc = float;
+    static __device__ __forceinline__ void unpack(uint2 w, Acc* a) {
+        a[0] = Ty<kF16>::load((unsigned short)(w.x & 0xffffu)); a[1] = Ty<kF16>::load((unsigned short)(w.x >> 16));
+        a[2] = Ty<kF16>::load((unsigned short)(w.y & 0xffffu)); a[3] = Ty<kF16>::load((unsigned short)(w.y >> 16));
+    }
+    static __device__ __forceinline__ uint2 pack(const Acc* a) {
+        uint32_t b[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) b[e] = Ty<kF16>::store(a[e]);
+        return make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
+    }
+};
+
+// 8 bytes at p (fewer at the payload's end; unaligned addresses byte by byte).
+__device__ __forceinline__ uint2 load8(const char* p, size_t valid) {
+    if (valid >= 8 && (reinterpret_cast<uintptr_t>(p) & 7) == 0) return *reinterpret_cast<const uint2*>(p);
+    uint2 v = make_uint2(0, 0);
+    char* b = reinterpret_cast<char*>(&v);
+    for (size_t k = 0; k < 8 && k < valid; ++k) b[k] = p[k];
+    return v;
+}
+__device__ __forceinline__ void store8(char* p, uint2 v, size_t valid) {
+    if (valid >= 8 && (reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+        *reinterpret_cast<uint2*>(p) = v;
+        return;
+    }
+    const char* b = reinterpret_cast<const char*>(&v);
+    for (size_t k = 0; k < 8 && k < valid; ++k) p[k] = b[k];
+}
+
+template <int D, int O>
+__global__ void __launch_bounds__(256) ll_allreduce_kernel(const __grid_constant__ LLParams p) {
+    const DevComm& c = p.comm;
+    const int r = c.rank, n = c.nranks;
+    const uint32_t epoch = (uint32_t)(load_state_u64(&c.state->ll_seq) + 1ull);
+    const int parity = (int)(epoch & 1u);
+    const size_t lines = (p.bytes + 7) / 8;
+    using P = Pack8<D>;
+    using Acc = typename P::Acc;
+    bool ok = true;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < lines && ok; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
+        const uint2 mine = load8(p.src + off, valid);
+        const uint4 line = make_uint4(mine.x, epoch, mine.y, epoch);
+        for (int q = 0; q < n; ++q)
+            if (q != r) st_line(ll_line(c, q, parity, r, i), line);
+        uint2 w[kMaxRanks];
+        for (int q = 0; q < n && ok; ++q) {
+            if (q == r) {
+                w[q] = mine;
+                continue;
+            }
+            const uint4* src = ll_line(c, r, parity, q, i);
+            uint4 v = ld_line(src);
+            if (v.y != epoch || v.w != epoch) {
+                const uint64_t t0 = globaltimer();
+                for (uint32_t it = 1;; ++it) {
+                    v = ld_line(src);
+                    if (v.y == epoch && v.w == epoch) break;
+                    if ((it & 255u) == 0) {
+                        const uint64_t waited = globaltimer() - t0;
+                        if ((waited > kAbortCheckAfterNs && *c.abort != 0) || waited > c.timeout_ns) {
+                            record_error(c, *c.abort != 0 ? kDevAborted : kDevTimeout, q, 0, epoch, waited);
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+            }
+            w[q] = make_uint2(v.x, v.z);
+        }
+        if (!ok) break;
+        // Ranks in order, so every rank rounds the same way and gets bit-identical results.
+        Acc acc[P::E], x[P::E];
+        P::unpack(w[0], acc);
+        for (int q = 1; q < n; ++q) {
+            P::unpack(w[q], x);
+#pragma unroll
+            for (int e = 0; e < P::E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < P::E; ++e) acc[e] = epilogue<Acc>(O, acc[e], n, p.scale);
+        store8(p.dst + off, P::pack(acc), valid);
+    }
+    finish_launch(c, 0, 0, 0, 0, 1);
+}
+
+template <int D>
+cudaError_t launch_op(const LLParams& p, int nctas, cudaStream_t s) {
+    switch (p.op) {
+    case kSum: ll_allreduce_kernel<D, kSum><<<nctas, 256, 0, s>>>(p); break;
+    case kMax: ll_allreduce_kernel<D, kMax><<<nctas, 256, 0, s>>>(p); break;
+    case kMin: ll_allreduce_kernel<D, kMin><<<nctas, 256, 0, s>>>(p); break;
+    case kAvg: ll_allreduce_kernel<D, kAvg><<<nctas, 256, 0, s>>>(p); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace dev
+
+cudaError_t LaunchAllReduceLL(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
+                              int op, float scale, cudaStream_t stream) {
+    using namespace dev;
+    const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
+    const unsigned long long lines = (bytes + 7) / 8;
+    if (c.nranks < 2 || c.ll_off == 0 || bytes == 0 || lines > kLLMaxLines) return cudaErrorInvalidValue;
+    LLParams p;
+    p.comm = c;
+    p.src = static_cast<const char*>(src);
+    p.dst = static_cast<char*>(dst);
+    p.bytes = bytes;
+    p.op = op;
+    p.scale = scale;
+    // One line per thread: 256-thread CTAs, as many as the lines need (up to 64).
+    const int nctas = (int)std::min<unsigned long long>(64, (lines + 255) / 256);
+    switch (dtype) {
+    case kF32: return launch_op<kF32>(p, nctas, stream);
+    case kF64: return launch_op<kF64>(p, nctas, stream);
+    case kI32: return launch_op<kI32>(p, nctas, stream);
+    case kI64: return launch_op<kI64>(p, nctas, stream);
+    case kBF16: return launch_op<kBF16>(p, nctas, stream);
+    case kF16: return launch_op<kF16>(p, nctas, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace bccl

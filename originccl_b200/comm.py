@@ -46,6 +46,7 @@ class Algo(enum.IntEnum):
     NVLS = 3
     RING = 4
     HYBRID = 5  # AllReduce: part through the switch (NVLS), the rest two-shot, in one launch
+    LL = 6      # AllReduce up to 128 KiB: data and epoch flags in one store, no barrier
 
 
 class CollFunc(enum.IntEnum):

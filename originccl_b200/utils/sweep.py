@@ -57,7 +57,7 @@ def run_sweep(comm, *, op: str, dtype: str, min_bytes: int, max_bytes: int, fact
     dt = getattr(torch, dtype)
     es = torch.empty((), dtype=dt).element_size()
     algo_v = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS,
-              "ring": Algo.RING, "hybrid": Algo.HYBRID}[algo]
+              "ring": Algo.RING, "hybrid": Algo.HYBRID, "ll": Algo.LL}[algo]
     rop = {"sum": ReduceOp.SUM, "max": ReduceOp.MAX, "min": ReduceOp.MIN, "avg": ReduceOp.AVG}[redop]
     nccl_op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
                "avg": dist.ReduceOp.AVG}[redop]
@@ -229,7 +229,7 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--iters", type=int, default=100)
     p.add_argument("--algo", default="auto",
-                   help="comma list of auto, oneshot, twoshot, nvls, ring, hybrid (each swept in turn)")
+                   help="comma list of auto, oneshot, twoshot, nvls, ring, hybrid, ll (each swept in turn)")
     p.add_argument("--variants", default="",
                    help="';'-separated environment variants, each a ','-separated list of NAME=VALUE set "
                         "while a fresh communicator initialises (e.g. 'BCCL_PIPE_LAG=2;BCCL_PIPE_LAG=1'); "
@@ -271,7 +271,7 @@ def main(argv=None) -> None:
             raise SystemExit(f"unsupported dtype {d}")
     algos = [a.strip() for a in args.algo.split(",") if a.strip()]
     for a in algos:
-        if a not in ("auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"):
+        if a not in ("auto", "oneshot", "twoshot", "nvls", "ring", "hybrid", "ll"):
             raise SystemExit(f"unknown algorithm {a}")
     places = [False, True] if args.both_places else [args.inplace]
     variants = [v.strip() for v in args.variants.split(";")] if args.variants else [""]

@@ -93,7 +93,7 @@ def run_suite(rank: int, world: int, sizes: List[int], algos: List[str], quick: 
     torch.cuda.set_device(dev)
     comm = occl.init_from_env(device=dev, blocking=True, timeout_ms=20000)
     algo_map = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS, "ring": Algo.RING,
-                "hybrid": Algo.HYBRID}
+                "hybrid": Algo.HYBRID, "ll": Algo.LL}
     ran = 0
     used = set()
     dtypes = ["float32", "bfloat16", "int32"] if quick else DTYPES

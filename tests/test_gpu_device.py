@@ -38,9 +38,9 @@ def test_single_rank_large_multi_round():
 @pytest.mark.multigpu
 def test_two_rank_suite_all_algorithms():
     _need(2)
-    res = _mp.run(2, gpu_cases.run_suite, [1, 33, 65537, (3 << 20) + 5],
-                  ["oneshot", "twoshot", "nvls", "ring", "hybrid", "auto"], timeout=900)
-    assert "ring" in res[0]["algorithms"]
+    res = _mp.run(2, gpu_cases.run_suite, [1, 33, 4099, 65537, (3 << 20) + 5],
+                  ["oneshot", "twoshot", "nvls", "ring", "hybrid", "ll", "auto"], timeout=900)
+    assert "ring" in res[0]["algorithms"] and "ll" in res[0]["algorithms"]
     assert "hybrid" in res[0]["algorithms"] or not res[0]["nvls"]
     assert "rs:nvls" in res[0]["algorithms"] or not res[0]["nvls"]
     assert res[0]["ran"] > 0
@@ -76,8 +76,8 @@ def test_all_gpu_suite():
     if n < 3:
         pytest.skip("needs 3+ GPUs")
     n = min(n, 8)
-    res = _mp.run(n, gpu_cases.run_suite, [5, 70001, (9 << 20) + 7], ["oneshot", "twoshot", "nvls", "hybrid"], True,
-                  timeout=900)
+    res = _mp.run(n, gpu_cases.run_suite, [5, 3001, 70001, (9 << 20) + 7], ["oneshot", "twoshot", "nvls", "hybrid", "ll"],
+                  True, timeout=900)
     assert res[0]["ran"] > 0
 
 
