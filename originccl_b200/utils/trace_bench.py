@@ -70,7 +70,7 @@ def trace_case(comm, op: str, nbytes: int, algo_name: str, dtype: str, buffers: 
     es = torch.empty((), dtype=dt).element_size()
     n = max(1, nbytes // es)
     algo = {"auto": Algo.AUTO, "oneshot": Algo.ONESHOT, "twoshot": Algo.TWOSHOT, "nvls": Algo.NVLS,
-            "ring": Algo.RING, "hybrid": Algo.HYBRID}[algo_name]
+            "ring": Algo.RING, "hybrid": Algo.HYBRID, "ll": Algo.LL}[algo_name]
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     nin = n * world if op == "reducescatter" else n
     nout = n * world if op == "allgather" else n
@@ -132,7 +132,7 @@ def main(argv=None) -> None:
                                                          "reducescatter"])
     p.add_argument("--bytes", default="128M", help="payload per rank (AllGather/ReduceScatter: per-rank block)")
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
-    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid"])
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot", "nvls", "ring", "hybrid", "ll"])
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"])
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--traced", type=int, default=3)
