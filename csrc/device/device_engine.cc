@@ -110,7 +110,8 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
     knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
-    knob_ll_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_MAX_BYTES", 64 << 10)));
+    // Measured on 2 x B200: 6.0-7.9 us up to 128 KiB against 10.5-14.1 us for the push engine.
+    knob_ll_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_MAX_BYTES", 128 << 10)));
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
