@@ -246,7 +246,9 @@ AlgoChoice Planner::ChooseAlgo(CollFunc func, DataType dtype, ReduceOp op, size_
     // bandwidth-optimal as one-shot pushes.
     if ((algo == Algo::kTwoShot || algo == Algo::kRing) && func != CollFunc::AllReduce) algo = Algo::kOneShot;
     if (algo == Algo::kHybrid && func != CollFunc::AllReduce) algo = Algo::kNvls;
-    if (algo == Algo::kLL && (func != CollFunc::AllReduce || bytes > (128u << 10))) algo = Algo::kOneShot;
+    if (algo == Algo::kLL && (func == CollFunc::Broadcast || func == CollFunc::Reduce || bytes > (2u << 20))) {
+        algo = Algo::kOneShot;
+    }
     if (algo == Algo::kHybrid && !nvls_ok) algo = Algo::kTwoShot;
     if (algo == Algo::kNvls && !nvls_ok) algo = (func == CollFunc::AllReduce && bytes > (256u << 10))
                                                     ? Algo::kTwoShot : Algo::kOneShot;

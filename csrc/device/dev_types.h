@@ -44,7 +44,7 @@ static_assert(kTpFlagsOff + kTpFlagsBytes <= kP2pPostedOff, "control region over
 
 // Low-latency AllReduce (ll.cu): 16-byte lines carrying 8 payload bytes and two epoch words,
 // [parity 2][source kMaxRanks][kLLMaxLines] per rank, after the native Send/Recv region.
-constexpr size_t kLLMaxLines = 16384;  // 128 KiB of payload per launch
+constexpr size_t kLLMaxLines = 262144;  // 2 MiB of payload per rank and launch (64 MiB of lines per rank)
 constexpr size_t kLLRegionBytes = 2ull * kMaxRanks * kLLMaxLines * 16;
 static_assert(kP2pConsumedOff + sizeof(uint64_t) * kMaxRanks * kP2pMaxChannels <= kCtrlBytes, "control region size");
 

@@ -110,8 +110,10 @@ bool DeviceEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, cons
     knob_pipe_kind_ = EnvInt("BCCL_PIPE_KIND", -1);
     knob_hybrid_frac_ = std::min(0.95, std::max(0.05, EnvInt("BCCL_HYBRID_NVLS_PERMILLE", 600) / 1000.0));
     knob_hybrid_ctas_ = EnvInt("BCCL_HYBRID_NVLS_CTAS", 0);
-    // Measured on 2 x B200: 6.0-7.9 us up to 128 KiB against 10.5-14.1 us for the push engine.
-    knob_ll_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_MAX_BYTES", 128 << 10)));
+    // Measured on 2 and 4 x B200 up to 128 KiB: 6.0-9.7 us against 10.5-18.1 us for the push
+    // engine and 9.5-16.2 us for NCCL; the one-shot push lost to NCCL from 256 KiB to 1 MiB.
+    knob_ll_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_MAX_BYTES", 512 << 10)));
+    knob_ll_block_max_ = static_cast<size_t>(std::max<long>(0, EnvInt("BCCL_LL_BLOCK_MAX_BYTES", 256 << 10)));
     knob_local_copy_ = EnvInt("BCCL_LOCAL_COPY", 1) != 0;
     knob_p2p_native_ = EnvInt("BCCL_P2P_NATIVE", 0) != 0;
     dc_.data_bytes = data_bytes_;
@@ -788,14 +790,17 @@ bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaS
                                             t.algo != Algo::kAuto ? t.algo : forced_);
         // An ungrouped small AllReduce runs the low-latency kernel: no barrier, one NVLink trip
         // (what the push engine would pay a fenced flag barrier for).
+        // AllGather / ReduceScatter too, up to knob_ll_block_max_ per rank block.
+        const bool ll_func = t.func == CollFunc::AllReduce || t.func == CollFunc::AllGather ||
+                             t.func == CollFunc::ReduceScatter;
+        const size_t ll_max = t.func == CollFunc::AllReduce ? knob_ll_max_ : knob_ll_block_max_;
         const bool want_ll = t.algo == Algo::kLL || (t.algo == Algo::kAuto && forced_ == Algo::kAuto &&
-                                                       c.algo == Algo::kOneShot && bytes <= knob_ll_max_);
-        if (t.func == CollFunc::AllReduce && nranks_ > 1 && ncoll == 1 && dc_.ll_off != 0 && want_ll &&
-            bytes <= kLLMaxLines * 8) {
+                                                       c.algo == Algo::kOneShot && bytes <= ll_max);
+        if (ll_func && nranks_ > 1 && ncoll == 1 && dc_.ll_off != 0 && want_ll && bytes <= kLLMaxLines * 8) {
             if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
             dc_.kernel_serial = ++kernel_serial_;
-            cudaError_t e = LaunchAllReduceLL(dc_, t.send_buf, t.recv_buf, t.count, static_cast<int>(t.dtype),
-                                              static_cast<int>(t.op), t.scale, stream);
+            cudaError_t e = LaunchCollectiveLL(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count,
+                                               static_cast<int>(t.dtype), static_cast<int>(t.op), t.scale, stream);
             if (e != cudaSuccess) {
                 LOG_ERROR("rank %d: low-latency AllReduce launch failed: %s", rank_, cudaGetErrorString(e));
                 return false;

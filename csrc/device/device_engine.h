@@ -122,7 +122,8 @@ private:
     long knob_pipe_kind_ = -1;
     double knob_hybrid_frac_ = 0.6;  // BCCL_HYBRID_NVLS_PERMILLE / 1000: bytes of a hybrid AllReduce through NVLS
     long knob_hybrid_ctas_ = 0;      // BCCL_HYBRID_NVLS_CTAS: its NVLS CTAs (0: the same share of the CTAs)
-    size_t knob_ll_max_ = 128u << 10;  // BCCL_LL_MAX_BYTES: largest ungrouped AllReduce on the low-latency kernel
+    size_t knob_ll_max_ = 512u << 10;  // BCCL_LL_MAX_BYTES: largest ungrouped AllReduce on the low-latency kernel
+    size_t knob_ll_block_max_ = 256u << 10;  // BCCL_LL_BLOCK_MAX_BYTES: same for AllGather / ReduceScatter blocks
     bool knob_local_copy_ = true;  // BCCL_LOCAL_COPY=0: one-rank collectives back on the push kernel
     bool knob_p2p_native_ = false; // BCCL_P2P_NATIVE=1: Send/Recv on the native kernel instead of NCCL
     const Planner* planner_ = nullptr;

@@ -53,7 +53,7 @@ enum class Algo : int {
     kNvls = 3,     // NVSwitch multicast: multimem.ld_reduce / multimem.st
     kRing = 4,     // neighbour-only pipeline (parity with the reference's ring)
     kHybrid = 5,   // AllReduce: part of the payload through the switch (NVLS), the rest two-shot
-    kLL = 6,       // AllReduce up to 128 KiB: data and epoch flags in one store, no barrier
+    kLL = 6,       // AllReduce / AllGather / ReduceScatter up to 2 MiB per rank: data and epoch flags in one store, no barrier
 };
 
 struct UniqueId {

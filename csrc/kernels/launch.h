@@ -39,9 +39,11 @@ cudaError_t LaunchNvls(const DevComm& c, int func, const void* src, void* dst, u
                        int op, int root, float scale, unsigned long long chunk, unsigned long long slot_bytes,
                        int nslots, int nctas, cudaStream_t stream);
 
-// Low-latency AllReduce of up to kLLMaxLines * 8 bytes (ll.cu): no barrier, one NVLink trip.
-cudaError_t LaunchAllReduceLL(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
-                              int op, float scale, cudaStream_t stream);
+// Low-latency AllReduce (func 0), AllGather (3) or ReduceScatter (4) of up to kLLMaxLines * 8
+// payload bytes per rank (ll.cu; count = elements of the payload or of one rank's block): no
+// barrier, one NVLink trip.
+cudaError_t LaunchCollectiveLL(const DevComm& c, int func, const void* src, void* dst, unsigned long long count,
+                               int dtype, int op, float scale, cudaStream_t stream);
 
 // Bounded-wait self-test: waits on a flag nothing sets; must time out and report.
 cudaError_t LaunchWaitProbe(const DevComm& c, unsigned long long timeout_ns, cudaStream_t stream);

@@ -1,4 +1,5 @@
-// Low-latency AllReduce for small payloads: data and synchronisation travel in the same store.
+// Low-latency AllReduce, ReduceScatter and AllGather for small payloads: data and
+// synchronisation travel in the same store.
 //
 // The push engine's small-message cost is its barrier: the NVLink data stores, a system-scope
 // fence that waits for them, a flag store, then the peer's poll. Here every 8 bytes of payload
@@ -9,8 +10,13 @@
 //
 //   rank r, launch epoch e (DevState::ll_seq + 1, the same on every rank), parity e & 1:
 //     for each of its lines i: store line(i, own payload, e) into buf[peer][parity][r][i]
-//                              poll buf[r][parity][p][i] for every peer p until epoch == e
+//     then for each of them:   poll buf[r][parity][p][i] for every peer p until epoch == e
 //                              out[i] = epilogue(reduce(own, peers in rank order))
+//
+// ReduceScatter sends line i of input block q to peer q and reduces line i of its own block;
+// AllGather sends its block's lines to every peer and writes the peers' lines into their output
+// blocks. Broadcast and Reduce are not run this way: their exchange is one-sided (the root only
+// sends, or only receives), so a sender could run two launches ahead of a slow receiver.
 //
 // Buffers alternate by parity; a rank writes parity e & 1 again only in launch e + 2, which it
 // can reach only after every peer has sent its launch e + 1 lines, i.e. after every peer's
@@ -132,8 +138,32 @@ __device__ __forceinline__ void store8(char* p, uint2 v, size_t valid) {
     for (size_t k = 0; k < 8 && k < valid; ++k) p[k] = b[k];
 }
 
-template <int D, int O>
-__global__ void __launch_bounds__(256) ll_allreduce_kernel(const __grid_constant__ LLParams p) {
+// Waits (bounded) until line `src` carries `epoch` in both halves; returns its payload.
+__device__ __forceinline__ bool ll_recv(const DevComm& c, const uint4* src, uint32_t epoch, int peer, uint2* out) {
+    uint4 v = ld_line(src);
+    if (v.y != epoch || v.w != epoch) {
+        const uint64_t t0 = globaltimer();
+        for (uint32_t it = 1;; ++it) {
+            v = ld_line(src);
+            if (v.y == epoch && v.w == epoch) break;
+            if ((it & 255u) == 0) {
+                const uint64_t waited = globaltimer() - t0;
+                if ((waited > kAbortCheckAfterNs && *c.abort != 0) || waited > c.timeout_ns) {
+                    record_error(c, *c.abort != 0 ? kDevAborted : kDevTimeout, peer, 0, epoch, waited);
+                    return false;
+                }
+            }
+        }
+    }
+    *out = make_uint2(v.x, v.z);
+    return true;
+}
+
+// AllReduce (RS = false: every peer gets this rank's payload line) and ReduceScatter (RS = true:
+// input = N blocks of p.bytes, peer q gets line i of block q); each thread then reduces line i
+// of its own part from every rank's contribution, in rank order.
+template <int D, int O, bool RS>
+__global__ void __launch_bounds__(256) ll_reduce_kernel(const __grid_constant__ LLParams p) {
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
     const uint32_t epoch = (uint32_t)(load_state_u64(&c.state->ll_seq) + 1ull);
@@ -141,37 +171,27 @@ __global__ void __launch_bounds__(256) ll_allreduce_kernel(const __grid_constant
     const size_t lines = (p.bytes + 7) / 8;
     using P = Pack8<D>;
     using Acc = typename P::Acc;
-    bool ok = true;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < lines && ok; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t first = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+    // Every line goes out before any is awaited, so a thread with several lines keeps one round
+    // trip in flight for all of them.
+    for (size_t i = first; i < lines; i += stride) {
         const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
-        const uint2 mine = load8(p.src + off, valid);
-        const uint4 line = make_uint4(mine.x, epoch, mine.y, epoch);
-        for (int q = 0; q < n; ++q)
-            if (q != r) st_line(ll_line(c, q, parity, r, i), line);
+        const uint2 mine = load8(p.src + (RS ? (size_t)r * p.bytes : 0) + off, valid);
+        for (int q = 0; q < n; ++q) {
+            if (q == r) continue;
+            const uint2 d = RS ? load8(p.src + (size_t)q * p.bytes + off, valid) : mine;
+            st_line(ll_line(c, q, parity, r, i), make_uint4(d.x, epoch, d.y, epoch));
+        }
+    }
+    bool ok = true;
+    for (size_t i = first; i < lines && ok; i += stride) {
+        const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
         uint2 w[kMaxRanks];
+        // This thread's own part of the input (read again: only this thread writes these bytes
+        // of the output, so an in-place call still sees its input here).
+        w[r] = load8(p.src + (RS ? (size_t)r * p.bytes : 0) + off, valid);
         for (int q = 0; q < n && ok; ++q) {
-            if (q == r) {
-                w[q] = mine;
-                continue;
-            }
-            const uint4* src = ll_line(c, r, parity, q, i);
-            uint4 v = ld_line(src);
-            if (v.y != epoch || v.w != epoch) {
-                const uint64_t t0 = globaltimer();
-                for (uint32_t it = 1;; ++it) {
-                    v = ld_line(src);
-                    if (v.y == epoch && v.w == epoch) break;
-                    if ((it & 255u) == 0) {
-                        const uint64_t waited = globaltimer() - t0;
-                        if ((waited > kAbortCheckAfterNs && *c.abort != 0) || waited > c.timeout_ns) {
-                            record_error(c, *c.abort != 0 ? kDevAborted : kDevTimeout, q, 0, epoch, waited);
-                            ok = false;
-                            break;
-                        }
-                    }
-                }
-            }
-            w[q] = make_uint2(v.x, v.z);
+            if (q != r) ok = ll_recv(c, ll_line(c, r, parity, q, i), epoch, q, &w[q]);
         }
         if (!ok) break;
         // Ranks in order, so every rank rounds the same way and gets bit-identical results.
@@ -189,27 +209,73 @@ __global__ void __launch_bounds__(256) ll_allreduce_kernel(const __grid_constant
     finish_launch(c, 0, 0, 0, 0, 1);
 }
 
-template <int D>
+// AllGather: every peer gets this rank's block line by line; the output's block q receives rank
+// q's lines (this rank's own block is copied locally).
+__global__ void __launch_bounds__(256) ll_allgather_kernel(const __grid_constant__ LLParams p) {
+    const DevComm& c = p.comm;
+    const int r = c.rank, n = c.nranks;
+    const uint32_t epoch = (uint32_t)(load_state_u64(&c.state->ll_seq) + 1ull);
+    const int parity = (int)(epoch & 1u);
+    const size_t lines = (p.bytes + 7) / 8;
+    const size_t first = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+    char* own = p.dst + (size_t)r * p.bytes;
+    for (size_t i = first; i < lines; i += stride) {
+        const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
+        const uint2 mine = load8(p.src + off, valid);
+        const uint4 line = make_uint4(mine.x, epoch, mine.y, epoch);
+        for (int q = 0; q < n; ++q)
+            if (q != r) st_line(ll_line(c, q, parity, r, i), line);
+        if (own != p.src) store8(own + off, mine, valid);
+    }
+    bool ok = true;
+    for (size_t i = first; i < lines && ok; i += stride) {
+        const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
+        for (int q = 0; q < n && ok; ++q) {
+            if (q == r) continue;
+            uint2 d;
+            ok = ll_recv(c, ll_line(c, r, parity, q, i), epoch, q, &d);
+            if (ok) store8(p.dst + (size_t)q * p.bytes + off, d, valid);
+        }
+    }
+    finish_launch(c, 0, 0, 0, 0, 1);
+}
+
+template <int D, bool RS>
 cudaError_t launch_op(const LLParams& p, int nctas, cudaStream_t s) {
     switch (p.op) {
-    case kSum: ll_allreduce_kernel<D, kSum><<<nctas, 256, 0, s>>>(p); break;
-    case kMax: ll_allreduce_kernel<D, kMax><<<nctas, 256, 0, s>>>(p); break;
-    case kMin: ll_allreduce_kernel<D, kMin><<<nctas, 256, 0, s>>>(p); break;
-    case kAvg: ll_allreduce_kernel<D, kAvg><<<nctas, 256, 0, s>>>(p); break;
+    case kSum: ll_reduce_kernel<D, kSum, RS><<<nctas, 256, 0, s>>>(p); break;
+    case kMax: ll_reduce_kernel<D, kMax, RS><<<nctas, 256, 0, s>>>(p); break;
+    case kMin: ll_reduce_kernel<D, kMin, RS><<<nctas, 256, 0, s>>>(p); break;
+    case kAvg: ll_reduce_kernel<D, kAvg, RS><<<nctas, 256, 0, s>>>(p); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
+template <bool RS>
+cudaError_t launch_dtype(const LLParams& p, int dtype, int nctas, cudaStream_t s) {
+    switch (dtype) {
+    case kF32: return launch_op<kF32, RS>(p, nctas, s);
+    case kF64: return launch_op<kF64, RS>(p, nctas, s);
+    case kI32: return launch_op<kI32, RS>(p, nctas, s);
+    case kI64: return launch_op<kI64, RS>(p, nctas, s);
+    case kBF16: return launch_op<kBF16, RS>(p, nctas, s);
+    case kF16: return launch_op<kF16, RS>(p, nctas, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 }  // namespace
 }  // namespace dev
 
-cudaError_t LaunchAllReduceLL(const DevComm& c, const void* src, void* dst, unsigned long long count, int dtype,
-                              int op, float scale, cudaStream_t stream) {
+cudaError_t LaunchCollectiveLL(const DevComm& c, int func, const void* src, void* dst, unsigned long long count,
+                               int dtype, int op, float scale, cudaStream_t stream) {
     using namespace dev;
     const unsigned long long bytes = count * (unsigned long long)dtype_size(dtype);
     const unsigned long long lines = (bytes + 7) / 8;
-    if (c.nranks < 2 || c.ll_off == 0 || bytes == 0 || lines > kLLMaxLines) return cudaErrorInvalidValue;
+    if (c.nranks < 2 || c.ll_off == 0 || bytes == 0 || lines > kLLMaxLines || (func != 0 && func != 3 && func != 4)) {
+        return cudaErrorInvalidValue;
+    }
     LLParams p;
     p.comm = c;
     p.src = static_cast<const char*>(src);
@@ -217,17 +283,14 @@ cudaError_t LaunchAllReduceLL(const DevComm& c, const void* src, void* dst, unsi
     p.bytes = bytes;
     p.op = op;
     p.scale = scale;
-    // One line per thread: 256-thread CTAs, as many as the lines need (up to 64).
-    const int nctas = (int)std::min<unsigned long long>(64, (lines + 255) / 256);
-    switch (dtype) {
-    case kF32: return launch_op<kF32>(p, nctas, stream);
-    case kF64: return launch_op<kF64>(p, nctas, stream);
-    case kI32: return launch_op<kI32>(p, nctas, stream);
-    case kI64: return launch_op<kI64>(p, nctas, stream);
-    case kBF16: return launch_op<kBF16>(p, nctas, stream);
-    case kF16: return launch_op<kF16>(p, nctas, stream);
-    default: return cudaErrorInvalidValue;
+    // One line per thread: 256-thread CTAs, as many as the lines need (up to two per SM; larger
+    // payloads loop, each thread taking every (grid * 256)-th line).
+    const int nctas = (int)std::min<unsigned long long>(296, (lines + 255) / 256);
+    if (func == 3) {
+        ll_allgather_kernel<<<nctas, 256, 0, stream>>>(p);
+        return cudaGetLastError();
     }
+    return func == 4 ? launch_dtype<true>(p, dtype, nctas, stream) : launch_dtype<false>(p, dtype, nctas, stream);
 }
 
 }  // namespace bccl

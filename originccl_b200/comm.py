@@ -46,7 +46,7 @@ class Algo(enum.IntEnum):
     NVLS = 3
     RING = 4
     HYBRID = 5  # AllReduce: part through the switch (NVLS), the rest two-shot, in one launch
-    LL = 6      # AllReduce up to 128 KiB: data and epoch flags in one store, no barrier
+    LL = 6      # AllReduce / AllGather / ReduceScatter up to 2 MiB per rank: data and epoch flags in one store, no barrier
 
 
 class CollFunc(enum.IntEnum):
