@@ -49,6 +49,12 @@ std::vector<TuningRow> DefaultTable() {
         {CollFunc::AllReduce, 2, 6 << 20, Algo::kTwoShot, 0},
         {CollFunc::AllReduce, 2, 48 << 20, Algo::kRing, 0},
         {CollFunc::AllReduce, 2, ~size_t(0), Algo::kTwoShot, 0},
+        // Four ranks (4 x B200, fp32, plain buffers): two-shot beats NVLS up to 16 MiB (93 vs
+        // 102 us there); above, the hybrid (NVLS on part of the payload, two-shot on the rest)
+        // wins (64 MiB: 243 us against NVLS 259 and two-shot 263; 256 MiB: 799 against 820 and 837).
+        {CollFunc::AllReduce, 4, 1 << 20, Algo::kOneShot, 0},
+        {CollFunc::AllReduce, 4, 16 << 20, Algo::kTwoShot, 0},
+        {CollFunc::AllReduce, 4, ~size_t(0), Algo::kHybrid, 0},
         // Three or more ranks (8 x B200): one-shot up to 1 MiB, pipelined two-shot up to 8 MiB,
         // NVLS above.
         {CollFunc::AllReduce, 0, 1 << 20, Algo::kOneShot, 0},

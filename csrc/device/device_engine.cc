@@ -249,10 +249,13 @@ bool DeviceEngine::TpAllGatherGemm(const void* x_local, const void* w, void* y, 
     if (nranks_ == 1) {
         e = LaunchGemmBf16(x_local, w, y, m, n, k, n, act, tp_err_, 0, stream);
     } else {
-        // Read per call (a fused op costs far more than a getenv), so benchmarks can compare both
-        // pushes in one process; the buffer is multicast-bound from its first allocation on.
-        const bool multicast = EnvInt("BCCL_TP_MULTICAST", 1) != 0;
-        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2, true)) return false;
+        // BCCL_TP_MULTICAST=1 pushes each gathered chunk once through the switch (multimem.st)
+        // instead of once per peer. Off by default: on 4 x B200 the multicast push ran 4.6% slower
+        // (1.636 vs 1.564 ms for a Llama-3-8B-shaped TP=4 MLP block). Read per call (a fused op
+        // costs far more than a getenv); the buffer is multicast-bound only if the knob was set
+        // when it was allocated, and a buffer without a multicast handle always takes the stores.
+        const bool multicast = EnvInt("BCCL_TP_MULTICAST", 0) != 0;
+        if (!EnsureTpBuffer(tp_xg_, &tp_xg_bytes_, static_cast<size_t>(m) * k * 2, multicast)) return false;
         const unsigned long long seq = ++tp_ag_calls_;
         const int par = static_cast<int>(seq & 1ull);
         TpArgs t;

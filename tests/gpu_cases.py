@@ -397,8 +397,10 @@ def run_dp(rank: int, world: int, hidden: int = 256, steps: int = 2) -> Dict:
         err = ((p.grad - ref).abs().max() / ref.abs().max().clamp_min(1e-12)).item()
         worst = max(worst, err)
         assert err < 1e-4, f"{n}: relative error {err}"
+    registered = dp.registered
+    dp.close()
     comm.destroy()
-    return {"buckets": grads.num_buckets, "small": len(grads.small_idx), "worst": worst}
+    return {"buckets": grads.num_buckets, "small": len(grads.small_idx), "worst": worst, "registered": registered}
 
 
 def run_zero_copy(rank: int, world: int) -> Dict:

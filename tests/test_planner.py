@@ -90,6 +90,9 @@ def test_algorithm_table():
     assert choose(AR, 64 << 20, 8, False)[0] == TWOSHOT       # no multicast -> two-shot
     assert choose(AR, 4 << 20, 2, True)[0] == TWOSHOT         # two ranks: pipelined push
     assert choose(AR, 32 << 20, 2, True)[0] == 4              # two ranks, mid sizes: ring
+    assert choose(AR, 16 << 20, 4, True)[0] == TWOSHOT        # four ranks: two-shot up to 16 MiB
+    assert choose(AR, 64 << 20, 4, True)[0] == 5              # then the hybrid
+    assert choose(AR, 64 << 20, 4, False)[0] == TWOSHOT       # which needs multicast
     assert choose(AR, 2 << 20, 2, True)[0] == ONESHOT         # two ranks: one-shot push up to 2 MiB
     assert choose(AR, 256 << 20, 2, True)[0] == TWOSHOT       # two ranks, large: two-shot
     assert choose(BC, 256 << 20, 2, True)[0] == ONESHOT       # two ranks: no NVLS for Broadcast
