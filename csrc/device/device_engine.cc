@@ -797,15 +797,18 @@ bool DeviceEngine::ExecuteCollectives(const std::vector<CollTask>& sorted, cudaS
         const bool ll_func = t.func == CollFunc::AllReduce || t.func == CollFunc::AllGather ||
                              t.func == CollFunc::ReduceScatter;
         const size_t ll_max = t.func == CollFunc::AllReduce ? knob_ll_max_ : knob_ll_block_max_;
-        const bool want_ll = t.algo == Algo::kLL || (t.algo == Algo::kAuto && forced_ == Algo::kAuto &&
+        // c.algo is kLL when the call, BCCL_ALGO or a tuning-file row asked for it.
+        const bool want_ll = c.algo == Algo::kLL || (t.algo == Algo::kAuto && forced_ == Algo::kAuto &&
                                                        c.algo == Algo::kOneShot && bytes <= ll_max);
-        if (ll_func && nranks_ > 1 && ncoll == 1 && dc_.ll_off != 0 && want_ll && bytes <= kLLMaxLines * 8) {
+        const bool ll_ok = ll_func && nranks_ > 1 && ncoll == 1 && dc_.ll_off != 0 && bytes <= kLLMaxLines * 8;
+        if (c.algo == Algo::kLL && !ll_ok) c.algo = Algo::kOneShot;  // grouped, one rank: the push engine
+        if (ll_ok && want_ll) {
             if (!FlushBatch(&batch, &stream_bytes, stream)) return false;
             dc_.kernel_serial = ++kernel_serial_;
             cudaError_t e = LaunchCollectiveLL(dc_, static_cast<int>(t.func), t.send_buf, t.recv_buf, t.count,
                                                static_cast<int>(t.dtype), static_cast<int>(t.op), t.scale, stream);
             if (e != cudaSuccess) {
-                LOG_ERROR("rank %d: low-latency AllReduce launch failed: %s", rank_, cudaGetErrorString(e));
+                LOG_ERROR("rank %d: low-latency launch failed: %s", rank_, cudaGetErrorString(e));
                 return false;
             }
             launches_++;

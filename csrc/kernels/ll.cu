@@ -186,22 +186,26 @@ __global__ void __launch_bounds__(256) ll_reduce_kernel(const __grid_constant__ 
     bool ok = true;
     for (size_t i = first; i < lines && ok; i += stride) {
         const size_t off = i * 8, valid = min((size_t)8, (size_t)p.bytes - off);
-        uint2 w[kMaxRanks];
-        // This thread's own part of the input (read again: only this thread writes these bytes
-        // of the output, so an in-place call still sees its input here).
-        w[r] = load8(p.src + (RS ? (size_t)r * p.bytes : 0) + off, valid);
-        for (int q = 0; q < n && ok; ++q) {
-            if (q != r) ok = ll_recv(c, ll_line(c, r, parity, q, i), epoch, q, &w[q]);
+        // Ranks in order, so every rank rounds the same way and gets bit-identical results; each
+        // contribution is folded in as it arrives (no per-rank array in local memory).
+        Acc acc[P::E], x[P::E];
+        for (int q = 0; q < n; ++q) {
+            uint2 w;
+            if (q == r) {
+                // Own part of the input, read again: only this thread writes these bytes of the
+                // output, so an in-place call still sees its input here.
+                w = load8(p.src + (RS ? (size_t)r * p.bytes : 0) + off, valid);
+            } else if (!ll_recv(c, ll_line(c, r, parity, q, i), epoch, q, &w)) {
+                ok = false;
+                break;
+            }
+            P::unpack(w, q == 0 ? acc : x);
+            if (q > 0) {
+#pragma unroll
+                for (int e = 0; e < P::E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
+            }
         }
         if (!ok) break;
-        // Ranks in order, so every rank rounds the same way and gets bit-identical results.
-        Acc acc[P::E], x[P::E];
-        P::unpack(w[0], acc);
-        for (int q = 1; q < n; ++q) {
-            P::unpack(w[q], x);
-#pragma unroll
-            for (int e = 0; e < P::E; ++e) acc[e] = combine<Acc>(O, acc[e], x[e]);
-        }
 #pragma unroll
         for (int e = 0; e < P::E; ++e) acc[e] = epilogue<Acc>(O, acc[e], n, p.scale);
         store8(p.dst + off, P::pack(acc), valid);
