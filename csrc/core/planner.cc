@@ -137,33 +137,33 @@ bool Planner::LoadTuningFile(const std::string& path) {
 
 bool Planner::ValidateCollectiveTask(const CollTask& task, int rank, int world_size) const {
     if (!IsCollective(task.func) || world_size <= 0 || rank < 0 || rank >= world_size) {
-        LOG_ERROR("rank %d: invalid collective function or communicator size", rank);
+        LOG_ERROR("rank %d: rejected: not a collective, or rank outside a communicator of %d", rank, world_size);
         return false;
     }
     const size_t es = ValidDtype(task.dtype) ? DataTypeSize(task.dtype) : 0;
     if (es == 0 || task.count > std::numeric_limits<size_t>::max() / es) {
-        LOG_ERROR("rank %d: invalid collective data type or count", rank);
+        LOG_ERROR("rank %d: rejected: unknown data type or element count too large for size_t bytes", rank);
         return false;
     }
     if (IsReducing(task.func) && !ValidOp(task.op)) {
-        LOG_ERROR("rank %d: invalid reduce operation", rank);
+        LOG_ERROR("rank %d: rejected: unknown reduction op %d", rank, static_cast<int>(task.op));
         return false;
     }
     const bool has_root = task.func == CollFunc::Broadcast || task.func == CollFunc::Reduce;
     if (has_root && (task.root < 0 || task.root >= world_size)) {
-        LOG_ERROR("rank %d: invalid root %d", rank, task.root);
+        LOG_ERROR("rank %d: rejected: root %d is not a rank of this communicator", rank, task.root);
         return false;
     }
     if ((task.func == CollFunc::AllGather || task.func == CollFunc::ReduceScatter) && task.count != 0 &&
         task.count > std::numeric_limits<size_t>::max() / static_cast<size_t>(world_size) / es) {
-        LOG_ERROR("rank %d: collective total buffer size overflows", rank);
+        LOG_ERROR("rank %d: rejected: count x %d ranks does not fit in size_t bytes", rank, world_size);
         return false;
     }
     if (task.count == 0) return true;
     const bool needs_send = task.func != CollFunc::Broadcast;
     const bool needs_recv = task.func != CollFunc::Reduce || rank == task.root;
     if ((needs_send && task.send_buf == nullptr) || (needs_recv && task.recv_buf == nullptr)) {
-        LOG_ERROR("rank %d: collective is missing a required buffer", rank);
+        LOG_ERROR("rank %d: rejected: null send or receive pointer for a non-empty collective", rank);
         return false;
     }
     return true;
@@ -171,16 +171,16 @@ bool Planner::ValidateCollectiveTask(const CollTask& task, int rank, int world_s
 
 bool Planner::ValidateP2p(const CollTask& task, int rank, int world_size) const {
     if (!IsP2p(task.func) || task.peer < 0 || task.peer >= world_size || task.peer == rank) {
-        LOG_ERROR("rank %d: invalid P2P peer %d", rank, task.peer);
+        LOG_ERROR("rank %d: rejected: peer %d is this rank or outside the communicator", rank, task.peer);
         return false;
     }
     const size_t es = ValidDtype(task.dtype) ? DataTypeSize(task.dtype) : 0;
     if (es == 0 || task.count > std::numeric_limits<size_t>::max() / es) {
-        LOG_ERROR("rank %d: invalid P2P data type or count", rank);
+        LOG_ERROR("rank %d: rejected: unknown data type or element count too large for a Send/Recv", rank);
         return false;
     }
     if (task.count != 0 && task.send_buf == nullptr && task.recv_buf == nullptr) {
-        LOG_ERROR("rank %d: P2P is missing its buffer", rank);
+        LOG_ERROR("rank %d: rejected: null buffer for a non-empty Send/Recv", rank);
         return false;
     }
     return true;
@@ -194,7 +194,7 @@ int Planner::P2pRoundOf(CollFunc func, int rank, int peer, int world_size) {
 
 bool Planner::SortTasks(std::vector<CollTask>& tasks, int rank, int world_size) const {
     if (world_size <= 0 || rank < 0 || rank >= world_size) {
-        LOG_ERROR("rank %d: invalid communicator size for task sorting", rank);
+        LOG_ERROR("rank %d: cannot order a group for a communicator of %d ranks", rank, world_size);
         return false;
     }
     std::vector<CollTask> colls, p2p;

@@ -166,6 +166,23 @@ def _sanitized_ninja_file(kind: str) -> str:
     return "\n".join(lines) + "\n"
 
 
+class _BuildLock:
+    """Serialises builds across processes (pytest-xdist workers may build at the same time; a
+    half-linked library is "file too short" for the process that loads it meanwhile)."""
+
+    def __enter__(self):
+        import fcntl
+        (ROOT / "build").mkdir(parents=True, exist_ok=True)
+        self._f = open(ROOT / "build" / ".lock", "w")
+        fcntl.flock(self._f, fcntl.LOCK_EX)
+        return self
+
+    def __exit__(self, *exc):
+        import fcntl
+        fcntl.flock(self._f, fcntl.LOCK_UN)
+        self._f.close()
+
+
 def build_sanitized(kind: str, verbose: bool = False) -> Path:
     """Builds libbccl.so and the example programs (bccl_check, bccl_transport_check) with
     AddressSanitizer + UndefinedBehaviorSanitizer (``"asan"``) or ThreadSanitizer (``"tsan"``)
@@ -174,6 +191,11 @@ def build_sanitized(kind: str, verbose: bool = False) -> Path:
     if kind not in SANITIZERS:
         raise ValueError(f"unknown sanitizer {kind!r} (asan, tsan)")
     build(verbose)  # the CUDA objects are shared with the regular build
+    with _BuildLock():
+        return _build_sanitized_locked(kind, verbose)
+
+
+def _build_sanitized_locked(kind: str, verbose: bool) -> Path:
     out = ROOT / "build" / f"san-{kind}"
     out.mkdir(parents=True, exist_ok=True)
     ninja_path = out / "build.ninja"
@@ -190,6 +212,11 @@ def build_sanitized(kind: str, verbose: bool = False) -> Path:
 
 def build(verbose: bool = False) -> Path:
     """Compiles everything (incrementally) and returns the path of libbccl.so."""
+    with _BuildLock():
+        return _build_locked(verbose)
+
+
+def _build_locked(verbose: bool) -> Path:
     BUILD.mkdir(parents=True, exist_ok=True)
     LIBDIR.mkdir(parents=True, exist_ok=True)
     ninja_path = BUILD / "build.ninja"
@@ -207,7 +234,62 @@ def build(verbose: bool = False) -> Path:
     return LIBDIR / "libbccl.so"
 
 
+def ptxas_report() -> list[dict]:
+    """Registers, spills, stack and static shared memory of every kernel, from ``ptxas -v`` on
+    each CUDA source compiled with the library's own flags (the object is thrown away). Returns
+    one dict per kernel entry: file, kernel (demangled), registers, spill_stores, spill_loads,
+    stack, smem."""
+    import re
+    import tempfile
+    _, cu = _sources()
+    nccl = nccl_include()
+    incs = [f"-I{CSRC}", f"-I{CSRC / 'include'}", f"-I{CUDA_HOME / 'include'}"] + ([f"-I{nccl}"] if nccl else [])
+    rows = []
+    with tempfile.TemporaryDirectory() as td:
+        for src in cu:
+            cmd = [str(CUDA_HOME / "bin" / "nvcc"), *ARCH.split(), "-lineinfo", "-O3", "-std=c++17",
+                   "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-v", *incs,
+                   "-c", str(src), "-o", os.path.join(td, "k.o")]
+            res = subprocess.run(cmd, capture_output=True, text=True)
+            if res.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src}:\n{res.stderr[-4000:]}")
+            cur = None
+            for line in res.stderr.splitlines():
+                m = re.search(r"Compiling entry function '([^']+)'", line)
+                if m:
+                    cur = {"file": str(src.relative_to(ROOT)), "mangled": m.group(1), "registers": 0,
+                           "spill_stores": 0, "spill_loads": 0, "stack": 0, "smem": 0}
+                    rows.append(cur)
+                    continue
+                if cur is None:
+                    continue
+                m = re.search(r"(\d+) bytes stack frame, (\d+) bytes spill stores, (\d+) bytes spill loads", line)
+                if m:
+                    cur["stack"], cur["spill_stores"], cur["spill_loads"] = map(int, m.groups())
+                m = re.search(r"Used (\d+) registers", line)
+                if m:
+                    cur["registers"] = int(m.group(1))
+                m = re.search(r"(\d+) bytes smem", line)
+                if m:
+                    cur["smem"] = int(m.group(1))
+    names = subprocess.run(["c++filt"], input="\n".join(r["mangled"] for r in rows), capture_output=True,
+                           text=True).stdout.splitlines() if shutil.which("c++filt") else []
+    for i, r in enumerate(rows):
+        r["kernel"] = names[i] if i < len(names) else r["mangled"]
+        del r["mangled"]
+    return rows
+
+
 if __name__ == "__main__":
+    if "--ptxas-report" in sys.argv:
+        print("| file | kernel | registers | spill stores | spill loads | stack | static smem |")
+        print("|---|---|---|---|---|---|---|")
+        for r in ptxas_report():
+            k = r["kernel"].replace("|", "\\|")
+            k = k if len(k) <= 150 else k[:147] + "..."
+            print(f"| {r['file']} | `{k}` | {r['registers']} | {r['spill_stores']} | {r['spill_loads']} | "
+                  f"{r['stack']} | {r['smem']} |")
+        sys.exit(0)
     kinds = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--sanitize=")]
     for k in kinds:
         print(build_sanitized(k, verbose="-v" in sys.argv))
