@@ -13,6 +13,11 @@ GPU). Rank 0 prints one JSON line:
   pinned host memory and a sample of the result read back every step.
 * ``nccl``: the same op (out of place on the same rotating inputs, or in place with
   ``--inplace``) through NCCL called directly on the same box, for comparison.
+* ``zero_copy_arms`` (N>1): the same out-of-place op timed again on the same tensors registered
+  with the communicator (``register``: peer memory, no staging copies; the default arm) and,
+  with ``--zero-copy-arms registered,symmetric``, on symmetric multicast-bound allocations
+  (``symmetric_empty``), each with its algorithm and error against NCCL's reduction. The
+  headline ``value`` stays on plain, unregistered tensors.
 
 ``--impl reference`` runs the reference's own code path; the reference is a CMake C++ project
 without a Python package and cannot be built on this image, so that arm prints an
@@ -56,6 +61,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--buffers", default="plain", choices=["plain", "registered", "symmetric"],
                    help="plain torch tensors (default); the same tensors registered with the communicator "
                         "(zero-copy over peer memory); or symmetric multicast-bound allocations (zero-copy NVLS)")
+    p.add_argument("--zero-copy-arms", default="registered",
+                   help="N>1, plain headline: comma list of extra arms that time the same op on other buffers "
+                        "('registered': the same tensors registered with the communicator; 'symmetric': "
+                        "multicast-bound allocations); 'none' to skip")
     return p.parse_args()
 
 
@@ -153,6 +162,7 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     launches = comm.kernel_launches - launches0
+    algorithm = comm.last_algorithm
     ms = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -244,6 +254,49 @@ def main() -> None:
         torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+
+    # Zero-copy arms (N>1, plain headline only): the same out-of-place AllReduce, same sizes and
+    # timing rules, first on the same torch tensors registered with the communicator (peer
+    # memory, no staging), then on symmetric multicast-bound allocations (NVLS without staging
+    # where the planner picks NVLS). Reported beside the headline, which stays on plain buffers.
+    zero_copy = None
+    arms = [a for a in args.zero_copy_arms.split(",") if a in ("registered", "symmetric")]
+    if world > 1 and args.buffers == "plain" and arms and not args.inplace:
+        zero_copy = {}
+        ref_last = reference_of(args.steps - 1)
+        for kind in arms:
+            if kind == "registered":
+                bufs = [*xs, y]
+                for t_ in bufs:
+                    comm.register(t_)
+            else:
+                bufs = [comm.symmetric_empty((count,), dtype) for _ in range(3)]
+                for dst_, src_ in zip(bufs[:2], xs):
+                    dst_.copy_(src_)
+                torch.cuda.synchronize()
+            zin, zout = bufs[:2], bufs[2]
+            for i in range(args.warmup):
+                comm.all_reduce(zin[i & 1], out=zout, algo=algo)
+            torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
+            s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0 = comm.kernel_launches
+            s3.record()
+            for i in range(args.steps):
+                comm.all_reduce(zin[i & 1], out=zout, algo=algo)
+            e3.record(); torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
+            tz = torch.tensor([s3.elapsed_time(e3) / args.steps], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tz, op=dist.ReduceOp.MAX)
+            zms = float(tz.item())
+            zerr = float((zout.float() - ref_last).abs().max().item())
+            zero_copy[kind] = {"ms_per_step": round(zms, 4),
+                               "busbw_gbs_per_rank": round(nbytes / (zms * 1e-3) / 1e9 * factor, 2),
+                               "algorithm": comm.last_algorithm, "gpu_launches": comm.kernel_launches - l0,
+                               "max_abs_err_vs_nccl_last_step": zerr}
+            if kind == "registered":
+                for t_ in bufs:
+                    comm.deregister(t_)
+            del bufs, zin, zout
+            torch.cuda.synchronize(); barrier()
     if rank == 0:
         out = {
             "metric": "AllReduce bus GB/s vs size at 2/4/8 B200 (max over ranks) vs reference & NCCL",
@@ -269,7 +322,7 @@ def main() -> None:
                 "busbw_gbs_summed_over_ranks": round(busbw * world, 2),
                 "inplace": args.inplace,
                 "algbw_gbs": round(algbw, 2),
-                "algorithm": comm.last_algorithm,
+                "algorithm": algorithm,
                 "buffers": args.buffers,
                 "nvls": comm.nvls_enabled,
                 "l2": "inputs larger than L2: two rotating 128 MiB inputs + a 128 MiB output per rank",
@@ -279,6 +332,7 @@ def main() -> None:
                 "baseline_number": "reference 7.52 GB/s busbw per rank, 4 ranks, 128 MiB fp32 (README.md:223)",
             },
             "nccl": nccl,
+            "zero_copy_arms": zero_copy,
             "e2e": {"value": round(e2e_value, 2),
                     "unit": "GB/s (bus bandwidth per rank)" if world > 1 else "GB/s (algbw of a one-rank copy)",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": nbytes,

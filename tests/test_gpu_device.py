@@ -182,7 +182,10 @@ def test_data_parallel_sync_two_ranks():
 def test_zero_copy_nvls_two_ranks():
     _need(2)
     res = _mp.run(2, gpu_cases.run_zero_copy, timeout=300)
-    assert res[0].get("skipped") or res[0]["algorithms"] == ["nvls_zero_copy"]
+    # The large cases run the zero-copy NVLS kernel; the smallest AllGather (4 KiB blocks) takes
+    # the low-latency kernel, which the planner prefers for small ungrouped blocks on any buffer.
+    assert res[0].get("skipped") or ("nvls_zero_copy" in res[0]["algorithms"] and
+                                     set(res[0]["algorithms"]) <= {"nvls_zero_copy", "ll"})
 
 
 def test_cuda_graph_replay_single_rank():
