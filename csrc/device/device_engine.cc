@@ -754,8 +754,13 @@ bool DeviceEngine::Execute(const std::vector<CollTask>& sorted, cudaStream_t str
         if (!EnsureP2pStream()) return false;
         CUDA_OK(cudaEventRecord(p2p_fork_, stream), "cudaEventRecord(p2p fork)");
         CUDA_OK(cudaStreamWaitEvent(p2p_stream_, p2p_fork_, 0), "cudaStreamWaitEvent(p2p fork)");
-        if (!p2p_.Run(p2p, p2p_stream_)) return false;
+        const bool p2p_ok = p2p_.Run(p2p, p2p_stream_);
         CUDA_OK(cudaEventRecord(p2p_join_, p2p_stream_), "cudaEventRecord(p2p join)");
+        if (!p2p_ok) {
+            // What was enqueued on the side stream still orders before the caller's later work.
+            CUDA_OK(cudaStreamWaitEvent(stream, p2p_join_, 0), "cudaStreamWaitEvent(p2p join)");
+            return false;
+        }
         p2p.clear();
         forked = true;
         num_sms_ = std::max(16, sms_all - kP2pReservedSms);
