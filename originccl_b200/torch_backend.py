@@ -7,8 +7,9 @@ between the processes of a machine, TCP between machines). Each communicator is 
 first collective that needs it; the unique id travels through the process group's store.
 Supported: all_reduce (SUM, AVG, MAX, MIN), broadcast, reduce, all_gather (list and tensor
 forms), reduce_scatter (list and tensor forms), their coalesced forms (one group, i.e. one
-batched kernel for small tensors), send / recv and barrier — the reference's operation set.
-AllToAll, gather and scatter, which the reference does not have, raise ``NotImplementedError``.
+batched kernel for small tensors), send / recv and barrier — the reference's operation set —
+plus all_to_all (list form, and all_to_all_single with equal or uneven splits), gather and
+scatter, which the reference does not have, as Send/Recv groups.
 DistributedDataParallel runs on it unchanged; :class:`AllReduceHook` is a DDP communication hook
 that fuses the gradient mean into the AllReduce and registers large bucket buffers for zero-copy.
 """
@@ -167,13 +168,51 @@ class BcclProcessGroup(dist.ProcessGroup):
         return _done([])
 
     # ------------------------------------------------------------------ not in the reference
+    # AllToAll, gather and scatter are not among the reference's collectives (OriginCCL
+    # include/types.h:30-38); here they are Send/Recv groups (its P2P semantics: FIFO per pair,
+    # one group), so they run wherever Send/Recv does.
+    @staticmethod
+    def _flat(t: torch.Tensor):
+        """(a contiguous 1-D view of t or of a contiguous copy, the copy or None)."""
+        if t.is_contiguous():
+            return t.reshape(-1), None
+        c = t.contiguous()
+        return c.reshape(-1), c
+
     def alltoall_base(self, output: torch.Tensor, input: torch.Tensor, output_split_sizes: List[int],
                       input_split_sizes: List[int], opts=None):
-        """dist.all_to_all_single with equal splits (Communicator.all_to_all); uneven splits are
-        not provided."""
-        if output_split_sizes or input_split_sizes:
-            raise NotImplementedError("bccl: all_to_all_single takes equal splits only")
-        self._comm(input).all_to_all(output, input)
+        """dist.all_to_all_single: rows [in_off(q), in_off(q) + input_split_sizes[q]) of input (dim 0)
+        go to rank q, rows from rank q land at out_off(q) of output; equal splits when the lists
+        are empty (Communicator.all_to_all). One Send/Recv group."""
+        comm = self._comm(input)
+        w, r = comm.world_size, comm.rank
+        if not output_split_sizes and not input_split_sizes:
+            comm.all_to_all(output, input)
+            return _done([output])
+        in_rows = list(input_split_sizes) if input_split_sizes else [input.shape[0] // w] * w
+        out_rows = list(output_split_sizes) if output_split_sizes else [output.shape[0] // w] * w
+        if len(in_rows) != w or len(out_rows) != w or sum(in_rows) != input.shape[0] or \
+                sum(out_rows) != output.shape[0] or in_rows[r] != out_rows[r]:
+            raise ValueError(f"bccl: all_to_all_single split sizes {in_rows} / {out_rows} do not match "
+                             f"shapes {tuple(input.shape)} / {tuple(output.shape)} on {w} ranks")
+        in_row = input[0].numel() if input.shape[0] else 0
+        out_row = output[0].numel() if output.shape[0] else 0
+        src, _ = self._flat(input)
+        dst, tmp = self._flat(output)
+        io = [sum(in_rows[:q]) * in_row for q in range(w)]
+        oo = [sum(out_rows[:q]) * out_row for q in range(w)]
+        if out_rows[r]:
+            dst[oo[r]:oo[r] + out_rows[r] * out_row].copy_(src[io[r]:io[r] + in_rows[r] * in_row])
+        with comm.group():
+            for q in range(w):
+                if q == r:
+                    continue
+                if in_rows[q]:
+                    comm.send(src[io[q]:io[q] + in_rows[q] * in_row], q)
+                if out_rows[q]:
+                    comm.recv(dst[oo[q]:oo[q] + out_rows[q] * out_row], q)
+        if tmp is not None:
+            output.copy_(tmp)
         return _done([output])
 
     def alltoall(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor], opts=None):
@@ -188,11 +227,47 @@ class BcclProcessGroup(dist.ProcessGroup):
                     comm.recv(outputs[q], q)
         return _done(outputs)
 
-    def gather(self, *args, **kwargs):
-        raise NotImplementedError("bccl: gather is not provided")
+    def gather(self, outputs: List[List[torch.Tensor]], inputs: List[torch.Tensor], opts=None):
+        """dist.gather: the root receives every rank's tensor into outputs[0][q] (one group)."""
+        root = opts.rootRank
+        comm = self._comm(inputs[0])
+        r = comm.rank
+        if r != root:
+            src, _ = self._flat(inputs[0])
+            comm.send(src, root)
+            return _done(outputs)
+        outs = outputs[0]
+        outs[r].copy_(inputs[0])
+        tmps = []
+        with comm.group():
+            for q in range(comm.world_size):
+                if q != r:
+                    dst, tmp = self._flat(outs[q])
+                    comm.recv(dst, q)
+                    if tmp is not None:
+                        tmps.append((outs[q], tmp))
+        for o, t in tmps:
+            o.copy_(t)
+        return _done(outputs)
 
-    def scatter(self, *args, **kwargs):
-        raise NotImplementedError("bccl: scatter is not provided")
+    def scatter(self, outputs: List[torch.Tensor], inputs: List[List[torch.Tensor]], opts=None):
+        """dist.scatter: the root sends inputs[0][q] to rank q, which receives it into outputs[0]."""
+        root = opts.rootRank
+        comm = self._comm(outputs[0])
+        r = comm.rank
+        if r != root:
+            dst, tmp = self._flat(outputs[0])
+            comm.recv(dst, root)
+            if tmp is not None:
+                outputs[0].copy_(tmp)
+            return _done(outputs)
+        ins = inputs[0]
+        outputs[0].copy_(ins[r])
+        with comm.group():
+            for q in range(comm.world_size):
+                if q != r:
+                    comm.send(self._flat(ins[q])[0], q)
+        return _done(outputs)
 
 
 class AllReduceHook:

@@ -58,13 +58,35 @@ def run_collectives(rank: int, world: int) -> Dict:
     outs = [torch.empty(2, dtype=torch.int64) for _ in range(world)]
     dist.all_to_all(outs, [torch.full((2,), 10 * rank + q, dtype=torch.int64) for q in range(world)])
     assert all(torch.all(o == 10 * q + rank) for q, o in enumerate(outs))
+    # Uneven splits (rows of dim 0): rank r sends (r + q) % 3 + 1 rows of 4 to rank q; its
+    # input block for q holds 1000 * r + 10 * q + row.
+    rows = lambda a, b: (a + b) % 3 + 1  # noqa: E731  rows rank a sends to rank b
+    send_rows = [rows(rank, q) for q in range(world)]
+    recv_rows = [rows(q, rank) for q in range(world)]
+    inp = torch.cat([torch.arange(send_rows[q], dtype=torch.float32)[:, None].repeat(1, 4) + 1000 * rank + 10 * q
+                     for q in range(world)])
+    out = torch.full((sum(recv_rows), 4), -1.0)
+    dist.all_to_all_single(out, inp, recv_rows, send_rows)
+    want = torch.cat([torch.arange(recv_rows[q], dtype=torch.float32)[:, None].repeat(1, 4) + 1000 * q + 10 * rank
+                      for q in range(world)])
+    assert torch.equal(out, want), (out, want)
+    # Splits that do not add up to the shapes are rejected before anything is sent.
     try:
-        dist.all_to_all_single(torch.empty(world), torch.empty(world), [1] * world, [1] * world)
-        raised = False
-    except (NotImplementedError, RuntimeError):
-        raised = True
+        dist.all_to_all_single(torch.empty(world), torch.empty(world), [2] * world, [1] * world)
+        rejected = False
+    except (ValueError, RuntimeError):
+        rejected = True
+    # gather / scatter to and from the last rank, with int64 values.
+    root = world - 1
+    gathered = [torch.empty(6, dtype=torch.int64) for _ in range(world)] if rank == root else None
+    dist.gather(torch.arange(6, dtype=torch.int64) * (rank + 1), gathered, dst=root)
+    if rank == root:
+        assert all(torch.equal(g, torch.arange(6, dtype=torch.int64) * (q + 1)) for q, g in enumerate(gathered))
+    piece = torch.empty(3)
+    dist.scatter(piece, [torch.full((3,), 7.0 * q) for q in range(world)] if rank == root else None, src=root)
+    assert torch.all(piece == 7.0 * rank)
     dist.destroy_process_group()
-    return {"uneven_alltoall_rejected": raised}
+    return {"bad_splits_rejected": rejected}
 
 
 def run_ddp(rank: int, world: int, hook: bool = False) -> Dict:
