@@ -9,6 +9,7 @@
 #include "core/planner.h"
 #include "device/device_engine.h"
 #include "kernels/gemm.h"
+#include "kernels/ll_epoch.h"
 #include "kernels/p2p_sched.h"
 
 #include <mutex>
@@ -344,6 +345,7 @@ int bcclGemmCheckError(void) {
 }
 
 int bcclP2pChannels(unsigned long long pair_bytes) { return bccl::P2pChannels(pair_bytes); }
+unsigned int bcclLLEpoch(unsigned long long seq) { return bccl::LLEpoch(seq); }
 
 int bcclP2pPlan(const unsigned long long* bytes, int nops, int nch, int ch, int max_out, int* op_out,
                 unsigned long long* off_out, unsigned long long* len_out) {

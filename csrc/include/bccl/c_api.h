@@ -148,6 +148,9 @@ int bcclPlannerP2pRound(int func, int rank, int peer, int world);
  * carries for operations of sizes bytes[0..nops), in message order: operation index, byte offset
  * and length of each (at most max_out); returns how many, or -1 on bad arguments. */
 int bcclP2pChannels(unsigned long long pair_bytes);
+/* Low-latency kernel hook (used by tests): the line epoch of the launch that follows `seq`
+ * earlier low-latency launches of a communicator. */
+unsigned int bcclLLEpoch(unsigned long long seq);
 int bcclP2pPlan(const unsigned long long* bytes, int nops, int nch, int ch, int max_out, int* op_out,
                 unsigned long long* off_out, unsigned long long* len_out);
 int bcclPlannerValidate(int rank, int world, int func, size_t count, int dtype, int op, int root, int peer,

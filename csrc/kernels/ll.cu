@@ -8,7 +8,7 @@
 // once both epoch words match the launch's epoch (a 16-byte store may reach the peer as two
 // 8-byte halves, hence two epoch words). No fence, no flag, no barrier: one NVLink trip.
 //
-//   rank r, launch epoch e (from DevState::ll_seq, the same on every rank), parity e & 1:
+//   rank r, launch epoch e (LLEpoch(DevState::ll_seq), the same on every rank), parity e & 1:
 //     for each of its lines i: store line(i, own payload, e) into buf[peer][parity][r][i]
 //     then for each of them:   poll buf[r][parity][p][i] for every peer p until epoch == e
 //                              out[i] = epilogue(reduce(own, peers in rank order))
@@ -29,6 +29,7 @@
 
 #include "kernels/common.cuh"
 #include "kernels/launch.h"
+#include "kernels/ll_epoch.h"
 
 namespace bccl {
 namespace dev {
@@ -46,14 +47,6 @@ struct LLParams {
 __device__ __forceinline__ uint4* ll_line(const DevComm& c, int owner, int parity, int src, size_t i) {
     char* base = c.uc[owner] + c.ll_off;
     return reinterpret_cast<uint4*>(base) + ((size_t)parity * kMaxRanks + src) * kLLMaxLines + i;
-}
-
-// Line epoch of the launch that follows `seq` earlier ones: 1, 2, ..., 2^32 - 2, then 1 again.
-// Never 0 (the value of a line that was never written) and always the other parity than the
-// previous launch's, also across the wrap (2^32 - 2 is even, 1 is odd), so the parity rule above
-// holds however many launches a communicator makes.
-__device__ __forceinline__ uint32_t ll_epoch(unsigned long long seq) {
-    return (uint32_t)(seq % 4294967294ull) + 1u;
 }
 
 __device__ __forceinline__ void st_line(uint4* p, uint4 v) {
@@ -174,7 +167,7 @@ template <int D, int O, bool RS>
 __global__ void __launch_bounds__(256) ll_reduce_kernel(const __grid_constant__ LLParams p) {
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
-    const uint32_t epoch = ll_epoch(load_state_u64(&c.state->ll_seq));
+    const uint32_t epoch = LLEpoch(load_state_u64(&c.state->ll_seq));
     const int parity = (int)(epoch & 1u);
     const size_t lines = (p.bytes + 7) / 8;
     using P = Pack8<D>;
@@ -226,7 +219,7 @@ __global__ void __launch_bounds__(256) ll_reduce_kernel(const __grid_constant__ 
 __global__ void __launch_bounds__(256) ll_allgather_kernel(const __grid_constant__ LLParams p) {
     const DevComm& c = p.comm;
     const int r = c.rank, n = c.nranks;
-    const uint32_t epoch = ll_epoch(load_state_u64(&c.state->ll_seq));
+    const uint32_t epoch = LLEpoch(load_state_u64(&c.state->ll_seq));
     const int parity = (int)(epoch & 1u);
     const size_t lines = (p.bytes + 7) / 8;
     const size_t first = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;

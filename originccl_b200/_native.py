@@ -102,6 +102,7 @@ def load(path: Path | None = None) -> ctypes.CDLL:
         "bcclDebugBandwidth": (ctypes.c_double, [vp, c_int, c_int, c_size, c_int, c_int]),
         "bcclPlannerP2pRound": (c_int, [c_int, c_int, c_int, c_int]),
         "bcclP2pChannels": (c_int, [ctypes.c_ulonglong]),
+        "bcclLLEpoch": (ctypes.c_uint, [ctypes.c_ulonglong]),
         "bcclP2pPlan": (c_int, [ctypes.POINTER(ctypes.c_ulonglong), c_int, c_int, c_int, c_int, ctypes.POINTER(c_int),
                                 ctypes.POINTER(ctypes.c_ulonglong), ctypes.POINTER(ctypes.c_ulonglong)]),
         "bcclPlannerValidate": (c_int, [c_int, c_int, c_int, c_size, c_int, c_int, c_int, c_int, c_int, c_int]),
