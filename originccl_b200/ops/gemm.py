@@ -27,10 +27,17 @@ def gemm(a, w, activation: Optional[str] = None, out=None):
         raise TypeError("gemm expects bfloat16 operands")
     if a.dim() != 2 or w.dim() != 2 or a.shape[1] != w.shape[1]:
         raise ValueError(f"shape mismatch: a {tuple(a.shape)} w {tuple(w.shape)}")
+    if activation not in _ACTS:
+        raise ValueError(f"gemm: activation {activation!r} (none, silu)")
+    if a.device != w.device or a.device.type != "cuda":
+        raise ValueError(f"gemm: operands must be CUDA tensors on one device, got {a.device} and {w.device}")
     a = a.contiguous()
     w = w.contiguous()
     m, k = a.shape
     n = w.shape[0]
+    if out is not None and (out.dtype != torch.bfloat16 or tuple(out.shape) != (m, n) or out.stride(1) != 1 or
+                            out.device != a.device):
+        raise ValueError(f"gemm: out must be a bfloat16 [{m}, {n}] tensor with unit column stride on {a.device}")
     if out is None:
         out = torch.empty(m, n, device=a.device, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream(a.device).cuda_stream
