@@ -50,3 +50,30 @@ def test_gemm_rejects_bad_operands():
         gemm.gemm(a, w, "relu")
     with pytest.raises(ValueError, match="CUDA"):
         gemm.gemm(a, w)
+
+
+def test_collectives_reject_mismatched_buffers_before_the_library():
+    """A host communicator (no GPU needed) checks sizes, dtypes and memory kind in Python."""
+    import numpy as np
+
+    import originccl_b200 as occl
+
+    comm = occl.Communicator().init(0, 1, None)  # one rank, host memory
+    try:
+        x = np.arange(8, dtype=np.float32)
+        with pytest.raises(ValueError, match="all_reduce"):
+            comm.all_reduce(x, out=np.zeros(4, dtype=np.float32))
+        with pytest.raises(ValueError, match="dtype"):
+            comm.all_reduce(x, out=np.zeros(8, dtype=np.float64))
+        with pytest.raises(ValueError, match="all_gather"):
+            comm.all_gather(np.zeros(7, dtype=np.float32), x)
+        with pytest.raises(ValueError, match="reduce_scatter"):
+            comm.reduce_scatter(np.zeros(8, dtype=np.float32), np.zeros(9, dtype=np.float32))
+        y = np.zeros(8, dtype=np.float32)
+        comm.all_reduce(x, out=y)  # matching buffers still run
+        assert np.array_equal(x, y)
+        if torch.cuda.is_available():
+            with pytest.raises(ValueError, match="CUDA"):
+                comm.all_reduce(torch.zeros(8, device="cuda"))
+    finally:
+        comm.destroy()
