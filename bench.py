@@ -259,22 +259,19 @@ def main() -> None:
     # timing rules, first on the same torch tensors registered with the communicator (peer
     # memory, no staging), then on symmetric multicast-bound allocations (NVLS without staging
     # where the planner picks NVLS). Reported beside the headline, which stays on plain buffers.
-    zero_copy = None
-    arms = [a for a in args.zero_copy_arms.split(",") if a in ("registered", "symmetric")]
-    if world > 1 and args.buffers == "plain" and arms and not args.inplace:
-        zero_copy = {}
-        ref_last = reference_of(args.steps - 1)
-        for kind in arms:
-            if kind == "registered":
-                bufs = [*xs, y]
-                for t_ in bufs:
-                    comm.register(t_)
-            else:
-                bufs = [comm.symmetric_empty((count,), dtype) for _ in range(3)]
-                for dst_, src_ in zip(bufs[:2], xs):
-                    dst_.copy_(src_)
-                torch.cuda.synchronize()
-            zin, zout = bufs[:2], bufs[2]
+    def zero_copy_arm(kind: str) -> dict:
+        """The same out-of-place AllReduce on registered tensors or symmetric allocations."""
+        if kind == "registered":
+            bufs = [*xs, y]
+            for t_ in bufs:
+                comm.register(t_)
+        else:
+            bufs = [comm.symmetric_empty((count,), dtype) for _ in range(3)]
+            for dst_, src_ in zip(bufs[:2], xs):
+                dst_.copy_(src_)
+            torch.cuda.synchronize()
+        zin, zout = bufs[:2], bufs[2]
+        try:
             for i in range(args.warmup):
                 comm.all_reduce(zin[i & 1], out=zout, algo=algo)
             torch.cuda.synchronize(); barrier(); torch.cuda.synchronize()
@@ -288,15 +285,29 @@ def main() -> None:
             dist.all_reduce(tz, op=dist.ReduceOp.MAX)
             zms = float(tz.item())
             zerr = float((zout.float() - ref_last).abs().max().item())
-            zero_copy[kind] = {"ms_per_step": round(zms, 4),
-                               "busbw_gbs_per_rank": round(nbytes / (zms * 1e-3) / 1e9 * factor, 2),
-                               "algorithm": comm.last_algorithm, "gpu_launches": comm.kernel_launches - l0,
-                               "max_abs_err_vs_nccl_last_step": zerr}
+            return {"ms_per_step": round(zms, 4),
+                    "busbw_gbs_per_rank": round(nbytes / (zms * 1e-3) / 1e9 * factor, 2),
+                    "algorithm": comm.last_algorithm, "gpu_launches": comm.kernel_launches - l0,
+                    "max_abs_err_vs_nccl_last_step": zerr}
+        finally:
             if kind == "registered":
                 for t_ in bufs:
                     comm.deregister(t_)
-            del bufs, zin, zout
             torch.cuda.synchronize(); barrier()
+
+    zero_copy = None
+    arms = [a for a in args.zero_copy_arms.split(",") if a in ("registered", "symmetric")]
+    if world > 1 and args.buffers == "plain" and arms and not args.inplace:
+        zero_copy = {}
+        ref_last = reference_of(args.steps - 1)
+        for kind in arms:
+            try:
+                zero_copy[kind] = zero_copy_arm(kind)
+            except Exception as e:  # noqa: BLE001  an extra arm must not cost the headline line
+                # A failing library call fails the same way on every rank (registration and the
+                # kernels' bounded waits are collective), so the ranks stay in step.
+                zero_copy[kind] = {"error": f"{type(e).__name__}: {e}"[:300]}
+                break
     if rank == 0:
         out = {
             "metric": "AllReduce bus GB/s vs size at 2/4/8 B200 (max over ranks) vs reference & NCCL",
@@ -343,7 +354,10 @@ def main() -> None:
                         "NCCL and e2e loops (NVML during a timed loop perturbs it)"},
         }
         print(json.dumps(out), flush=True)
-    comm.destroy()
+    try:
+        comm.destroy()
+    except Exception as e:  # noqa: BLE001  after a failed extra arm; the line is out already
+        print(f"rank {rank}: communicator teardown: {e}", file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
