@@ -325,24 +325,29 @@ class Communicator:
         return int(handle), 1
 
     # ---------------------------------------------------------------- argument checks
+    # On the per-call path of every collective: a few attribute reads for torch tensors.
     def _where(self, t: Any) -> None:
         """t must live where this communicator's kernels or threads can address it: device
         memory for a device communicator, host memory for a host one (a pointer of the other
         kind would be dereferenced by a kernel or by memcpy)."""
         on_gpu = getattr(t, "is_cuda", False)
-        if on_gpu != (self.device >= 0):
+        if on_gpu is not (self.device >= 0):
             raise ValueError(f"bccl: a {'device' if self.device >= 0 else 'host'} communicator got a "
                              f"{'CUDA' if on_gpu else 'host'} buffer")
 
-    def _pair(self, name: str, a: Any, b: Any, na: int, nb: int) -> None:
-        """a and b hold na and nb elements of one dtype (b may be a itself: in place)."""
-        self._where(a)
-        if b is a or b is None:
+    def _pair(self, name: str, a: Any, b: Any, nb: int) -> None:
+        """a is in this communicator's memory; b (unless None or a itself: in place) too, with
+        a's dtype and nb elements."""
+        gpu = self.device >= 0
+        if getattr(a, "is_cuda", False) is not gpu:
+            self._where(a)
+        if b is None or b is a:
             return
-        self._where(b)
-        if b.dtype != a.dtype or _numel(a) != na or _numel(b) != nb:
-            raise ValueError(f"bccl: {name} needs {na} and {nb} elements of one dtype, got {_numel(a)} "
-                             f"{a.dtype} and {_numel(b)} {b.dtype}")
+        if getattr(b, "is_cuda", False) is not gpu:
+            self._where(b)
+        if b.dtype != a.dtype or _numel(b) != nb:
+            raise ValueError(f"bccl: {name}: the other buffer needs {nb} elements of dtype {a.dtype}, got "
+                             f"{_numel(b)} of {b.dtype}")
 
     # ---------------------------------------------------------------- collectives
     def all_reduce(self, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, out: Any = None, scale: float = 1.0,
@@ -350,7 +355,7 @@ class Communicator:
         """out = reduce(tensor over ranks) * scale; in place when ``out`` is None."""
         out = tensor if out is None else out
         n = _numel(tensor)
-        self._pair("all_reduce", tensor, out, n, n)
+        self._pair("all_reduce", tensor, out, n)
         s, has = self._stream(stream)
         self._check(self._lib.bcclAllReduce(self._h, _ptr(tensor), _ptr(out), _numel(tensor), int(_dtype_of(tensor)),
                                             int(op), float(scale), int(algo), s, has))
@@ -359,7 +364,7 @@ class Communicator:
     def broadcast(self, tensor: Any, root: int, *, src: Any = None, algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
         """Every rank's ``tensor`` receives the root's data (``src`` on the root when out of place)."""
         n = _numel(tensor)
-        self._pair("broadcast", tensor, src, n, n)
+        self._pair("broadcast", tensor, src, n)
         s, has = self._stream(stream)
         self._check(self._lib.bcclBroadcast(self._h, _ptr(src) if src is not None else _ptr(tensor), _ptr(tensor),
                                             _numel(tensor), int(_dtype_of(tensor)), int(root), int(algo), s, has))
@@ -370,7 +375,7 @@ class Communicator:
         """The root's ``out`` (default: ``tensor``) receives the reduction; other ranks' out may be None."""
         dst = out if out is not None else (tensor if self.rank == root else None)
         n = _numel(tensor)
-        self._pair("reduce", tensor, dst, n, n)
+        self._pair("reduce", tensor, dst, n)
         s, has = self._stream(stream)
         self._check(self._lib.bcclReduce(self._h, _ptr(tensor), _ptr(dst), _numel(tensor), int(_dtype_of(tensor)),
                                          int(op), int(root), int(algo), s, has))
@@ -379,7 +384,7 @@ class Communicator:
     def all_gather(self, out: Any, tensor: Any, *, algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
         """out (world_size * numel) = concatenation of every rank's tensor in rank order."""
         n = _numel(tensor)
-        self._pair("all_gather", tensor, out, n, n * self.world_size)
+        self._pair("all_gather", tensor, out, n * self.world_size)
         s, has = self._stream(stream)
         self._check(self._lib.bcclAllGatherAlgo(self._h, _ptr(tensor), _ptr(out), _numel(tensor),
                                                 int(_dtype_of(tensor)), int(algo), s, has))
@@ -389,7 +394,7 @@ class Communicator:
                        stream: Any = None) -> Any:
         """out (numel) = this rank's block of reduce(tensor (world_size * numel))."""
         n = _numel(out)
-        self._pair("reduce_scatter", out, tensor, n, n * self.world_size)
+        self._pair("reduce_scatter", out, tensor, n * self.world_size)
         s, has = self._stream(stream)
         self._check(self._lib.bcclReduceScatterAlgo(self._h, _ptr(tensor), _ptr(out), _numel(out),
                                                     int(_dtype_of(out)), int(op), int(algo), s, has))
