@@ -14,6 +14,20 @@ import os
 import sys
 
 
+def measured_peak_tflops(default: float = 1383.8) -> float:
+    """The sustained cuBLAS bf16 peak measured on this pool's B200s (``bf16_tflops_sustained`` in
+    the repository's MEASURED_PEAKS.json, written per machine pool), else ``default`` (an earlier
+    measurement of the same loop)."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        import json
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except (OSError, ValueError, KeyError, TypeError):
+        return default
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--tokens", type=int, default=8192)
@@ -21,13 +35,16 @@ def main(argv=None) -> None:
     p.add_argument("--ffn", type=int, default=28672)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--iters", type=int, default=20)
-    p.add_argument("--gemm-peak-tflops", type=float, default=1383.8, help="measured sustained cuBLAS bf16 peak")
+    p.add_argument("--gemm-peak-tflops", type=float, default=None,
+                   help="sustained bf16 GEMM peak for the roofline (default: MEASURED_PEAKS.json, else 1383.8)")
     p.add_argument("--nvlink-gbs", type=float, default=770.0)
     p.add_argument("--out", default="", help="also append the record to this JSON-lines file")
     p.add_argument("--variants", default="",
                    help="also time the fused MLP under each environment variant, e.g. "
                         "'BCCL_GEMM_BN=auto,BCCL_TP_PUSH_WARPS=2,BCCL_GEMM_BN=auto;BCCL_TP_PUSH_WARPS=2'")
     args = p.parse_args(argv)
+    if args.gemm_peak_tflops is None:
+        args.gemm_peak_tflops = measured_peak_tflops()
     import torch
     import torch.distributed as dist
 
@@ -115,6 +132,7 @@ def main(argv=None) -> None:
              "ffn": args.ffn, "ours_ms": round(ours, 4), "nccl_cublas_ms": round(ref, 4),
              "speedup": round(ref / ours, 3), "tflops_per_gpu": round(flops / ours / 1e9, 1),
              "roofline_ms": round(roof_ms, 4), "fraction_of_roofline": round(roof_ms / ours, 3),
+             "gemm_peak_tflops": args.gemm_peak_tflops, "nvlink_gbs": args.nvlink_gbs,
              "max_rel_diff_vs_reference": rel, "gemm_kernel": gemm_op.kernel_name(args.tokens, args.ffn // world),
              "breakdown": bd, "variants_ms": variants})
     comm.destroy()
