@@ -339,12 +339,16 @@ class Communicator:
         """a is in this communicator's memory; b (unless None or a itself: in place) too, with
         a's dtype and nb elements."""
         gpu = self.device >= 0
-        if getattr(a, "is_cuda", False) is not gpu:
-            self._where(a)
+        try:  # torch tensors: five attribute reads when everything matches
+            if a.is_cuda is gpu and (b is None or b is a or
+                                     (b.is_cuda is gpu and b.dtype == a.dtype and b.numel() == nb)):
+                return
+        except AttributeError:  # numpy arrays (host memory)
+            pass
+        self._where(a)
         if b is None or b is a:
             return
-        if getattr(b, "is_cuda", False) is not gpu:
-            self._where(b)
+        self._where(b)
         if b.dtype != a.dtype or _numel(b) != nb:
             raise ValueError(f"bccl: {name}: the other buffer needs {nb} elements of dtype {a.dtype}, got "
                              f"{_numel(b)} of {b.dtype}")
@@ -357,8 +361,10 @@ class Communicator:
         n = _numel(tensor)
         self._pair("all_reduce", tensor, out, n)
         s, has = self._stream(stream)
-        self._check(self._lib.bcclAllReduce(self._h, _ptr(tensor), _ptr(out), _numel(tensor), int(_dtype_of(tensor)),
-                                            int(op), float(scale), int(algo), s, has))
+        # DataType / ReduceOp / Algo are IntEnums: ctypes takes them as ints.
+        src = _ptr(tensor)
+        self._check(self._lib.bcclAllReduce(self._h, src, src if out is tensor else _ptr(out), n, _dtype_of(tensor),
+                                            op, float(scale), algo, s, has))
         return out
 
     def broadcast(self, tensor: Any, root: int, *, src: Any = None, algo: Algo = Algo.AUTO, stream: Any = None) -> Any:
@@ -386,8 +392,7 @@ class Communicator:
         n = _numel(tensor)
         self._pair("all_gather", tensor, out, n * self.world_size)
         s, has = self._stream(stream)
-        self._check(self._lib.bcclAllGatherAlgo(self._h, _ptr(tensor), _ptr(out), _numel(tensor),
-                                                int(_dtype_of(tensor)), int(algo), s, has))
+        self._check(self._lib.bcclAllGatherAlgo(self._h, _ptr(tensor), _ptr(out), n, _dtype_of(tensor), algo, s, has))
         return out
 
     def reduce_scatter(self, out: Any, tensor: Any, op: ReduceOp = ReduceOp.SUM, *, algo: Algo = Algo.AUTO,
@@ -396,8 +401,8 @@ class Communicator:
         n = _numel(out)
         self._pair("reduce_scatter", out, tensor, n * self.world_size)
         s, has = self._stream(stream)
-        self._check(self._lib.bcclReduceScatterAlgo(self._h, _ptr(tensor), _ptr(out), _numel(out),
-                                                    int(_dtype_of(out)), int(op), int(algo), s, has))
+        self._check(self._lib.bcclReduceScatterAlgo(self._h, _ptr(tensor), _ptr(out), n, _dtype_of(out), op, algo,
+                                                    s, has))
         return out
 
     def send(self, tensor: Any, peer: int, *, stream: Any = None) -> None:
