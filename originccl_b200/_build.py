@@ -75,10 +75,10 @@ def _ninja_file() -> str:
         "  deps = gcc",
         "  description = NVCC $out",
         "rule link",
-        f"  command = $nvcc {ARCH} -shared -cudart static -o $out $in -ldl -lpthread -lrt",
+        f"  command = $nvcc {ARCH} -shared -cudart static -o $out.tmp $in -ldl -lpthread -lrt && mv -f $out.tmp $out",
         "  description = LINK $out",
         "rule linkexe",
-        "  command = $cxx -o $out $in -lpthread",
+        "  command = $cxx -o $out.tmp $in -lpthread && mv -f $out.tmp $out",
         "  description = LINK $out",
         "rule cc",
         f"  command = gcc -MMD -MF $out.d -O2 -g -std=c11 -Wall -Wextra -pedantic -I{CSRC / 'include'} -c $in -o $out",
@@ -86,8 +86,8 @@ def _ninja_file() -> str:
         "  deps = gcc",
         "  description = CC $out",
         "rule linkexample",
-        f"  command = $cxx -o $out $in -L{LIBDIR} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} -lcudart "
-        f"-Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread",
+        f"  command = $cxx -o $out.tmp $in -L{LIBDIR} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} -lcudart "
+        f"-Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread && mv -f $out.tmp $out",
         "  description = LINK $out",
     ]
     objs = []
@@ -143,11 +143,12 @@ def _sanitized_ninja_file(kind: str) -> str:
         "  deps = gcc",
         "  description = CXX $out",
         "rule link",
-        f"  command = g++ {san} -shared -o $out $in -L{CUDA_HOME / 'lib64'} -lcudart_static -ldl -lpthread -lrt",
+        f"  command = g++ {san} -shared -o $out.tmp $in -L{CUDA_HOME / 'lib64'} -lcudart_static -ldl -lpthread -lrt "
+        "&& mv -f $out.tmp $out",
         "  description = LINK $out",
         "rule linkexe",
-        f"  command = g++ {san} -o $out $in -L{out} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} "
-        f"-lcudart -Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread",
+        f"  command = g++ {san} -o $out.tmp $in -L{out} -lbccl -Wl,-rpath,'$$ORIGIN' -L{CUDA_HOME / 'lib64'} "
+        f"-lcudart -Wl,-rpath,{CUDA_HOME / 'lib64'} -lpthread && mv -f $out.tmp $out",
         "  description = LINK $out",
     ]
     objs = []
@@ -167,8 +168,9 @@ def _sanitized_ninja_file(kind: str) -> str:
 
 
 class _BuildLock:
-    """Serialises builds across processes (pytest-xdist workers may build at the same time; a
-    half-linked library is "file too short" for the process that loads it meanwhile)."""
+    """Serialises builds across processes (pytest-xdist workers may build at the same time). Links
+    write a temporary file and rename it into place, so a process that loads a library or program
+    while another relinks it sees the old or the new file, never a half-written one."""
 
     def __enter__(self):
         import fcntl
