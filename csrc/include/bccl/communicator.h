@@ -99,6 +99,10 @@ public:
     // same order. AllReduce / AllGather / ReduceScatter of at least 1 MiB whose buffers lie in
     // registered memory, at the same offset on every rank, then read and write the peers'
     // buffers directly instead of staging. Host communicators accept and ignore it.
+    // Each rank decides from its own registrations whether a call runs zero-copy, so a call's
+    // buffers must be registered on every rank or on none: deregister (collectively) before the
+    // memory is freed or handed to other tensors, since a reused range would still count as
+    // registered on this rank only.
     bool RegisterBuffer(void* ptr, size_t bytes);
     bool DeregisterBuffer(void* ptr);
     bool Barrier();

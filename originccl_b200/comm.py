@@ -540,8 +540,11 @@ class Communicator:
         """Collective: lets the peers address ``tensor``'s memory (CUDA IPC) so that AllReduce,
         AllGather and ReduceScatter of at least 1 MiB on it (or on a view at the same offset on
         every rank) run without staging copies. Every rank registers its own tensor of the same
-        size, in the same order; deregister before the memory is freed. Host communicators
-        ignore it. Returns ``tensor``."""
+        size, in the same order. Each rank decides from its own registrations whether a call runs
+        zero-copy, so a call's buffers must be registered on every rank or on none: deregister
+        before the memory is freed or reused by other tensors (PyTorch's caching allocator hands
+        freed blocks to new tensors, whose collectives would otherwise count as registered on this
+        rank only). Host communicators ignore it. Returns ``tensor``."""
         self._check(self._lib.bcclCommRegister(self._h, _ptr(tensor), _nbytes(tensor)))
         return tensor
 
