@@ -289,6 +289,8 @@ bool HostEngine::Init(const CommConfig& cfg, Bootstrap* bs, FdPasser* fp, const 
             p2p_recv_[p].reset(new Shared(p2p_tcp_[p]));
         }
     }
+    chan_seq_.reset(new std::atomic<uint64_t>[n_channels_]());
+    cv_chan_.reset(new std::condition_variable[n_channels_]);
     for (int c = 0; c < n_channels_; ++c) workers_.emplace_back(&HostEngine::WorkerLoop, this, c);
     if (!bs->Barrier()) return false;
     inited_ = true;
@@ -335,7 +337,7 @@ void HostEngine::Finalize() {
         std::lock_guard<std::mutex> lk(mu_);
         stop_.store(true);
     }
-    cv_job_.notify_all();
+    for (int c = 0; c < static_cast<int>(workers_.size()); ++c) cv_chan_[c].notify_all();
     for (auto& t : workers_)
         if (t.joinable()) t.join();
     workers_.clear();
@@ -362,23 +364,24 @@ void HostEngine::WorkerLoop(int ch) {
         CPU_SET(static_cast<int>((view_.local_rank * n_channels_ + ch) % std::max<long>(ncores, 1)), &set);
         if (sched_setaffinity(0, sizeof(set), &set) != 0) LOG_WARN("rank %d: pinning channel %d failed", rank_, ch);
     }
+    std::atomic<uint64_t>& my_seq = chan_seq_[ch];
     uint64_t seen = 0;
     for (;;) {
-        if (job_seq_.load(std::memory_order_acquire) == seen && !stop_.load(std::memory_order_acquire)) {
+        if (my_seq.load(std::memory_order_acquire) == seen && !stop_.load(std::memory_order_acquire)) {
             if (spin_) {
                 const auto until = Clock::now() + std::chrono::microseconds(kSpinUs);
-                for (uint32_t i = 0; job_seq_.load(std::memory_order_acquire) == seen && !stop_.load(); ++i) {
+                for (uint32_t i = 0; my_seq.load(std::memory_order_acquire) == seen && !stop_.load(); ++i) {
                     CpuRelax();
                     if ((i & 255u) == 255u && Clock::now() > until) break;
                 }
             }
             std::unique_lock<std::mutex> lk(mu_);
-            cv_job_.wait(lk, [&] { return stop_.load() || job_seq_.load() != seen; });
+            cv_chan_[ch].wait(lk, [&] { return stop_.load() || my_seq.load() != seen; });
         }
         if (stop_.load()) return;
-        seen = job_seq_.load(std::memory_order_acquire);
-        // job_ was written before job_seq_ was bumped and is not rewritten until every channel
-        // finished this job, so reading it here needs no lock.
+        seen = my_seq.load(std::memory_order_acquire);
+        // job_ was written before this channel's sequence number was bumped and is not rewritten
+        // until every woken channel finished this job, so reading it here needs no lock.
         const std::function<bool(int)> job = job_;
         if (!job(ch)) job_ok_.store(false);
         if (job_pending_.fetch_sub(1, std::memory_order_acq_rel) == 1) {
@@ -388,16 +391,20 @@ void HostEngine::WorkerLoop(int ch) {
     }
 }
 
-bool HostEngine::RunOnChannels(const std::function<bool(int)>& fn, int inline_ch) {
+bool HostEngine::RunOnChannels(const std::function<bool(int)>& fn, int inline_ch, const std::vector<int>& busy) {
+    std::vector<int> woken;
     {
         std::lock_guard<std::mutex> lk(mu_);
-        // Channel inline_ch runs on the calling thread; its worker only reports in.
-        job_ = [&fn, inline_ch](int ch) { return ch == inline_ch ? true : fn(ch); };
+        // Channel inline_ch runs on the calling thread; the workers of the other busy channels
+        // run theirs; the remaining workers are not woken at all.
+        job_ = fn;
         job_ok_.store(true);
-        job_pending_.store(n_channels_);
-        job_seq_.fetch_add(1, std::memory_order_release);
+        for (int ch : busy)
+            if (ch != inline_ch) woken.push_back(ch);
+        job_pending_.store(static_cast<int>(woken.size()));
+        for (int ch : woken) chan_seq_[ch].fetch_add(1, std::memory_order_release);
     }
-    cv_job_.notify_all();
+    for (int ch : woken) cv_chan_[ch].notify_one();
     if (inline_ch >= 0 && !fn(inline_ch)) job_ok_.store(false);
     if (spin_) {
         const auto until = Clock::now() + std::chrono::microseconds(kSpinUs);
@@ -1008,10 +1015,11 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
                 if (!RunSlice(ch, *u.task, u.e0, u.e1)) return false;
             return true;
         };
-        int busy = 0, last = -1;
+        std::vector<int> busy;
+        int last = -1;
         for (int ch = 0; ch < n_channels_; ++ch) {
             if (!plan[static_cast<size_t>(ch)].empty()) {
-                ++busy;
+                busy.push_back(ch);
                 last = ch;
             }
         }
@@ -1019,9 +1027,9 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
         // no hand-off to a worker. Otherwise the workers run the others while this thread runs
         // the last one. The per-channel barriers are in shared memory, so which thread of a rank
         // runs a channel does not matter to the other ranks.
-        if (busy == 1) {
+        if (busy.size() == 1) {
             if (!run(last)) return false;
-        } else if (!RunOnChannels(run, last)) {
+        } else if (!RunOnChannels(run, last, busy)) {
             return false;
         }
     }

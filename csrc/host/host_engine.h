@@ -130,9 +130,9 @@ private:
                         const std::vector<size_t>& send_bytes, const std::vector<void*>& recv,
                         const std::vector<size_t>& recv_bytes);
     bool RunP2p(const std::vector<CollTask>& tasks);
-    // Runs fn(ch) for every channel on the channel threads and waits; channel inline_ch (if >= 0)
-    // runs on the calling thread instead.
-    bool RunOnChannels(const std::function<bool(int)>& fn, int inline_ch = -1);
+    // Runs fn(ch) for every channel in `busy` and waits: channel inline_ch (one of them) on the
+    // calling thread, the others on their channel threads; channels not in `busy` stay asleep.
+    bool RunOnChannels(const std::function<bool(int)>& fn, int inline_ch, const std::vector<int>& busy);
     void WorkerLoop(int ch);
     char* Slot(int ch, int rank) { return chans_[ch].slots + static_cast<size_t>(rank) * slot_bytes_; }
     // Switches channel ch to the other buffer set; called at the start of every chunk.
@@ -173,9 +173,12 @@ private:
     // Channel worker pool.
     std::vector<std::thread> workers_;
     std::mutex mu_;
-    std::condition_variable cv_job_, cv_done_;
+    std::condition_variable cv_done_;
+    // Per channel: jobs handed to its worker so far, and the worker's wake-up. Only channels
+    // with work in a job are woken (not the one the caller runs itself, not idle ones).
+    std::unique_ptr<std::atomic<uint64_t>[]> chan_seq_;
+    std::unique_ptr<std::condition_variable[]> cv_chan_;
     std::function<bool(int)> job_;
-    std::atomic<uint64_t> job_seq_{0};
     std::atomic<int> job_pending_{0};
     std::atomic<bool> job_ok_{true};
     std::atomic<bool> stop_{false};
