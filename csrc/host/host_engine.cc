@@ -1036,9 +1036,10 @@ bool HostEngine::Execute(const std::vector<CollTask>& sorted) {
     return RunP2p(p2p);
 }
 
-// The whole batch becomes one job per channel thread. A collective of at least
-// split_bytes_ (BCCL_HOST_SPLIT_BYTES; default 256 KiB with four channels, else 1 MiB) is cut into one slice per channel; a smaller one goes whole to the channel with
-// the fewest bytes so far (ties: lowest index). The plan depends only on the sorted task list,
+// The whole batch becomes one job per channel thread. A collective of at least split_bytes_
+// (BCCL_HOST_SPLIT_BYTES; default 256 KiB with four channels, else 1 MiB) is cut into one slice
+// per channel; a smaller one goes whole to the channel with the fewest bytes so far (ties: lowest
+// index). The plan depends only on the sorted task list,
 // which every rank builds identically, so channel c runs the same slices in the same order on
 // every rank and the per-channel barriers and connections line up. This is the reference's
 // dynamic executor's goal (many small collectives spread over the channels instead of each one
